@@ -1,0 +1,438 @@
+"""Benchmark of the NVFP4 MoE layer on B200 (driver contract: one JSON line).
+
+Workload (the decode metric's batched configuration):
+one Qwen3.5-MoE-shape layer (hidden 2048, 256 routed experts x intermediate
+512, top-8 + shared expert), 32 independent BF16 tokens per step, all 257
+experts resident in HBM. A step is one layer forward over one batch. Inputs
+rotate through a pool of distinct token batches (so the routed experts
+change step to step) and L2 is flushed (256 MiB write) before every step,
+outside that step's CUDA-event pair.
+
+  value      tokens/s over all ranks, device time (sum of per-step events,
+             max over ranks)
+  e2e        the same metric through the lab-style C-ABI call sequence with
+             host buffers: buffer upload (pinned host -> device), bank
+             forward, runtime synchronize, buffer download, wall clock
+  roofline   dominant kernel (moe_gate_up): algorithmic bytes per launch /
+             its average CUDA-event duration, against MEASURED_PEAKS hbm_gbs
+  cpu_baseline  the C restatement of the lab's CPU path (oracle/cpu_moe.c)
+             on this host's cores, on a bounded sample
+
+--gpus N (under torchrun) runs N independent replicas, one bank per GPU and
+a distinct token stream per rank (weak scaling, no collective).
+--impl reference times the lab's CPU path (the C restatement) for the same
+workload and prints its own JSON line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+PKG_ROOT = ROOT / "x2-nvfp4-lab_b200"
+for _p in (ROOT, PKG_ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+E, H, I = 256, 2048, 512
+PER_PROJ_BYTES = H * I // 2 + H * I // 16  # packed + scales of one projection
+METRIC = "MoE layer decode tokens/s (µs/token = 1e6 / value)"
+UNIT = "tokens/s"
+WORKLOAD = "config1_decode_batch32"
+
+
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--tokens", type=int, default=32)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    return p.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def measured_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": smax,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# --------------------------------------------------------------- CPU leg
+
+
+def cpu_baseline_measure(tokens: int, seed: int, min_seconds: float = 10.0, max_steps: int = 200) -> dict:
+    """Time the C restatement of the lab's CPU path (oracle/cpu_moe.c) on a
+    full-size synthetic bank: batches of `tokens` tokens until at least
+    `min_seconds` of CPU work (at least 2 batches, at most `max_steps`)."""
+    import numpy as np
+
+    from oracle import cpu_oracle, synthetic_np
+
+    from vllm_nvfp4_cuda import synthetic
+
+    threads = os.cpu_count() or 1
+    # Full 257-expert bank generated on the host (torch CPU), device layout.
+    meta = synthetic.synthetic_router(E, H, seed)
+    packed = [np.empty((E + 1) * H * I // 2, dtype=np.uint8) for _ in range(3)]
+    scales = [np.empty((E + 1) * H * I // 16, dtype=np.uint8) for _ in range(3)]
+    inv = np.zeros((3, E + 1), dtype=np.float32)
+    pp, ps = H * I // 2, H * I // 16
+    for e in range(E + 1):
+        for p in range(3):
+            pk, sc, div = synthetic.synthetic_expert_projection(e, p, H, I, seed, device="cpu")
+            packed[p][e * pp:(e + 1) * pp] = pk.numpy().reshape(-1)
+            scales[p][e * ps:(e + 1) * ps] = sc.numpy().reshape(-1)
+            inv[p, e] = np.float32(1.0) / np.float32(div)
+    router = np.ascontiguousarray(np.concatenate(
+        [meta.router_bf16.numpy().view(np.uint16), meta.shared_gate_bf16.numpy().view(np.uint16)[None]]))
+    dense = cpu_oracle.DenseBank(E, H, I, packed, scales, inv, router, None)
+    x = synthetic_np.tokens_f32(tokens, H, seed + 998)
+    dense.forward(x[:1], threads=threads)  # warm
+    xs = [synthetic_np.tokens_f32(tokens, H, seed + s) for s in range(8)]
+    steps = 0
+    t0 = time.perf_counter()
+    while steps < max_steps and (steps < 2 or time.perf_counter() - t0 < min_seconds):
+        dense.forward(xs[steps % len(xs)], threads=threads)
+        steps += 1
+    dt = time.perf_counter() - t0
+    return {
+        "value": round(tokens * steps / dt, 3),
+        "unit": UNIT,
+        "cores": threads,
+        "kind": "port",
+        "sample": f"{steps} steps x {tokens} tokens of {WORKLOAD} on the full 257-expert bank "
+                  f"(C restatement of nvfp4_cpu.cpp neon_row + layer, {threads} threads)",
+        "seconds": round(dt, 3),
+    }
+
+
+def run_reference(args) -> int:
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    cpu = cpu_baseline_measure(args.tokens, args.seed, min_seconds=min(20.0, 2.0 * max(1, args.steps)))
+    steps = int(cpu["sample"].split()[0])
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": cpu["value"],
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": steps,
+        "warmup": 1,
+        "ms_per_step": round(1000.0 * args.tokens / cpu["value"], 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded BASELINE distributions; no checkpoint on this machine)",
+        "config": {"workload": WORKLOAD, "tokens_per_step": args.tokens, "experts": E, "hidden": H,
+                   "intermediate": I, "implementation": "lab CPU path restated in C (oracle/cpu_moe.c); "
+                   "the NEON original needs arm_neon.h and does not build on x86-64"},
+        "cpu_baseline": cpu,
+        "e2e": {"value": cpu["value"], "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------- GPU leg
+
+
+def run_ours(args) -> int:
+    import numpy as np
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+
+    from vllm_nvfp4_cuda import synthetic
+    from vllm_nvfp4_cuda.runtime import Runtime
+
+    T = args.tokens
+    rt = Runtime()
+    bank, meta = synthetic.build_bank(rt, E, H, I, args.seed)
+    stream = torch.cuda.Stream()
+    pool_n = 16
+    pool = [synthetic.synthetic_tokens(T, H, 1000 * (rank + 1) + i) for i in range(pool_n)]
+    res_pool = [synthetic.synthetic_tokens(T, H, 5000 * (rank + 1) + i) for i in range(pool_n)]
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+
+    # Routing of every pool batch -> algorithmic bytes of each step.
+    uniq = []
+    for i in range(pool_n):
+        with torch.cuda.stream(stream):
+            bank.forward(pool[i], residual=res_pool[i], out=out, stream=stream)
+        stream.synchronize()
+        r = bank.last_routing(T)
+        uniq.append(len(set(r.ids[:, :8].reshape(-1).tolist())))
+    gate_up_bytes = [(u + 1) * 2 * PER_PROJ_BYTES + T * H * 2 + T * 9 * I * 2 for u in uniq]
+    step_bytes = [(u + 1) * 3 * PER_PROJ_BYTES + (E + 1) * H * 2 + 3 * T * H * 2 for u in uniq]
+
+    def step(i):
+        bank.forward(pool[i % pool_n], residual=res_pool[i % pool_n], out=out, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            flush.zero_()
+            step(i)
+    stream.synchronize()
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    rt.set_trace_enabled(True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            for i in range(args.steps):
+                flush.zero_()
+                starts[i].record(stream)
+                step(i)
+                ends[i].record(stream)
+        stream.synchronize()
+        rt.synchronize()
+    events = rt.trace_events()
+    rt.set_trace_enabled(False)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = float(sum(step_ms))
+    if pg:
+        t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * T * args.steps / (total_ms / 1000.0)
+
+    by_op: dict[str, list[float]] = {}
+    for ev in events:
+        by_op.setdefault(ev.operation, []).append(ev.duration_ns / 1e6)
+    gu = by_op.get("moe_gate_up", [])
+    gu_bytes = sum(gate_up_bytes[i % pool_n] for i in range(len(gu)))
+    gu_ms = sum(gu)
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs")
+    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else None
+    traffic_path = ROOT / "profiles" / "traffic.json"
+    traffic = None
+    if traffic_path.exists():
+        traffic = json.loads(traffic_path.read_text()).get(f"moe_gate_up_T{T}")
+    layer_bytes = sum(step_bytes[i % pool_n] for i in range(args.steps))
+
+    # T=1 latency (BASELINE config 0 target), same protocol.
+    lat = []
+    with torch.cuda.stream(stream):
+        x1 = [p[:1].contiguous() for p in pool]
+        o1 = torch.empty(1, H, dtype=torch.bfloat16, device="cuda")
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(40)]
+        for i in range(45):
+            flush.zero_()
+            if i >= 5:
+                ev[i - 5][0].record(stream)
+            bank.forward(x1[i % pool_n], out=o1, stream=stream)
+            if i >= 5:
+                ev[i - 5][1].record(stream)
+    stream.synchronize()
+    lat = sorted(a.elapsed_time(b) * 1000.0 for a, b in ev)
+
+    # End to end through the lab-style C-ABI sequence with host buffers.
+    host_x = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
+    host_r = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
+    for i in range(pool_n):
+        host_x[i].copy_(pool[i].cpu())
+        host_r[i].copy_(res_pool[i].cpu())
+    host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    xb = rt.create_buffer(T * H * 2)
+    rb = rt.create_buffer(T * H * 2)
+    ob = rt.create_buffer(T * H * 2)
+    hx = [h.view(torch.int16).numpy() for h in host_x]
+    hr = [h.view(torch.int16).numpy() for h in host_r]
+    ho = host_out.view(torch.int16).numpy()
+    import ctypes as C
+
+    def e2e_step(i):
+        xb.upload(hx[i % pool_n])
+        rb.upload(hr[i % pool_n])
+        bank.forward_device(xb, T, ob, residual=rb)
+        rt.synchronize()
+        rt._check(rt.lib.nvfp4_buffer_download(ob.handle, 0, C.c_void_p(ho.ctypes.data), ho.nbytes),
+                  "buffer_download")
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    if pg:
+        pg.barrier()
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        e2e_step(i)
+    e2e_s = time.perf_counter() - t0
+    if pg:
+        t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e_value = world * T * args.steps / e2e_s
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_measure(T, args.seed)
+
+    if rank == 0:
+        clk = clocks.summary()
+        line = {
+            "metric": METRIC,
+            "value": round(value, 1),
+            "unit": UNIT,
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(total_ms / args.steps, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "nvfp4 weights x f16 activations, f32 accumulate; bf16 I/O",
+            "data": "synthetic (seeded BASELINE distributions; no checkpoint on this machine)",
+            "config": {
+                "workload": WORKLOAD,
+                "tokens_per_step": T,
+                "global_batch": T * world,
+                "experts": E,
+                "hidden": H,
+                "intermediate": I,
+                "top_k": 8,
+                "shared_expert": True,
+                "layers": 1,
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "l2": "flushed before every step (256 MiB write) outside the per-step CUDA events",
+                "inputs": f"pool of {pool_n} distinct token batches per rank",
+                "mean_unique_routed_experts": round(float(np.mean(uniq)), 2),
+            },
+            "us_per_token": round(1e6 / value * world, 4) if world == 1 else None,
+            "layer_hbm_gbs": round(layer_bytes / (total_ms / 1000.0) / 1e9, 1),
+            "decode_t1_us": {"median": round(lat[len(lat) // 2], 3), "p10": round(lat[len(lat) // 10], 3),
+                             "p90": round(lat[(9 * len(lat)) // 10], 3)},
+            "kernels_ms_avg": {k: round(sum(v) / len(v), 5) for k, v in by_op.items()},
+            "roofline": {
+                "kernel": "moe_gate_up",
+                "bound": "hbm",
+                "achieved": round(achieved, 1) if achieved else None,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": round(achieved / peak, 4) if achieved and peak else None,
+                "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst copy), of measured" if peak else "missing",
+                "traffic": traffic,
+                "algorithmic_bytes_per_launch": round(gu_bytes / max(1, len(gu))),
+            },
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2},
+            "gpu_launches": 3 * args.steps,
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    for b in (xb, rb, ob):
+        b.close()
+    bank.close()
+    rt.close()
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    return 0
+
+
+def main() -> int:
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

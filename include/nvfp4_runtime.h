@@ -1,0 +1,368 @@
+/*
+ * nvfp4_runtime.h - C ABI of the B200 (sm_100a) NVFP4 mixture-of-experts bank.
+ *
+ * This is a drop-in replacement for the MoE-bank slice of the lab runtime's
+ * C ABI (native_nvfp4/runtime/nvfp4_runtime.h in hotschmoe/x2-nvfp4-lab).
+ * Every symbol marked "reference:" keeps the reference's name, argument order,
+ * argument meaning and status codes; the line cited is the declaration it
+ * replaces. Symbols marked "additive:" have no reference counterpart; they
+ * follow the same conventions (status return, thread-local last error,
+ * asynchronous enqueue on the runtime's in-order stream).
+ *
+ * Conventions shared by every entry point
+ *  - Functions return nvfp4_status; on failure nvfp4_last_error() returns a
+ *    thread-local message. It is cleared by the next successful call.
+ *  - "enqueue" functions are asynchronous on the runtime's single in-order
+ *    CUDA stream; results are valid after nvfp4_runtime_synchronize().
+ *  - Host arrays passed to upload functions are copied before the call
+ *    returns; the caller may free them afterwards.
+ *  - A runtime must outlive every buffer and bank created from it.
+ *  - There is no CPU execution path: every compute entry point launches CUDA
+ *    kernels built for sm_100a and fails with NVFP4_STATUS_CUDA_ERROR when no
+ *    such device is present.
+ */
+#ifndef NVFP4_RUNTIME_H
+#define NVFP4_RUNTIME_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#define NVFP4_API __attribute__((visibility("default")))
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* reference: nvfp4_runtime.h:21,23,25 (opaque handles). */
+typedef struct nvfp4_runtime nvfp4_runtime;
+typedef struct nvfp4_moe_bank nvfp4_moe_bank;
+typedef struct nvfp4_buffer nvfp4_buffer;
+
+/* reference: nvfp4_runtime.h:33-39. Code 2 keeps its slot; on this backend it
+ * reports a CUDA runtime error instead of an OpenCL one. */
+typedef enum nvfp4_status {
+    NVFP4_STATUS_OK = 0,
+    NVFP4_STATUS_INVALID_ARGUMENT = 1,
+    NVFP4_STATUS_OPENCL_ERROR = 2,
+    NVFP4_STATUS_CUDA_ERROR = 2,
+    NVFP4_STATUS_IO_ERROR = 3,
+    NVFP4_STATUS_INTERNAL_ERROR = 4,
+} nvfp4_status;
+
+/* reference: nvfp4_runtime.h:48-52. kernel_ns is the summed device time of
+ * the operations enqueued since the previous synchronize. */
+typedef struct nvfp4_profile {
+    uint64_t upload_ns;
+    uint64_t kernel_ns;
+    uint64_t download_ns;
+} nvfp4_profile;
+
+/* reference: nvfp4_runtime.h:54-66. */
+enum {
+    NVFP4_TRACE_SCOPE_CAPACITY = 96,
+    NVFP4_TRACE_OPERATION_CAPACITY = 64,
+};
+
+typedef struct nvfp4_trace_event {
+    char scope[NVFP4_TRACE_SCOPE_CAPACITY];
+    char operation[NVFP4_TRACE_OPERATION_CAPACITY];
+    uint64_t queued_ns;
+    uint64_t submit_ns;
+    uint64_t start_ns;
+    uint64_t end_ns;
+} nvfp4_trace_event;
+
+/* reference: nvfp4_runtime.h:75-87. svm_capabilities is always 0 here. */
+typedef struct nvfp4_device_info {
+    char platform_name[256];
+    char device_name[256];
+    char device_version[256];
+    char driver_version[256];
+    uint64_t global_memory_bytes;
+    uint64_t max_allocation_bytes;
+    uint64_t global_cache_bytes;
+    uint64_t local_memory_bytes;
+    uint32_t compute_units;
+    uint32_t max_clock_mhz;
+    uint32_t svm_capabilities;
+} nvfp4_device_info;
+
+/* ---------------------------------------------------------------- runtime */
+
+/* reference: nvfp4_runtime.h:91-93. kernel_source_path is accepted for
+ * signature compatibility and ignored (kernels are compiled ahead of time);
+ * it may be NULL. Binds the current CUDA device and creates one in-order
+ * non-blocking stream. */
+NVFP4_API nvfp4_status nvfp4_runtime_create(
+    const char * kernel_source_path,
+    nvfp4_runtime ** out_runtime);
+
+/* reference: nvfp4_runtime.h:95-100. */
+NVFP4_API void nvfp4_runtime_destroy(nvfp4_runtime * runtime);
+NVFP4_API const char * nvfp4_runtime_device_name(const nvfp4_runtime * runtime);
+NVFP4_API const char * nvfp4_last_error(void);
+NVFP4_API nvfp4_status nvfp4_runtime_last_profile(
+    const nvfp4_runtime * runtime,
+    nvfp4_profile * out_profile);
+
+/* reference: nvfp4_runtime.h:102-104. */
+NVFP4_API nvfp4_status nvfp4_runtime_query_device(
+    const nvfp4_runtime * runtime,
+    nvfp4_device_info * out_info);
+
+/* reference: nvfp4_runtime.h:106. Waits for the stream, then publishes
+ * last_profile.kernel_ns and (when tracing) the completed trace. */
+NVFP4_API nvfp4_status nvfp4_runtime_synchronize(nvfp4_runtime * runtime);
+
+/* reference: nvfp4_runtime.h:111-122. Trace timestamps come from CUDA event
+ * pairs around each enqueued operation. */
+NVFP4_API nvfp4_status nvfp4_runtime_trace_set_enabled(
+    nvfp4_runtime * runtime,
+    int enabled);
+NVFP4_API nvfp4_status nvfp4_runtime_trace_set_scope(
+    nvfp4_runtime * runtime,
+    const char * scope);
+NVFP4_API size_t nvfp4_runtime_trace_count(
+    const nvfp4_runtime * runtime);
+NVFP4_API nvfp4_status nvfp4_runtime_trace_read(
+    const nvfp4_runtime * runtime,
+    size_t index,
+    nvfp4_trace_event * out_event);
+
+/* additive: the runtime's cudaStream_t, so a host framework can order its
+ * own work against the runtime's queue. */
+NVFP4_API void * nvfp4_runtime_stream(const nvfp4_runtime * runtime);
+
+/* additive: number of streaming multiprocessors of the bound device. */
+NVFP4_API int nvfp4_runtime_sm_count(const nvfp4_runtime * runtime);
+
+/* ---------------------------------------------------------------- buffers */
+
+/* reference: nvfp4_runtime.h:179-203. Device memory from cudaMalloc. */
+NVFP4_API nvfp4_status nvfp4_buffer_create(
+    nvfp4_runtime * runtime,
+    size_t bytes,
+    nvfp4_buffer ** out_buffer);
+NVFP4_API void nvfp4_buffer_destroy(nvfp4_buffer * buffer);
+NVFP4_API nvfp4_status nvfp4_buffer_upload(
+    nvfp4_buffer * buffer,
+    size_t offset,
+    const void * data,
+    size_t bytes);
+NVFP4_API nvfp4_status nvfp4_buffer_download(
+    const nvfp4_buffer * buffer,
+    size_t offset,
+    void * data,
+    size_t bytes);
+NVFP4_API nvfp4_status nvfp4_buffer_copy_enqueue(
+    const nvfp4_buffer * source,
+    size_t source_offset,
+    nvfp4_buffer * destination,
+    size_t destination_offset,
+    size_t bytes);
+
+/* additive: the buffer's device address and its size in bytes. */
+NVFP4_API void * nvfp4_buffer_device_pointer(const nvfp4_buffer * buffer);
+NVFP4_API size_t nvfp4_buffer_bytes(const nvfp4_buffer * buffer);
+
+/* ------------------------------------------------------ graph primitives */
+
+/* reference: nvfp4_runtime.h:345-350. dst[i] = a[i] + b[i]. */
+NVFP4_API nvfp4_status nvfp4_add_device_enqueue_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_buffer * a,
+    const nvfp4_buffer * b,
+    int elements,
+    nvfp4_buffer * dst);
+
+/* reference: nvfp4_runtime.h:352-358. dst = (reset ? 0 : dst) + scale*source. */
+NVFP4_API nvfp4_status nvfp4_weighted_accumulate_device_enqueue_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_buffer * source,
+    float scale,
+    nvfp4_buffer * dst,
+    int elements,
+    int reset);
+
+/* reference: nvfp4_runtime.h:360-365. dst = gate*sigmoid(gate)*up. */
+NVFP4_API nvfp4_status nvfp4_silu_mul_device_enqueue_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_buffer * gate,
+    const nvfp4_buffer * up,
+    int elements,
+    nvfp4_buffer * dst);
+
+/* reference: nvfp4_runtime.h:367-374. Row-wise FP32 RMSNorm. */
+NVFP4_API nvfp4_status nvfp4_rmsnorm_device_enqueue_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_buffer * x,
+    const nvfp4_buffer * weight,
+    int rows,
+    int cols,
+    float epsilon,
+    nvfp4_buffer * dst);
+
+/* reference: nvfp4_runtime.h:384-390. dst[r] = sum_c bf16(W[r,c]) * x[c]
+ * with x FP32; products accumulate in FP64 and round to FP32 once. */
+NVFP4_API nvfp4_status nvfp4_bf16_gemv_device_enqueue(
+    nvfp4_runtime * runtime,
+    const nvfp4_buffer * weights,
+    const nvfp4_buffer * x,
+    int rows,
+    int cols,
+    nvfp4_buffer * dst);
+
+/* additive: BF16 RMSNorm over [rows, cols] with an FP32 statistic and a BF16
+ * weight, BF16 output (the pre-norm of the resident layer stack). */
+NVFP4_API nvfp4_status nvfp4_rmsnorm_device_enqueue_bf16(
+    nvfp4_runtime * runtime,
+    const nvfp4_buffer * x,
+    const nvfp4_buffer * weight,
+    int rows,
+    int cols,
+    float epsilon,
+    nvfp4_buffer * dst);
+
+/* ------------------------------------------------------------- MoE bank */
+
+/* reference: nvfp4_runtime.h:392-403 (implemented at
+ * native_nvfp4/runtime/nvfp4_runtime.cpp:1780-1856). Expert indices
+ * [0, experts) are routed; index `experts` is the always-on shared expert.
+ * experts in [8,256]; hidden and intermediate positive multiples of 16;
+ * router_bytes == experts*hidden*2; shared_gate_bytes == hidden*2.
+ * This backend additionally needs hidden and intermediate to be multiples
+ * of 128 and reports INVALID_ARGUMENT otherwise. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_create(
+    nvfp4_runtime * runtime,
+    const uint16_t * router_bf16,
+    size_t router_bytes,
+    const uint16_t * shared_gate_bf16,
+    size_t shared_gate_bytes,
+    int experts,
+    int hidden,
+    int intermediate,
+    nvfp4_moe_bank ** out_bank);
+
+/* reference: nvfp4_runtime.h:405-414 (nvfp4_runtime.cpp:1858-1911).
+ * projection: 0=gate [intermediate,hidden], 1=up [intermediate,hidden],
+ * 2=down [hidden,intermediate]. packed is row-major E2M1 pairs (low nibble =
+ * even column), scales_e4m3 one byte per 16 columns. weight_global_scale is a
+ * divisor: dequantised w = E2M1 * E4M3(scale) / weight_global_scale.
+ * Scale bytes are stored with the sign bit cleared and 0x7F mapped to 0, the
+ * reference's scale-decoding rule (nvfp4_gemv.cl:14-27). Synchronises the
+ * runtime stream before writing, as the reference does. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection(
+    nvfp4_moe_bank * bank,
+    int expert,
+    int projection,
+    const uint8_t * packed,
+    size_t packed_bytes,
+    const uint8_t * scales_e4m3,
+    size_t scale_bytes,
+    float weight_global_scale);
+
+/* reference: nvfp4_runtime.h:416-419 (nvfp4_runtime.cpp:1913-2074).
+ * Single-token decode: x FP32 [hidden], dst FP32 [hidden] =
+ * sum_k w_k * expert_k(x) + sigmoid(shared_gate . x) * shared(x), without
+ * the residual. Requires every routed and shared projection uploaded. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_decode_device_enqueue_f32(
+    nvfp4_moe_bank * bank,
+    const nvfp4_buffer * x,
+    nvfp4_buffer * dst);
+
+/* reference: nvfp4_runtime.h:421 (nvfp4_runtime.cpp:2076-2082). Drains the
+ * stream first. */
+NVFP4_API void nvfp4_moe_bank_destroy(nvfp4_moe_bank * bank);
+
+/* additive: upload one projection from DEVICE memory (same layout and
+ * semantics as nvfp4_moe_bank_upload_projection). Enqueued on the runtime
+ * stream; the source must stay valid until the next synchronize. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection_device(
+    nvfp4_moe_bank * bank,
+    int expert,
+    int projection,
+    const void * packed_device,
+    size_t packed_bytes,
+    const void * scales_device,
+    size_t scale_bytes,
+    float weight_global_scale);
+
+/* additive: flags for the batched forward. */
+enum {
+    NVFP4_MOE_ADD_RESIDUAL = 1u << 0,
+};
+
+/* additive: batched layer forward with BF16 I/O. x and residual are BF16
+ * [tokens, hidden] buffers, dst BF16 [tokens, hidden]:
+ *   dst = (flags & NVFP4_MOE_ADD_RESIDUAL ? residual : 0)
+ *         + sum_k w_k * expert_k(x) + sigmoid(shared_gate . x) * shared(x).
+ * residual may be NULL when the flag is clear. tokens >= 1. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_forward_device_enqueue_bf16(
+    nvfp4_moe_bank * bank,
+    const nvfp4_buffer * x,
+    const nvfp4_buffer * residual,
+    int tokens,
+    int flags,
+    nvfp4_buffer * dst);
+
+/* additive: the same forward on raw device pointers, enqueued on `stream`
+ * (a cudaStream_t; NULL selects the runtime's stream). For host frameworks
+ * whose tensors are not nvfp4_buffer objects. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(
+    nvfp4_moe_bank * bank,
+    const void * x_bf16,
+    const void * residual_bf16,
+    void * dst_bf16,
+    int tokens,
+    int flags,
+    void * stream);
+
+/* additive: routing introspection of the most recent forward or decode.
+ * Call after nvfp4_runtime_synchronize(). Any output pointer may be NULL.
+ *   ids      int32 [tokens, 9]  top-8 ids by descending logit (lowest id on
+ *                               ties), slot 8 = experts (the shared expert)
+ *   weights  float [tokens, 9]  renormalised top-8 softmax, slot 8 = sigmoid
+ *   counts   int32 [experts]    tokens routed to each expert
+ *   perm     int32 [tokens*8]   dispatch permutation: flat (token*8 + k)
+ *                               indices grouped by expert ascending, tokens
+ *                               ascending within an expert
+ * max_tokens bounds the ids/weights/perm writes; *out_tokens receives the
+ * token count of the last call. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_last_routing(
+    nvfp4_moe_bank * bank,
+    int max_tokens,
+    int32_t * ids,
+    float * weights,
+    int32_t * counts,
+    int32_t * perm,
+    int * out_tokens);
+
+/* additive: router logits of the most recent forward or decode, FP32
+ * [tokens, experts + 1]; column `experts` holds the shared-gate logit. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_last_logits(
+    nvfp4_moe_bank * bank,
+    int max_tokens,
+    float * logits,
+    int * out_tokens);
+
+/* additive: FP32 per-expert router logit bias [experts] (the skewed-routing
+ * configuration). Routing uses logit_e = fp32(router_e . x) + bias_e; pass
+ * NULL to clear. Synchronises the runtime stream before writing. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_set_router_bias(
+    nvfp4_moe_bank * bank,
+    const float * bias,
+    int experts);
+
+/* additive: bank geometry and resident device bytes. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_info(
+    const nvfp4_moe_bank * bank,
+    int * experts,
+    int * hidden,
+    int * intermediate,
+    size_t * resident_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* NVFP4_RUNTIME_H */

@@ -1,0 +1,234 @@
+"""CUDA path vs the CPU oracle, through the C ABI (needs an sm_100a GPU).
+
+Routing ids, dispatch permutations and counts are compared bit-exactly;
+router logits bit-exactly (same FP64 lane order on both sides); layer
+outputs within the BASELINE tolerance: relative RMSE <= 2e-3 and
+max-abs-relative <= 1e-2 against the FP32 dequantise-then-matmul oracle.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import synthetic_np
+from oracle.nvfp4_oracle import BankHost, QuantizedMatrix, max_abs_rel, moe_layer, rel_rmse, router_logits
+
+from helpers import MAX_ABS_REL_TOL, REL_RMSE_TOL, bf16_tensor_to_f32, bits_to_bf16_tensor, upload_bank
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def small_host():
+    return synthetic_np.make_bank(16, 256, 128, 21)
+
+
+@pytest.fixture(scope="module")
+def wide_host():
+    # 256 experts (the real top-8 of 256 selection) at a reduced width.
+    return synthetic_np.make_bank(256, 512, 256, 22)
+
+
+@pytest.fixture(scope="module")
+def small_bank(cuda_runtime, small_host):
+    bank = upload_bank(cuda_runtime, small_host)
+    yield bank
+    bank.close()
+
+
+@pytest.fixture(scope="module")
+def wide_bank(cuda_runtime, wide_host):
+    bank = upload_bank(cuda_runtime, wide_host)
+    yield bank
+    bank.close()
+
+
+def check_routing(bank, ref, T):
+    r = bank.last_routing(T)
+    np.testing.assert_array_equal(r.ids, ref.ids)
+    np.testing.assert_allclose(r.weights, ref.weights, rtol=2e-6, atol=1e-7)
+    np.testing.assert_array_equal(r.counts, ref.counts)
+    np.testing.assert_array_equal(r.perm, ref.perm)
+
+
+def test_reference_decode_abi_f32(cuda_runtime, small_bank, small_host):
+    rt = cuda_runtime
+    H = small_host.hidden
+    x = (synthetic_np.tokens_f32(1, H, 31) * np.float32(0.2)).astype(np.float32)
+    xb = rt.upload_buffer(np.ascontiguousarray(x[0]))
+    out = rt.create_buffer(H * 4)
+    small_bank.decode_device(xb, out)
+    rt.synchronize()
+    got = out.download((1, H))
+    ref = moe_layer(small_host, x)
+    np.testing.assert_array_equal(small_bank.last_logits(1).view(np.uint32), ref.logits.view(np.uint32))
+    check_routing(small_bank, ref, 1)
+    assert rel_rmse(got, ref.out) <= REL_RMSE_TOL
+    assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL
+    xb.close()
+    out.close()
+
+
+@pytest.mark.parametrize("T", [1, 2, 3, 8, 9, 16, 31, 32, 33, 64])
+def test_forward_bf16_batched(cuda_runtime, wide_bank, wide_host, T):
+    import torch
+
+    H = wide_host.hidden
+    xbits = synthetic_np.tokens_bf16(T, H, 100 + T)
+    rbits = synthetic_np.tokens_bf16(T, H, 200 + T)
+    x = bits_to_bf16_tensor(xbits)
+    res = bits_to_bf16_tensor(rbits)
+    out = wide_bank.forward(x, residual=res)
+    torch.cuda.synchronize()
+    ref = moe_layer(wide_host, synthetic_np.bf16_bits_to_f32(xbits), synthetic_np.bf16_bits_to_f32(rbits))
+    logits = wide_bank.last_logits(T)
+    np.testing.assert_array_equal(logits.view(np.uint32), ref.logits.view(np.uint32))
+    check_routing(wide_bank, ref, T)
+    got = bf16_tensor_to_f32(out)
+    assert rel_rmse(got, ref.out) <= REL_RMSE_TOL
+    assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL
+    # The MoE contribution alone (residual removed) stays within tolerance too.
+    moe_only = ref.out - synthetic_np.bf16_bits_to_f32(rbits)
+    assert rel_rmse(got - synthetic_np.bf16_bits_to_f32(rbits), moe_only) <= 2e-2
+
+
+def test_forward_without_residual_and_buffers(cuda_runtime, small_bank, small_host):
+    rt = cuda_runtime
+    T, H = 5, small_host.hidden
+    xbits = synthetic_np.tokens_bf16(T, H, 41)
+    xb = rt.upload_buffer(np.ascontiguousarray(xbits))
+    out = rt.create_buffer(T * H * 2)
+    small_bank.forward_device(xb, T, out)
+    rt.synchronize()
+    got = synthetic_np.bf16_bits_to_f32(out.download((T, H), np.uint16))
+    ref = moe_layer(small_host, synthetic_np.bf16_bits_to_f32(xbits))
+    check_routing(small_bank, ref, T)
+    assert rel_rmse(got, ref.out) <= REL_RMSE_TOL
+    xb.close()
+    out.close()
+
+
+def test_forward_more_than_64_tokens(cuda_runtime, small_bank, small_host):
+    import torch
+
+    T, H = 150, small_host.hidden
+    xbits = synthetic_np.tokens_bf16(T, H, 51)
+    rbits = synthetic_np.tokens_bf16(T, H, 52)
+    out = small_bank.forward(bits_to_bf16_tensor(xbits), residual=bits_to_bf16_tensor(rbits))
+    torch.cuda.synchronize()
+    ref = moe_layer(small_host, synthetic_np.bf16_bits_to_f32(xbits), synthetic_np.bf16_bits_to_f32(rbits))
+    got = bf16_tensor_to_f32(out)
+    assert rel_rmse(got, ref.out) <= REL_RMSE_TOL
+    assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL
+
+
+def test_skewed_routing(cuda_runtime):
+    import torch
+
+    host = synthetic_np.make_bank(64, 256, 128, 61, skew=True)
+    bank = upload_bank(cuda_runtime, host)
+    T, H = 48, 256
+    xbits = synthetic_np.tokens_bf16(T, H, 62)
+    out = bank.forward(bits_to_bf16_tensor(xbits))
+    torch.cuda.synchronize()
+    ref = moe_layer(host, synthetic_np.bf16_bits_to_f32(xbits))
+    check_routing(bank, ref, T)
+    # Skew concentrates load on the top-ranked experts.
+    assert ref.counts.max() >= 3 * ref.counts.mean()
+    assert rel_rmse(bf16_tensor_to_f32(out), ref.out) <= REL_RMSE_TOL
+    bank.close()
+
+
+def test_config0_full_size_bank(cuda_runtime):
+    """BASELINE config 0 and 1 shapes (256 x 512 experts, hidden 2048) with a
+    GPU-generated bank; the oracle receives the selected experts' bytes."""
+    import torch
+
+    from vllm_nvfp4_cuda import synthetic
+
+    E, H, I, seed = 256, 2048, 512, 0
+    bank, meta = synthetic.build_bank(cuda_runtime, E, H, I, seed)
+    for T in (1, 4, 32):
+        x = synthetic.synthetic_tokens(T, H, seed + T)
+        out = bank.forward(x)
+        torch.cuda.synchronize()
+        r = bank.last_routing(T)
+        needed = sorted(set(r.ids.reshape(-1).tolist()))
+        host = BankHost(E, H, I, meta.router_bf16.numpy().view(np.uint16), meta.shared_gate_bf16.numpy().view(np.uint16))
+        for e in needed:
+            for p in range(3):
+                packed, scales, div = synthetic.synthetic_expert_projection(e, p, H, I, seed)
+                host.projections[p][e] = QuantizedMatrix(packed.cpu().numpy(), scales.cpu().numpy(), div)
+        xf = x.to(torch.float32).cpu().numpy()
+        ref = moe_layer(host, xf)
+        check_routing(bank, ref, T)
+        got = bf16_tensor_to_f32(out)
+        assert rel_rmse(got, ref.out) <= REL_RMSE_TOL, T
+        assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL, T
+    bank.close()
+
+
+def test_graph_primitives(cuda_runtime):
+    rt = cuda_runtime
+    rng = np.random.default_rng(5)
+    n = 3000
+    a = rng.standard_normal(n).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    ba, bb = rt.upload_buffer(a), rt.upload_buffer(b)
+    out = rt.create_buffer(n * 4)
+    rt.add_device(ba, bb, n, out)
+    rt.synchronize()
+    np.testing.assert_allclose(out.download((n,)), a + b, rtol=3e-5, atol=3e-5)
+    rt.silu_mul_device(ba, bb, n, out)
+    rt.synchronize()
+    np.testing.assert_allclose(out.download((n,)), a / (1 + np.exp(-a)) * b, rtol=3e-5, atol=3e-5)
+    rt.weighted_accumulate_device(ba, 0.5, out, n, reset=True)
+    rt.weighted_accumulate_device(bb, 2.0, out, n)
+    rt.synchronize()
+    np.testing.assert_allclose(out.download((n,)), 0.5 * a + 2.0 * b, rtol=3e-5, atol=3e-5)
+    rows, cols = 3, 1000
+    w = (rng.standard_normal(cols).astype(np.float32) + 1).astype(np.float32)
+    bw = rt.upload_buffer(w)
+    rt.rmsnorm_device(ba, bw, rows, cols, 1e-6, out)
+    rt.synchronize()
+    xa = a[: rows * cols].reshape(rows, cols)
+    ref = xa / np.sqrt(np.mean(xa * xa, axis=1, keepdims=True) + 1e-6) * w
+    np.testing.assert_allclose(out.download((rows, cols)), ref, rtol=3e-5, atol=3e-5)
+    # BF16 router GEMV (FP64 accumulation) against the oracle's lane-ordered dot.
+    wr = synthetic_np.router_bf16(40, 256, 9)
+    x = rng.standard_normal(256).astype(np.float32)
+    bw16, bx = rt.upload_buffer(np.ascontiguousarray(wr)), rt.upload_buffer(x)
+    bo = rt.create_buffer(40 * 4)
+    rt.bf16_gemv_device(bw16, bx, 40, 256, bo)
+    rt.synchronize()
+    np.testing.assert_allclose(bo.download((40,)), router_logits(wr, x[None])[0], rtol=1e-6, atol=1e-6)
+    for buf in (ba, bb, out, bw, bw16, bx, bo):
+        buf.close()
+
+
+def test_trace_profile_and_errors(cuda_runtime, small_bank, small_host):
+    rt = cuda_runtime
+    H = small_host.hidden
+    x = rt.upload_buffer(np.zeros(H, dtype=np.float32))
+    out = rt.create_buffer(H * 4)
+    rt.set_trace_enabled(True)
+    rt.set_trace_scope("moe.layer.00.experts")
+    small_bank.decode_device(x, out)
+    prof = rt.synchronize()
+    events = rt.trace_events()
+    rt.set_trace_enabled(False)
+    assert prof.kernel_ns > 0
+    assert [e.operation for e in events] == ["moe_route", "moe_gate_up", "moe_down"]
+    assert events[0].scope == "moe.layer.00.experts" and events[0].duration_ns > 0
+    # Argument validation mirrors the lab's messages and status codes.
+    with pytest.raises(RuntimeError, match=r"\(1\): invalid MoE bank decode buffers"):
+        small_bank.decode_device(x, rt.create_buffer(4))
+    with pytest.raises(ValueError):
+        small_bank.upload_projection(0, 3, np.zeros((1, 1), np.uint8), np.zeros((1, 1), np.uint8), 1.0)
+    partial = rt.create_moe_bank(small_host.router_bf16, small_host.shared_gate_bf16, small_host.intermediate)
+    with pytest.raises(RuntimeError, match="requires every routed and shared projection"):
+        partial.decode_device(x, out)
+    partial.close()
+    x.close()
+    out.close()

@@ -1,0 +1,457 @@
+// MoE bank entry points of the C ABI.
+//
+// Storage mirrors the lab's contiguous bank (native_nvfp4/runtime/
+// nvfp4_runtime.cpp:392-429,1780-1856): for each projection one array of
+// (experts+1) matrices, expert `experts` being the shared expert, plus one
+// FP32 inverse-global-scale table [3][experts+1] indexed
+// projection*(experts+1)+expert. The BF16 router and the shared-expert gate
+// row are stored as one [(experts+1), hidden] matrix so that the routing
+// kernel treats the shared gate as router row `experts`.
+#include "internal.h"
+#include "moe_decode.cuh"
+
+#include <cmath>
+#include <cstring>
+#include <limits>
+#include <memory>
+
+using namespace nvfp4;
+
+struct nvfp4_moe_bank {
+    nvfp4_runtime *runtime = nullptr;
+    int experts = 0;
+    int hidden = 0;
+    int intermediate = 0;
+    uint8_t *packed[3] = {nullptr, nullptr, nullptr};
+    uint8_t *scales[3] = {nullptr, nullptr, nullptr};
+    float *inv_scales = nullptr;   // device [3][experts+1]
+    uint16_t *router = nullptr;    // device [(experts+1)][hidden]
+    float *router_bias = nullptr;  // device [experts] or null
+    void *scratch = nullptr;
+    DecodeScratch ds{};
+    std::vector<uint8_t> uploaded;
+    size_t uploaded_projections = 0;
+    int last_tokens = 0;
+    int last_path = 0;             // 1 = decode path (routing record valid)
+    size_t resident_bytes = 0;
+
+    ~nvfp4_moe_bank() {
+        for (int p = 0; p < 3; ++p) {
+            if (packed[p]) cudaFree(packed[p]);
+            if (scales[p]) cudaFree(scales[p]);
+        }
+        if (inv_scales) cudaFree(inv_scales);
+        if (router) cudaFree(router);
+        if (router_bias) cudaFree(router_bias);
+        if (scratch) cudaFree(scratch);
+    }
+
+    size_t rows(int projection) const { return projection < 2 ? intermediate : hidden; }
+    size_t cols(int projection) const { return projection < 2 ? hidden : intermediate; }
+    size_t per_packed() const { return static_cast<size_t>(hidden) * intermediate / 2; }
+    size_t per_scales() const { return static_cast<size_t>(hidden) * intermediate / 16; }
+};
+
+namespace {
+
+__global__ void sanitize_scales_kernel(uint8_t *dst, const uint8_t *src, size_t n) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
+         i += (size_t)gridDim.x * blockDim.x) {
+        const uint8_t b = src[i] & 0x7Fu;
+        dst[i] = b == 0x7Fu ? 0u : b;
+    }
+}
+
+void mark_uploaded(nvfp4_moe_bank *bank, int expert, int projection) {
+    const size_t slots = static_cast<size_t>(bank->experts) + 1;
+    const size_t index = static_cast<size_t>(projection) * slots + expert;
+    if (!bank->uploaded[index]) {
+        bank->uploaded[index] = 1;
+        ++bank->uploaded_projections;
+    }
+}
+
+nvfp4_status check_upload_args(const nvfp4_moe_bank *bank, int expert, int projection,
+                               const void *packed, size_t packed_bytes, const void *scales,
+                               size_t scale_bytes, float weight_global_scale) {
+    if (!bank || !bank->runtime || !packed || !scales || expert < 0 || expert > bank->experts ||
+        projection < 0 || projection > 2 || weight_global_scale == 0.0f ||
+        !std::isfinite(weight_global_scale))
+        return fail_invalid("invalid MoE bank projection upload arguments");
+    if (packed_bytes != bank->per_packed() || scale_bytes != bank->per_scales())
+        return fail_invalid("MoE bank projection byte counts do not match dimensions");
+    return NVFP4_STATUS_OK;
+}
+
+// Enqueue the three decode-path kernels for `tokens` <= kDecodeMaxTokens,
+// each between a pair of profiling events (trace operations moe_route,
+// moe_gate_up, moe_down). Caller holds the runtime's queue mutex.
+void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const void *residual,
+                    void *out, int out_f32, int tokens, cudaStream_t stream) {
+    const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
+    const int sms = bank->runtime->sm_count;
+    RouteArgs ra{};
+    ra.router = bank->router;
+    ra.x = x;
+    ra.x_is_f32 = x_is_f32;
+    ra.T = tokens;
+    ra.E = E;
+    ra.H = H;
+    ra.inv_scales = bank->inv_scales;
+    ra.bias = bank->router_bias;
+    ra.e_first = 0;
+    ra.e_count = E;
+    ra.shared_here = 1;
+    ra.s = bank->ds;
+    nvfp4_runtime *rt = bank->runtime;
+    rt->profiled("moe_route", stream, [&](cudaStream_t s) {
+        check_cuda(launch_route(ra, s), "moe_route_kernel");
+    });
+
+    GateUpArgs ga{};
+    ga.gate_packed = bank->packed[0];
+    ga.gate_scales = bank->scales[0];
+    ga.up_packed = bank->packed[1];
+    ga.up_scales = bank->scales[1];
+    ga.inv_scales = bank->inv_scales;
+    ga.E = E;
+    ga.H = H;
+    ga.I = I;
+    ga.s = bank->ds;
+    rt->profiled("moe_gate_up", stream, [&](cudaStream_t s) {
+        check_cuda(launch_gate_up(ga, tokens, sms * 2, s), "moe_gate_up_kernel");
+    });
+
+    DownArgs da{};
+    da.down_packed = bank->packed[2];
+    da.down_scales = bank->scales[2];
+    da.residual = residual;
+    da.out = out;
+    da.out_f32 = out_f32;
+    da.T = tokens;
+    da.E = E;
+    da.H = H;
+    da.I = I;
+    da.s = bank->ds;
+    rt->profiled("moe_down", stream, [&](cudaStream_t s) {
+        check_cuda(launch_down(da, sms * 2, s), "moe_down_kernel");
+    });
+}
+
+// Batched BF16 forward: decode-path launches over slices of at most
+// kDecodeMaxTokens tokens.
+void enqueue_forward_bf16(nvfp4_moe_bank *bank, const void *x, const void *residual, void *out,
+                          int tokens, cudaStream_t stream) {
+    const size_t row_bytes = static_cast<size_t>(bank->hidden) * 2;
+    for (int t0 = 0; t0 < tokens; t0 += kDecodeMaxTokens) {
+        const int n = tokens - t0 < kDecodeMaxTokens ? tokens - t0 : kDecodeMaxTokens;
+        const uint8_t *xs = static_cast<const uint8_t *>(x) + t0 * row_bytes;
+        const uint8_t *rs = residual ? static_cast<const uint8_t *>(residual) + t0 * row_bytes : nullptr;
+        uint8_t *os = static_cast<uint8_t *>(out) + t0 * row_bytes;
+        enqueue_decode(bank, xs, 0, rs, os, 0, n, stream);
+    }
+    bank->last_tokens = tokens;
+    bank->last_path = tokens <= kDecodeMaxTokens ? 1 : 0;
+}
+
+}  // namespace
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
+                                                        const uint16_t *router_bf16,
+                                                        size_t router_bytes,
+                                                        const uint16_t *shared_gate_bf16,
+                                                        size_t shared_gate_bytes, int experts,
+                                                        int hidden, int intermediate,
+                                                        nvfp4_moe_bank **out_bank) {
+    if (!runtime || !router_bf16 || !shared_gate_bf16 || !out_bank || experts < 8 ||
+        experts > 256 || hidden <= 0 || intermediate <= 0 || hidden % 16 != 0 ||
+        intermediate % 16 != 0 ||
+        router_bytes != static_cast<size_t>(experts) * hidden * sizeof(uint16_t) ||
+        shared_gate_bytes != static_cast<size_t>(hidden) * sizeof(uint16_t))
+        return fail_invalid("invalid MoE bank creation arguments");
+    if (hidden % 128 != 0 || intermediate % 128 != 0)
+        return fail_invalid("this CUDA backend needs hidden and intermediate to be multiples of 128");
+    *out_bank = nullptr;
+    try {
+        auto holder = std::make_unique<nvfp4_moe_bank>();
+        holder->runtime = runtime;
+        holder->experts = experts;
+        holder->hidden = hidden;
+        holder->intermediate = intermediate;
+        const size_t slots = static_cast<size_t>(experts) + 1;
+        if (static_cast<size_t>(hidden) >
+            std::numeric_limits<size_t>::max() / static_cast<size_t>(intermediate) / slots)
+            throw std::overflow_error("MoE bank dimensions overflow size_t");
+        const size_t elements = slots * static_cast<size_t>(hidden) * intermediate;
+        std::lock_guard<std::mutex> lock(runtime->queue_mutex);
+        for (int p = 0; p < 3; ++p) {
+            check_cuda(cudaMalloc(&holder->packed[p], elements / 2), "cudaMalloc(MoE bank packed)");
+            check_cuda(cudaMalloc(&holder->scales[p], elements / 16), "cudaMalloc(MoE bank scales)");
+            check_cuda(cudaMemsetAsync(holder->packed[p], 0, elements / 2, runtime->stream),
+                       "cudaMemsetAsync(MoE bank packed)");
+            check_cuda(cudaMemsetAsync(holder->scales[p], 0, elements / 16, runtime->stream),
+                       "cudaMemsetAsync(MoE bank scales)");
+        }
+        check_cuda(cudaMalloc(&holder->inv_scales, 3 * slots * sizeof(float)),
+                   "cudaMalloc(MoE bank inverse scales)");
+        check_cuda(cudaMemsetAsync(holder->inv_scales, 0, 3 * slots * sizeof(float), runtime->stream),
+                   "cudaMemsetAsync(MoE bank inverse scales)");
+        const size_t router_all = slots * static_cast<size_t>(hidden) * sizeof(uint16_t);
+        check_cuda(cudaMalloc(&holder->router, router_all), "cudaMalloc(MoE bank router)");
+        check_cuda(cudaMemcpy(holder->router, router_bf16, router_bytes, cudaMemcpyHostToDevice),
+                   "cudaMemcpy(MoE bank router)");
+        check_cuda(cudaMemcpy(reinterpret_cast<uint8_t *>(holder->router) + router_bytes,
+                              shared_gate_bf16, shared_gate_bytes, cudaMemcpyHostToDevice),
+                   "cudaMemcpy(MoE bank shared gate)");
+        const size_t scratch = decode_scratch_bytes(experts, hidden, intermediate);
+        check_cuda(cudaMalloc(&holder->scratch, scratch), "cudaMalloc(MoE bank scratch)");
+        check_cuda(cudaMemsetAsync(holder->scratch, 0, scratch, runtime->stream),
+                   "cudaMemsetAsync(MoE bank scratch)");
+        decode_scratch_carve(holder->ds, holder->scratch, experts, hidden, intermediate);
+        check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize(MoE bank create)");
+        holder->uploaded.assign(slots * 3, 0);
+        holder->resident_bytes = 3 * (elements / 2 + elements / 16) + 3 * slots * sizeof(float) +
+                                 router_all;
+        clear_last_error();
+        *out_bank = holder.release();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection(
+    nvfp4_moe_bank *bank, int expert, int projection, const uint8_t *packed, size_t packed_bytes,
+    const uint8_t *scales_e4m3, size_t scale_bytes, float weight_global_scale) {
+    const nvfp4_status st = check_upload_args(bank, expert, projection, packed, packed_bytes,
+                                              scales_e4m3, scale_bytes, weight_global_scale);
+    if (st != NVFP4_STATUS_OK) return st;
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(MoE bank upload)");
+        const size_t pp = bank->per_packed(), ps = bank->per_scales();
+        std::vector<uint8_t> clean(scales_e4m3, scales_e4m3 + ps);
+        for (uint8_t &b : clean) {
+            b &= 0x7Fu;
+            if (b == 0x7Fu) b = 0u;
+        }
+        check_cuda(cudaMemcpy(bank->packed[projection] + static_cast<size_t>(expert) * pp, packed, pp,
+                              cudaMemcpyHostToDevice),
+                   "cudaMemcpy(MoE bank packed upload)");
+        check_cuda(cudaMemcpy(bank->scales[projection] + static_cast<size_t>(expert) * ps,
+                              clean.data(), ps, cudaMemcpyHostToDevice),
+                   "cudaMemcpy(MoE bank scale upload)");
+        const float inv = 1.0f / weight_global_scale;
+        const size_t slots = static_cast<size_t>(bank->experts) + 1;
+        check_cuda(cudaMemcpy(bank->inv_scales + static_cast<size_t>(projection) * slots + expert, &inv,
+                              sizeof(float), cudaMemcpyHostToDevice),
+                   "cudaMemcpy(MoE bank inverse scale)");
+        mark_uploaded(bank, expert, projection);
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection_device(
+    nvfp4_moe_bank *bank, int expert, int projection, const void *packed_device,
+    size_t packed_bytes, const void *scales_device, size_t scale_bytes, float weight_global_scale) {
+    const nvfp4_status st = check_upload_args(bank, expert, projection, packed_device, packed_bytes,
+                                              scales_device, scale_bytes, weight_global_scale);
+    if (st != NVFP4_STATUS_OK) return st;
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        const size_t pp = bank->per_packed(), ps = bank->per_scales();
+        check_cuda(cudaMemcpyAsync(bank->packed[projection] + static_cast<size_t>(expert) * pp,
+                                   packed_device, pp, cudaMemcpyDeviceToDevice, rt->stream),
+                   "cudaMemcpyAsync(MoE bank packed upload)");
+        const int grid = static_cast<int>((ps + 255) / 256 < 4096 ? (ps + 255) / 256 : 4096);
+        sanitize_scales_kernel<<<grid, 256, 0, rt->stream>>>(
+            bank->scales[projection] + static_cast<size_t>(expert) * ps,
+            static_cast<const uint8_t *>(scales_device), ps);
+        check_cuda(cudaGetLastError(), "sanitize_scales_kernel");
+        const float inv = 1.0f / weight_global_scale;
+        const size_t slots = static_cast<size_t>(bank->experts) + 1;
+        // cudaMemcpyAsync from pageable memory stages the value before returning.
+        check_cuda(cudaMemcpyAsync(bank->inv_scales + static_cast<size_t>(projection) * slots + expert,
+                                   &inv, sizeof(float), cudaMemcpyHostToDevice, rt->stream),
+                   "cudaMemcpyAsync(MoE bank inverse scale)");
+        mark_uploaded(bank, expert, projection);
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_decode_device_enqueue_f32(nvfp4_moe_bank *bank,
+                                                                           const nvfp4_buffer *x,
+                                                                           nvfp4_buffer *dst) {
+    if (!bank || !bank->runtime || !x || x->runtime != bank->runtime || !dst ||
+        dst->runtime != bank->runtime ||
+        x->bytes < static_cast<size_t>(bank->hidden) * sizeof(float) ||
+        dst->bytes < static_cast<size_t>(bank->hidden) * sizeof(float))
+        return fail_invalid("invalid MoE bank decode buffers");
+    const size_t slots = static_cast<size_t>(bank->experts) + 1;
+    if (bank->uploaded_projections != slots * 3)
+        return fail_invalid("MoE bank decode requires every routed and shared projection");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        enqueue_decode(bank, x->data, 1, nullptr, dst->data, 1, 1, rt->stream);
+        bank->last_tokens = 1;
+        bank->last_path = 1;
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(nvfp4_moe_bank *bank,
+                                                                 const void *x_bf16,
+                                                                 const void *residual_bf16,
+                                                                 void *dst_bf16, int tokens, int flags,
+                                                                 void *stream) {
+    if (!bank || !bank->runtime || !x_bf16 || !dst_bf16 || tokens <= 0 ||
+        (flags & ~static_cast<int>(NVFP4_MOE_ADD_RESIDUAL)) != 0 ||
+        ((flags & NVFP4_MOE_ADD_RESIDUAL) && !residual_bf16))
+        return fail_invalid("invalid MoE bank forward arguments");
+    const size_t slots = static_cast<size_t>(bank->experts) + 1;
+    if (bank->uploaded_projections != slots * 3)
+        return fail_invalid("MoE bank forward requires every routed and shared projection");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        const void *res = (flags & NVFP4_MOE_ADD_RESIDUAL) ? residual_bf16 : nullptr;
+        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : rt->stream;
+        enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s);
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_device_enqueue_bf16(
+    nvfp4_moe_bank *bank, const nvfp4_buffer *x, const nvfp4_buffer *residual, int tokens,
+    int flags, nvfp4_buffer *dst) {
+    if (!bank || !bank->runtime || !x || x->runtime != bank->runtime || !dst ||
+        dst->runtime != bank->runtime || tokens <= 0)
+        return fail_invalid("invalid MoE bank forward buffers");
+    const size_t bytes = static_cast<size_t>(tokens) * bank->hidden * 2;
+    if (x->bytes < bytes || dst->bytes < bytes)
+        return fail_invalid("MoE bank forward buffer capacity is too small");
+    if (flags & NVFP4_MOE_ADD_RESIDUAL) {
+        if (!residual || residual->runtime != bank->runtime || residual->bytes < bytes)
+            return fail_invalid("MoE bank forward residual buffer is missing or too small");
+    }
+    return nvfp4_moe_bank_forward_ptr_bf16(bank, x->data, residual ? residual->data : nullptr,
+                                          dst->data, tokens, flags, nullptr);
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_last_routing(nvfp4_moe_bank *bank, int max_tokens,
+                                                              int32_t *ids, float *weights,
+                                                              int32_t *counts, int32_t *perm,
+                                                              int *out_tokens) {
+    if (!bank || !bank->runtime || max_tokens < 0) return fail_invalid("invalid routing query");
+    if (bank->last_tokens == 0) return fail_invalid("no forward has run on this bank");
+    if (!bank->last_path)
+        return fail_invalid("routing record is kept for calls of at most 64 tokens");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(last_routing)");
+        const int T = bank->last_tokens < max_tokens ? bank->last_tokens : max_tokens;
+        if (ids)
+            check_cuda(cudaMemcpy(ids, bank->ds.ids, sizeof(int32_t) * T * kSlots, cudaMemcpyDeviceToHost),
+                       "cudaMemcpy(routing ids)");
+        if (weights)
+            check_cuda(cudaMemcpy(weights, bank->ds.weights, sizeof(float) * T * kSlots,
+                                  cudaMemcpyDeviceToHost),
+                       "cudaMemcpy(routing weights)");
+        if (counts)
+            check_cuda(cudaMemcpy(counts, bank->ds.counts, sizeof(int32_t) * bank->experts,
+                                  cudaMemcpyDeviceToHost),
+                       "cudaMemcpy(routing counts)");
+        if (perm && T == bank->last_tokens)
+            check_cuda(cudaMemcpy(perm, bank->ds.perm, sizeof(int32_t) * T * kTopK, cudaMemcpyDeviceToHost),
+                       "cudaMemcpy(routing perm)");
+        if (out_tokens) *out_tokens = bank->last_tokens;
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_last_logits(nvfp4_moe_bank *bank, int max_tokens,
+                                                             float *logits, int *out_tokens) {
+    if (!bank || !bank->runtime || max_tokens < 0 || !logits) return fail_invalid("invalid logits query");
+    if (bank->last_tokens == 0) return fail_invalid("no forward has run on this bank");
+    if (!bank->last_path)
+        return fail_invalid("routing record is kept for calls of at most 64 tokens");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(last_logits)");
+        const int T = bank->last_tokens < max_tokens ? bank->last_tokens : max_tokens;
+        check_cuda(cudaMemcpy(logits, bank->ds.logits, sizeof(float) * T * (bank->experts + 1),
+                              cudaMemcpyDeviceToHost),
+                   "cudaMemcpy(router logits)");
+        if (out_tokens) *out_tokens = bank->last_tokens;
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_router_bias(nvfp4_moe_bank *bank,
+                                                                 const float *bias, int experts) {
+    if (!bank || !bank->runtime || (bias && experts != bank->experts))
+        return fail_invalid("router bias must have one value per routed expert");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(router bias)");
+        if (!bias) {
+            if (bank->router_bias) cudaFree(bank->router_bias);
+            bank->router_bias = nullptr;
+        } else {
+            if (!bank->router_bias)
+                check_cuda(cudaMalloc(&bank->router_bias, sizeof(float) * bank->experts),
+                           "cudaMalloc(router bias)");
+            check_cuda(cudaMemcpy(bank->router_bias, bias, sizeof(float) * bank->experts,
+                                  cudaMemcpyHostToDevice),
+                       "cudaMemcpy(router bias)");
+        }
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_info(const nvfp4_moe_bank *bank, int *experts,
+                                                      int *hidden, int *intermediate,
+                                                      size_t *resident_bytes) {
+    if (!bank) return fail_invalid("bank is required");
+    if (experts) *experts = bank->experts;
+    if (hidden) *hidden = bank->hidden;
+    if (intermediate) *intermediate = bank->intermediate;
+    if (resident_bytes) *resident_bytes = bank->resident_bytes;
+    clear_last_error();
+    return NVFP4_STATUS_OK;
+}
+
+extern "C" NVFP4_API void nvfp4_moe_bank_destroy(nvfp4_moe_bank *bank) {
+    if (bank && bank->runtime && bank->runtime->stream) {
+        std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
+        cudaStreamSynchronize(bank->runtime->stream);
+    }
+    delete bank;
+}

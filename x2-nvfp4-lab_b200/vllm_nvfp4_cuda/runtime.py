@@ -1,0 +1,611 @@
+"""Thin ctypes ownership layer over libnvfp4_moe_cuda.so (sm_100a).
+
+Mirrors the lab's ``vllm_nvfp4_opencl/runtime.py``: the same classes
+(``Profile``, ``TraceEvent``, ``DeviceBuffer``, ``MoeBank``, ``Runtime``), the
+same method names, argument meaning and error behaviour
+(``RuntimeError(f"{op} failed ({status}): {message}")``, runtime.py:820-823),
+and the same process-wide ``get_runtime()`` singleton behind a lock
+(runtime.py:1964-1976). There is no CPU execution path: when the CUDA
+library or an sm_100a device is missing, construction raises.
+
+Additions over the lab surface are marked "additive" and cover BF16 batched
+forwards on torch tensors, routing introspection and device-side uploads.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import os
+import threading
+from dataclasses import dataclass
+from pathlib import Path
+
+import numpy as np
+
+LIB_NAME = "libnvfp4_moe_cuda.so"
+NVFP4_MOE_ADD_RESIDUAL = 1
+
+
+class Profile(C.Structure):
+    _fields_ = [
+        ("upload_ns", C.c_uint64),
+        ("kernel_ns", C.c_uint64),
+        ("download_ns", C.c_uint64),
+    ]
+
+
+class _NativeTraceEvent(C.Structure):
+    _fields_ = [
+        ("scope", C.c_char * 96),
+        ("operation", C.c_char * 64),
+        ("queued_ns", C.c_uint64),
+        ("submit_ns", C.c_uint64),
+        ("start_ns", C.c_uint64),
+        ("end_ns", C.c_uint64),
+    ]
+
+
+class _DeviceInfo(C.Structure):
+    _fields_ = [
+        ("platform_name", C.c_char * 256),
+        ("device_name", C.c_char * 256),
+        ("device_version", C.c_char * 256),
+        ("driver_version", C.c_char * 256),
+        ("global_memory_bytes", C.c_uint64),
+        ("max_allocation_bytes", C.c_uint64),
+        ("global_cache_bytes", C.c_uint64),
+        ("local_memory_bytes", C.c_uint64),
+        ("compute_units", C.c_uint32),
+        ("max_clock_mhz", C.c_uint32),
+        ("svm_capabilities", C.c_uint32),
+    ]
+
+
+@dataclass(frozen=True)
+class TraceEvent:
+    scope: str
+    operation: str
+    queued_ns: int
+    submit_ns: int
+    start_ns: int
+    end_ns: int
+
+    @property
+    def duration_ns(self) -> int:
+        return self.end_ns - self.start_ns
+
+    @property
+    def queue_delay_ns(self) -> int:
+        return self.start_ns - self.queued_ns
+
+
+def default_library_path() -> Path:
+    return Path(__file__).resolve().parent / "lib" / LIB_NAME
+
+
+def runtime_paths() -> tuple[Path, None]:
+    """(library, kernel source). The second element is always None: kernels
+    are compiled ahead of time. ``VLLM_NVFP4_CUDA_LIB`` overrides the library
+    path (the lab's ``VLLM_NVFP4_OPENCL_DLL``, runtime.py:64-77)."""
+    configured = os.environ.get("VLLM_NVFP4_CUDA_LIB")
+    return (Path(configured).resolve() if configured else default_library_path(), None)
+
+
+def provider_enabled() -> tuple[bool, str | None]:
+    """Opt-in gate of the vLLM provider (runtime.py:80-91): requires
+    ``VLLM_NVFP4_CUDA=1`` and the built library."""
+    if os.environ.get("VLLM_NVFP4_CUDA") != "1":
+        return False, "set VLLM_NVFP4_CUDA=1 to opt into the CUDA NVFP4 backend"
+    lib, _ = runtime_paths()
+    if not lib.is_file():
+        return False, f"missing runtime artifact: {lib}"
+    return True, None
+
+
+_SIGNATURES: dict[str, tuple[list, object]] = {
+    "nvfp4_last_error": ([], C.c_char_p),
+    "nvfp4_runtime_create": ([C.c_char_p, C.POINTER(C.c_void_p)], C.c_int),
+    "nvfp4_runtime_destroy": ([C.c_void_p], None),
+    "nvfp4_runtime_device_name": ([C.c_void_p], C.c_char_p),
+    "nvfp4_runtime_last_profile": ([C.c_void_p, C.POINTER(Profile)], C.c_int),
+    "nvfp4_runtime_query_device": ([C.c_void_p, C.POINTER(_DeviceInfo)], C.c_int),
+    "nvfp4_runtime_synchronize": ([C.c_void_p], C.c_int),
+    "nvfp4_runtime_trace_set_enabled": ([C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_runtime_trace_set_scope": ([C.c_void_p, C.c_char_p], C.c_int),
+    "nvfp4_runtime_trace_count": ([C.c_void_p], C.c_size_t),
+    "nvfp4_runtime_trace_read": ([C.c_void_p, C.c_size_t, C.POINTER(_NativeTraceEvent)], C.c_int),
+    "nvfp4_runtime_stream": ([C.c_void_p], C.c_void_p),
+    "nvfp4_runtime_sm_count": ([C.c_void_p], C.c_int),
+    "nvfp4_buffer_create": ([C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)], C.c_int),
+    "nvfp4_buffer_destroy": ([C.c_void_p], None),
+    "nvfp4_buffer_upload": ([C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t], C.c_int),
+    "nvfp4_buffer_download": ([C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t], C.c_int),
+    "nvfp4_buffer_copy_enqueue": ([C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t], C.c_int),
+    "nvfp4_buffer_device_pointer": ([C.c_void_p], C.c_void_p),
+    "nvfp4_buffer_bytes": ([C.c_void_p], C.c_size_t),
+    "nvfp4_add_device_enqueue_f32": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_weighted_accumulate_device_enqueue_f32": (
+        [C.c_void_p, C.c_void_p, C.c_float, C.c_void_p, C.c_int, C.c_int], C.c_int),
+    "nvfp4_silu_mul_device_enqueue_f32": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_rmsnorm_device_enqueue_f32": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p], C.c_int),
+    "nvfp4_rmsnorm_device_enqueue_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p], C.c_int),
+    "nvfp4_bf16_gemv_device_enqueue": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_moe_bank_create": (
+        [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_int,
+         C.POINTER(C.c_void_p)], C.c_int),
+    "nvfp4_moe_bank_upload_projection": (
+        [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_float], C.c_int),
+    "nvfp4_moe_bank_upload_projection_device": (
+        [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_float], C.c_int),
+    "nvfp4_moe_bank_decode_device_enqueue_f32": ([C.c_void_p, C.c_void_p, C.c_void_p], C.c_int),
+    "nvfp4_moe_bank_forward_device_enqueue_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_moe_bank_forward_ptr_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_moe_bank_last_routing": (
+        [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int)], C.c_int),
+    "nvfp4_moe_bank_last_logits": ([C.c_void_p, C.c_int, C.c_void_p, C.POINTER(C.c_int)], C.c_int),
+    "nvfp4_moe_bank_set_router_bias": ([C.c_void_p, C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_moe_bank_info": (
+        [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)],
+        C.c_int),
+    "nvfp4_moe_bank_destroy": ([C.c_void_p], None),
+}
+
+
+def load_library(path: Path | None = None) -> C.CDLL:
+    """Load the CUDA library and declare every entry point's signature."""
+    lib_path = path or runtime_paths()[0]
+    if not Path(lib_path).is_file():
+        raise RuntimeError(
+            f"{LIB_NAME} not found at {lib_path}; build it with x2-nvfp4-lab_b200/build.py"
+        )
+    lib = C.CDLL(str(lib_path))
+    for name, (argtypes, restype) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = argtypes
+        fn.restype = restype
+    return lib
+
+
+def _ptr(array: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(array.ctypes.data)
+
+
+def _tensor_ptr(tensor) -> C.c_void_p:
+    return C.c_void_p(tensor.data_ptr())
+
+
+class DeviceBuffer:
+    def __init__(self, runtime: "Runtime", handle: C.c_void_p, bytes_: int):
+        self.runtime = runtime
+        self.handle = handle
+        self.bytes = bytes_
+
+    @property
+    def device_pointer(self) -> int:
+        return int(self.runtime.lib.nvfp4_buffer_device_pointer(self.handle) or 0)
+
+    def upload(self, array: np.ndarray, offset: int = 0) -> None:
+        if not array.flags.c_contiguous:
+            raise ValueError("upload array must be contiguous")
+        self.runtime._check(
+            self.runtime.lib.nvfp4_buffer_upload(self.handle, offset, _ptr(array), array.nbytes),
+            "buffer_upload",
+        )
+
+    def download(self, shape: tuple[int, ...], dtype: np.dtype | None = None) -> np.ndarray:
+        if dtype is None:
+            dtype = np.dtype(np.float32)
+        output = np.empty(shape, dtype=dtype)
+        if output.nbytes > self.bytes:
+            raise ValueError("download shape exceeds device-buffer capacity")
+        self.runtime._check(
+            self.runtime.lib.nvfp4_buffer_download(self.handle, 0, _ptr(output), output.nbytes),
+            "buffer_download",
+        )
+        return output
+
+    def close(self) -> None:
+        if self.handle:
+            self.runtime.lib.nvfp4_buffer_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+@dataclass
+class Routing:
+    """additive: routing record of the most recent bank call."""
+
+    ids: np.ndarray       # int32 [T, 9], slot 8 = shared expert id
+    weights: np.ndarray   # float32 [T, 9], slot 8 = sigmoid(shared logit)
+    counts: np.ndarray    # int32 [experts]
+    perm: np.ndarray      # int32 [T*8]
+
+
+class MoeBank:
+    def __init__(self, runtime: "Runtime", handle: C.c_void_p, experts: int, hidden: int, intermediate: int):
+        self.runtime = runtime
+        self.handle = handle
+        self.experts = experts
+        self.hidden = hidden
+        self.intermediate = intermediate
+
+    def _shape(self, projection: int) -> tuple[int, int]:
+        return (self.intermediate, self.hidden) if projection < 2 else (self.hidden, self.intermediate)
+
+    def upload_projection(
+        self,
+        expert: int,
+        projection: int,
+        packed: np.ndarray,
+        scales: np.ndarray,
+        checkpoint_global_scale: float,
+    ) -> None:
+        """Same checks and meaning as the lab (runtime.py:321-358):
+        ``checkpoint_global_scale`` is the divisor 1/weight_scale_2."""
+        if projection not in (0, 1, 2):
+            raise ValueError("projection must be 0=gate, 1=up, or 2=down")
+        rows, cols = self._shape(projection)
+        if (
+            not 0 <= expert <= self.experts
+            or packed.shape != (rows, cols // 2)
+            or scales.shape != (rows, cols // 16)
+            or packed.dtype != np.uint8
+            or scales.dtype != np.uint8
+            or not packed.flags.c_contiguous
+            or not scales.flags.c_contiguous
+        ):
+            raise ValueError("invalid contiguous uint8 MoE projection")
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_upload_projection(
+                self.handle, expert, projection, _ptr(packed), packed.nbytes, _ptr(scales), scales.nbytes,
+                checkpoint_global_scale,
+            ),
+            "nvfp4_moe_bank_upload_projection",
+        )
+
+    def upload_expert(self, expert: int, projections: list[tuple[np.ndarray, np.ndarray, float]]) -> None:
+        if len(projections) != 3:
+            raise ValueError("an MoE expert requires gate, up, and down projections")
+        for projection, values in enumerate(projections):
+            self.upload_projection(expert, projection, *values)
+
+    def upload_projection_tensor(self, expert: int, projection: int, packed, scales,
+                                 checkpoint_global_scale: float) -> None:
+        """additive: upload from contiguous CUDA uint8 tensors (enqueued on the
+        runtime stream; keep the tensors alive until the next synchronize)."""
+        rows, cols = self._shape(projection)
+        if (
+            tuple(packed.shape) != (rows, cols // 2)
+            or tuple(scales.shape) != (rows, cols // 16)
+            or not packed.is_cuda
+            or not scales.is_cuda
+            or not packed.is_contiguous()
+            or not scales.is_contiguous()
+        ):
+            raise ValueError("invalid contiguous CUDA uint8 MoE projection")
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_upload_projection_device(
+                self.handle, expert, projection, _tensor_ptr(packed), packed.numel(), _tensor_ptr(scales),
+                scales.numel(), float(checkpoint_global_scale),
+            ),
+            "nvfp4_moe_bank_upload_projection_device",
+        )
+
+    def decode_device(self, x: DeviceBuffer, out: DeviceBuffer) -> DeviceBuffer:
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_decode_device_enqueue_f32(self.handle, x.handle, out.handle),
+            "nvfp4_moe_bank_decode_device_enqueue_f32",
+        )
+        return out
+
+    def forward_device(self, x: DeviceBuffer, tokens: int, out: DeviceBuffer,
+                       residual: DeviceBuffer | None = None) -> DeviceBuffer:
+        """additive: BF16 [tokens, hidden] buffers; residual added when given."""
+        flags = NVFP4_MOE_ADD_RESIDUAL if residual is not None else 0
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_forward_device_enqueue_bf16(
+                self.handle, x.handle, residual.handle if residual is not None else None, tokens, flags,
+                out.handle,
+            ),
+            "nvfp4_moe_bank_forward_device_enqueue_bf16",
+        )
+        return out
+
+    def forward(self, x, residual=None, out=None, stream=None):
+        """additive: torch BF16 [tokens, hidden] CUDA tensors; enqueued on
+        ``stream`` (a torch.cuda.Stream) or torch's current stream."""
+        import torch
+
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError("x must be a CUDA bfloat16 tensor [tokens, hidden]")
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        flags = 0
+        if residual is not None:
+            if residual.shape != x.shape or residual.dtype != torch.bfloat16 or not residual.is_cuda:
+                raise ValueError("residual must match x")
+            residual = residual.contiguous()
+            flags = NVFP4_MOE_ADD_RESIDUAL
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_forward_ptr_bf16(
+                self.handle, _tensor_ptr(x), _tensor_ptr(residual) if residual is not None else None,
+                _tensor_ptr(out), x.shape[0], flags, C.c_void_p(s.cuda_stream),
+            ),
+            "nvfp4_moe_bank_forward_ptr_bf16",
+        )
+        return out
+
+    def last_routing(self, max_tokens: int) -> Routing:
+        """additive: routing of the most recent call (synchronises)."""
+        ids = np.zeros((max_tokens, 9), dtype=np.int32)
+        weights = np.zeros((max_tokens, 9), dtype=np.float32)
+        counts = np.zeros(self.experts, dtype=np.int32)
+        perm = np.zeros(max_tokens * 8, dtype=np.int32)
+        tokens = C.c_int(0)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_last_routing(
+                self.handle, max_tokens, _ptr(ids), _ptr(weights), _ptr(counts), _ptr(perm), C.byref(tokens)
+            ),
+            "nvfp4_moe_bank_last_routing",
+        )
+        t = min(tokens.value, max_tokens)
+        return Routing(ids[:t], weights[:t], counts, perm[: t * 8])
+
+    def last_logits(self, max_tokens: int) -> np.ndarray:
+        logits = np.zeros((max_tokens, self.experts + 1), dtype=np.float32)
+        tokens = C.c_int(0)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_last_logits(self.handle, max_tokens, _ptr(logits), C.byref(tokens)),
+            "nvfp4_moe_bank_last_logits",
+        )
+        return logits[: min(tokens.value, max_tokens)]
+
+    def set_router_bias(self, bias: np.ndarray | None) -> None:
+        """additive: FP32 per-expert router logit bias (None clears it)."""
+        if bias is None:
+            self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_router_bias(self.handle, None, 0),
+                                "nvfp4_moe_bank_set_router_bias")
+            return
+        bias = np.ascontiguousarray(bias, dtype=np.float32)
+        if bias.shape != (self.experts,):
+            raise ValueError("router bias must be float32 [experts]")
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_set_router_bias(self.handle, _ptr(bias), self.experts),
+            "nvfp4_moe_bank_set_router_bias",
+        )
+
+    @property
+    def resident_bytes(self) -> int:
+        size = C.c_size_t(0)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_info(self.handle, None, None, None, C.byref(size)),
+            "nvfp4_moe_bank_info",
+        )
+        return int(size.value)
+
+    def close(self) -> None:
+        if self.handle:
+            self.runtime.lib.nvfp4_moe_bank_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Runtime:
+    def __init__(self, lib_path: Path | None = None, kernel_path: Path | None = None):
+        self.lib = load_library(lib_path)
+        self.handle = C.c_void_p()
+        self._check(
+            self.lib.nvfp4_runtime_create(
+                str(kernel_path).encode() if kernel_path else None, C.byref(self.handle)
+            ),
+            "runtime_create",
+        )
+
+    def _check(self, status: int, operation: str) -> None:
+        if status:
+            error = (self.lib.nvfp4_last_error() or b"").decode(errors="replace")
+            raise RuntimeError(f"{operation} failed ({status}): {error}")
+
+    @property
+    def device_name(self) -> str:
+        value = self.lib.nvfp4_runtime_device_name(self.handle)
+        return value.decode(errors="replace") if value else "unknown"
+
+    @property
+    def stream_handle(self) -> int:
+        """additive: the runtime's cudaStream_t as an integer."""
+        return int(self.lib.nvfp4_runtime_stream(self.handle) or 0)
+
+    @property
+    def sm_count(self) -> int:
+        return int(self.lib.nvfp4_runtime_sm_count(self.handle))
+
+    def query_device(self) -> dict:
+        info = _DeviceInfo()
+        self._check(self.lib.nvfp4_runtime_query_device(self.handle, C.byref(info)), "runtime_query_device")
+        return {
+            "platform_name": info.platform_name.decode(),
+            "device_name": info.device_name.decode(),
+            "device_version": info.device_version.decode(),
+            "driver_version": info.driver_version.decode(),
+            "global_memory_bytes": int(info.global_memory_bytes),
+            "global_cache_bytes": int(info.global_cache_bytes),
+            "compute_units": int(info.compute_units),
+            "max_clock_mhz": int(info.max_clock_mhz),
+        }
+
+    def last_profile(self) -> Profile:
+        profile = Profile()
+        self._check(self.lib.nvfp4_runtime_last_profile(self.handle, C.byref(profile)), "runtime_last_profile")
+        return profile
+
+    def synchronize(self) -> Profile:
+        self._check(self.lib.nvfp4_runtime_synchronize(self.handle), "runtime_synchronize")
+        return self.last_profile()
+
+    def set_trace_enabled(self, enabled: bool) -> None:
+        self._check(self.lib.nvfp4_runtime_trace_set_enabled(self.handle, int(enabled)), "runtime_trace_set_enabled")
+
+    def set_trace_scope(self, scope: str) -> None:
+        encoded = scope.encode("utf-8")
+        if len(encoded) >= 96:
+            raise ValueError("trace scope must be shorter than 96 UTF-8 bytes")
+        self._check(self.lib.nvfp4_runtime_trace_set_scope(self.handle, encoded), "runtime_trace_set_scope")
+
+    def trace_events(self) -> list[TraceEvent]:
+        count = int(self.lib.nvfp4_runtime_trace_count(self.handle))
+        events = []
+        for index in range(count):
+            native = _NativeTraceEvent()
+            self._check(self.lib.nvfp4_runtime_trace_read(self.handle, index, C.byref(native)), "runtime_trace_read")
+            events.append(
+                TraceEvent(
+                    scope=bytes(native.scope).split(b"\0", 1)[0].decode(),
+                    operation=bytes(native.operation).split(b"\0", 1)[0].decode(),
+                    queued_ns=int(native.queued_ns),
+                    submit_ns=int(native.submit_ns),
+                    start_ns=int(native.start_ns),
+                    end_ns=int(native.end_ns),
+                )
+            )
+        return events
+
+    def create_buffer(self, bytes_: int) -> DeviceBuffer:
+        if bytes_ <= 0:
+            raise ValueError("device-buffer size must be positive")
+        handle = C.c_void_p()
+        self._check(self.lib.nvfp4_buffer_create(self.handle, bytes_, C.byref(handle)), "buffer_create")
+        return DeviceBuffer(self, handle, bytes_)
+
+    def upload_buffer(self, array: np.ndarray) -> DeviceBuffer:
+        buffer = self.create_buffer(array.nbytes)
+        try:
+            buffer.upload(array)
+        except Exception:
+            buffer.close()
+            raise
+        return buffer
+
+    def copy_buffer_device(self, source: DeviceBuffer, destination: DeviceBuffer, bytes_: int,
+                           source_offset: int = 0, destination_offset: int = 0) -> None:
+        if bytes_ <= 0 or source_offset < 0 or destination_offset < 0:
+            raise ValueError("buffer copy ranges must be nonnegative and nonempty")
+        self._check(
+            self.lib.nvfp4_buffer_copy_enqueue(source.handle, source_offset, destination.handle,
+                                               destination_offset, bytes_),
+            "buffer_copy_enqueue",
+        )
+
+    def create_moe_bank(self, router_bf16: np.ndarray, shared_gate_bf16: np.ndarray, intermediate: int) -> MoeBank:
+        """Same checks as the lab (runtime.py:986-1024): router BF16 bits
+        [8..256, hidden], shared gate BF16 bits [hidden]."""
+        if (
+            router_bf16.ndim != 2
+            or router_bf16.dtype != np.uint16
+            or not router_bf16.flags.c_contiguous
+            or router_bf16.shape[0] < 8
+            or router_bf16.shape[0] > 256
+            or intermediate <= 0
+            or intermediate % 16 != 0
+        ):
+            raise ValueError("router must be contiguous BF16 bits [8..256, hidden]")
+        shared_gate_bf16 = np.ascontiguousarray(shared_gate_bf16.reshape(-1))
+        if shared_gate_bf16.dtype != np.uint16 or shared_gate_bf16.size != router_bf16.shape[1]:
+            raise ValueError("shared gate must be BF16 bits [hidden]")
+        experts, hidden = router_bf16.shape
+        handle = C.c_void_p()
+        self._check(
+            self.lib.nvfp4_moe_bank_create(
+                self.handle, _ptr(router_bf16), router_bf16.nbytes, _ptr(shared_gate_bf16),
+                shared_gate_bf16.nbytes, experts, hidden, intermediate, C.byref(handle),
+            ),
+            "nvfp4_moe_bank_create",
+        )
+        return MoeBank(self, handle, experts, hidden, intermediate)
+
+    def add_device(self, a: DeviceBuffer, b: DeviceBuffer, elements: int, out: DeviceBuffer) -> DeviceBuffer:
+        self._check(self.lib.nvfp4_add_device_enqueue_f32(self.handle, a.handle, b.handle, elements, out.handle),
+                    "add_device_enqueue_f32")
+        return out
+
+    def silu_mul_device(self, gate: DeviceBuffer, up: DeviceBuffer, elements: int, out: DeviceBuffer) -> DeviceBuffer:
+        self._check(
+            self.lib.nvfp4_silu_mul_device_enqueue_f32(self.handle, gate.handle, up.handle, elements, out.handle),
+            "silu_mul_device_enqueue_f32",
+        )
+        return out
+
+    def weighted_accumulate_device(self, source: DeviceBuffer, scale: float, out: DeviceBuffer, elements: int,
+                                   *, reset: bool = False) -> DeviceBuffer:
+        self._check(
+            self.lib.nvfp4_weighted_accumulate_device_enqueue_f32(self.handle, source.handle, scale, out.handle,
+                                                                  elements, int(reset)),
+            "weighted_accumulate_device_enqueue_f32",
+        )
+        return out
+
+    def rmsnorm_device(self, x: DeviceBuffer, weight: DeviceBuffer, rows: int, cols: int, epsilon: float,
+                       out: DeviceBuffer) -> DeviceBuffer:
+        self._check(
+            self.lib.nvfp4_rmsnorm_device_enqueue_f32(self.handle, x.handle, weight.handle, rows, cols, epsilon,
+                                                      out.handle),
+            "rmsnorm_device_enqueue_f32",
+        )
+        return out
+
+    def rmsnorm_device_bf16(self, x: DeviceBuffer, weight: DeviceBuffer, rows: int, cols: int, epsilon: float,
+                            out: DeviceBuffer) -> DeviceBuffer:
+        """additive: BF16 RMSNorm."""
+        self._check(
+            self.lib.nvfp4_rmsnorm_device_enqueue_bf16(self.handle, x.handle, weight.handle, rows, cols, epsilon,
+                                                       out.handle),
+            "rmsnorm_device_enqueue_bf16",
+        )
+        return out
+
+    def bf16_gemv_device(self, weights: DeviceBuffer, x: DeviceBuffer, rows: int, cols: int,
+                         out: DeviceBuffer) -> DeviceBuffer:
+        self._check(
+            self.lib.nvfp4_bf16_gemv_device_enqueue(self.handle, weights.handle, x.handle, rows, cols, out.handle),
+            "bf16_gemv_device_enqueue",
+        )
+        return out
+
+    def close(self) -> None:
+        if self.handle:
+            self.lib.nvfp4_runtime_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+
+_runtime: Runtime | None = None
+_runtime_lock = threading.Lock()
+
+
+def get_runtime() -> Runtime:
+    """Process-wide runtime (runtime.py:1964-1976). Raises when the provider
+    is not enabled; there is no fallback."""
+    global _runtime
+    with _runtime_lock:
+        if _runtime is None:
+            enabled, reason = provider_enabled()
+            if not enabled:
+                raise RuntimeError(reason)
+            _runtime = Runtime(*runtime_paths())
+        return _runtime
