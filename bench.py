@@ -243,6 +243,7 @@ def run_ours(args) -> int:
     res_pool = [synthetic.synthetic_tokens(T, H, 5000 * (rank + 1) + i) for i in range(pool_n)]
     out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    torch.cuda.synchronize()
 
     # Routing of every pool batch -> algorithmic bytes of each step.
     uniq = []

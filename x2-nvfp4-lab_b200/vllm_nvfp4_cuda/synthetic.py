@@ -126,6 +126,8 @@ def build_bank(runtime, experts: int, hidden: int, intermediate: int, seed: int,
         for p in range(3):
             packed, scales, divisor = synthetic_expert_projection(e, p, hidden, intermediate, seed, layer, device)
             if packed.is_cuda:
+                # The upload runs on the runtime's own stream: wait for torch's.
+                torch.cuda.current_stream(packed.device).synchronize()
                 bank.upload_projection_tensor(e, p, packed, scales, divisor)
                 keep.append((packed, scales))
             else:
