@@ -88,9 +88,11 @@ def test_forward_bf16_batched(cuda_runtime, wide_bank, wide_host, T):
     got = bf16_tensor_to_f32(out)
     assert rel_rmse(got, ref.out) <= REL_RMSE_TOL
     assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL
-    # The MoE contribution alone (residual removed) stays within tolerance too.
+    # Element-wise: within one BF16 rounding of the output plus the BASELINE
+    # relative tolerance on the MoE contribution.
     moe_only = ref.out - synthetic_np.bf16_bits_to_f32(rbits)
-    assert rel_rmse(got - synthetic_np.bf16_bits_to_f32(rbits), moe_only) <= 2e-2
+    bound = np.abs(ref.out) * 2.0**-8 + MAX_ABS_REL_TOL * np.max(np.abs(moe_only))
+    assert np.all(np.abs(got - ref.out) <= bound)
 
 
 def test_forward_without_residual_and_buffers(cuda_runtime, small_bank, small_host):
