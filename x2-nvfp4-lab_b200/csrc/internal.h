@@ -70,9 +70,21 @@ struct nvfp4_runtime {
     cudaEvent_t acquire_event();
     void release_event(cudaEvent_t event);
     // Record an event pair around `launch` on `on_stream` (the runtime stream
-    // when null). Caller holds queue_mutex.
+    // when null). Caller holds queue_mutex. Nothing is recorded while the
+    // stream is being captured into a CUDA graph.
     template <typename F>
     void profiled(const char *operation, cudaStream_t on_stream, F &&launch);
+    // Per-kernel pairs when tracing, one pair per API call otherwise.
+    template <typename F>
+    void profiled_kernel(const char *operation, cudaStream_t on_stream, F &&launch) {
+        if (trace_enabled) profiled(operation, on_stream, launch);
+        else launch(on_stream ? on_stream : stream);
+    }
+    template <typename F>
+    void profiled_call(const char *operation, cudaStream_t on_stream, F &&launch) {
+        if (trace_enabled) launch(on_stream ? on_stream : stream);
+        else profiled(operation, on_stream, launch);
+    }
 };
 
 struct nvfp4_buffer {
@@ -94,7 +106,9 @@ inline uint64_t host_now_ns() {
 template <typename F>
 void nvfp4_runtime::profiled(const char *operation, cudaStream_t on_stream, F &&launch) {
     cudaStream_t s = on_stream ? on_stream : stream;
-    if (pending.size() >= nvfp4::kMaxPendingEvents) {
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(s, &capture) != cudaSuccess) capture = cudaStreamCaptureStatusNone;
+    if (pending.size() >= nvfp4::kMaxPendingEvents || capture != cudaStreamCaptureStatusNone) {
         launch(s);
         return;
     }

@@ -104,7 +104,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ra.shared_here = 1;
     ra.s = bank->ds;
     nvfp4_runtime *rt = bank->runtime;
-    rt->profiled("moe_route", stream, [&](cudaStream_t s) {
+    rt->profiled_kernel("moe_route", stream, [&](cudaStream_t s) {
         check_cuda(launch_route(ra, s), "moe_route_kernel");
     });
 
@@ -118,7 +118,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ga.H = H;
     ga.I = I;
     ga.s = bank->ds;
-    rt->profiled("moe_gate_up", stream, [&](cudaStream_t s) {
+    rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
         check_cuda(launch_gate_up(ga, tokens, sms * 2, s), "moe_gate_up_kernel");
     });
 
@@ -133,7 +133,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     da.H = H;
     da.I = I;
     da.s = bank->ds;
-    rt->profiled("moe_down", stream, [&](cudaStream_t s) {
+    rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
         check_cuda(launch_down(da, sms * 2, s), "moe_down_kernel");
     });
 }
@@ -301,7 +301,9 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_decode_device_enqueue_f32(nvfp4
     try {
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
-        enqueue_decode(bank, x->data, 1, nullptr, dst->data, 1, 1, rt->stream);
+        rt->profiled_call("moe_bank_decode", nullptr, [&](cudaStream_t s) {
+            enqueue_decode(bank, x->data, 1, nullptr, dst->data, 1, 1, s);
+        });
         bank->last_tokens = 1;
         bank->last_path = 1;
         clear_last_error();
@@ -327,8 +329,9 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(nvfp4_moe_bank
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
         const void *res = (flags & NVFP4_MOE_ADD_RESIDUAL) ? residual_bf16 : nullptr;
-        cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : rt->stream;
-        enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s);
+        rt->profiled_call("moe_bank_forward", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+            enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s);
+        });
         clear_last_error();
         return NVFP4_STATUS_OK;
     } catch (const std::exception &error) {

@@ -2,6 +2,8 @@
 #include "moe_decode.cuh"
 
 #include <cfloat>
+#include <map>
+#include <mutex>
 
 namespace nvfp4 {
 
@@ -577,10 +579,24 @@ __global__ void __launch_bounds__(256) moe_down_kernel(DownArgs a) {
     }
 }
 
+// Raise a kernel's dynamic shared-memory limit once per device (the
+// attribute call costs microseconds of host time, so it is not repeated on
+// every launch).
 template <typename K>
 cudaError_t set_smem(K kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return cudaSuccess;
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    static std::mutex m;
+    static std::map<std::pair<int, const void *>, size_t> done;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lock(m);
+    auto key = std::make_pair(dev, reinterpret_cast<const void *>(kernel));
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) done[key] = bytes;
+    return err;
 }
 
 }  // namespace
