@@ -361,6 +361,42 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_info(
     int * intermediate,
     size_t * resident_bytes);
 
+/* ------------------------------------------------ allocation-free routing */
+
+/* No counterpart in the reference. Router logits, top-8 selection with the
+ * lowest id on ties, renormalised weights, the sigmoid shared-expert gate and
+ * the dispatch permutation for up to 64 tokens -- the same kernel the MoE
+ * bank runs first -- for callers that must not allocate device memory while
+ * they route (their device memory is planned and owned by the host framework,
+ * or allocation is forbidden on their latency-critical path). The kernel's
+ * working memory is one 1 MiB array in the library's device globals instead
+ * of memory from cudaMalloc; this function allocates nothing.
+ *   router_bf16  device BF16 [experts + 1, hidden]; the last row is the
+ *                shared-expert gate
+ *   x_bf16       device BF16 [tokens, hidden]
+ *   ids          device int32 [tokens, 9]  (slot 8 = experts)
+ *   weights      device float [tokens, 9]  (slot 8 = sigmoid gate)
+ *   counts       device int32 [experts] or NULL
+ *   perm         device int32 [tokens * 8] or NULL
+ *   stream       cudaStream_t (NULL = legacy default stream)
+ * Limits: 1 <= tokens <= 64, 8 <= experts <= 256, hidden a multiple of 128
+ * and at most 4096; larger sizes return NVFP4_STATUS_INVALID_ARGUMENT.
+ * Every call shares the one array and it keeps the previous call's
+ * contents; calls whose kernels overlap on the GPU race and must be ordered.
+ * The first call on each device looks up the array's address; make it before
+ * any stream capture. */
+NVFP4_API nvfp4_status nvfp4_moe_route_static_scratch(
+    const void * router_bf16,
+    const void * x_bf16,
+    int tokens,
+    int experts,
+    int hidden,
+    int32_t * ids,
+    float * weights,
+    int32_t * counts,
+    int32_t * perm,
+    void * stream);
+
 #ifdef __cplusplus
 }
 #endif

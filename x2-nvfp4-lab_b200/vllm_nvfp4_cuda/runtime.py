@@ -153,6 +153,9 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
         [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_int), C.POINTER(C.c_size_t)],
         C.c_int),
     "nvfp4_moe_bank_destroy": ([C.c_void_p], None),
+    "nvfp4_moe_route_static_scratch": (
+        [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+         C.c_void_p], C.c_int),
 }
 
 
