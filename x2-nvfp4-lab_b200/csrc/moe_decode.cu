@@ -9,12 +9,15 @@ namespace nvfp4 {
 
 namespace {
 
-constexpr int kRouteRowsPerCta = 8;   // one warp per router row
+constexpr int kRouteRowsPerCta = 4;   // one warp per router row, 128 threads
+constexpr int kRouteTokens = 8;       // tokens accumulated together (independent FP64 chains)
 
-// Tokens staged in shared memory at once by the routing kernel (FP32 rows).
-__host__ __device__ inline int route_token_tile(int H) {
-    const int fit = (192 * 1024) / (H * 4);
-    return fit < 1 ? 1 : (fit > 8 ? 8 : fit);
+// Monotone map of a float to uint32 for redux.sync; -0 and +0 map alike so
+// equal logits compare equal, as in the lab's selection loop.
+__device__ __forceinline__ unsigned float_order_key(float v) {
+    v = (v == 0.0f) ? 0.0f : v;
+    const unsigned b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
 // ---------------------------------------------------------------- routing
@@ -27,8 +30,12 @@ __host__ __device__ inline int route_token_tile(int H) {
 // (or BF16) value is exact in FP64, so fma == mul+add and the oracle can
 // reproduce the value bit for bit by following the same order. An optional
 // per-expert FP32 bias is added to the rounded logit.
-__global__ void __launch_bounds__(256) moe_route_kernel(RouteArgs a) {
-    extern __shared__ __align__(16) float xs[];  // [route_token_tile(H)][H]
+//
+// Each warp owns one router row and accumulates up to kRouteTokens tokens
+// at once (independent FMA chains); tokens are staged in shared memory as
+// FP32 rows.
+__global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
+    extern __shared__ __align__(16) float xs[];  // [kRouteTokens][H]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = a.E + 1;
     const int row = blockIdx.x * kRouteRowsPerCta + warp;
@@ -54,41 +61,56 @@ __global__ void __launch_bounds__(256) moe_route_kernel(RouteArgs a) {
         }
     }
 
-    const int tile = route_token_tile(H);
-    for (int t0 = 0; t0 < a.T; t0 += tile) {
-        const int tt = min(tile, a.T - t0);
+    for (int t0 = 0; t0 < a.T; t0 += kRouteTokens) {
+        const int tt = min(kRouteTokens, a.T - t0);
         __syncthreads();
-        for (int i = threadIdx.x; i < tt * H; i += blockDim.x) {
-            const int j = i / H, k = i - j * H;
-            float v;
+        for (int i = threadIdx.x; i < tt * (H / 4); i += blockDim.x) {
+            const int j = i / (H / 4), k = (i - j * (H / 4)) * 4;
+            float4 v;
             if (a.x_is_f32) {
-                v = static_cast<const float *>(a.x)[(size_t)(t0 + j) * H + k];
+                v = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) +
+                                                           (size_t)(t0 + j) * H + k));
             } else {
-                v = bf16_bits_to_f32(static_cast<const uint16_t *>(a.x)[(size_t)(t0 + j) * H + k]);
+                const uint2 b = __ldg(reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(a.x) +
+                                                                      (size_t)(t0 + j) * H + k));
+                v = make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
+                                bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
             }
-            xs[j * H + k] = v;
+            *reinterpret_cast<float4 *>(xs + j * H + k) = v;
         }
         __syncthreads();
         if (row < R) {
             const uint16_t *w = a.router + (size_t)row * H;
-            for (int j = 0; j < tt; ++j) {
-                double acc = 0.0;
-                const float *xr = xs + j * H;
-                for (int q = 0; q < chunks; ++q) {
-                    const int k = q * 128 + lane * 4;
-                    const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(w + k));
-                    const float4 xv = *reinterpret_cast<const float4 *>(xr + k);
-                    acc = fma((double)bf16_bits_to_f32(wv.x & 0xFFFFu), (double)xv.x, acc);
-                    acc = fma((double)bf16_bits_to_f32(wv.x >> 16), (double)xv.y, acc);
-                    acc = fma((double)bf16_bits_to_f32(wv.y & 0xFFFFu), (double)xv.z, acc);
-                    acc = fma((double)bf16_bits_to_f32(wv.y >> 16), (double)xv.w, acc);
-                }
+            double acc[kRouteTokens];
 #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-                if (lane == 0) {
-                    float lv = (float)acc;
-                    if (a.bias && row < a.E) lv += a.bias[row];
-                    s.logits[(size_t)(t0 + j) * R + row] = lv;
+            for (int j = 0; j < kRouteTokens; ++j) acc[j] = 0.0;
+            for (int q = 0; q < chunks; ++q) {
+                const int k = q * 128 + lane * 4;
+                const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(w + k));
+                const double w0 = bf16_bits_to_f32(wv.x & 0xFFFFu), w1 = bf16_bits_to_f32(wv.x >> 16);
+                const double w2 = bf16_bits_to_f32(wv.y & 0xFFFFu), w3 = bf16_bits_to_f32(wv.y >> 16);
+#pragma unroll
+                for (int j = 0; j < kRouteTokens; ++j) {
+                    if (j < tt) {
+                        const float4 xv = *reinterpret_cast<const float4 *>(xs + j * H + k);
+                        acc[j] = fma(w0, (double)xv.x, acc[j]);
+                        acc[j] = fma(w1, (double)xv.y, acc[j]);
+                        acc[j] = fma(w2, (double)xv.z, acc[j]);
+                        acc[j] = fma(w3, (double)xv.w, acc[j]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < kRouteTokens; ++j) {
+                if (j < tt) {
+                    double v = acc[j];
+#pragma unroll
+                    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+                    if (lane == 0) {
+                        float lv = (float)v;
+                        if (a.bias && row < a.E) lv += a.bias[row];
+                        s.logits[(size_t)(t0 + j) * R + row] = lv;
+                    }
                 }
             }
         }
@@ -128,6 +150,7 @@ __global__ void __launch_bounds__(256) moe_route_kernel(RouteArgs a) {
         int top_i[kTopK];
 #pragma unroll
         for (int slot = 0; slot < kTopK; ++slot) {
+            // Local best: strictly greater wins, so the lowest id survives ties.
             float bv = -FLT_MAX;
             int bi = 0;
 #pragma unroll
@@ -138,15 +161,12 @@ __global__ void __launch_bounds__(256) moe_route_kernel(RouteArgs a) {
                     bi = e;
                 }
             }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                if (route_better(ov, oi, bv, bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
-            }
+            // Warp best: largest value, then the lowest id among equal values.
+            const unsigned key = float_order_key(bv);
+            const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+            const unsigned imin = __reduce_min_sync(0xffffffffu, key == kmax ? (unsigned)bi : 0xffffffffu);
+            bi = (int)imin;
+            bv = __shfl_sync(0xffffffffu, bv, bi & 31);
             top_v[slot] = bv;
             top_i[slot] = bi;
             if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
@@ -599,6 +619,8 @@ cudaError_t set_smem(K kernel, size_t bytes) {
     return err;
 }
 
+constexpr size_t kSmemLimit = 227 * 1024;
+
 }  // namespace
 
 size_t decode_scratch_bytes(int E, int H, int I) {
@@ -637,10 +659,11 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream) {
     const int R = a.E + 1;
     const int grid = (R + kRouteRowsPerCta - 1) / kRouteRowsPerCta;
-    const size_t smem = (size_t)route_token_tile(a.H) * a.H * sizeof(float);
+    const size_t smem = (size_t)kRouteTokens * a.H * sizeof(float);
+    if (smem > kSmemLimit) return cudaErrorInvalidValue;
     cudaError_t err = set_smem(moe_route_kernel, smem);
     if (err != cudaSuccess) return err;
-    moe_route_kernel<<<grid, 256, smem, stream>>>(a);
+    moe_route_kernel<<<grid, kRouteRowsPerCta * 32, smem, stream>>>(a);
     return cudaGetLastError();
 }
 
@@ -648,8 +671,6 @@ template <int NT>
 static size_t gate_up_smem(int H) {
     return (size_t)NT * 8 * act_tile_stride_bytes(H) + (size_t)8 * 2 * NT * 4 * 32 * 4;
 }
-
-constexpr size_t kSmemLimit = 227 * 1024;
 
 template <int NT>
 static cudaError_t launch_gate_up_nt(const GateUpArgs &a, int items_ub, int grid_cap, cudaStream_t stream) {
