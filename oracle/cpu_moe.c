@@ -14,7 +14,7 @@
  * Threading follows nvfp4_cpu_gemv_impl (nvfp4_cpu.cpp:163-204): rows are
  * split into contiguous ranges, one std::thread-equivalent per range.
  *
- * Layer: router and shared-gate logits in FP64 in the CUDA routing kernel's
+ * Layer: router and shared-gate logits in FP32 in the CUDA routing kernel's
  * lane order (bit-identical to it and to nvfp4_oracle.router_logits), top-8
  * with the lowest id on ties and renormalised weights (nvfp4_gemv.cl:
  * 1249-1295), gate/up/SiLU*up/down per selected expert
@@ -160,24 +160,25 @@ int nvfp4_oracle_cpu_gemv(const uint8_t *packed, const uint8_t *scales, int rows
 
 /* --------------------------------------------------------------- routing */
 
-/* FP64 dot in the CUDA routing kernel's lane order (see file header). */
+/* FP32 dot in the CUDA routing kernel's lane order (see file header). */
 static float router_dot(const uint16_t *w, const float *x, int H) {
-    double lane[32];
+    float lane[32];
     for (int l = 0; l < 32; ++l) {
-        double acc = 0.0;
+        float acc = 0.0f;
         for (int j = 0; j < H / 128; ++j)
             for (int e = 0; e < 4; ++e) {
                 const int k = j * 128 + 4 * l + e;
-                acc = acc + (double)bf16_to_float(w[k]) * (double)x[k];
+                const float prod = bf16_to_float(w[k]) * x[k];
+                acc = acc + prod;
             }
         lane[l] = acc;
     }
     for (int off = 16; off >= 1; off >>= 1) {
-        double next[32];
+        float next[32];
         for (int l = 0; l < 32; ++l) next[l] = lane[l] + lane[l ^ off];
         memcpy(lane, next, sizeof(lane));
     }
-    return (float)lane[0];
+    return lane[0];
 }
 
 /* ------------------------------------------------------------------ layer */

@@ -25,8 +25,8 @@ Extensions beyond the lab (which only decodes one token):
   block scale E4M3_RNE(blockamax/6/g), E2M1 round-to-nearest with ties to
   the even code;
 * a bit-reproducible router dot product: BF16 weights times FP32/BF16
-  activations accumulated in FP64 in the documented lane order used by the
-  CUDA routing kernel, rounded to FP32 once.
+  activations accumulated in FP32 in the documented lane order used by the
+  CUDA routing kernel.
 
 Parity is pinned against golden vectors produced by running the reference's
 own Python oracle functions (see ``tests/golden/make_golden.py``).
@@ -187,25 +187,28 @@ def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
 
 def router_logits(router_bf16: np.ndarray, x: np.ndarray) -> np.ndarray:
     """[T, R] float32 logits of BF16 rows [R, H] against x [T, H] (float32 or
-    BF16-valued). FP64 accumulation in the CUDA routing kernel's order: lane l
-    (0..31) owns columns j*128 + 4l + e, adds them with j then e ascending,
-    then the 32 lane sums combine by an xor butterfly (16, 8, 4, 2, 1); one
-    rounding to FP32 at the end. Every product is exact in FP64."""
-    w = bf16_bits_to_f32(router_bf16).astype(np.float64)
-    x = np.asarray(x, dtype=np.float32).astype(np.float64)
+    BF16-valued), in FP32 as the lab's bf16_gemv_subgroup accumulates
+    (nvfp4_gemv.cl:1223-1247), with the CUDA routing kernel's fixed order:
+    lane l (0..31) owns columns j*128 + 4l + e and adds (w*x rounded to FP32)
+    to its FP32 sum with j then e ascending; the 32 lane sums then combine by
+    an xor butterfly (16, 8, 4, 2, 1). Every operation is one IEEE FP32
+    rounding, so the result is reproduced bit for bit."""
+    w = bf16_bits_to_f32(router_bf16)
+    x = np.asarray(x, dtype=np.float32)
     R, H = w.shape
     T = x.shape[0]
     assert H % 128 == 0
     wv = w.reshape(R, H // 128, 32, 4)
     xv = x.reshape(T, H // 128, 32, 4)
-    acc = np.zeros((T, R, 32), dtype=np.float64)
+    acc = np.zeros((T, R, 32), dtype=np.float32)
     for j in range(H // 128):
         for e in range(4):
-            acc = acc + xv[:, None, j, :, e] * wv[None, :, j, :, e]
+            prod = (xv[:, None, j, :, e] * wv[None, :, j, :, e]).astype(np.float32)
+            acc = (acc + prod).astype(np.float32)
     for off in (16, 8, 4, 2, 1):
         idx = np.arange(32) ^ off
-        acc = acc + acc[:, :, idx]
-    return acc[:, :, 0].astype(np.float32)
+        acc = (acc + acc[:, :, idx]).astype(np.float32)
+    return acc[:, :, 0].copy()
 
 
 def top8_route(logits: np.ndarray, top_k: int = TOP_K) -> tuple[np.ndarray, np.ndarray]:

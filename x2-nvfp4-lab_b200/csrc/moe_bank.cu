@@ -29,6 +29,7 @@ struct nvfp4_moe_bank {
     float *router_bias = nullptr;  // device [experts] or null
     void *scratch = nullptr;
     DecodeScratch ds{};
+    StreamMaps maps{};             // TMA descriptors over packed/scales
     std::vector<uint8_t> uploaded;
     size_t uploaded_projections = 0;
     int last_tokens = 0;
@@ -119,7 +120,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ga.I = I;
     ga.s = bank->ds;
     rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
-        check_cuda(launch_gate_up(ga, tokens, sms * 2, s), "moe_gate_up_kernel");
+        check_cuda(launch_gate_up_tma(bank->maps, ga, tokens, sms, s), "moe_gate_up_tma_kernel");
     });
 
     DownArgs da{};
@@ -128,13 +129,14 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     da.residual = residual;
     da.out = out;
     da.out_f32 = out_f32;
+    da.shared_here = 1;
     da.T = tokens;
     da.E = E;
     da.H = H;
     da.I = I;
     da.s = bank->ds;
     rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
-        check_cuda(launch_down(da, sms * 2, s), "moe_down_kernel");
+        check_cuda(launch_down_tma(bank->maps, da, sms, s), "moe_down_tma_kernel");
     });
 }
 
@@ -208,6 +210,8 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
         check_cuda(cudaMemsetAsync(holder->scratch, 0, scratch, runtime->stream),
                    "cudaMemsetAsync(MoE bank scratch)");
         decode_scratch_carve(holder->ds, holder->scratch, experts, hidden, intermediate);
+        check_cuda(make_stream_maps(holder->maps, holder->packed, holder->scales, experts, hidden, intermediate),
+                   "cuTensorMapEncodeTiled(MoE bank)");
         check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize(MoE bank create)");
         holder->uploaded.assign(slots * 3, 0);
         holder->resident_bytes = 3 * (elements / 2 + elements / 16) + 3 * slots * sizeof(float) +

@@ -1,30 +1,35 @@
 // Decode-path kernels of the NVFP4 MoE layer (tokens <= kDecodeMaxTokens).
 //
 // Three launches per layer on one stream:
-//   1. moe_route_kernel    router + shared-gate logits (FP64 fixed-order dot),
-//                          then, in the last CTA to finish, top-8 + softmax
-//                          renormalisation + sigmoid shared gate + dispatch
-//                          (per-expert histogram, offsets, stable permutation,
-//                          compacted active-expert work list).
-//   2. moe_gate_up_kernel  gate and up NVFP4 GEMVs of every (active expert,
-//                          32-row tile), SiLU(gate)*up fused in the epilogue.
-//   3. moe_down_kernel     down NVFP4 GEMV of every active expert for a
-//                          16-row slice of the output, weighted combine over
-//                          experts and the residual add fused in the epilogue.
+//   1. moe_route_kernel        router + shared-gate logits (FP32, fixed
+//                              order), top-8 + softmax renormalisation +
+//                              sigmoid shared gate per 4-token block, then
+//                              dispatch (per-expert histogram, offsets, stable
+//                              permutation, compacted active-expert list).
+//   2. moe_gate_up_tma_kernel  gate and up NVFP4 GEMVs of every (active
+//                              expert, 32-row tile), SiLU(gate)*up fused.
+//   3. moe_down_tma_kernel     down NVFP4 GEMV of every (active expert,
+//                              64-row tile); the last CTA per tile combines
+//                              the nine slots and adds the residual.
 // The lab runs the same layer as seven launches (nvfp4_runtime.cpp:1943-2066:
 // router GEMV, shared-gate GEMV, top-8, gate/up, SiLU, down, reduce).
 #pragma once
 
 #include "nvfp4_common.cuh"
 
+#include <cuda.h>
+
 namespace nvfp4 {
 
 constexpr int kDecodeMaxTokens = 64;
 constexpr int kTopK = 8;
 constexpr int kSlots = kTopK + 1;  // slot 8 is the shared expert
+constexpr int kRouteTickets = 1 + kDecodeMaxTokens / 4;
 
 // Device scratch of one bank for the decode path. All pointers are device
 // addresses; sizes are for kDecodeMaxTokens tokens and E routed experts.
+// The fields the routing kernel touches come first (decode_route_scratch_bytes
+// covers exactly them); the expert-GEMV buffers follow.
 struct DecodeScratch {
     float *logits;          // [T][E+1], column E = shared-gate logit
     __half *x_f16;          // [T][H]
@@ -33,16 +38,24 @@ struct DecodeScratch {
     int *counts;            // [E]
     int *offsets;           // [E+1]
     int *perm;              // [T*8]
+    int *inv_pos;           // [T*8] position of (token, slot) in perm order, -1 if not computed here
     int *n_active;          // [1]
     int *active_expert;     // [E+1]
     int *tok_start;         // [E+1]
     int *tok_count;         // [E+1]
     int *tok_list;          // [T*9]
-    int *pos_tab;           // [(E+1)][kDecodeMaxTokens]
     float *coef_tab;        // [(E+1)][kDecodeMaxTokens]
-    uint32_t *ntile_mask;   // [E+1]
-    __half *act;            // [T*9][I]
-    unsigned *ticket;       // [1]
+    unsigned *ticket;       // [kRouteTickets] dispatch ticket, then one per 4-token block
+    int *error;             // [1] device-side wait timeout flag
+    __half *act;            // [T*9][I]      SiLU(gate)*up per (token, slot)
+    float *ypart;           // [T*9][H]      scaled down-projection per (token, slot)
+    unsigned *tile_count;   // [H/64]        finished experts per 64-row output tile
+};
+
+// TMA descriptors over a bank's packed and scale arrays (gate, up, down).
+struct StreamMaps {
+    CUtensorMap packed[3];
+    CUtensorMap scales[3];
 };
 
 struct RouteArgs {
@@ -69,17 +82,24 @@ struct DownArgs {
     const void *residual;     // BF16 [T][H] or nullptr
     void *out;                // BF16 or FP32 [T][H]
     int out_f32;
+    int shared_here;          // 1 if the shared expert's slot is summed here
     int T, E, H, I;
     DecodeScratch s;
 };
 
 // Launch helpers (defined in moe_decode.cu).
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream);
-cudaError_t launch_gate_up(const GateUpArgs &a, int T, int grid_cap, cudaStream_t stream);
-cudaError_t launch_down(const DownArgs &a, int grid_cap, cudaStream_t stream);
 
-// Scratch byte size for a bank of E experts, hidden H, intermediate I.
+// TMA-pipelined expert GEMVs (moe_stream.cu).
+cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *const scales[3], int E, int H,
+                             int I);
+cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, int sms, cudaStream_t stream);
+cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream);
+
+// Scratch byte size for a bank of E experts, hidden H, intermediate I, and
+// the prefix of it that the routing kernel alone uses.
 size_t decode_scratch_bytes(int E, int H, int I);
+size_t decode_route_scratch_bytes(int E, int H);
 size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I);
 
 }  // namespace nvfp4

@@ -1,0 +1,501 @@
+// TMA-fed expert GEMVs of the decode path.
+//
+// Both kernels are persistent: one producer warp streams weight tiles into a
+// ring of shared-memory stages with 2D TMA loads (no multicast), four
+// consumer warps decode E2M1 x E4M3 to f16 in registers and run m16n8k16
+// MMAs against the FP16 tokens, and mbarriers hand stages back and forth.
+// Every mbarrier wait is bounded (tma_util.cuh) and reports a timeout through
+// the scratch error word.
+//
+// moe_gate_up_tma_kernel  item = (active expert, 32 rows of the intermediate
+//                          dimension); gate and up tiles stream together,
+//                          SiLU(gate) * up is written as FP16.
+// moe_down_tma_kernel     item = (active expert, 64 rows of hidden); each
+//                          expert's FP32 output, scaled by routing weight and
+//                          inverse global scale, is written per (token, slot);
+//                          the last CTA to finish a 64-row tile sums the nine
+//                          slots in slot order (the lab's reduce,
+//                          nvfp4_gemv.cl:1443-1457) and adds the residual.
+//
+// Weight tiles land in shared memory with the 128-byte TMA swizzle: 16-byte
+// unit u of row r sits at r*128 + ((u ^ (r & 7)) << 4). Lane (g, c) reads
+// units 2c and 2c+1 of rows g and g+8, which maps the eight lanes of each
+// LDS.128 phase onto eight distinct bank groups.
+#include "moe_decode.cuh"
+#include "tma_util.cuh"
+
+namespace nvfp4 {
+
+namespace {
+
+constexpr int kBoxK = 256;            // K elements per TMA box (128 bytes)
+constexpr int kBoxBytes = 128;
+constexpr int kConsumerWarps = 4;
+constexpr int kThreads = (kConsumerWarps + 1) * 32;
+
+constexpr int kGuRows = 32;
+constexpr int kGuBoxes = 4;           // boxes per stage and projection
+constexpr int kGuStages = 5;
+constexpr int kGuPacked = kGuBoxes * kGuRows * kBoxBytes;   // 16 KB per projection
+constexpr int kGuScales = kGuRows * kGuBoxes * 16;          // 2 KB per projection
+constexpr int kGuStageBytes = 2 * kGuPacked + 2 * kGuScales;
+
+constexpr int kDnRows = 64;
+constexpr int kDnBoxes = 4;
+constexpr int kDnStages = 6;
+constexpr int kDnPacked = kDnBoxes * kDnRows * kBoxBytes;   // 32 KB
+constexpr int kDnScales = kDnRows * kDnBoxes * 16;          // 4 KB
+constexpr int kDnStageBytes = kDnPacked + kDnScales;
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+    return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+// Decode one 16-byte unit (32 columns, two E4M3 blocks) of a row into 16
+// f16x2 words multiplied by their block scales; `sc` holds the two scale
+// bytes (low byte = first block).
+__device__ __forceinline__ void decode_unit(const uint4 &u, uint16_t sc, uint32_t (&h)[16]) {
+    const uint32_t s2 = e4m3x2_to_f16x2(sc);
+    const uint32_t m0 = f16x2_lo_lo(s2), m1 = f16x2_hi_hi(s2);
+    const uint32_t *w = &u.x;
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+        uint32_t t[4];
+        e2m1x8_to_f16x8(w[v], t);
+        const uint32_t m = v < 2 ? m0 : m1;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) h[4 * v + j] = hmul2_u32(t[j], m);
+    }
+}
+
+// ------------------------------------------------------------ gate / up
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_gate_up_tma_kernel(const __grid_constant__ CUtensorMap tm_gp, const __grid_constant__ CUtensorMap tm_gs,
+                           const __grid_constant__ CUtensorMap tm_up, const __grid_constant__ CUtensorMap tm_us,
+                           GateUpArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kGuStages * kGuStageBytes);
+    uint64_t *empty = full + kGuStages;
+    float *red = reinterpret_cast<float *>(empty + kGuStages);  // [2 mtile][2 proj][NT][4][32]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const DecodeScratch &s = a.s;
+    int *err = s.error;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kGuStages; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int H = a.H, I = a.I, E = a.E;
+    const int nact = *s.n_active;
+    const int mtiles = I / kGuRows;
+    const int items = nact * mtiles;
+    const int kboxes = (H + kBoxK - 1) / kBoxK;
+    const int slices = (kboxes + kGuBoxes - 1) / kGuBoxes;
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            prefetch_tensormap(&tm_gp);
+            prefetch_tensormap(&tm_up);
+            prefetch_tensormap(&tm_gs);
+            prefetch_tensormap(&tm_us);
+            uint32_t it = 0;
+            for (int item = blockIdx.x; item < items; item += gridDim.x) {
+                const int ai = item / mtiles, mt = item - ai * mtiles;
+                const int y = s.active_expert[ai] * I + mt * kGuRows;
+                const int ntok = s.tok_count[ai];
+                for (int tg = 0; tg < ntok; tg += NT * 8) {
+                    for (int sl = 0; sl < slices; ++sl, ++it) {
+                        const int st = it % kGuStages;
+                        const uint32_t ph = (it / kGuStages) & 1u;
+                        if (!mbar_wait(empty + st, ph ^ 1u, err)) return;
+                        mbar_arrive_expect_tx(full + st, kGuStageBytes);
+                        uint8_t *stage = smem + st * kGuStageBytes;
+#pragma unroll
+                        for (int b = 0; b < kGuBoxes; ++b) {
+                            const int x = (sl * kGuBoxes + b) * kBoxBytes;
+                            tma_load_2d(stage + b * kGuRows * kBoxBytes, &tm_gp, full + st, x, y);
+                            tma_load_2d(stage + kGuPacked + b * kGuRows * kBoxBytes, &tm_up, full + st, x, y);
+                        }
+                        tma_load_2d(stage + 2 * kGuPacked, &tm_gs, full + st, sl * kGuBoxes * 16, y);
+                        tma_load_2d(stage + 2 * kGuPacked + kGuScales, &tm_us, full + st, sl * kGuBoxes * 16, y);
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    const int mtile = warp & 1, kh = warp >> 1;
+    const int g = lane >> 2, c = lane & 3;
+    const int r0 = mtile * 16 + g, r1 = r0 + 8;
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int ai = item / mtiles, mt = item - ai * mtiles;
+        const int e = s.active_expert[ai];
+        const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+        const float inv_gate = a.inv_scales[e];
+        const float inv_up = a.inv_scales[(E + 1) + e];
+        for (int tg = 0; tg < ntok; tg += NT * 8) {
+            const int ncols = min(NT * 8, ntok - tg);
+            const __half *xrow[NT];
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+                const int j = tg + n * 8 + g;
+                xrow[n] = (n * 8 + g < ncols) ? s.x_f16 + (size_t)s.tok_list[tstart + j] * H : nullptr;
+            }
+            float cg[NT][4], cu[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) cg[n][r] = cu[n][r] = 0.0f;
+
+            for (int sl = 0; sl < slices; ++sl, ++it) {
+                const int st = it % kGuStages;
+                const uint32_t ph = (it / kGuStages) & 1u;
+                if (!mbar_wait(full + st, ph, err)) return;
+                const uint8_t *stage = smem + st * kGuStageBytes;
+                const uint8_t *gsc = stage + 2 * kGuPacked;
+                const uint8_t *usc = gsc + kGuScales;
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb) {
+                    const int b = kh * 2 + bb;
+                    const int kb = sl * kGuBoxes + b;
+                    if (kb >= kboxes) break;
+                    const uint8_t *gbox = stage + b * kGuRows * kBoxBytes;
+                    const uint8_t *ubox = stage + kGuPacked + b * kGuRows * kBoxBytes;
+                    const uint32_t sg0 = lds32(gsc + r0 * 64 + b * 16 + 4 * c);
+                    const uint32_t sg1 = lds32(gsc + r1 * 64 + b * 16 + 4 * c);
+                    const uint32_t su0 = lds32(usc + r0 * 64 + b * 16 + 4 * c);
+                    const uint32_t su1 = lds32(usc + r1 * 64 + b * 16 + 4 * c);
+#pragma unroll
+                    for (int uu = 0; uu < 2; ++uu) {
+                        const int unit = ((2 * c + uu) ^ g) << 4;
+                        uint32_t hg0[16], hg1[16], hu0[16], hu1[16];
+                        decode_unit(lds128(gbox + r0 * kBoxBytes + unit), (uint16_t)(sg0 >> (16 * uu)), hg0);
+                        decode_unit(lds128(gbox + r1 * kBoxBytes + unit), (uint16_t)(sg1 >> (16 * uu)), hg1);
+                        decode_unit(lds128(ubox + r0 * kBoxBytes + unit), (uint16_t)(su0 >> (16 * uu)), hu0);
+                        decode_unit(lds128(ubox + r1 * kBoxBytes + unit), (uint16_t)(su1 >> (16 * uu)), hu1);
+                        const int kcol = kb * kBoxK + 64 * c + 32 * uu;
+#pragma unroll
+                        for (int n = 0; n < NT; ++n) {
+                            if (n * 8 >= ncols) break;
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) {
+                                uint4 bv = make_uint4(0u, 0u, 0u, 0u);
+                                if (xrow[n]) bv = __ldg(reinterpret_cast<const uint4 *>(xrow[n] + kcol + 8 * w));
+                                mma_16816(cg[n], hg0[4 * w], hg1[4 * w], hg0[4 * w + 1], hg1[4 * w + 1], bv.x, bv.y);
+                                mma_16816(cg[n], hg0[4 * w + 2], hg1[4 * w + 2], hg0[4 * w + 3], hg1[4 * w + 3], bv.z,
+                                          bv.w);
+                                mma_16816(cu[n], hu0[4 * w], hu1[4 * w], hu0[4 * w + 1], hu1[4 * w + 1], bv.x, bv.y);
+                                mma_16816(cu[n], hu0[4 * w + 2], hu1[4 * w + 2], hu0[4 * w + 3], hu1[4 * w + 3], bv.z,
+                                          bv.w);
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + st);
+            }
+            // Fixed-order reduction of the two K halves, then SiLU(gate)*up.
+            if (kh == 1) {
+#pragma unroll
+                for (int n = 0; n < NT; ++n)
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        red[(((mtile * 2 + 0) * NT + n) * 4 + r) * 32 + lane] = cg[n][r];
+                        red[(((mtile * 2 + 1) * NT + n) * 4 + r) * 32 + lane] = cu[n][r];
+                    }
+            }
+            named_barrier(1, kConsumerWarps * 32);
+            if (kh == 0) {
+#pragma unroll
+                for (int n = 0; n < NT; ++n) {
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) {
+                        const int col = n * 8 + 2 * c + (r & 1);
+                        if (col < ncols) {
+                            const float gs = cg[n][r] + red[(((mtile * 2 + 0) * NT + n) * 4 + r) * 32 + lane];
+                            const float us = cu[n][r] + red[(((mtile * 2 + 1) * NT + n) * 4 + r) * 32 + lane];
+                            const float gate = gs * inv_gate;
+                            const float up = us * inv_up;
+                            const int rl = (r >= 2) ? r1 : r0;
+                            s.act[(size_t)(tstart + tg + col) * I + mt * kGuRows + rl] =
+                                __float2half_rn(gate / (1.0f + expf(-gate)) * up);
+                        }
+                    }
+                }
+            }
+            named_barrier(1, kConsumerWarps * 32);
+        }
+    }
+}
+
+// ------------------------------------------------------- down + combine
+
+template <int NT>
+__global__ void __launch_bounds__(kThreads, 1)
+    moe_down_tma_kernel(const __grid_constant__ CUtensorMap tm_dp, const __grid_constant__ CUtensorMap tm_ds,
+                        DownArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kDnStages * kDnStageBytes);
+    uint64_t *empty = full + kDnStages;
+    int *flag = reinterpret_cast<int *>(empty + kDnStages);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const DecodeScratch &s = a.s;
+    int *err = s.error;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kDnStages; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, kConsumerWarps);
+        }
+        fence_barrier_init();
+    }
+    __syncthreads();
+    const int H = a.H, I = a.I, T = a.T;
+    const int nact = *s.n_active;
+    const int rtiles = H / kDnRows;
+    const int items = nact * rtiles;
+    const int kboxes = (I + kBoxK - 1) / kBoxK;
+    const int slices = (kboxes + kDnBoxes - 1) / kDnBoxes;
+    const int stage_boxes = kboxes < kDnBoxes ? kboxes : kDnBoxes;
+    const uint32_t stage_tx = stage_boxes * kDnRows * kBoxBytes + kDnRows * stage_boxes * 16;
+
+    if (warp == kConsumerWarps) {
+        if (lane == 0) {
+            prefetch_tensormap(&tm_dp);
+            prefetch_tensormap(&tm_ds);
+            uint32_t it = 0;
+            for (int item = blockIdx.x; item < items; item += gridDim.x) {
+                const int ai = item / rtiles, rt = item - ai * rtiles;
+                const int y = s.active_expert[ai] * H + rt * kDnRows;
+                const int ntok = s.tok_count[ai];
+                for (int tg = 0; tg < ntok; tg += NT * 8) {
+                    for (int sl = 0; sl < slices; ++sl, ++it) {
+                        const int st = it % kDnStages;
+                        const uint32_t ph = (it / kDnStages) & 1u;
+                        if (!mbar_wait(empty + st, ph ^ 1u, err)) return;
+                        mbar_arrive_expect_tx(full + st, stage_tx);
+                        uint8_t *stage = smem + st * kDnStageBytes;
+                        for (int b = 0; b < stage_boxes; ++b)
+                            tma_load_2d(stage + b * kDnRows * kBoxBytes, &tm_dp, full + st,
+                                        (sl * kDnBoxes + b) * kBoxBytes, y);
+                        tma_load_2d(stage + kDnPacked, &tm_ds, full + st, sl * kDnBoxes * 16, y);
+                    }
+                }
+            }
+        }
+        return;
+    }
+
+    const int g = lane >> 2, c = lane & 3;
+    const int r0 = warp * 16 + g, r1 = r0 + 8;
+    const int sstride = stage_boxes * 16;  // scale bytes per row in a stage
+    uint32_t it = 0;
+    for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int ai = item / rtiles, rt = item - ai * rtiles;
+        const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+        for (int tg = 0; tg < ntok; tg += NT * 8) {
+            const int ncols = min(NT * 8, ntok - tg);
+            const __half *arow[NT];
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+                arow[n] = (n * 8 + g < ncols) ? s.act + (size_t)(tstart + tg + n * 8 + g) * I : nullptr;
+            float cd[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) cd[n][r] = 0.0f;
+            for (int sl = 0; sl < slices; ++sl, ++it) {
+                const int st = it % kDnStages;
+                const uint32_t ph = (it / kDnStages) & 1u;
+                if (!mbar_wait(full + st, ph, err)) return;
+                const uint8_t *stage = smem + st * kDnStageBytes;
+                const uint8_t *sc = stage + kDnPacked;
+                for (int b = 0; b < stage_boxes; ++b) {
+                    const int kb = sl * kDnBoxes + b;
+                    if (kb >= kboxes) break;
+                    const uint8_t *box = stage + b * kDnRows * kBoxBytes;
+                    const uint32_t s0 = lds32(sc + r0 * sstride + b * 16 + 4 * c);
+                    const uint32_t s1 = lds32(sc + r1 * sstride + b * 16 + 4 * c);
+#pragma unroll
+                    for (int uu = 0; uu < 2; ++uu) {
+                        const int unit = ((2 * c + uu) ^ g) << 4;
+                        uint32_t h0[16], h1[16];
+                        decode_unit(lds128(box + r0 * kBoxBytes + unit), (uint16_t)(s0 >> (16 * uu)), h0);
+                        decode_unit(lds128(box + r1 * kBoxBytes + unit), (uint16_t)(s1 >> (16 * uu)), h1);
+                        const int kcol = kb * kBoxK + 64 * c + 32 * uu;
+#pragma unroll
+                        for (int n = 0; n < NT; ++n) {
+                            if (n * 8 >= ncols) break;
+#pragma unroll
+                            for (int w = 0; w < 4; ++w) {
+                                uint4 bv = make_uint4(0u, 0u, 0u, 0u);
+                                if (arow[n]) bv = __ldcg(reinterpret_cast<const uint4 *>(arow[n] + kcol + 8 * w));
+                                mma_16816(cd[n], h0[4 * w], h1[4 * w], h0[4 * w + 1], h1[4 * w + 1], bv.x, bv.y);
+                                mma_16816(cd[n], h0[4 * w + 2], h1[4 * w + 2], h0[4 * w + 3], h1[4 * w + 3], bv.z,
+                                          bv.w);
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(empty + st);
+            }
+            // Scaled partial output of this expert for each of its tokens.
+#pragma unroll
+            for (int n = 0; n < NT; ++n) {
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    const int col = n * 8 + 2 * c + (r & 1);
+                    if (col < ncols) {
+                        const int j = tg + col;
+                        const int t = s.tok_list[tstart + j];
+                        const float coef = s.coef_tab[ai * kDecodeMaxTokens + t];
+                        const int row = rt * kDnRows + ((r >= 2) ? r1 : r0);
+                        s.ypart[(size_t)(tstart + j) * H + row] = coef * cd[n][r];
+                    }
+                }
+            }
+        }
+        // The last item to finish this 64-row tile combines it.
+        __threadfence();
+        named_barrier(1, kConsumerWarps * 32);
+        if (threadIdx.x == 0) {
+            const unsigned old = atomicAdd(s.tile_count + rt, 1u);
+            *flag = (old == (unsigned)(nact - 1)) ? 1 : 0;
+        }
+        named_barrier(1, kConsumerWarps * 32);
+        if (*flag) {
+            __threadfence();
+            for (int i = threadIdx.x; i < T * kDnRows; i += kConsumerWarps * 32) {
+                const int t = i / kDnRows, h = rt * kDnRows + (i - t * kDnRows);
+                float v = 0.0f;
+#pragma unroll
+                for (int k = 0; k < kTopK; ++k) {
+                    const int pos = __ldcg(s.inv_pos + t * kTopK + k);
+                    if (pos >= 0) v += __ldcg(s.ypart + (size_t)pos * H + h);
+                }
+                if (a.shared_here) v += __ldcg(s.ypart + (size_t)(T * kTopK + t) * H + h);
+                const size_t o = (size_t)t * H + h;
+                if (a.out_f32) {
+                    static_cast<float *>(a.out)[o] = v;
+                } else {
+                    if (a.residual) v += bf16_bits_to_f32(static_cast<const uint16_t *>(a.residual)[o]);
+                    static_cast<uint16_t *>(a.out)[o] = f32_to_bf16_bits(v);
+                }
+            }
+            named_barrier(1, kConsumerWarps * 32);
+            if (threadIdx.x == 0) s.tile_count[rt] = 0u;
+        }
+        named_barrier(1, kConsumerWarps * 32);
+    }
+}
+
+template <typename K>
+cudaError_t set_smem_once(K kernel, size_t bytes) {
+    static int done_device = -1;
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (done_device == dev) return cudaSuccess;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) done_device = dev;
+    return err;
+}
+
+template <int NT>
+cudaError_t launch_gate_up_tma_nt(const StreamMaps &m, const GateUpArgs &a, int items_ub, int sms,
+                                  cudaStream_t stream) {
+    const size_t smem = 1024 + kGuStages * kGuStageBytes + 2 * kGuStages * 8 + 2 * 2 * NT * 4 * 32 * 4;
+    cudaError_t err = set_smem_once(moe_gate_up_tma_kernel<NT>, smem);
+    if (err != cudaSuccess) return err;
+    const int grid = items_ub < sms ? items_ub : sms;
+    moe_gate_up_tma_kernel<NT><<<grid, kThreads, smem, stream>>>(m.packed[0], m.scales[0], m.packed[1],
+                                                                  m.scales[1], a);
+    return cudaGetLastError();
+}
+
+template <int NT>
+cudaError_t launch_down_tma_nt(const StreamMaps &m, const DownArgs &a, int items_ub, int sms,
+                               cudaStream_t stream) {
+    const size_t smem = 1024 + kDnStages * kDnStageBytes + 2 * kDnStages * 8 + 16;
+    cudaError_t err = set_smem_once(moe_down_tma_kernel<NT>, smem);
+    if (err != cudaSuccess) return err;
+    const int grid = items_ub < sms ? items_ub : sms;
+    moe_down_tma_kernel<NT><<<grid, kThreads, smem, stream>>>(m.packed[2], m.scales[2], a);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t make_tensor_map_u8(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows,
+                               uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+    using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (err != cudaSuccess) return err;
+        if (q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {box_bytes, box_rows};
+    const cuuint32_t elem[2] = {1, 1};
+    const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
+                              elem, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
+}
+
+cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *const scales[3], int E, int H,
+                             int I) {
+    const uint64_t slots = static_cast<uint64_t>(E) + 1;
+    for (int p = 0; p < 3; ++p) {
+        const uint64_t rows = slots * (p < 2 ? I : H);
+        const uint64_t k = p < 2 ? H : I;
+        const uint32_t box_rows = p < 2 ? kGuRows : kDnRows;
+        const uint32_t scale_box = (p < 2 ? kGuBoxes : (((k + kBoxK - 1) / kBoxK) < kDnBoxes
+                                                          ? (uint32_t)((k + kBoxK - 1) / kBoxK) : kDnBoxes)) * 16;
+        cudaError_t err = make_tensor_map_u8(&m.packed[p], packed[p], k / 2, rows, kBoxBytes, box_rows,
+                                             CU_TENSOR_MAP_SWIZZLE_128B);
+        if (err != cudaSuccess) return err;
+        err = make_tensor_map_u8(&m.scales[p], scales[p], k / 16, rows, scale_box, box_rows,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (err != cudaSuccess) return err;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, int sms, cudaStream_t stream) {
+    const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
+    const int items_ub = (routed_ub + 1) * (a.I / kGuRows);
+    if (T <= 8) return launch_gate_up_tma_nt<1>(m, a, items_ub, sms, stream);
+    if (T <= 16) return launch_gate_up_tma_nt<2>(m, a, items_ub, sms, stream);
+    return launch_gate_up_tma_nt<4>(m, a, items_ub, sms, stream);
+}
+
+cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream) {
+    const int T = a.T;
+    const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
+    const int items_ub = (routed_ub + 1) * (a.H / kDnRows);
+    if (T <= 8) return launch_down_tma_nt<1>(m, a, items_ub, sms, stream);
+    if (T <= 16) return launch_down_tma_nt<2>(m, a, items_ub, sms, stream);
+    return launch_down_tma_nt<4>(m, a, items_ub, sms, stream);
+}
+
+}  // namespace nvfp4

@@ -17,8 +17,8 @@
 // process exits.
 //
 // Sharing: every call, on every stream, uses the same array, which keeps
-// whatever the last call left in it. The call clears the one word that has
-// to start at zero (the last-block ticket) before launching. Two calls whose
+// whatever the last call left in it. The call clears the words that have to
+// start at zero (the last-block tickets) before launching. Two calls whose
 // kernels overlap on the GPU -- different streams without ordering, or
 // several threads -- race on the array and produce garbage; order them.
 //
@@ -74,7 +74,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_route_static_scratch(
         return fail_invalid("static-scratch routing takes 8 to 256 experts");
     if (hidden <= 0 || hidden % 128 != 0 || hidden > kRouteStaticMaxHidden)
         return fail_invalid("static-scratch routing needs hidden to be a multiple of 128, at most 4096");
-    const size_t tables = decode_scratch_bytes(experts, hidden, kRouteStaticCarveIntermediate);
+    const size_t tables = decode_route_scratch_bytes(experts, hidden);
     const size_t inv_bytes = 3 * (static_cast<size_t>(experts) + 1) * sizeof(float);
     if (tables + inv_bytes > kRouteStaticScratchBytes)
         return fail_invalid("routing working set exceeds the 1 MiB static scratch array");
@@ -90,9 +90,10 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_route_static_scratch(
         if (counts) ds.counts = counts;
         if (perm) ds.perm = perm;
         float *inv_scales = reinterpret_cast<float *>(static_cast<unsigned char *>(base) + tables);
-        // The ticket must start at zero; the inverse-scale table only feeds
+        // The tickets must start at zero; the inverse-scale table only feeds
         // internal per-expert coefficients, zero is a valid value.
-        check_cuda(cudaMemsetAsync(ds.ticket, 0, sizeof(unsigned), s), "cudaMemsetAsync(ticket)");
+        check_cuda(cudaMemsetAsync(ds.ticket, 0, kRouteTickets * sizeof(unsigned), s),
+                   "cudaMemsetAsync(tickets)");
         check_cuda(cudaMemsetAsync(inv_scales, 0, inv_bytes, s), "cudaMemsetAsync(inverse scales)");
         RouteArgs ra{};
         ra.router = static_cast<const uint16_t *>(router_bf16);
