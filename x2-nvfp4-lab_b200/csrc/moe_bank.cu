@@ -51,15 +51,24 @@ struct nvfp4_moe_bank {
     size_t cols(int projection) const { return projection < 2 ? hidden : intermediate; }
     size_t per_packed() const { return static_cast<size_t>(hidden) * intermediate / 2; }
     size_t per_scales() const { return static_cast<size_t>(hidden) * intermediate / 16; }
+    // Device row pitch of a projection's scale bytes: cols/16 rounded up to
+    // 16 so every row starts on a 16-byte boundary (a TMA requirement); the
+    // padding bytes stay zero.
+    size_t scale_pitch(int projection) const { return (cols(projection) / 16 + 15) & ~size_t(15); }
+    size_t scales_per_expert(int projection) const { return rows(projection) * scale_pitch(projection); }
 };
 
 namespace {
 
-__global__ void sanitize_scales_kernel(uint8_t *dst, const uint8_t *src, size_t n) {
+// Copy `rows` rows of `cols` scale bytes into a pitched destination,
+// clearing the sign bit and mapping 0x7F to 0 (the lab's decoding rule).
+__global__ void sanitize_scales_kernel(uint8_t *dst, size_t pitch, const uint8_t *src, size_t rows, size_t cols) {
+    const size_t n = rows * cols;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n;
          i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / cols, c = i - r * cols;
         const uint8_t b = src[i] & 0x7Fu;
-        dst[i] = b == 0x7Fu ? 0u : b;
+        dst[r * pitch + c] = b == 0x7Fu ? 0u : b;
     }
 }
 
@@ -186,13 +195,15 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
             throw std::overflow_error("MoE bank dimensions overflow size_t");
         const size_t elements = slots * static_cast<size_t>(hidden) * intermediate;
         std::lock_guard<std::mutex> lock(runtime->queue_mutex);
+        size_t scale_bytes_all = 0;
         for (int p = 0; p < 3; ++p) {
+            const size_t sb = slots * holder->scales_per_expert(p);
+            scale_bytes_all += sb;
             check_cuda(cudaMalloc(&holder->packed[p], elements / 2), "cudaMalloc(MoE bank packed)");
-            check_cuda(cudaMalloc(&holder->scales[p], elements / 16), "cudaMalloc(MoE bank scales)");
+            check_cuda(cudaMalloc(&holder->scales[p], sb), "cudaMalloc(MoE bank scales)");
             check_cuda(cudaMemsetAsync(holder->packed[p], 0, elements / 2, runtime->stream),
                        "cudaMemsetAsync(MoE bank packed)");
-            check_cuda(cudaMemsetAsync(holder->scales[p], 0, elements / 16, runtime->stream),
-                       "cudaMemsetAsync(MoE bank scales)");
+            check_cuda(cudaMemsetAsync(holder->scales[p], 0, sb, runtime->stream), "cudaMemsetAsync(MoE bank scales)");
         }
         check_cuda(cudaMalloc(&holder->inv_scales, 3 * slots * sizeof(float)),
                    "cudaMalloc(MoE bank inverse scales)");
@@ -214,8 +225,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
                    "cuTensorMapEncodeTiled(MoE bank)");
         check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize(MoE bank create)");
         holder->uploaded.assign(slots * 3, 0);
-        holder->resident_bytes = 3 * (elements / 2 + elements / 16) + 3 * slots * sizeof(float) +
-                                 router_all;
+        holder->resident_bytes = 3 * (elements / 2) + scale_bytes_all + 3 * slots * sizeof(float) + router_all;
         clear_last_error();
         *out_bank = holder.release();
         return NVFP4_STATUS_OK;
@@ -243,9 +253,11 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection(
         check_cuda(cudaMemcpy(bank->packed[projection] + static_cast<size_t>(expert) * pp, packed, pp,
                               cudaMemcpyHostToDevice),
                    "cudaMemcpy(MoE bank packed upload)");
-        check_cuda(cudaMemcpy(bank->scales[projection] + static_cast<size_t>(expert) * ps,
-                              clean.data(), ps, cudaMemcpyHostToDevice),
-                   "cudaMemcpy(MoE bank scale upload)");
+        const size_t scols = bank->cols(projection) / 16, pitch = bank->scale_pitch(projection);
+        check_cuda(cudaMemcpy2D(bank->scales[projection] + static_cast<size_t>(expert) *
+                                                               bank->scales_per_expert(projection),
+                                pitch, clean.data(), scols, scols, bank->rows(projection), cudaMemcpyHostToDevice),
+                   "cudaMemcpy2D(MoE bank scale upload)");
         const float inv = 1.0f / weight_global_scale;
         const size_t slots = static_cast<size_t>(bank->experts) + 1;
         check_cuda(cudaMemcpy(bank->inv_scales + static_cast<size_t>(projection) * slots + expert, &inv,
@@ -274,8 +286,9 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection_device(
                    "cudaMemcpyAsync(MoE bank packed upload)");
         const int grid = static_cast<int>((ps + 255) / 256 < 4096 ? (ps + 255) / 256 : 4096);
         sanitize_scales_kernel<<<grid, 256, 0, rt->stream>>>(
-            bank->scales[projection] + static_cast<size_t>(expert) * ps,
-            static_cast<const uint8_t *>(scales_device), ps);
+            bank->scales[projection] + static_cast<size_t>(expert) * bank->scales_per_expert(projection),
+            bank->scale_pitch(projection), static_cast<const uint8_t *>(scales_device), bank->rows(projection),
+            bank->cols(projection) / 16);
         check_cuda(cudaGetLastError(), "sanitize_scales_kernel");
         const float inv = 1.0f / weight_global_scale;
         const size_t slots = static_cast<size_t>(bank->experts) + 1;

@@ -438,8 +438,8 @@ cudaError_t launch_down_tma_nt(const StreamMaps &m, const DownArgs &a, int items
 
 }  // namespace
 
-cudaError_t make_tensor_map_u8(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows,
-                               uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
+cudaError_t make_tensor_map_u8(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t pitch,
+                               uint64_t rows, uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle swizzle) {
     using EncodeFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -453,7 +453,7 @@ cudaError_t make_tensor_map_u8(CUtensorMap *map, const void *base, uint64_t row_
         encode = reinterpret_cast<EncodeFn>(fn);
     }
     const cuuint64_t dims[2] = {row_bytes, rows};
-    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint64_t strides[1] = {pitch};
     const cuuint32_t box[2] = {box_bytes, box_rows};
     const cuuint32_t elem[2] = {1, 1};
     const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box,
@@ -471,10 +471,11 @@ cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *c
         const uint32_t box_rows = p < 2 ? kGuRows : kDnRows;
         const uint32_t scale_box = (p < 2 ? kGuBoxes : (((k + kBoxK - 1) / kBoxK) < kDnBoxes
                                                           ? (uint32_t)((k + kBoxK - 1) / kBoxK) : kDnBoxes)) * 16;
-        cudaError_t err = make_tensor_map_u8(&m.packed[p], packed[p], k / 2, rows, kBoxBytes, box_rows,
+        cudaError_t err = make_tensor_map_u8(&m.packed[p], packed[p], k / 2, k / 2, rows, kBoxBytes, box_rows,
                                              CU_TENSOR_MAP_SWIZZLE_128B);
         if (err != cudaSuccess) return err;
-        err = make_tensor_map_u8(&m.scales[p], scales[p], k / 16, rows, scale_box, box_rows,
+        err = make_tensor_map_u8(&m.scales[p], scales[p], k / 16, (k / 16 + 15) & ~uint64_t(15), rows, scale_box,
+                                 box_rows,
                                  CU_TENSOR_MAP_SWIZZLE_NONE);
         if (err != cudaSuccess) return err;
     }

@@ -84,9 +84,10 @@ __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
-// Host: encode a 2D uint8 tensor map over a row-major [rows, row_bytes]
-// array with a box of [box_rows, box_bytes] and the given swizzle.
-cudaError_t make_tensor_map_u8(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t rows,
-                               uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle swizzle);
+// Host: encode a 2D uint8 tensor map over a row-major array of `rows` rows
+// holding `row_bytes` valid bytes each at a row pitch of `pitch` bytes (a
+// multiple of 16), with a box of [box_rows, box_bytes] and the given swizzle.
+cudaError_t make_tensor_map_u8(CUtensorMap *map, const void *base, uint64_t row_bytes, uint64_t pitch,
+                               uint64_t rows, uint32_t box_bytes, uint32_t box_rows, CUtensorMapSwizzle swizzle);
 
 }  // namespace nvfp4
