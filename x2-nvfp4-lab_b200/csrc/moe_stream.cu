@@ -24,6 +24,8 @@
 #include "moe_decode.cuh"
 #include "tma_util.cuh"
 
+#include <atomic>
+
 namespace nvfp4 {
 
 namespace {
@@ -401,15 +403,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Raise a kernel's dynamic shared-memory limit once per device. `done` is a
+// per-kernel bitmask of devices already configured.
 template <typename K>
-cudaError_t set_smem_once(K kernel, size_t bytes) {
-    static int done_device = -1;
+cudaError_t set_smem_once(K kernel, size_t bytes, std::atomic<uint64_t> &done) {
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
-    if (done_device == dev) return cudaSuccess;
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load() & bit)) return cudaSuccess;
     err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-    if (err == cudaSuccess) done_device = dev;
+    if (err == cudaSuccess) done.fetch_or(bit);
     return err;
 }
 
@@ -417,7 +421,8 @@ template <int NT>
 cudaError_t launch_gate_up_tma_nt(const StreamMaps &m, const GateUpArgs &a, int items_ub, int sms,
                                   cudaStream_t stream) {
     const size_t smem = 1024 + kGuStages * kGuStageBytes + 2 * kGuStages * 8 + 2 * 2 * NT * 4 * 32 * 4;
-    cudaError_t err = set_smem_once(moe_gate_up_tma_kernel<NT>, smem);
+    static std::atomic<uint64_t> done{0};
+    cudaError_t err = set_smem_once(moe_gate_up_tma_kernel<NT>, smem, done);
     if (err != cudaSuccess) return err;
     const int grid = items_ub < sms ? items_ub : sms;
     moe_gate_up_tma_kernel<NT><<<grid, kThreads, smem, stream>>>(m.packed[0], m.scales[0], m.packed[1],
@@ -429,7 +434,8 @@ template <int NT>
 cudaError_t launch_down_tma_nt(const StreamMaps &m, const DownArgs &a, int items_ub, int sms,
                                cudaStream_t stream) {
     const size_t smem = 1024 + kDnStages * kDnStageBytes + 2 * kDnStages * 8 + 16;
-    cudaError_t err = set_smem_once(moe_down_tma_kernel<NT>, smem);
+    static std::atomic<uint64_t> done{0};
+    cudaError_t err = set_smem_once(moe_down_tma_kernel<NT>, smem, done);
     if (err != cudaSuccess) return err;
     const int grid = items_ub < sms ? items_ub : sms;
     moe_down_tma_kernel<NT><<<grid, kThreads, smem, stream>>>(m.packed[2], m.scales[2], a);
