@@ -17,6 +17,10 @@
 //                          slots in slot order (the lab's reduce,
 //                          nvfp4_gemv.cl:1443-1457) and adds the residual.
 //
+// A 256-column box may extend past the end of K (K is a multiple of 128):
+// TMA fills the weight side with zeros and the token side is not loaded
+// there, so no stale value can enter a product.
+//
 // Weight tiles land in shared memory with the 128-byte TMA swizzle: 16-byte
 // unit u of row r sits at r*128 + ((u ^ (r & 7)) << 4). Lane (g, c) reads
 // units 2c and 2c+1 of rows g and g+8, which maps the eight lanes of each
@@ -193,7 +197,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int w = 0; w < 4; ++w) {
                                 uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-                                if (xrow[n]) bv = __ldg(reinterpret_cast<const uint4 *>(xrow[n] + kcol + 8 * w));
+                                if (xrow[n] && kcol < H) bv = __ldg(reinterpret_cast<const uint4 *>(xrow[n] + kcol + 8 * w));
                                 mma_16816(cg[n], hg0[4 * w], hg1[4 * w], hg0[4 * w + 1], hg1[4 * w + 1], bv.x, bv.y);
                                 mma_16816(cg[n], hg0[4 * w + 2], hg1[4 * w + 2], hg0[4 * w + 3], hg1[4 * w + 3], bv.z,
                                           bv.w);
@@ -342,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int w = 0; w < 4; ++w) {
                                 uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-                                if (arow[n]) bv = __ldcg(reinterpret_cast<const uint4 *>(arow[n] + kcol + 8 * w));
+                                if (arow[n] && kcol < I) bv = __ldcg(reinterpret_cast<const uint4 *>(arow[n] + kcol + 8 * w));
                                 mma_16816(cd[n], h0[4 * w], h1[4 * w], h0[4 * w + 1], h1[4 * w + 1], bv.x, bv.y);
                                 mma_16816(cd[n], h0[4 * w + 2], h1[4 * w + 2], h0[4 * w + 3], h1[4 * w + 3], bv.z,
                                           bv.w);
