@@ -318,6 +318,7 @@ def run_ours(args) -> int:
     x1 = [p[:1].contiguous() for p in pool]
     o1 = torch.empty(1, H, dtype=torch.bfloat16, device="cuda")
     torch.cuda.synchronize()
+    rt.set_trace_enabled(True)
     with torch.cuda.stream(stream):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(40)]
         torch.cuda._sleep(int(2e5) * 45)
@@ -329,6 +330,11 @@ def run_ours(args) -> int:
             if i >= 5:
                 ev[i - 5][1].record(stream)
     stream.synchronize()
+    rt.synchronize()
+    t1_ops: dict[str, list[float]] = {}
+    for evt in rt.trace_events()[-3 * 40:]:
+        t1_ops.setdefault(evt.operation, []).append(evt.duration_ns / 1e3)
+    rt.set_trace_enabled(False)
     lat = sorted(a.elapsed_time(b) * 1000.0 for a, b in ev)
 
     # End to end through the lab-style C-ABI sequence with host buffers.
@@ -407,6 +413,7 @@ def run_ours(args) -> int:
             "decode_t1_us": {"median": round(lat[len(lat) // 2], 3), "p10": round(lat[len(lat) // 10], 3),
                              "p90": round(lat[(9 * len(lat)) // 10], 3)},
             "kernels_ms_avg": {k: round(sum(v) / len(v), 5) for k, v in by_op.items()},
+            "decode_t1_kernels_us": {k: round(statistics.median(v), 3) for k, v in t1_ops.items()},
             "roofline": {
                 "kernel": "moe_gate_up",
                 "bound": "hbm",

@@ -10,6 +10,7 @@
 #include <mutex>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 namespace nvfp4 {
@@ -63,6 +64,9 @@ struct nvfp4_runtime {
     std::vector<cudaEvent_t> event_pool;
     std::vector<nvfp4_trace_event> last_trace;
     nvfp4_profile last_profile{0, 0, 0};
+    // Device-side timeout words of the banks on this runtime: a pinned
+    // host-mapped copy that kernels store to, and the device word they poll.
+    std::vector<std::pair<volatile int *, int *>> error_words;
     cudaEvent_t epoch_event = nullptr;      // device-time origin of the trace
     uint64_t epoch_host_ns = 0;             // host clock when epoch was recorded
     bool epoch_valid = false;

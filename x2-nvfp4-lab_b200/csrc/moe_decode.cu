@@ -1,6 +1,8 @@
 // Decode-path kernels; see moe_decode.cuh for the launch sequence.
 #include "moe_decode.cuh"
+#include "tma_util.cuh"
 
+#include <atomic>
 #include <cfloat>
 
 namespace nvfp4 {
@@ -19,11 +21,6 @@ __device__ __forceinline__ unsigned float_order_key(float v) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-__device__ __forceinline__ float load_x(const RouteArgs &a, int t, int k) {
-    if (a.x_is_f32) return __ldg(static_cast<const float *>(a.x) + (size_t)t * a.H + k);
-    return bf16_bits_to_f32(__ldg(static_cast<const uint16_t *>(a.x) + (size_t)t * a.H + k));
-}
-
 // ---------------------------------------------------------------- routing
 //
 // Router logit of token t and row r (row E = shared gate), FP32 throughout
@@ -35,9 +32,13 @@ __device__ __forceinline__ float load_x(const RouteArgs &a, int t, int k) {
 // The order is fixed, so the oracle reproduces every logit bit for bit.
 //
 // Grid: x = blocks of 4 router rows (one warp each), y = blocks of 4 tokens.
-// The last CTA of a token block to finish runs top-8 for those tokens (one
-// warp per token); the last token block to finish then dispatches.
+// Each CTA first copies its tokens (a contiguous [tt][H] range of x in the
+// caller's format) into shared memory with 16-byte cp.async, so the dot
+// products read x without further global round trips. The last CTA of a
+// token block to finish runs top-8 for those tokens (one warp per token); the
+// last token block to finish then dispatches.
 __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
+    extern __shared__ __align__(16) uint8_t route_xs[];   // [tt][H] of x, BF16 or FP32
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = a.E + 1;
     const int row = blockIdx.x * kRouteRowsPerCta + warp;
@@ -46,25 +47,54 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     const int t0 = blockIdx.y * kRouteTokens;
     const int tt = min(kRouteTokens, a.T - t0);
     DecodeScratch &s = a.s;
+    const int esz = a.x_is_f32 ? 4 : 2;
+
+    // Router rows do not depend on the tokens: start their loads first.
+    uint2 wv[kRouteChunkBatch];
+    const uint16_t *w = a.router + (size_t)min(row, R - 1) * H;
+#pragma unroll
+    for (int q = 0; q < kRouteChunkBatch; ++q)
+        if (q < chunks) wv[q] = __ldg(reinterpret_cast<const uint2 *>(w + q * 128 + lane * 4));
+    {
+        const uint8_t *src = static_cast<const uint8_t *>(a.x) + (size_t)t0 * H * esz;
+        if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
+            const int n16 = tt * H * esz / 16;
+            for (int i = threadIdx.x; i < n16; i += blockDim.x) cp_async16(route_xs + 16 * i, src + 16 * i);
+            cp_async_wait_all();
+        } else if (a.x_is_f32) {
+            for (int i = threadIdx.x; i < tt * H; i += blockDim.x)
+                reinterpret_cast<float *>(route_xs)[i] = __ldg(reinterpret_cast<const float *>(src) + i);
+        } else {
+            for (int i = threadIdx.x; i < tt * H; i += blockDim.x)
+                reinterpret_cast<uint16_t *>(route_xs)[i] = __ldg(reinterpret_cast<const uint16_t *>(src) + i);
+        }
+    }
+    __syncthreads();
 
     // FP16 copy of x for the expert GEMVs (row block 0 converts its tokens).
     if (blockIdx.x == 0) {
-        for (int j = 0; j < tt; ++j)
-            for (int k = threadIdx.x * 2; k < H; k += blockDim.x * 2)
-                *reinterpret_cast<__half2 *>(s.x_f16 + (size_t)(t0 + j) * H + k) =
-                    __floats2half2_rn(load_x(a, t0 + j, k), load_x(a, t0 + j, k + 1));
+        for (int i = threadIdx.x; i < tt * H / 2; i += blockDim.x) {
+            float2 v;
+            if (a.x_is_f32) {
+                v = reinterpret_cast<const float2 *>(route_xs)[i];
+            } else {
+                const uint32_t b = reinterpret_cast<const uint32_t *>(route_xs)[i];
+                v = make_float2(bf16_bits_to_f32(b & 0xFFFFu), bf16_bits_to_f32(b >> 16));
+            }
+            reinterpret_cast<__half2 *>(s.x_f16 + (size_t)t0 * H)[i] = __floats2half2_rn(v.x, v.y);
+        }
     }
 
     if (row < R) {
-        const uint16_t *w = a.router + (size_t)row * H;
         float acc[kRouteTokens];
 #pragma unroll
         for (int j = 0; j < kRouteTokens; ++j) acc[j] = 0.0f;
         for (int qb = 0; qb < chunks; qb += kRouteChunkBatch) {
-            uint2 wv[kRouteChunkBatch];
+            if (qb > 0) {
 #pragma unroll
-            for (int q = 0; q < kRouteChunkBatch; ++q)
-                if (qb + q < chunks) wv[q] = __ldg(reinterpret_cast<const uint2 *>(w + (qb + q) * 128 + lane * 4));
+                for (int q = 0; q < kRouteChunkBatch; ++q)
+                    if (qb + q < chunks) wv[q] = __ldg(reinterpret_cast<const uint2 *>(w + (qb + q) * 128 + lane * 4));
+            }
 #pragma unroll
             for (int q = 0; q < kRouteChunkBatch; ++q) {
                 if (qb + q >= chunks) break;
@@ -76,11 +106,9 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
                     if (j < tt) {
                         float4 xv;
                         if (a.x_is_f32) {
-                            xv = __ldg(reinterpret_cast<const float4 *>(static_cast<const float *>(a.x) +
-                                                                         (size_t)(t0 + j) * H + k));
+                            xv = *reinterpret_cast<const float4 *>(route_xs + ((size_t)j * H + k) * 4);
                         } else {
-                            const uint2 b = __ldg(reinterpret_cast<const uint2 *>(
-                                static_cast<const uint16_t *>(a.x) + (size_t)(t0 + j) * H + k));
+                            const uint2 b = *reinterpret_cast<const uint2 *>(route_xs + ((size_t)j * H + k) * 2);
                             xv = make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
                                              bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
                         }
@@ -335,7 +363,29 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream) {
     const int R = a.E + 1;
     const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
-    moe_route_kernel<<<grid, kRouteRowsPerCta * 32, 0, stream>>>(a);
+    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2);
+    if (smem > 48 * 1024) {
+        // Raise the limit to all the shared memory a CTA may hold, once per
+        // device (bit d of `done`).
+        static std::atomic<uint64_t> done{0};
+        int dev = 0;
+        cudaError_t err = cudaGetDevice(&dev);
+        if (err != cudaSuccess) return err;
+        const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+        if (!bit || !(done.load() & bit)) {
+            cudaFuncAttributes fa{};
+            err = cudaFuncGetAttributes(&fa, moe_route_kernel);
+            if (err != cudaSuccess) return err;
+            int optin = 0;
+            err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+            if (err != cudaSuccess) return err;
+            err = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       optin - (int)fa.sharedSizeBytes);
+            if (err != cudaSuccess) return err;
+            done.fetch_or(bit);
+        }
+    }
+    moe_route_kernel<<<grid, kRouteRowsPerCta * 32, smem, stream>>>(a);
     return cudaGetLastError();
 }
 

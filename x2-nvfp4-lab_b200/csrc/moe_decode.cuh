@@ -9,8 +9,10 @@
 //   2. moe_gate_up_tma_kernel  gate and up NVFP4 GEMVs of every (active
 //                              expert, 32-row tile), SiLU(gate)*up fused.
 //   3. moe_down_tma_kernel     down NVFP4 GEMV of every (active expert,
-//                              64-row tile); the last CTA per tile combines
-//                              the nine slots and adds the residual.
+//                              64-row tile), scaled per (token, slot).
+//   4. moe_combine_kernel      sum of the nine slots + residual.
+// Launches 2-4 use programmatic dependent launch, so each one's prologue
+// (barrier init, tensor-map prefetch) overlaps its predecessor's tail.
 // The lab runs the same layer as seven launches (nvfp4_runtime.cpp:1943-2066:
 // router GEMV, shared-gate GEMV, top-8, gate/up, SiLU, down, reduce).
 #pragma once
@@ -50,12 +52,14 @@ struct DecodeScratch {
     __half *act;            // [T*9][I]      SiLU(gate)*up per (token, slot)
     float *ypart;           // [T*9][H]      scaled down-projection per (token, slot)
     unsigned *tile_count;   // [H/64]        finished experts per 64-row output tile
+    int *host_error;        // pinned host-mapped word the host reads at synchronize, or nullptr
 };
 
 // TMA descriptors over a bank's packed and scale arrays (gate, up, down).
 struct StreamMaps {
     CUtensorMap packed[3];
-    CUtensorMap scales[3];
+    CUtensorMap scales[3];       // box of 64 scale bytes (four 256-column boxes)
+    CUtensorMap scales_half[3];  // box of 32 scale bytes (two 256-column boxes)
 };
 
 struct RouteArgs {

@@ -1,30 +1,38 @@
-// TMA-fed expert GEMVs of the decode path.
+// TMA-fed expert GEMVs and the combine kernel of the decode path.
 //
-// Both kernels are persistent: one producer warp streams weight tiles into a
-// ring of shared-memory stages with 2D TMA loads (no multicast), four
+// Both GEMV kernels are persistent: one producer warp streams weight tiles
+// into a ring of shared-memory stages with 2D TMA loads into its own CTA, four
 // consumer warps decode E2M1 x E4M3 to f16 in registers and run m16n8k16
-// MMAs against the FP16 tokens, and mbarriers hand stages back and forth.
-// Every mbarrier wait is bounded (tma_util.cuh) and reports a timeout through
-// the scratch error word.
+// MMAs against FP16 token rows held in shared memory, and mbarriers hand
+// stages back and forth. Every mbarrier wait is bounded (tma_util.cuh) and
+// reports a timeout through the scratch error word.
 //
 // moe_gate_up_tma_kernel  item = (active expert, 32 rows of the intermediate
-//                          dimension); gate and up tiles stream together,
+//                          dimension); gate and up tiles stream together;
 //                          SiLU(gate) * up is written as FP16.
 // moe_down_tma_kernel     item = (active expert, 64 rows of hidden); each
-//                          expert's FP32 output, scaled by routing weight and
-//                          inverse global scale, is written per (token, slot);
-//                          the last CTA to finish a 64-row tile sums the nine
-//                          slots in slot order (the lab's reduce,
-//                          nvfp4_gemv.cl:1443-1457) and adds the residual.
-//
-// A 256-column box may extend past the end of K (K is a multiple of 128):
-// TMA fills the weight side with zeros and the token side is not loaded
-// there, so no stale value can enter a product.
+//                          expert's output, scaled by routing weight and
+//                          inverse global scale, is written per (token, slot).
+// moe_combine_kernel      out = sum of the nine slots in slot order (the lab's
+//                          reduce, nvfp4_gemv.cl:1443-1457) + residual.
+// In both GEMVs the producer warp also copies the item's FP16 token rows for
+// the stage's K range into the stage (cp.async, completing on the same
+// mbarrier as the TMA bytes), so consumers read both operands from shared
+// memory. A token group holds up to NT*8 tokens; an expert with more tokens
+// streams its tiles once per group.
 //
 // Weight tiles land in shared memory with the 128-byte TMA swizzle: 16-byte
 // unit u of row r sits at r*128 + ((u ^ (r & 7)) << 4). Lane (g, c) reads
-// units 2c and 2c+1 of rows g and g+8, which maps the eight lanes of each
-// LDS.128 phase onto eight distinct bank groups.
+// units 2c and 2c+1 of rows g and g+8, i.e. columns [64c, 64c+64) of each
+// 256-column box, so the eight lanes of an LDS.128 phase hit eight distinct
+// bank groups. Token rows use the same column split: a row stores 64-column
+// segments at a 144-byte stride and rows at a pitch of 4 mod 8 sixteen-byte
+// units, so the four lanes of a row and the eight rows of a phase land on
+// distinct bank groups.
+//
+// A 256-column box may extend past the end of K (K is a multiple of 128):
+// TMA fills the weight side with zeros and the token side is not read there,
+// so no stale value can enter a product.
 #include "moe_decode.cuh"
 #include "tma_util.cuh"
 
@@ -38,23 +46,26 @@ constexpr int kBoxK = 256;            // K elements per TMA box (128 bytes)
 constexpr int kBoxBytes = 128;
 constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;
-
 constexpr int kGuRows = 32;
-constexpr int kGuBoxes = 4;           // boxes per stage and projection
-constexpr int kGuStages = 5;
-constexpr int kGuPacked = kGuBoxes * kGuRows * kBoxBytes;   // 16 KB per projection
-constexpr int kGuScales = kGuRows * kGuBoxes * 16;          // 2 KB per projection
-constexpr int kGuStageBytes = 2 * kGuPacked + 2 * kGuScales;
-
 constexpr int kDnRows = 64;
-constexpr int kDnBoxes = 4;
-constexpr int kDnStages = 6;
-constexpr int kDnPacked = kDnBoxes * kDnRows * kBoxBytes;   // 32 KB
-constexpr int kDnScales = kDnRows * kDnBoxes * 16;          // 4 KB
-constexpr int kDnStageBytes = kDnPacked + kDnScales;
+
+__host__ __device__ constexpr int tok_pitch(int k) {
+    return (k / 64) * 144 + 16 * ((4 - ((k / 64) * 9) % 8 + 8) % 8);
+}
+
+__device__ __forceinline__ int tok_offset(int pitch, int j, int k) {
+    return j * pitch + (k >> 6) * 144 + (k & 63) * 2;
+}
 
 __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
     return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+// Publish the recorded wait failure (its site code) to the bank's
+// host-visible word (a plain store: no atomics on host memory).
+__device__ __forceinline__ void publish_timeout(const DecodeScratch &s) {
+    const int code = *reinterpret_cast<volatile int *>(s.error);
+    if (s.host_error) *reinterpret_cast<volatile int *>(s.host_error) = code != 0 ? code : kErrWaitTimeout;
 }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
@@ -79,67 +90,100 @@ __device__ __forceinline__ void decode_unit(const uint4 &u, uint16_t sc, uint32_
 
 // ------------------------------------------------------------ gate / up
 
-template <int NT>
+template <int NT, int BOXES, int S>
+struct GuCfg {
+    static constexpr int kPacked = BOXES * kGuRows * kBoxBytes;   // per projection
+    static constexpr int kScales = kGuRows * BOXES * 16;          // per projection
+    static constexpr int kTokPitch = tok_pitch(BOXES * kBoxK);
+    static constexpr int kTok = NT * 8 * kTokPitch;
+    static constexpr int kStage = (2 * kPacked + 2 * kScales + kTok + 1023) & ~1023;
+    static constexpr int kRed = 2 * 2 * NT * 4 * 32 * 4;
+};
+
+template <int NT, int BOXES, int S>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_gate_up_tma_kernel(const __grid_constant__ CUtensorMap tm_gp, const __grid_constant__ CUtensorMap tm_gs,
                            const __grid_constant__ CUtensorMap tm_up, const __grid_constant__ CUtensorMap tm_us,
                            GateUpArgs a) {
+    using Cfg = GuCfg<NT, BOXES, S>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = align1024(smem_raw);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kGuStages * kGuStageBytes);
-    uint64_t *empty = full + kGuStages;
-    float *red = reinterpret_cast<float *>(empty + kGuStages);  // [2 mtile][2 proj][NT][4][32]
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStage);
+    uint64_t *empty = full + S;
+    float *red = reinterpret_cast<float *>(empty + S);        // [2 mtile][2 proj][NT][4][32]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const DecodeScratch &s = a.s;
     int *err = s.error;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kGuStages; ++i) {
-            mbar_init(full + i, 1);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1 + 32);  // TMA transaction arrive + one cp.async arrive per producer lane
             mbar_init(empty + i, kConsumerWarps);
         }
         fence_barrier_init();
+        prefetch_tensormap(&tm_gp);
+        prefetch_tensormap(&tm_up);
+        prefetch_tensormap(&tm_gs);
+        prefetch_tensormap(&tm_us);
     }
     __syncthreads();
+    pdl_wait();  // the routing kernel's outputs are read from here on
+    pdl_launch_dependents();
     const int H = a.H, I = a.I, E = a.E;
     const int nact = *s.n_active;
     const int mtiles = I / kGuRows;
     const int items = nact * mtiles;
     const int kboxes = (H + kBoxK - 1) / kBoxK;
-    const int slices = (kboxes + kGuBoxes - 1) / kGuBoxes;
+    const int slices = (kboxes + BOXES - 1) / BOXES;
+    constexpr int kSK = BOXES * kBoxK;
+    constexpr uint32_t kTx = 2 * Cfg::kPacked + 2 * Cfg::kScales;
 
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            prefetch_tensormap(&tm_gp);
-            prefetch_tensormap(&tm_up);
-            prefetch_tensormap(&tm_gs);
-            prefetch_tensormap(&tm_us);
-            uint32_t it = 0;
-            for (int item = blockIdx.x; item < items; item += gridDim.x) {
-                const int ai = item / mtiles, mt = item - ai * mtiles;
-                const int y = s.active_expert[ai] * I + mt * kGuRows;
-                const int ntok = s.tok_count[ai];
-                for (int tg = 0; tg < ntok; tg += NT * 8) {
-                    for (int sl = 0; sl < slices; ++sl, ++it) {
-                        const int st = it % kGuStages;
-                        const uint32_t ph = (it / kGuStages) & 1u;
-                        if (!mbar_wait(empty + st, ph ^ 1u, err)) return;
-                        mbar_arrive_expect_tx(full + st, kGuStageBytes);
-                        uint8_t *stage = smem + st * kGuStageBytes;
-#pragma unroll
-                        for (int b = 0; b < kGuBoxes; ++b) {
-                            const int x = (sl * kGuBoxes + b) * kBoxBytes;
-                            tma_load_2d(stage + b * kGuRows * kBoxBytes, &tm_gp, full + st, x, y);
-                            tma_load_2d(stage + kGuPacked + b * kGuRows * kBoxBytes, &tm_up, full + st, x, y);
-                        }
-                        tma_load_2d(stage + 2 * kGuPacked, &tm_gs, full + st, sl * kGuBoxes * 16, y);
-                        tma_load_2d(stage + 2 * kGuPacked + kGuScales, &tm_us, full + st, sl * kGuBoxes * 16, y);
+        uint32_t it = 0;
+        for (int item = blockIdx.x; item < items; item += gridDim.x) {
+            const int ai = item / mtiles, mt = item - ai * mtiles;
+            const int y = s.active_expert[ai] * I + mt * kGuRows;
+            const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+            for (int tg = 0; tg < ntok; tg += NT * 8) {
+                const int ncols = min(NT * 8, ntok - tg);
+                for (int sl = 0; sl < slices; ++sl, ++it) {
+                    const int st = it % S;
+                    const uint32_t ph = (it / S) & 1u;
+                    int ok = 1;
+                    if (lane == 0) ok = mbar_wait(empty + st, ph ^ 1u, err, kSiteGateUpEmpty) ? 1 : 0;
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                        if (lane == 0) publish_timeout(s);
+                        return;
                     }
+                    uint8_t *stage = smem + st * Cfg::kStage;
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(full + st, kTx);
+#pragma unroll
+                        for (int b = 0; b < BOXES; ++b) {
+                            const int x = (sl * BOXES + b) * kBoxBytes;
+                            tma_load_2d(stage + b * kGuRows * kBoxBytes, &tm_gp, full + st, x, y);
+                            tma_load_2d(stage + Cfg::kPacked + b * kGuRows * kBoxBytes, &tm_up, full + st, x, y);
+                        }
+                        tma_load_2d(stage + 2 * Cfg::kPacked, &tm_gs, full + st, sl * BOXES * 16, y);
+                        tma_load_2d(stage + 2 * Cfg::kPacked + Cfg::kScales, &tm_us, full + st, sl * BOXES * 16, y);
+                    }
+                    uint8_t *tok = stage + 2 * Cfg::kPacked + 2 * Cfg::kScales;
+                    constexpr int per_row = kSK / 8;
+                    for (int i = lane; i < ncols * per_row; i += 32) {
+                        const int j = i / per_row, kk = (i - j * per_row) * 8;
+                        const int k = sl * kSK + kk;
+                        if (k < H)
+                            cp_async16(tok + tok_offset(Cfg::kTokPitch, j, kk),
+                                       s.x_f16 + (size_t)s.tok_list[tstart + tg + j] * H + k);
+                    }
+                    cp_async_arrive_noinc(full + st);
                 }
             }
         }
         return;
     }
 
+    constexpr int kBoxesPerWarp = BOXES / 2;
+    bool failed = false;
     const int mtile = warp & 1, kh = warp >> 1;
     const int g = lane >> 2, c = lane & 3;
     const int r0 = mtile * 16 + g, r1 = r0 + 8;
@@ -152,12 +196,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv_up = a.inv_scales[(E + 1) + e];
         for (int tg = 0; tg < ntok; tg += NT * 8) {
             const int ncols = min(NT * 8, ntok - tg);
-            const __half *xrow[NT];
-#pragma unroll
-            for (int n = 0; n < NT; ++n) {
-                const int j = tg + n * 8 + g;
-                xrow[n] = (n * 8 + g < ncols) ? s.x_f16 + (size_t)s.tok_list[tstart + j] * H : nullptr;
-            }
             float cg[NT][4], cu[NT][4];
 #pragma unroll
             for (int n = 0; n < NT; ++n)
@@ -165,39 +203,53 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int r = 0; r < 4; ++r) cg[n][r] = cu[n][r] = 0.0f;
 
             for (int sl = 0; sl < slices; ++sl, ++it) {
-                const int st = it % kGuStages;
-                const uint32_t ph = (it / kGuStages) & 1u;
-                if (!mbar_wait(full + st, ph, err)) return;
-                const uint8_t *stage = smem + st * kGuStageBytes;
-                const uint8_t *gsc = stage + 2 * kGuPacked;
-                const uint8_t *usc = gsc + kGuScales;
+                const int st = it % S;
+                const uint32_t ph = (it / S) & 1u;
+                // After a failed wait the warp keeps walking the loops (without
+                // waiting or computing) so the named barriers below still see
+                // all four consumer warps.
+                if (failed) continue;
+                if (!mbar_wait(full + st, ph, err, kSiteGateUpFull)) {
+                    publish_timeout(s);
+                    failed = true;
+                    continue;
+                }
+                const uint8_t *stage = smem + st * Cfg::kStage;
+                const uint8_t *gsc = stage + 2 * Cfg::kPacked;
+                const uint8_t *usc = gsc + Cfg::kScales;
+                const uint8_t *tok = usc + Cfg::kScales;
 #pragma unroll
-                for (int bb = 0; bb < 2; ++bb) {
-                    const int b = kh * 2 + bb;
-                    const int kb = sl * kGuBoxes + b;
+                for (int bb = 0; bb < kBoxesPerWarp; ++bb) {
+                    const int b = kh * kBoxesPerWarp + bb;
+                    const int kb = sl * BOXES + b;
                     if (kb >= kboxes) break;
                     const uint8_t *gbox = stage + b * kGuRows * kBoxBytes;
-                    const uint8_t *ubox = stage + kGuPacked + b * kGuRows * kBoxBytes;
-                    const uint32_t sg0 = lds32(gsc + r0 * 64 + b * 16 + 4 * c);
-                    const uint32_t sg1 = lds32(gsc + r1 * 64 + b * 16 + 4 * c);
-                    const uint32_t su0 = lds32(usc + r0 * 64 + b * 16 + 4 * c);
-                    const uint32_t su1 = lds32(usc + r1 * 64 + b * 16 + 4 * c);
+                    const uint8_t *ubox = stage + Cfg::kPacked + b * kGuRows * kBoxBytes;
+                    const uint32_t sg0 = lds32(gsc + r0 * (BOXES * 16) + b * 16 + 4 * c);
+                    const uint32_t sg1 = lds32(gsc + r1 * (BOXES * 16) + b * 16 + 4 * c);
+                    const uint32_t su0 = lds32(usc + r0 * (BOXES * 16) + b * 16 + 4 * c);
+                    const uint32_t su1 = lds32(usc + r1 * (BOXES * 16) + b * 16 + 4 * c);
 #pragma unroll
                     for (int uu = 0; uu < 2; ++uu) {
+                        const int kloc = b * kBoxK + 64 * c + 32 * uu;
+                        // Lanes past the end of K keep issuing the warp-wide
+                        // MMAs with zero token operands (the weight side is
+                        // zero-filled by TMA there).
+                        const bool kin = sl * kSK + kloc < H;
                         const int unit = ((2 * c + uu) ^ g) << 4;
                         uint32_t hg0[16], hg1[16], hu0[16], hu1[16];
                         decode_unit(lds128(gbox + r0 * kBoxBytes + unit), (uint16_t)(sg0 >> (16 * uu)), hg0);
                         decode_unit(lds128(gbox + r1 * kBoxBytes + unit), (uint16_t)(sg1 >> (16 * uu)), hg1);
                         decode_unit(lds128(ubox + r0 * kBoxBytes + unit), (uint16_t)(su0 >> (16 * uu)), hu0);
                         decode_unit(lds128(ubox + r1 * kBoxBytes + unit), (uint16_t)(su1 >> (16 * uu)), hu1);
-                        const int kcol = kb * kBoxK + 64 * c + 32 * uu;
 #pragma unroll
                         for (int n = 0; n < NT; ++n) {
                             if (n * 8 >= ncols) break;
+                            const bool have = n * 8 + g < ncols;
 #pragma unroll
                             for (int w = 0; w < 4; ++w) {
                                 uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-                                if (xrow[n] && kcol < H) bv = __ldg(reinterpret_cast<const uint4 *>(xrow[n] + kcol + 8 * w));
+                                if (have && kin) bv = lds128(tok + tok_offset(Cfg::kTokPitch, n * 8 + g, kloc + 8 * w));
                                 mma_16816(cg[n], hg0[4 * w], hg1[4 * w], hg0[4 * w + 1], hg1[4 * w + 1], bv.x, bv.y);
                                 mma_16816(cg[n], hg0[4 * w + 2], hg1[4 * w + 2], hg0[4 * w + 3], hg1[4 * w + 3], bv.z,
                                           bv.w);
@@ -245,58 +297,85 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-// ------------------------------------------------------- down + combine
+// ------------------------------------------------------------------ down
 
-template <int NT>
+template <int NT, int BOXES, int S>
+struct DnCfg {
+    static constexpr int kPacked = BOXES * kDnRows * kBoxBytes;
+    static constexpr int kScales = kDnRows * BOXES * 16;
+    static constexpr int kTokPitch = tok_pitch(BOXES * kBoxK);
+    static constexpr int kTok = NT * 8 * kTokPitch;
+    static constexpr int kStage = (kPacked + kScales + kTok + 1023) & ~1023;
+};
+
+template <int NT, int BOXES, int S>
 __global__ void __launch_bounds__(kThreads, 1)
     moe_down_tma_kernel(const __grid_constant__ CUtensorMap tm_dp, const __grid_constant__ CUtensorMap tm_ds,
                         DownArgs a) {
+    using Cfg = DnCfg<NT, BOXES, S>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = align1024(smem_raw);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + kDnStages * kDnStageBytes);
-    uint64_t *empty = full + kDnStages;
-    int *flag = reinterpret_cast<int *>(empty + kDnStages);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStage);
+    uint64_t *empty = full + S;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const DecodeScratch &s = a.s;
     int *err = s.error;
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kDnStages; ++i) {
-            mbar_init(full + i, 1);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1 + 32);  // TMA transaction arrive + one cp.async arrive per producer lane
             mbar_init(empty + i, kConsumerWarps);
         }
         fence_barrier_init();
+        prefetch_tensormap(&tm_dp);
+        prefetch_tensormap(&tm_ds);
     }
     __syncthreads();
-    const int H = a.H, I = a.I, T = a.T;
+    pdl_wait();  // routing tables and gate/up activations are read from here on
+    pdl_launch_dependents();
+    const int H = a.H, I = a.I;
     const int nact = *s.n_active;
     const int rtiles = H / kDnRows;
     const int items = nact * rtiles;
     const int kboxes = (I + kBoxK - 1) / kBoxK;
-    const int slices = (kboxes + kDnBoxes - 1) / kDnBoxes;
-    const int stage_boxes = kboxes < kDnBoxes ? kboxes : kDnBoxes;
-    const uint32_t stage_tx = stage_boxes * kDnRows * kBoxBytes + kDnRows * stage_boxes * 16;
+    const int slices = (kboxes + BOXES - 1) / BOXES;
+    constexpr int kSK = BOXES * kBoxK;
+    constexpr uint32_t kTx = Cfg::kPacked + Cfg::kScales;
 
     if (warp == kConsumerWarps) {
-        if (lane == 0) {
-            prefetch_tensormap(&tm_dp);
-            prefetch_tensormap(&tm_ds);
-            uint32_t it = 0;
-            for (int item = blockIdx.x; item < items; item += gridDim.x) {
-                const int ai = item / rtiles, rt = item - ai * rtiles;
-                const int y = s.active_expert[ai] * H + rt * kDnRows;
-                const int ntok = s.tok_count[ai];
-                for (int tg = 0; tg < ntok; tg += NT * 8) {
-                    for (int sl = 0; sl < slices; ++sl, ++it) {
-                        const int st = it % kDnStages;
-                        const uint32_t ph = (it / kDnStages) & 1u;
-                        if (!mbar_wait(empty + st, ph ^ 1u, err)) return;
-                        mbar_arrive_expect_tx(full + st, stage_tx);
-                        uint8_t *stage = smem + st * kDnStageBytes;
-                        for (int b = 0; b < stage_boxes; ++b)
-                            tma_load_2d(stage + b * kDnRows * kBoxBytes, &tm_dp, full + st,
-                                        (sl * kDnBoxes + b) * kBoxBytes, y);
-                        tma_load_2d(stage + kDnPacked, &tm_ds, full + st, sl * kDnBoxes * 16, y);
+        uint32_t it = 0;
+        for (int item = blockIdx.x; item < items; item += gridDim.x) {
+            const int ai = item / rtiles, rt = item - ai * rtiles;
+            const int y = s.active_expert[ai] * H + rt * kDnRows;
+            const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+            for (int tg = 0; tg < ntok; tg += NT * 8) {
+                const int ncols = min(NT * 8, ntok - tg);
+                for (int sl = 0; sl < slices; ++sl, ++it) {
+                    const int st = it % S;
+                    const uint32_t ph = (it / S) & 1u;
+                    int ok = 1;
+                    if (lane == 0) ok = mbar_wait(empty + st, ph ^ 1u, err, kSiteDownEmpty) ? 1 : 0;
+                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                        if (lane == 0) publish_timeout(s);
+                        return;
                     }
+                    uint8_t *stage = smem + st * Cfg::kStage;
+                    if (lane == 0) {
+                        mbar_arrive_expect_tx(full + st, kTx);
+                        for (int b = 0; b < BOXES; ++b)
+                            tma_load_2d(stage + b * kDnRows * kBoxBytes, &tm_dp, full + st,
+                                        (sl * BOXES + b) * kBoxBytes, y);
+                        tma_load_2d(stage + Cfg::kPacked, &tm_ds, full + st, sl * BOXES * 16, y);
+                    }
+                    uint8_t *tok = stage + Cfg::kPacked + Cfg::kScales;
+                    const int per_row = kSK / 8;
+                    for (int i = lane; i < ncols * per_row; i += 32) {
+                        const int j = i / per_row, kk = (i - j * per_row) * 8;
+                        const int k = sl * kSK + kk;
+                        if (k < I)
+                            cp_async16(tok + tok_offset(Cfg::kTokPitch, j, kk),
+                                       s.act + (size_t)(tstart + tg + j) * I + k);
+                    }
+                    cp_async_arrive_noinc(full + st);
                 }
             }
         }
@@ -305,48 +384,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int g = lane >> 2, c = lane & 3;
     const int r0 = warp * 16 + g, r1 = r0 + 8;
-    const int sstride = stage_boxes * 16;  // scale bytes per row in a stage
     uint32_t it = 0;
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int ai = item / rtiles, rt = item - ai * rtiles;
         const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
         for (int tg = 0; tg < ntok; tg += NT * 8) {
             const int ncols = min(NT * 8, ntok - tg);
-            const __half *arow[NT];
-#pragma unroll
-            for (int n = 0; n < NT; ++n)
-                arow[n] = (n * 8 + g < ncols) ? s.act + (size_t)(tstart + tg + n * 8 + g) * I : nullptr;
             float cd[NT][4];
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) cd[n][r] = 0.0f;
             for (int sl = 0; sl < slices; ++sl, ++it) {
-                const int st = it % kDnStages;
-                const uint32_t ph = (it / kDnStages) & 1u;
-                if (!mbar_wait(full + st, ph, err)) return;
-                const uint8_t *stage = smem + st * kDnStageBytes;
-                const uint8_t *sc = stage + kDnPacked;
-                for (int b = 0; b < stage_boxes; ++b) {
-                    const int kb = sl * kDnBoxes + b;
+                const int st = it % S;
+                const uint32_t ph = (it / S) & 1u;
+                if (!mbar_wait(full + st, ph, err, kSiteDownFull)) {
+                    publish_timeout(s);
+                    return;
+                }
+                const uint8_t *stage = smem + st * Cfg::kStage;
+                const uint8_t *sc = stage + Cfg::kPacked;
+                const uint8_t *tok = sc + Cfg::kScales;
+#pragma unroll
+                for (int b = 0; b < BOXES; ++b) {
+                    const int kb = sl * BOXES + b;
                     if (kb >= kboxes) break;
                     const uint8_t *box = stage + b * kDnRows * kBoxBytes;
-                    const uint32_t s0 = lds32(sc + r0 * sstride + b * 16 + 4 * c);
-                    const uint32_t s1 = lds32(sc + r1 * sstride + b * 16 + 4 * c);
+                    const uint32_t s0 = lds32(sc + r0 * (BOXES * 16) + b * 16 + 4 * c);
+                    const uint32_t s1 = lds32(sc + r1 * (BOXES * 16) + b * 16 + 4 * c);
 #pragma unroll
                     for (int uu = 0; uu < 2; ++uu) {
+                        const int kloc = b * kBoxK + 64 * c + 32 * uu;
+                        const bool kin = sl * kSK + kloc < I;  // see gate/up
                         const int unit = ((2 * c + uu) ^ g) << 4;
                         uint32_t h0[16], h1[16];
                         decode_unit(lds128(box + r0 * kBoxBytes + unit), (uint16_t)(s0 >> (16 * uu)), h0);
                         decode_unit(lds128(box + r1 * kBoxBytes + unit), (uint16_t)(s1 >> (16 * uu)), h1);
-                        const int kcol = kb * kBoxK + 64 * c + 32 * uu;
 #pragma unroll
                         for (int n = 0; n < NT; ++n) {
                             if (n * 8 >= ncols) break;
+                            const bool have = n * 8 + g < ncols;
 #pragma unroll
                             for (int w = 0; w < 4; ++w) {
                                 uint4 bv = make_uint4(0u, 0u, 0u, 0u);
-                                if (arow[n] && kcol < I) bv = __ldcg(reinterpret_cast<const uint4 *>(arow[n] + kcol + 8 * w));
+                                if (have && kin) bv = lds128(tok + tok_offset(Cfg::kTokPitch, n * 8 + g, kloc + 8 * w));
                                 mma_16816(cd[n], h0[4 * w], h1[4 * w], h0[4 * w + 1], h1[4 * w + 1], bv.x, bv.y);
                                 mma_16816(cd[n], h0[4 * w + 2], h1[4 * w + 2], h0[4 * w + 3], h1[4 * w + 3], bv.z,
                                           bv.w);
@@ -373,39 +454,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
-        // The last item to finish this 64-row tile combines it.
-        __threadfence();
-        named_barrier(1, kConsumerWarps * 32);
-        if (threadIdx.x == 0) {
-            const unsigned old = atomicAdd(s.tile_count + rt, 1u);
-            *flag = (old == (unsigned)(nact - 1)) ? 1 : 0;
-        }
-        named_barrier(1, kConsumerWarps * 32);
-        if (*flag) {
-            __threadfence();
-            for (int i = threadIdx.x; i < T * kDnRows; i += kConsumerWarps * 32) {
-                const int t = i / kDnRows, h = rt * kDnRows + (i - t * kDnRows);
-                float v = 0.0f;
-#pragma unroll
-                for (int k = 0; k < kTopK; ++k) {
-                    const int pos = __ldcg(s.inv_pos + t * kTopK + k);
-                    if (pos >= 0) v += __ldcg(s.ypart + (size_t)pos * H + h);
-                }
-                if (a.shared_here) v += __ldcg(s.ypart + (size_t)(T * kTopK + t) * H + h);
-                const size_t o = (size_t)t * H + h;
-                if (a.out_f32) {
-                    static_cast<float *>(a.out)[o] = v;
-                } else {
-                    if (a.residual) v += bf16_bits_to_f32(static_cast<const uint16_t *>(a.residual)[o]);
-                    static_cast<uint16_t *>(a.out)[o] = f32_to_bf16_bits(v);
-                }
-            }
-            named_barrier(1, kConsumerWarps * 32);
-            if (threadIdx.x == 0) s.tile_count[rt] = 0u;
-        }
-        named_barrier(1, kConsumerWarps * 32);
     }
 }
+
+// ------------------------------------------------------------- combine
+
+__global__ void __launch_bounds__(256) moe_combine_kernel(DownArgs a) {
+    pdl_wait();
+    pdl_launch_dependents();
+    const DecodeScratch &s = a.s;
+    const int H = a.H, T = a.T;
+    const int t = blockIdx.y;
+    int pos[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) pos[k] = s.inv_pos[t * kTopK + k];
+    for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
+        float v = 0.0f;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k)
+            if (pos[k] >= 0) v += s.ypart[(size_t)pos[k] * H + h];
+        if (a.shared_here) v += s.ypart[(size_t)(T * kTopK + t) * H + h];
+        const size_t o = (size_t)t * H + h;
+        if (a.out_f32) {
+            static_cast<float *>(a.out)[o] = v;
+        } else {
+            if (a.residual) v += bf16_bits_to_f32(static_cast<const uint16_t *>(a.residual)[o]);
+            static_cast<uint16_t *>(a.out)[o] = f32_to_bf16_bits(v);
+        }
+    }
+}
+
+// --------------------------------------------------------------- launches
 
 // Raise a kernel's dynamic shared-memory limit once per device. `done` is a
 // per-kernel bitmask of devices already configured.
@@ -421,29 +500,49 @@ cudaError_t set_smem_once(K kernel, size_t bytes, std::atomic<uint64_t> &done) {
     return err;
 }
 
-template <int NT>
-cudaError_t launch_gate_up_tma_nt(const StreamMaps &m, const GateUpArgs &a, int items_ub, int sms,
-                                  cudaStream_t stream) {
-    const size_t smem = 1024 + kGuStages * kGuStageBytes + 2 * kGuStages * 8 + 2 * 2 * NT * 4 * 32 * 4;
-    static std::atomic<uint64_t> done{0};
-    cudaError_t err = set_smem_once(moe_gate_up_tma_kernel<NT>, smem, done);
-    if (err != cudaSuccess) return err;
-    const int grid = items_ub < sms ? items_ub : sms;
-    moe_gate_up_tma_kernel<NT><<<grid, kThreads, smem, stream>>>(m.packed[0], m.scales[0], m.packed[1],
-                                                                  m.scales[1], a);
-    return cudaGetLastError();
+// Launch with programmatic stream serialisation: the kernel may start while
+// its predecessor drains and calls griddepcontrol.wait before reading it.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-template <int NT>
-cudaError_t launch_down_tma_nt(const StreamMaps &m, const DownArgs &a, int items_ub, int sms,
+template <int NT, int BOXES, int S>
+cudaError_t launch_gate_up_cfg(const StreamMaps &m, const GateUpArgs &a, int items_ub, int sms,
                                cudaStream_t stream) {
-    const size_t smem = 1024 + kDnStages * kDnStageBytes + 2 * kDnStages * 8 + 16;
+    using Cfg = GuCfg<NT, BOXES, S>;
+    const size_t smem = 1024 + S * Cfg::kStage + 2 * S * 8 + Cfg::kRed;
     static std::atomic<uint64_t> done{0};
-    cudaError_t err = set_smem_once(moe_down_tma_kernel<NT>, smem, done);
+    cudaError_t err = set_smem_once(moe_gate_up_tma_kernel<NT, BOXES, S>, smem, done);
     if (err != cudaSuccess) return err;
     const int grid = items_ub < sms ? items_ub : sms;
-    moe_down_tma_kernel<NT><<<grid, kThreads, smem, stream>>>(m.packed[2], m.scales[2], a);
-    return cudaGetLastError();
+    const CUtensorMap &gs = BOXES == 4 ? m.scales[0] : m.scales_half[0];
+    const CUtensorMap &us = BOXES == 4 ? m.scales[1] : m.scales_half[1];
+    return launch_pdl(moe_gate_up_tma_kernel<NT, BOXES, S>, dim3(grid), dim3(kThreads), smem, stream, m.packed[0], gs,
+                      m.packed[1], us, a);
+}
+
+template <int NT, int BOXES, int S>
+cudaError_t launch_down_cfg(const StreamMaps &m, const DownArgs &a, int items_ub, int sms, cudaStream_t stream) {
+    using Cfg = DnCfg<NT, BOXES, S>;
+    const size_t smem = 1024 + S * Cfg::kStage + 2 * S * 8;
+    static std::atomic<uint64_t> done{0};
+    cudaError_t err = set_smem_once(moe_down_tma_kernel<NT, BOXES, S>, smem, done);
+    if (err != cudaSuccess) return err;
+    const int grid = items_ub < sms ? items_ub : sms;
+    return launch_pdl(moe_down_tma_kernel<NT, BOXES, S>, dim3(grid), dim3(kThreads), smem, stream, m.packed[2],
+                      m.scales_half[2], a);
 }
 
 }  // namespace
@@ -478,14 +577,16 @@ cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *c
     for (int p = 0; p < 3; ++p) {
         const uint64_t rows = slots * (p < 2 ? I : H);
         const uint64_t k = p < 2 ? H : I;
+        const uint64_t pitch = (k / 16 + 15) & ~uint64_t(15);
         const uint32_t box_rows = p < 2 ? kGuRows : kDnRows;
-        const uint32_t scale_box = (p < 2 ? kGuBoxes : (((k + kBoxK - 1) / kBoxK) < kDnBoxes
-                                                          ? (uint32_t)((k + kBoxK - 1) / kBoxK) : kDnBoxes)) * 16;
         cudaError_t err = make_tensor_map_u8(&m.packed[p], packed[p], k / 2, k / 2, rows, kBoxBytes, box_rows,
                                              CU_TENSOR_MAP_SWIZZLE_128B);
         if (err != cudaSuccess) return err;
-        err = make_tensor_map_u8(&m.scales[p], scales[p], k / 16, (k / 16 + 15) & ~uint64_t(15), rows, scale_box,
-                                 box_rows,
+        // Scale boxes cover four (scales) or two (scales_half) 256-column boxes.
+        err = make_tensor_map_u8(&m.scales[p], scales[p], k / 16, pitch, rows, 64, box_rows,
+                                 CU_TENSOR_MAP_SWIZZLE_NONE);
+        if (err != cudaSuccess) return err;
+        err = make_tensor_map_u8(&m.scales_half[p], scales[p], k / 16, pitch, rows, 32, box_rows,
                                  CU_TENSOR_MAP_SWIZZLE_NONE);
         if (err != cudaSuccess) return err;
     }
@@ -495,18 +596,25 @@ cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *c
 cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, int sms, cudaStream_t stream) {
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.I / kGuRows);
-    if (T <= 8) return launch_gate_up_tma_nt<1>(m, a, items_ub, sms, stream);
-    if (T <= 16) return launch_gate_up_tma_nt<2>(m, a, items_ub, sms, stream);
-    return launch_gate_up_tma_nt<4>(m, a, items_ub, sms, stream);
+    if (T <= 8) return launch_gate_up_cfg<1, 2, 7>(m, a, items_ub, sms, stream);
+    if (T <= 16) return launch_gate_up_cfg<2, 2, 5>(m, a, items_ub, sms, stream);
+    return launch_gate_up_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
 }
 
 cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream) {
     const int T = a.T;
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.H / kDnRows);
-    if (T <= 8) return launch_down_tma_nt<1>(m, a, items_ub, sms, stream);
-    if (T <= 16) return launch_down_tma_nt<2>(m, a, items_ub, sms, stream);
-    return launch_down_tma_nt<4>(m, a, items_ub, sms, stream);
+    cudaError_t err;
+    if (T <= 8)
+        err = launch_down_cfg<1, 2, 6>(m, a, items_ub, sms, stream);
+    else if (T <= 16)
+        err = launch_down_cfg<2, 2, 4>(m, a, items_ub, sms, stream);
+    else
+        err = launch_down_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
+    if (err != cudaSuccess) return err;
+    const dim3 grid((a.H + 255) / 256, T);
+    return launch_pdl(moe_combine_kernel, grid, dim3(256), 0, stream, a);
 }
 
 }  // namespace nvfp4

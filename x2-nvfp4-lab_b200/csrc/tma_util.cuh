@@ -3,7 +3,7 @@
 // Every wait on an mbarrier is bounded: after kSpinLimit polls the waiting
 // thread records a timeout in a caller-supplied error word and gives up, so
 // a kernel can never spin forever on a barrier that is not completed.
-// No load here uses cluster multicast.
+// Every copy here lands in the issuing CTA's own shared memory only.
 #pragma once
 
 #include <cuda.h>
@@ -12,11 +12,29 @@
 
 namespace nvfp4 {
 
-constexpr uint32_t kSpinLimit = 1u << 26;   // polls before a wait gives up
+constexpr uint32_t kSpinLimit = 1u << 26;          // polls before a drain wait gives up
+constexpr unsigned long long kWaitLimitNs = 1000000000ull;  // wall-clock bound of one wait (1 s)
 constexpr int kErrWaitTimeout = 1;
+// Codes recorded by a wait that gave up (kernel, barrier).
+enum WaitSite : int {
+    kSiteGateUpEmpty = 11,
+    kSiteGateUpFull = 12,
+    kSiteDownEmpty = 21,
+    kSiteDownFull = 22,
+    kSiteGemmEmpty = 31,
+    kSiteGemmFull = 32,
+    kSiteGemmAccEmpty = 33,
+    kSiteGemmAccFull = 34,
+};
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
 __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
@@ -48,16 +66,25 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for the phase with the given parity to complete. Returns false (and
-// records kErrWaitTimeout in *err) after kSpinLimit polls, or at once when
-// another thread already recorded an error.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
-    for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// Wait for the phase with the given parity to complete. Gives up after
+// kWaitLimitNs of wall-clock time, recording `site` (a nonzero code naming
+// the wait) in *err unless an earlier failure is recorded there, or at once
+// when another thread already recorded a failure. Returns false on giving up.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int site = kErrWaitTimeout) {
+    unsigned long long t0 = 0;
+    for (uint32_t i = 0;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 1023u) == 1023u && *reinterpret_cast<volatile int *>(err) != 0) return false;
+        if ((i & 63u) == 63u) {
+            if (*reinterpret_cast<volatile int *>(err) != 0) return false;
+            const unsigned long long now = global_ns();
+            if (t0 == 0) {
+                t0 = now;
+            } else if (now - t0 > kWaitLimitNs) {
+                atomicCAS(err, 0, site);
+                return false;
+            }
+        }
     }
-    atomicExch(err, kErrWaitTimeout);
-    return false;
 }
 
 // 2D tiled TMA load into this CTA's shared memory, completing on `bar`.
@@ -68,6 +95,44 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+
+// Four-row gather: rows r0..r3 of a 2D tensor map whose box is one row of
+// `box bytes`, starting at column x, land in consecutive box-sized slots at
+// `dst` (the tensor map's swizzle applies per destination address).
+__device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int r0, int r1,
+                                            int r2, int r3) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
+        : "memory");
+}
+
+// Contiguous global -> shared bulk copy (both addresses 16-byte aligned,
+// bytes a multiple of 16), completing on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// 4-byte global -> shared copy (cp.async.ca).
+__device__ __forceinline__ void cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// 16-byte global -> shared copy that bypasses L1 (cp.async.cg).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// Arrive on `bar` once every cp.async this thread issued so far has landed.
+// The arrival is not pre-counted: the barrier's init count must include it.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
