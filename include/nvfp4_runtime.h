@@ -361,6 +361,47 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_info(
     int * intermediate,
     size_t * resident_bytes);
 
+/* additive: activation terms of the prefill path (calls above 64 tokens).
+ * The prefill expert GEMMs run on FP4 tensor cores: each activation row is
+ * fed as the sum of `terms` NVFP4 rows (term j+1 quantises what terms 1..j
+ * left over; all share the row's FP32 global scale amax/2688). x_terms
+ * applies to the layer input, act_terms to SiLU(gate)*up. 1 = plain NVFP4
+ * activations (fastest); the default 4/3 keeps the layer within 2e-3
+ * relative RMSE of FP32 activations. Takes effect at the next forward. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_set_prefill_terms(
+    nvfp4_moe_bank * bank,
+    int x_terms,
+    int act_terms);
+
+/* additive: allocate the prefill working memory for calls of up to
+ * max_tokens tokens (capped at 16384 per pass) now, so that later forwards
+ * neither allocate nor synchronise (needed before CUDA-graph capture). */
+NVFP4_API nvfp4_status nvfp4_moe_bank_reserve_prefill(
+    nvfp4_moe_bank * bank,
+    int max_tokens);
+
+/* additive: the prefill path's activation quantiser on its own. src is BF16
+ * (src_is_f16 = 0) or FP16 [rows, cols] device memory, cols a multiple of
+ * 64. Outputs (device):
+ *   codes        uint8 [terms, rows, cols/2]  E2M1 pairs, low nibble = even
+ *                column, zero magnitude always with a clear sign bit
+ *   scale_words  uint32 [terms, rows, cols/64] four E4M3 block scales per
+ *                word, lowest byte = lowest block
+ *   row_scales   float [rows] g = amax/2688 (1 for an all-zero row)
+ * Per term and 16-column block: s = E4M3_RN((blockamax/6)/g), d = s*g,
+ * code = E2M1_RN(r * RN(1/d)) (0 when d is 0), r -= code*d. stream is a
+ * cudaStream_t (NULL = legacy default stream). */
+NVFP4_API nvfp4_status nvfp4_quantize_rows_enqueue(
+    const void * src,
+    int src_is_f16,
+    int rows,
+    int cols,
+    int terms,
+    void * codes,
+    void * scale_words,
+    void * row_scales,
+    void * stream);
+
 /* ------------------------------------------------ allocation-free routing */
 
 /* No counterpart in the reference. Router logits, top-8 selection with the

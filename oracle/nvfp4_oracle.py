@@ -324,6 +324,107 @@ def moe_layer(bank: BankHost, x: np.ndarray, residual: np.ndarray | None = None)
     return LayerResult(out, logits, ids9, w9, counts, offsets, perm)
 
 
+# ------------------------------------------------- prefill activation terms
+
+
+@dataclass
+class RowTerms:
+    codes: np.ndarray        # [terms, rows, cols/2] uint8 (low nibble = even column)
+    words: np.ndarray        # [terms, rows, cols/64] uint32 (four E4M3 block scales, low byte first)
+    g: np.ndarray            # [rows] float32
+    approx: np.ndarray       # [rows, cols] float32: sum of the dequantised terms
+
+
+def quantize_rows_split(x: np.ndarray, terms: int) -> RowTerms:
+    """The prefill path's activation quantiser (this library's definition;
+    the lab quantises no activations). Per row g = amax/2688 in FP32 (1 for
+    an all-zero row); per term and 16-column block of the remainder r:
+    s = E4M3_RNE((bamax/6)/g), d = s*g, code = E2M1_RNE(r * RN(1/d)) with a
+    zero magnitude always unsigned (0 when d is 0), r -= code*d -- every
+    operation rounded to FP32 separately, as the CUDA kernel does."""
+    x = np.asarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    f32 = np.float32
+    amax = np.max(np.abs(x), axis=1).astype(f32)
+    g = np.where(amax > 0, (amax / f32(2688.0)).astype(f32), f32(1.0)).astype(f32)
+    r = x.reshape(rows, cols // 16, 16).copy()
+    approx = np.zeros_like(r)
+    codes_all, words_all = [], []
+    for _ in range(terms):
+        bamax = np.max(np.abs(r), axis=2).astype(f32)
+        target = ((bamax / f32(6.0)).astype(f32) / g[:, None]).astype(f32)
+        s = e4m3_encode_rne(target)
+        denom = (decode_e4m3_scale(s).astype(f32) * g[:, None]).astype(f32)
+        with np.errstate(divide="ignore"):
+            inv = np.where(denom != 0, (f32(1.0) / denom).astype(f32), f32(0.0)).astype(f32)
+        q = (r * inv[:, :, None]).astype(f32)
+        codes = e2m1_encode_rne(q)
+        codes = np.where((codes & 7) == 0, 0, codes).astype(np.uint8)
+        deq = (E2M1[codes] * denom[:, :, None]).astype(f32)
+        approx = (approx + deq).astype(f32)
+        r = (r - deq).astype(f32)
+        flat = codes.reshape(rows, cols)
+        codes_all.append((flat[:, 0::2] | (flat[:, 1::2] << 4)).astype(np.uint8))
+        sb = s.reshape(rows, cols // 64, 4).astype(np.uint32)
+        words_all.append(sb[..., 0] | (sb[..., 1] << 8) | (sb[..., 2] << 16) | (sb[..., 3] << 24))
+    # approx is accumulated in term order; the GEMM sums exact products of
+    # the terms, so this is the value it multiplies.
+    return RowTerms(np.stack(codes_all), np.stack(words_all).astype(np.uint32), g,
+                    approx.reshape(rows, cols))
+
+
+def dequantize_terms(t: RowTerms) -> np.ndarray:
+    """Sum of the dequantised terms in float64 (what the tensor cores add)."""
+    terms, rows, half = t.codes.shape
+    cols = half * 2
+    total = np.zeros((rows, cols), dtype=np.float64)
+    for j in range(terms):
+        c = np.empty((rows, cols), dtype=np.uint8)
+        c[:, 0::2] = t.codes[j] & 0xF
+        c[:, 1::2] = t.codes[j] >> 4
+        sb = np.stack([(t.words[j] >> (8 * b)) & 0xFF for b in range(4)], axis=-1).reshape(rows, cols // 16)
+        sv = decode_e4m3_scale(sb.astype(np.uint8)).astype(np.float64)
+        total += E2M1[c].astype(np.float64) * np.repeat(sv, 16, axis=1) * t.g.astype(np.float64)[:, None]
+    return total
+
+
+def moe_layer_prefill(bank: BankHost, x: np.ndarray, residual: np.ndarray | None = None,
+                      x_terms: int = 4, act_terms: int = 3) -> LayerResult:
+    """The layer as the prefill path computes it: routing exactly as
+    moe_layer; expert inputs replaced by their x_terms NVFP4 terms;
+    SiLU(gate)*up rounded to FP16 and replaced by its act_terms terms before
+    the down projection; products and sums in float64."""
+    x = np.asarray(x, dtype=np.float32)
+    T, H = x.shape
+    E = bank.experts
+    logits = router_logits(bank.router_all(), x)
+    if bank.router_bias is not None:
+        logits[:, :E] = (logits[:, :E] + np.asarray(bank.router_bias, dtype=np.float32)).astype(np.float32)
+    ids, weights = top8_route(logits[:, :E])
+    shared_w = sigmoid32(logits[:, E])
+    counts, offsets, perm = dispatch(ids, E)
+    xq = dequantize_terms(quantize_rows_split(x, x_terms))
+
+    def expert(e: int, rows: np.ndarray) -> np.ndarray:
+        xin = xq[rows]
+        gate = xin @ bank.weight(e, 0).astype(np.float64).T
+        up = xin @ bank.weight(e, 1).astype(np.float64).T
+        act = (gate / (1.0 + np.exp(-gate)) * up).astype(np.float32).astype(np.float16).astype(np.float32)
+        aq = dequantize_terms(quantize_rows_split(act, act_terms))
+        return aq @ bank.weight(e, 2).astype(np.float64).T
+
+    out = np.zeros((T, H), dtype=np.float64)
+    for e in np.unique(ids):
+        rows, slots = np.nonzero(ids == e)
+        out[rows] += weights[rows, slots].astype(np.float64)[:, None] * expert(int(e), rows)
+    out += shared_w.astype(np.float64)[:, None] * expert(E, np.arange(T))
+    if residual is not None:
+        out += np.asarray(residual, dtype=np.float64)
+    ids9 = np.concatenate([ids, np.full((T, 1), E, dtype=np.int32)], axis=1)
+    w9 = np.concatenate([weights, shared_w[:, None]], axis=1).astype(np.float32)
+    return LayerResult(out, logits, ids9, w9, counts, offsets, perm)
+
+
 # ------------------------------------------------------------- comparisons
 
 

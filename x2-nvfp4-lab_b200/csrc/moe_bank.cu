@@ -9,6 +9,7 @@
 // kernel treats the shared gate as router row `experts`.
 #include "internal.h"
 #include "moe_decode.cuh"
+#include "moe_prefill.cuh"
 
 #include <cmath>
 #include <cstring>
@@ -35,8 +36,22 @@ struct nvfp4_moe_bank {
     int last_tokens = 0;
     int last_path = 0;             // 1 = decode path (routing record valid)
     size_t resident_bytes = 0;
+    int *host_error = nullptr;     // pinned host-mapped timeout word (DecodeScratch::host_error)
+    // Prefill path (token batches above the decode limit).
+    uint8_t *sf_atoms[3] = {nullptr, nullptr, nullptr};  // weight scales in tcgen05 atom layout
+    float wnorm_max = 0.0f;        // max L2 norm of the routed router rows
+    void *pscratch = nullptr;
+    PrefillScratch ps{};
+    PrefillMaps pmaps{};
+    int prefill_tokens = 0;        // token capacity of pscratch
+    int terms_x = 4, terms_act = 3;
+    int scratch_terms_x = 0, scratch_terms_act = 0;
 
     ~nvfp4_moe_bank() {
+        if (host_error) cudaFreeHost(host_error);
+        for (int p = 0; p < 3; ++p)
+            if (sf_atoms[p]) cudaFree(sf_atoms[p]);
+        if (pscratch) cudaFree(pscratch);
         for (int p = 0; p < 3; ++p) {
             if (packed[p]) cudaFree(packed[p]);
             if (scales[p]) cudaFree(scales[p]);
@@ -149,20 +164,124 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     });
 }
 
-// Batched BF16 forward: decode-path launches over slices of at most
-// kDecodeMaxTokens tokens.
+bool prefill_supported(const nvfp4_moe_bank *bank) {
+    return bank->hidden % 256 == 0 && bank->intermediate % 256 == 0;
+}
+
+// Make the prefill scratch hold `tokens` tokens at the bank's term counts.
+// Reallocation drains the runtime stream first; it is a no-op when the
+// scratch is already large enough (reserve it up front for graph capture).
+void ensure_prefill(nvfp4_moe_bank *bank, int tokens) {
+    if (tokens <= bank->prefill_tokens && bank->scratch_terms_x == bank->terms_x &&
+        bank->scratch_terms_act == bank->terms_act)
+        return;
+    const int cap = tokens > bank->prefill_tokens ? ((tokens + 255) / 256) * 256 : bank->prefill_tokens;
+    nvfp4_runtime *rt = bank->runtime;
+    check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(prefill scratch)");
+    check_cuda(cudaDeviceSynchronize(), "cudaDeviceSynchronize(prefill scratch)");
+    if (bank->pscratch) {
+        cudaFree(bank->pscratch);
+        bank->pscratch = nullptr;
+        bank->prefill_tokens = 0;
+    }
+    const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
+    const size_t bytes = prefill_scratch_bytes(cap, E, H, I, bank->terms_x, bank->terms_act);
+    check_cuda(cudaMalloc(&bank->pscratch, bytes), "cudaMalloc(MoE bank prefill scratch)");
+    check_cuda(cudaMemset(bank->pscratch, 0, bytes), "cudaMemset(MoE bank prefill scratch)");
+    prefill_scratch_carve(bank->ps, bank->pscratch, cap, E, H, I, bank->terms_x, bank->terms_act);
+    bank->ps.error = bank->ds.error;
+    bank->ps.host_error = bank->ds.host_error;
+    check_cuda(make_prefill_act_maps(bank->pmaps, bank->ps, bank->terms_x, bank->terms_act),
+               "cuTensorMapEncodeTiled(MoE bank prefill activations)");
+    bank->prefill_tokens = cap;
+    bank->scratch_terms_x = bank->terms_x;
+    bank->scratch_terms_act = bank->terms_act;
+}
+
+// Prefill-path launches for `tokens` <= bank->prefill_tokens (BF16 in/out).
+void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, void *out, int tokens,
+                     cudaStream_t stream) {
+    const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
+    const int sms = bank->runtime->sm_count;
+    nvfp4_runtime *rt = bank->runtime;
+    const PrefillScratch &ps = bank->ps;
+    PrefillRouteArgs ra{};
+    ra.router = bank->router;
+    ra.x = static_cast<const uint16_t *>(x);
+    ra.bias = bank->router_bias;
+    ra.inv_scales = bank->inv_scales;
+    ra.wnorm_max = bank->wnorm_max;
+    ra.T = tokens;
+    ra.E = E;
+    ra.H = H;
+    rt->profiled_kernel("moe_route", stream, [&](cudaStream_t s) {
+        check_cuda(launch_prefill_route(ra, ps, s), "prefill routing kernels");
+    });
+    rt->profiled_kernel("moe_quantize", stream, [&](cudaStream_t s) {
+        check_cuda(launch_quantize_rows(x, 0, tokens, H, bank->terms_x, ps.xq, ps.xsf, ps.gx, ps.max_tokens, s),
+                   "quantize_rows_kernel(x)");
+    });
+    GemmArgs ga{};
+    ga.sfa[0] = bank->sf_atoms[0];
+    ga.sfa[1] = bank->sf_atoms[1];
+    ga.sfb = ps.xsf;
+    ga.Rb = ps.max_tokens;
+    ga.J = bank->terms_x;
+    ga.K = H;
+    ga.M = I;
+    ga.E = E;
+    ga.inv_scales = bank->inv_scales;
+    ga.proj = 0;
+    ga.s = ps;
+    rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
+        check_cuda(launch_gemm_gate_up(bank->pmaps, ga, sms, s), "moe_gemm_kernel(gate/up)");
+    });
+    const int P = tokens * kSlots;
+    rt->profiled_kernel("moe_quantize", stream, [&](cudaStream_t s) {
+        check_cuda(launch_quantize_rows(ps.act, 1, P, I, bank->terms_act, ps.aq, ps.asf, ps.ga,
+                                        ps.max_tokens * kSlots, s),
+                   "quantize_rows_kernel(act)");
+    });
+    GemmArgs gd = ga;
+    gd.sfa[0] = bank->sf_atoms[2];
+    gd.sfa[1] = bank->sf_atoms[2];
+    gd.sfb = ps.asf;
+    gd.Rb = ps.max_tokens * kSlots;
+    gd.J = bank->terms_act;
+    gd.K = I;
+    gd.M = H;
+    gd.proj = 2;
+    rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
+        check_cuda(launch_gemm_down(bank->pmaps, gd, sms, s), "moe_gemm_kernel(down)");
+    });
+    rt->profiled_kernel("moe_combine", stream, [&](cudaStream_t s) {
+        check_cuda(launch_prefill_combine(ps, tokens, residual, out, s), "prefill_combine_kernel");
+    });
+}
+
+constexpr int kPrefillMaxSlice = 16384;
+
+// Batched BF16 forward: the decode path up to kDecodeMaxTokens tokens, the
+// prefill path above it (in slices of at most kPrefillMaxSlice tokens), or
+// decode-path slices when the bank's shape has no prefill kernels.
 void enqueue_forward_bf16(nvfp4_moe_bank *bank, const void *x, const void *residual, void *out,
                           int tokens, cudaStream_t stream) {
     const size_t row_bytes = static_cast<size_t>(bank->hidden) * 2;
-    for (int t0 = 0; t0 < tokens; t0 += kDecodeMaxTokens) {
-        const int n = tokens - t0 < kDecodeMaxTokens ? tokens - t0 : kDecodeMaxTokens;
+    const bool prefill = tokens > kDecodeMaxTokens && prefill_supported(bank);
+    const int slice = prefill ? (tokens < kPrefillMaxSlice ? tokens : kPrefillMaxSlice) : kDecodeMaxTokens;
+    if (prefill) ensure_prefill(bank, slice);
+    for (int t0 = 0; t0 < tokens; t0 += slice) {
+        const int n = tokens - t0 < slice ? tokens - t0 : slice;
         const uint8_t *xs = static_cast<const uint8_t *>(x) + t0 * row_bytes;
         const uint8_t *rs = residual ? static_cast<const uint8_t *>(residual) + t0 * row_bytes : nullptr;
         uint8_t *os = static_cast<uint8_t *>(out) + t0 * row_bytes;
-        enqueue_decode(bank, xs, 0, rs, os, 0, n, stream);
+        if (prefill)
+            enqueue_prefill(bank, xs, rs, os, n, stream);
+        else
+            enqueue_decode(bank, xs, 0, rs, os, 0, n, stream);
     }
     bank->last_tokens = tokens;
-    bank->last_path = tokens <= kDecodeMaxTokens ? 1 : 0;
+    bank->last_path = tokens <= kDecodeMaxTokens ? 1 : (prefill && tokens <= slice ? 2 : 0);
 }
 
 }  // namespace
@@ -221,11 +340,42 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
         check_cuda(cudaMemsetAsync(holder->scratch, 0, scratch, runtime->stream),
                    "cudaMemsetAsync(MoE bank scratch)");
         decode_scratch_carve(holder->ds, holder->scratch, experts, hidden, intermediate);
+        check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&holder->host_error), sizeof(int), cudaHostAllocMapped),
+                   "cudaHostAlloc(MoE bank error word)");
+        *holder->host_error = 0;
+        check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&holder->ds.host_error), holder->host_error, 0),
+                   "cudaHostGetDevicePointer(MoE bank error word)");
         check_cuda(make_stream_maps(holder->maps, holder->packed, holder->scales, experts, hidden, intermediate),
                    "cuTensorMapEncodeTiled(MoE bank)");
+        for (int p = 0; p < 3; ++p) {
+            const size_t ab = slots * holder->rows(p) * (holder->cols(p) / 16);
+            check_cuda(cudaMalloc(&holder->sf_atoms[p], ab), "cudaMalloc(MoE bank scale atoms)");
+            check_cuda(cudaMemsetAsync(holder->sf_atoms[p], 0, ab, runtime->stream),
+                       "cudaMemsetAsync(MoE bank scale atoms)");
+        }
+        check_cuda(make_prefill_weight_maps(holder->pmaps, holder->packed, experts, hidden, intermediate),
+                   "cuTensorMapEncodeTiled(MoE bank prefill)");
+        {
+            // Largest routed router-row norm: bounds the approximate-logit
+            // error of the prefill router (rounded up by a relative 1e-6).
+            double mx = 0.0;
+            for (int e = 0; e < experts; ++e) {
+                double ss = 0.0;
+                for (int k = 0; k < hidden; ++k) {
+                    uint32_t bits = static_cast<uint32_t>(router_bf16[static_cast<size_t>(e) * hidden + k]) << 16;
+                    float w;
+                    std::memcpy(&w, &bits, 4);
+                    ss += static_cast<double>(w) * w;
+                }
+                mx = ss > mx ? ss : mx;
+            }
+            holder->wnorm_max = static_cast<float>(std::sqrt(mx) * (1.0 + 1e-6));
+        }
         check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize(MoE bank create)");
         holder->uploaded.assign(slots * 3, 0);
-        holder->resident_bytes = 3 * (elements / 2) + scale_bytes_all + 3 * slots * sizeof(float) + router_all;
+        holder->resident_bytes = 3 * (elements / 2) + scale_bytes_all + 3 * (elements / 16) +
+                                 3 * slots * sizeof(float) + router_all;
+        runtime->error_words.emplace_back(holder->host_error, holder->ds.error);
         clear_last_error();
         *out_bank = holder.release();
         return NVFP4_STATUS_OK;
@@ -258,6 +408,10 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection(
                                                                bank->scales_per_expert(projection),
                                 pitch, clean.data(), scols, scols, bank->rows(projection), cudaMemcpyHostToDevice),
                    "cudaMemcpy2D(MoE bank scale upload)");
+        check_cuda(launch_scale_atoms(bank->sf_atoms[projection], bank->scales[projection], pitch,
+                                      (int)bank->rows(projection), (int)scols, expert * (int)bank->rows(projection),
+                                      rt->stream),
+                   "scale_atoms_kernel");
         const float inv = 1.0f / weight_global_scale;
         const size_t slots = static_cast<size_t>(bank->experts) + 1;
         check_cuda(cudaMemcpy(bank->inv_scales + static_cast<size_t>(projection) * slots + expert, &inv,
@@ -290,6 +444,11 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection_device(
             bank->scale_pitch(projection), static_cast<const uint8_t *>(scales_device), bank->rows(projection),
             bank->cols(projection) / 16);
         check_cuda(cudaGetLastError(), "sanitize_scales_kernel");
+        check_cuda(launch_scale_atoms(bank->sf_atoms[projection], bank->scales[projection],
+                                      bank->scale_pitch(projection), (int)bank->rows(projection),
+                                      (int)(bank->cols(projection) / 16), expert * (int)bank->rows(projection),
+                                      rt->stream),
+                   "scale_atoms_kernel");
         const float inv = 1.0f / weight_global_scale;
         const size_t slots = static_cast<size_t>(bank->experts) + 1;
         // cudaMemcpyAsync from pageable memory stages the value before returning.
@@ -380,25 +539,28 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_last_routing(nvfp4_moe_bank *ba
     if (!bank || !bank->runtime || max_tokens < 0) return fail_invalid("invalid routing query");
     if (bank->last_tokens == 0) return fail_invalid("no forward has run on this bank");
     if (!bank->last_path)
-        return fail_invalid("routing record is kept for calls of at most 64 tokens");
+        return fail_invalid("routing record is kept for calls that ran as one decode or prefill pass");
     try {
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
         check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(last_routing)");
         const int T = bank->last_tokens < max_tokens ? bank->last_tokens : max_tokens;
+        const bool pre = bank->last_path == 2;
+        const int *src_ids = pre ? bank->ps.ids : bank->ds.ids;
+        const float *src_w = pre ? bank->ps.weights : bank->ds.weights;
+        const int *src_counts = pre ? bank->ps.counts : bank->ds.counts;
+        const int *src_perm = pre ? bank->ps.perm : bank->ds.perm;
         if (ids)
-            check_cuda(cudaMemcpy(ids, bank->ds.ids, sizeof(int32_t) * T * kSlots, cudaMemcpyDeviceToHost),
+            check_cuda(cudaMemcpy(ids, src_ids, sizeof(int32_t) * T * kSlots, cudaMemcpyDeviceToHost),
                        "cudaMemcpy(routing ids)");
         if (weights)
-            check_cuda(cudaMemcpy(weights, bank->ds.weights, sizeof(float) * T * kSlots,
-                                  cudaMemcpyDeviceToHost),
+            check_cuda(cudaMemcpy(weights, src_w, sizeof(float) * T * kSlots, cudaMemcpyDeviceToHost),
                        "cudaMemcpy(routing weights)");
         if (counts)
-            check_cuda(cudaMemcpy(counts, bank->ds.counts, sizeof(int32_t) * bank->experts,
-                                  cudaMemcpyDeviceToHost),
+            check_cuda(cudaMemcpy(counts, src_counts, sizeof(int32_t) * bank->experts, cudaMemcpyDeviceToHost),
                        "cudaMemcpy(routing counts)");
         if (perm && T == bank->last_tokens)
-            check_cuda(cudaMemcpy(perm, bank->ds.perm, sizeof(int32_t) * T * kTopK, cudaMemcpyDeviceToHost),
+            check_cuda(cudaMemcpy(perm, src_perm, sizeof(int32_t) * T * kTopK, cudaMemcpyDeviceToHost),
                        "cudaMemcpy(routing perm)");
         if (out_tokens) *out_tokens = bank->last_tokens;
         clear_last_error();
@@ -412,8 +574,8 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_last_logits(nvfp4_moe_bank *ban
                                                              float *logits, int *out_tokens) {
     if (!bank || !bank->runtime || max_tokens < 0 || !logits) return fail_invalid("invalid logits query");
     if (bank->last_tokens == 0) return fail_invalid("no forward has run on this bank");
-    if (!bank->last_path)
-        return fail_invalid("routing record is kept for calls of at most 64 tokens");
+    if (bank->last_path != 1)
+        return fail_invalid("router logits are kept for calls of at most 64 tokens");
     try {
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
@@ -469,9 +631,60 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_info(const nvfp4_moe_bank *bank
 }
 
 extern "C" NVFP4_API void nvfp4_moe_bank_destroy(nvfp4_moe_bank *bank) {
-    if (bank && bank->runtime && bank->runtime->stream) {
+    if (bank && bank->runtime) {
         std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
-        cudaStreamSynchronize(bank->runtime->stream);
+        if (bank->runtime->stream) cudaStreamSynchronize(bank->runtime->stream);
+        auto &words = bank->runtime->error_words;
+        for (size_t i = 0; i < words.size(); ++i) {
+            if (words[i].second == bank->ds.error) {
+                words.erase(words.begin() + static_cast<std::ptrdiff_t>(i));
+                break;
+            }
+        }
     }
     delete bank;
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_prefill_terms(nvfp4_moe_bank *bank, int x_terms,
+                                                                   int act_terms) {
+    if (!bank || !bank->runtime || x_terms < 1 || x_terms > kMaxTerms || act_terms < 1 || act_terms > kMaxTerms)
+        return fail_invalid("prefill activation terms must be between 1 and 4");
+    std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
+    bank->terms_x = x_terms;
+    bank->terms_act = act_terms;
+    clear_last_error();
+    return NVFP4_STATUS_OK;
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_reserve_prefill(nvfp4_moe_bank *bank, int max_tokens) {
+    if (!bank || !bank->runtime || max_tokens < 1) return fail_invalid("invalid prefill reservation");
+    if (!prefill_supported(bank))
+        return fail_invalid("the prefill path needs hidden and intermediate to be multiples of 256");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        ensure_prefill(bank, max_tokens < kPrefillMaxSlice ? max_tokens : kPrefillMaxSlice);
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_quantize_rows_enqueue(const void *src, int src_is_f16, int rows, int cols,
+                                                              int terms, void *codes, void *scale_words,
+                                                              void *row_scales, void *stream) {
+    if (!src || !codes || !scale_words || !row_scales || rows < 1 || cols < 64 || cols % 64 != 0 || terms < 1 ||
+        terms > kMaxTerms || (src_is_f16 != 0 && src_is_f16 != 1))
+        return fail_invalid("invalid row quantisation arguments");
+    try {
+        check_cuda(launch_quantize_rows(src, src_is_f16, rows, cols, terms, static_cast<uint8_t *>(codes),
+                                        static_cast<uint32_t *>(scale_words), static_cast<float *>(row_scales), rows,
+                                        static_cast<cudaStream_t>(stream)),
+                   "quantize_rows_kernel");
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
 }

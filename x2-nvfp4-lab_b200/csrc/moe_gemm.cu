@@ -1,0 +1,408 @@
+// Grouped expert GEMMs of the prefill path on tcgen05 block-scaled NVFP4 MMA.
+//
+// One persistent CTA per SM walks (column tile, weight-row tile) pairs. A
+// column tile is up to 128 consecutive slot rows of one expert group (the
+// dispatch order keeps an expert's rows together); a weight-row tile is 128
+// rows of that expert's projection(s). Warp roles:
+//   warp 0     producer: per 256-column K stage, TMA tile loads of the weight
+//              rows (128-byte swizzle), one bulk copy of their scale-factor
+//              atoms, four-row TMA gathers of the J activation-term rows, and
+//              4-byte cp.async gathers of the activation scale words straight
+//              into scale-factor atom layout; all complete on the stage's
+//              mbarrier.
+//   warp 1     MMA issuer: one thread copies the stage's scale atoms into
+//              tensor memory (tcgen05.cp 32x128b.warpx4) and issues
+//              kind::mxf4nvf4 MMAs (M 128, N 128, K 64) into FP32
+//              accumulators in tensor memory, then commits the stage back to
+//              the producer and, after the last stage, the accumulator to
+//              the epilogue. Warp 1 also owns the tensor-memory allocation.
+//   warps 2-5  epilogue: tcgen05.ld of the accumulator rows of their
+//              sub-partition, per-column scaling, then
+//              gate/up: act = SiLU(gate) * up as FP16 [slot row][I];
+//              down:    y = coef * acc as FP16 [slot row][H].
+// Every mbarrier wait is bounded; on a timeout the CTA records the error,
+// drains its copies and MMAs in flight, frees its tensor memory and exits.
+#include "moe_prefill.cuh"
+#include "tcgen05_util.cuh"
+#include "tma_util.cuh"
+
+#include <atomic>
+
+namespace nvfp4 {
+
+namespace {
+
+constexpr int kGemmThreads = 192;
+constexpr int kTileBytes = kPrefillTileM * 128;  // 128 rows x 128 bytes (256 FP4 columns)
+constexpr int kSfStage = 4 * 512;                // four 64-column scale atoms
+constexpr int kStageK = 256;
+
+template <int NA, int J, int S>
+struct GemmCfg {
+    static constexpr int kA = NA * kTileBytes;
+    static constexpr int kB = J * kTileBytes;
+    static constexpr int kSfa = NA * kSfStage;
+    static constexpr int kSfb = J * kSfStage;
+    static constexpr int kStage = kA + kB + kSfa + kSfb;
+    static constexpr uint32_t kTx = kA + kB + kSfa;       // bytes tracked by the stage's transaction count
+    static constexpr int kColAcc1 = 128;
+    static constexpr int kColSfa = NA * 128;
+    static constexpr int kColSfb = kColSfa + NA * 16;
+    static constexpr int kColsUsed = kColSfb + J * 16;
+    static constexpr uint32_t kTmemCols = kColsUsed <= 256 ? 256u : 512u;
+    static constexpr size_t kSmem = 1024 + (size_t)S * kStage + 1024;
+    static_assert(kStage % 1024 == 0, "stage must keep 1024-byte tile alignment");
+    static_assert(kColsUsed <= 512, "tensor memory overflow");
+};
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+    return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ __half f32_to_f16_sat(float v) {
+    uint16_t h;
+    asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(h) : "f"(v));
+    return __ushort_as_half(h);
+}
+
+// Bounded wait that ignores the shared error word (used to drain copies in
+// flight after a failure). Returns false if the phase never completed.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+    const unsigned long long t0 = global_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void report(const PrefillScratch &s) {
+    const int code = *reinterpret_cast<volatile int *>(s.error);
+    if (s.host_error) *reinterpret_cast<volatile int *>(s.host_error) = code != 0 ? code : kErrWaitTimeout;
+}
+
+struct TileInfo {
+    int ai, e, n0, nvalid, mt;
+};
+
+__device__ __forceinline__ TileInfo tile_info(const PrefillScratch &s, int tile, int mtiles) {
+    TileInfo t;
+    const int ct = tile / mtiles;
+    t.mt = tile - ct * mtiles;
+    t.ai = s.tile_group[ct];
+    t.n0 = s.tile_n0[ct];
+    t.e = s.active_expert[t.ai];
+    t.nvalid = min(kPrefillTileN, s.tok_start[t.ai] + s.tok_count[t.ai] - t.n0);
+    return t;
+}
+
+template <int MODE, int J, int S>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
+                    const __grid_constant__ CUtensorMap tm_b, GemmArgs a) {
+    constexpr int NA = MODE == 0 ? 2 : 1;
+    using Cfg = GemmCfg<NA, J, S>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * Cfg::kStage);
+    uint64_t *empty = full + S;
+    uint64_t *acc_full = empty + S;
+    uint64_t *acc_empty = acc_full + 1;
+    uint64_t *drain = acc_empty + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
+    float *colscale = reinterpret_cast<float *>(tmem_slot + 4);  // [128]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const PrefillScratch &s = a.s;
+    int *err = s.error;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1 + 32);  // producer lane 0 (bytes) + one cp.async arrival per producer lane
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm_a0);
+        if (NA == 2) prefetch_tensormap(&tm_a1);
+        prefetch_tensormap(&tm_b);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, Cfg::kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // routing tables and activation terms are read from here on
+    pdl_launch_dependents();
+
+    const int mtiles = a.M / kPrefillTileM;
+    const int total = *s.n_tiles * mtiles;
+    const int kstages = a.K / kStageK;
+    const int kw = a.K / 64;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            const TileInfo ti = tile_info(s, tile, mtiles);
+            int grow[4], srow[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const int ig = 4 * lane + q, is = lane + 32 * q;
+                const int pg = ti.n0 + (ig < ti.nvalid ? ig : 0);
+                const int ps = ti.n0 + (is < ti.nvalid ? is : 0);
+                grow[q] = MODE == 0 ? s.tok_list[pg] : pg;
+                srow[q] = MODE == 0 ? s.tok_list[ps] : ps;
+            }
+            const int arow = ti.e * a.M + ti.mt * kPrefillTileM;
+            const size_t sfa_off = (size_t)(arow / kPrefillTileM) * kw * 512;
+            for (int ks = 0; ks < kstages; ++ks, ++it) {
+                const int st = it % S;
+                const uint32_t ph = (it / S) & 1u;
+                int okw = 1;
+                if (lane == 0) okw = mbar_wait(empty + st, ph ^ 1u, err, kSiteGemmEmpty) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, okw, 0)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *stage = smem + (size_t)st * Cfg::kStage;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(full + st, Cfg::kTx);
+                    tma_load_2d(stage, &tm_a0, full + st, ks * 128, arow);
+                    if (NA == 2) tma_load_2d(stage + kTileBytes, &tm_a1, full + st, ks * 128, arow);
+                    bulk_g2s(stage + Cfg::kA + Cfg::kB, a.sfa[0] + sfa_off + (size_t)ks * kSfStage, kSfStage,
+                             full + st);
+                    if (NA == 2)
+                        bulk_g2s(stage + Cfg::kA + Cfg::kB + kSfStage, a.sfa[1] + sfa_off + (size_t)ks * kSfStage,
+                                 kSfStage, full + st);
+                }
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+                    const int rb = j * a.Rb;
+                    tma_gather4(stage + Cfg::kA + j * kTileBytes + lane * 512, &tm_b, full + st, ks * 128,
+                                rb + grow[0], rb + grow[1], rb + grow[2], rb + grow[3]);
+                }
+                uint8_t *sfb = stage + Cfg::kA + Cfg::kB + Cfg::kSfa;
+#pragma unroll
+                for (int j = 0; j < J; ++j) {
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t *src = a.sfb + ((size_t)j * a.Rb + srow[q]) * kw + ks * 4;
+#pragma unroll
+                        for (int at = 0; at < 4; ++at)
+                            cp_async4(sfb + j * kSfStage + at * 512 + lane * 16 + q * 4, src + at);
+                    }
+                }
+                cp_async_arrive_noinc(full + st);
+            }
+        }
+        if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
+            // Drain: wait for the copies of the last stages issued.
+            cp_async_wait_all();
+            if (lane == 0) {
+                const uint32_t first = it > (uint32_t)S ? it - S : 0u;
+                for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_mxf4nvf4(kPrefillTileN);
+            const uint32_t smem_base = smem_u32(smem);
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
+                if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1u, err, kSiteGemmAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                for (int ks = 0; ks < kstages; ++ks, ++it) {
+                    const int st = it % S;
+                    const uint32_t ph = (it / S) & 1u;
+                    if (!mbar_wait(full + st, ph, err, kSiteGemmFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    tc::fence_proxy_async_smem();
+                    const uint32_t sb = smem_base + (uint32_t)st * Cfg::kStage;
+                    const uint32_t sfa = sb + Cfg::kA + Cfg::kB;
+                    const uint32_t sfb = sfa + Cfg::kSfa;
+#pragma unroll
+                    for (int at = 0; at < 4; ++at) {
+                        tc::cp_sf_atom(tmem + Cfg::kColSfa + 4 * at, tc::smem_desc_sf(sfa + at * 512));
+                        if (NA == 2)
+                            tc::cp_sf_atom(tmem + Cfg::kColSfa + 16 + 4 * at,
+                                           tc::smem_desc_sf(sfa + kSfStage + at * 512));
+#pragma unroll
+                        for (int j = 0; j < J; ++j)
+                            tc::cp_sf_atom(tmem + Cfg::kColSfb + 16 * j + 4 * at,
+                                           tc::smem_desc_sf(sfb + j * kSfStage + at * 512));
+                    }
+#pragma unroll
+                    for (int at = 0; at < 4; ++at) {
+#pragma unroll
+                        for (int j = 0; j < J; ++j) {
+                            const uint32_t acc = (ks | at | j) != 0 ? 1u : 0u;
+                            const uint64_t bdesc = tc::smem_desc_sw128(sb + Cfg::kA + j * kTileBytes + 32 * at);
+                            tc::mma_mxf4nvf4(tmem, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc,
+                                             tmem + Cfg::kColSfa + 4 * at, tmem + Cfg::kColSfb + 16 * j + 4 * at,
+                                             acc);
+                            if (NA == 2)
+                                tc::mma_mxf4nvf4(tmem + Cfg::kColAcc1, tc::smem_desc_sw128(sb + kTileBytes + 32 * at),
+                                                 bdesc, idesc, tmem + Cfg::kColSfa + 16 + 4 * at,
+                                                 tmem + Cfg::kColSfb + 16 * j + 4 * at, acc);
+                        }
+                    }
+                    tc::commit(empty + st);
+                }
+                if (!ok) break;
+                tc::commit(acc_full);
+            }
+            // Every MMA of this CTA has completed before tensor memory is freed.
+            tc::commit(drain);
+            mbar_wait_drain(drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------- epilogue
+        const int sub = warp & 3;
+        const int et = threadIdx.x - 64;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
+        uint32_t tcount = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
+            const TileInfo ti = tile_info(s, tile, mtiles);
+            {
+                float cs = 0.0f;
+                if (et < ti.nvalid) {
+                    const int p = ti.n0 + et;
+                    cs = MODE == 0 ? s.gx[s.tok_list[p]] : s.coef[p] * s.ga[p];
+                }
+                colscale[et] = cs;
+            }
+            // One thread waits for the accumulator and the decision is
+            // shared, so every epilogue warp leaves the loop together.
+            if (et == 0) *acc_ok = mbar_wait(acc_full, tcount & 1u, err, kSiteGemmAccFull) ? 1 : 0;
+            named_barrier(1, 128);
+            if (!*reinterpret_cast<volatile int *>(acc_ok)) break;
+            tc::fence_after_sync();
+            const int m = ti.mt * kPrefillTileM + 32 * sub + lane;
+            if (MODE == 0) {
+                const float ig = a.inv_scales[ti.e], iu = a.inv_scales[(a.E + 1) + ti.e];
+                for (int c0 = 0; c0 < kPrefillTileN; c0 += 32) {
+                    if (c0 >= ti.nvalid) break;
+                    uint32_t rg[32], ru[32];
+                    tc::ld_32x32b_x32(lane_base + c0, rg);
+                    tc::ld_32x32b_x32(lane_base + Cfg::kColAcc1 + c0, ru);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) {
+                        if (c0 + n < ti.nvalid) {
+                            const float cs = colscale[c0 + n];
+                            const float gate = __uint_as_float(rg[n]) * (ig * cs);
+                            const float up = __uint_as_float(ru[n]) * (iu * cs);
+                            s.act[(size_t)(ti.n0 + c0 + n) * a.M + m] = f32_to_f16_sat(gate / (1.0f + expf(-gate)) * up);
+                        }
+                    }
+                }
+            } else {
+                for (int c0 = 0; c0 < kPrefillTileN; c0 += 32) {
+                    if (c0 >= ti.nvalid) break;
+                    uint32_t r[32];
+                    tc::ld_32x32b_x32(lane_base + c0, r);
+                    tc::wait_ld();
+#pragma unroll
+                    for (int n = 0; n < 32; ++n)
+                        if (c0 + n < ti.nvalid)
+                            s.ypart[(size_t)(ti.n0 + c0 + n) * a.M + m] =
+                                f32_to_f16_sat(__uint_as_float(r[n]) * colscale[c0 + n]);
+                }
+            }
+            tc::fence_before_sync();
+            named_barrier(1, 128);
+            if (et == 0) mbar_arrive(acc_empty);
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, Cfg::kTmemCols);
+    }
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile int *>(err) != 0) report(s);
+}
+
+template <typename K>
+cudaError_t set_smem_once(K kernel, size_t bytes, std::atomic<uint64_t> &done) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load() & bit)) return cudaSuccess;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) done.fetch_or(bit);
+    return err;
+}
+
+template <int MODE, int J, int S>
+cudaError_t launch_cfg(const CUtensorMap &a0, const CUtensorMap &a1, const CUtensorMap &b, const GemmArgs &a,
+                       int grid, cudaStream_t stream) {
+    constexpr int NA = MODE == 0 ? 2 : 1;
+    using Cfg = GemmCfg<NA, J, S>;
+    static std::atomic<uint64_t> done{0};
+    cudaError_t err = set_smem_once(moe_gemm_kernel<MODE, J, S>, Cfg::kSmem, done);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_gemm_kernel<MODE, J, S>, a0, a1, b, a);
+}
+
+int gemm_grid(const GemmArgs &a, int sms) {
+    const long long coltiles = (long long)a.s.max_tiles;
+    const long long tiles = coltiles * (a.M / kPrefillTileM);
+    return (int)(tiles < sms ? tiles : sms);
+}
+
+}  // namespace
+
+cudaError_t launch_gemm_gate_up(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream) {
+    if (a.K % kStageK != 0 || a.M % kPrefillTileM != 0) return cudaErrorInvalidValue;
+    const int grid = gemm_grid(a, sms);
+    switch (a.J) {
+        case 1: return launch_cfg<0, 1, 4>(m.w[0], m.w[1], m.xq, a, grid, stream);
+        case 2: return launch_cfg<0, 2, 3>(m.w[0], m.w[1], m.xq, a, grid, stream);
+        case 3: return launch_cfg<0, 3, 2>(m.w[0], m.w[1], m.xq, a, grid, stream);
+        case 4: return launch_cfg<0, 4, 2>(m.w[0], m.w[1], m.xq, a, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_gemm_down(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream) {
+    if (a.K % kStageK != 0 || a.M % kPrefillTileM != 0) return cudaErrorInvalidValue;
+    const int grid = gemm_grid(a, sms);
+    switch (a.J) {
+        case 1: return launch_cfg<1, 1, 6>(m.w[2], m.w[2], m.aq, a, grid, stream);
+        case 2: return launch_cfg<1, 2, 4>(m.w[2], m.w[2], m.aq, a, grid, stream);
+        case 3: return launch_cfg<1, 3, 3>(m.w[2], m.w[2], m.aq, a, grid, stream);
+        case 4: return launch_cfg<1, 4, 2>(m.w[2], m.w[2], m.aq, a, grid, stream);
+        default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace nvfp4

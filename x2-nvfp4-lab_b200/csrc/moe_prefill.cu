@@ -1,0 +1,653 @@
+// Prefill path: routing, dispatch, activation quantisation and combine
+// kernels (the tcgen05 expert GEMMs are in moe_gemm.cu).
+#include "moe_prefill.cuh"
+#include "tma_util.cuh"
+
+#include <cfloat>
+
+namespace nvfp4 {
+
+namespace {
+
+constexpr int kLogitsTile = 64;       // tokens x router rows per CTA of the logits kernel
+constexpr int kSelectWarps = 8;       // tokens per CTA of the select kernel
+constexpr int kMaxCandidates = 64;
+// Margin of the approximate logits: |approx - exact| <= kMarginRel * |w| * |x|.
+// Both are FP32 sums of the same exactly representable BF16 x BF16 products;
+// an FP32 sum of K terms is within K * 2^-24 * sum|p| of the exact sum, and
+// sum|p| <= |w| * |x|, so 2^-8 covers K up to 2^14 with a wide reserve for
+// the tensor core's accumulation order.
+constexpr float kMarginRel = 1.0f / 256.0f;
+
+__device__ __forceinline__ unsigned float_order_key(float v) {
+    v = (v == 0.0f) ? 0.0f : v;
+    const unsigned b = __float_as_uint(v);
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------ approximate logits
+//
+// approx[t][e] = sum_k x[t,k] * W[e,k] with BF16 tensor-core MMAs (FP32
+// accumulation, order unspecified). Warp w of a CTA covers 16 tokens x 64
+// router rows; lane (g, c) loads columns [16c, 16c+16) of each 64-column
+// chunk for its rows, and the four k16 steps of the chunk map the MMA's
+// k-slots {2c, 2c+1, 2c+8, 2c+9} to columns 16c + 4i + {0, 1, 2, 3}, the
+// same mapping on both operands.
+__global__ void __launch_bounds__(128) prefill_logits_kernel(PrefillRouteArgs a, float *approx, int Rp) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, c = lane & 3;
+    const int R = a.E + 1, H = a.H;
+    const int t0 = blockIdx.x * kLogitsTile + warp * 16;
+    const int e0 = blockIdx.y * kLogitsTile;
+    const int ta = min(t0 + g, a.T - 1), tb = min(t0 + g + 8, a.T - 1);
+    const uint16_t *xa = a.x + (size_t)ta * H + 16 * c;
+    const uint16_t *xb = a.x + (size_t)tb * H + 16 * c;
+    const uint16_t *wr[8];
+#pragma unroll
+    for (int n = 0; n < 8; ++n) wr[n] = a.router + (size_t)min(e0 + 8 * n + g, R - 1) * H + 16 * c;
+    float acc[8][4];
+#pragma unroll
+    for (int n = 0; n < 8; ++n)
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[n][r] = 0.0f;
+    for (int k = 0; k < H; k += 64) {
+        const uint4 xa0 = __ldg(reinterpret_cast<const uint4 *>(xa + k));
+        const uint4 xa1 = __ldg(reinterpret_cast<const uint4 *>(xa + k + 8));
+        const uint4 xb0 = __ldg(reinterpret_cast<const uint4 *>(xb + k));
+        const uint4 xb1 = __ldg(reinterpret_cast<const uint4 *>(xb + k + 8));
+        const uint32_t A[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
+        const uint32_t B[8] = {xb0.x, xb0.y, xb0.z, xb0.w, xb1.x, xb1.y, xb1.z, xb1.w};
+#pragma unroll
+        for (int n = 0; n < 8; ++n) {
+            const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(wr[n] + k));
+            const uint4 w1 = __ldg(reinterpret_cast<const uint4 *>(wr[n] + k + 8));
+            const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                mma_bf16_16816(acc[n], A[2 * i], B[2 * i], A[2 * i + 1], B[2 * i + 1], W[2 * i], W[2 * i + 1]);
+        }
+    }
+#pragma unroll
+    for (int n = 0; n < 8; ++n) {
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const int t = t0 + g + (r >= 2 ? 8 : 0);
+            const int e = e0 + 8 * n + 2 * c + (r & 1);
+            if (t < a.T && e < R) approx[(size_t)t * Rp + e] = acc[n][r];
+        }
+    }
+}
+
+// Exact router logit of row `row` for token row `x` in the lab's FP32 order
+// (lane l owns columns j*128 + 4l + e; product and sum rounded separately;
+// xor butterfly 16..1), identical to the decode routing kernel's order.
+__device__ __forceinline__ float exact_logit(const uint16_t *w, const uint16_t *x, int H, int lane) {
+    float acc = 0.0f;
+    for (int k = lane * 4; k < H; k += 128) {
+        const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(w + k));
+        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + k));
+        acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.x & 0xFFFFu), bf16_bits_to_f32(xv.x & 0xFFFFu)));
+        acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.x >> 16), bf16_bits_to_f32(xv.x >> 16)));
+        acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.y & 0xFFFFu), bf16_bits_to_f32(xv.y & 0xFFFFu)));
+        acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.y >> 16), bf16_bits_to_f32(xv.y >> 16)));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
+    return acc;
+}
+
+// One warp per token: approximate top-8 boundary, exact logits of every
+// expert within twice the margin of it (a superset of the exact top-8), then
+// the exact top-8 (lowest id on ties), renormalised softmax weights and the
+// sigmoid shared gate -- the same selection and weight arithmetic as the
+// decode routing kernel. Also records the token in its 64-token block's
+// per-expert bit masks for dispatch.
+__global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_kernel(PrefillRouteArgs a, PrefillScratch s,
+                                                                          int Rp) {
+    __shared__ int s_cand[kSelectWarps][kMaxCandidates];
+    __shared__ float s_val[kSelectWarps][kMaxCandidates];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kSelectWarps + warp;
+    if (t >= a.T) return;
+    const int E = a.E, H = a.H;
+    const uint16_t *x = a.x + (size_t)t * H;
+
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        float val = -FLT_MAX;
+        if (e < E) {
+            val = s.approx[(size_t)t * Rp + e];
+            if (a.bias) val += a.bias[e];
+        }
+        v[i] = val;
+    }
+    // 8th largest approximate logit.
+    float a8 = -FLT_MAX;
+    {
+        unsigned taken = 0;
+        for (int slot = 0; slot < kTopK; ++slot) {
+            float bv = -FLT_MAX;
+            int bi = -1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (!((taken >> i) & 1u) && lane + 32 * i < E && (bi < 0 || v[i] > bv)) {
+                    bv = v[i];
+                    bi = i;
+                }
+            const unsigned key = bi < 0 ? 0u : float_order_key(bv);
+            const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+            const unsigned owner = __ffs(__ballot_sync(0xffffffffu, key == kmax && bi >= 0)) - 1;
+            if (lane == (int)owner) taken |= 1u << bi;
+            a8 = __shfl_sync(0xffffffffu, bv, owner);
+        }
+    }
+    // |x| for the margin.
+    float ss = 0.0f;
+    for (int k = lane * 4; k < H; k += 128) {
+        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + k));
+        const float x0 = bf16_bits_to_f32(xv.x & 0xFFFFu), x1 = bf16_bits_to_f32(xv.x >> 16);
+        const float x2 = bf16_bits_to_f32(xv.y & 0xFFFFu), x3 = bf16_bits_to_f32(xv.y >> 16);
+        ss += x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float delta = kMarginRel * a.wnorm_max * sqrtf(ss) * 1.0001f + 1e-30f;
+    const float thresh = a8 - 2.0f * delta;
+
+    // Candidate list (expert ids ascending within each lane's stride).
+    int n = 0;
+    bool overflow = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        const bool cand = e < E && v[i] >= thresh;
+        const unsigned m = __ballot_sync(0xffffffffu, cand);
+        const int idx = n + __popc(m & ((1u << lane) - 1u));
+        if (cand && idx < kMaxCandidates) s_cand[warp][idx] = e;
+        n += __popc(m);
+    }
+    if (n > kMaxCandidates) {
+        overflow = true;
+        n = 0;
+    }
+    __syncwarp();
+    // Exact logits; on overflow every expert is evaluated in a streaming
+    // top-8 (rare: it needs a very flat logit distribution).
+    float top_v[kTopK];
+    int top_i[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+        top_v[k] = -FLT_MAX;
+        top_i[k] = 0x7fffffff;
+    }
+    if (!overflow) {
+        for (int i = 0; i < n; ++i) {
+            const int e = s_cand[warp][i];
+            float val = exact_logit(a.router + (size_t)e * H, x, H, lane);
+            if (a.bias) val = __fadd_rn(val, a.bias[e]);
+            if (lane == 0) s_val[warp][i] = val;
+        }
+        __syncwarp();
+        // Top-8 of the candidates: lane holds candidates lane and lane+32.
+        float cv[2];
+        int ci[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const int idx = lane + 32 * h;
+            cv[h] = idx < n ? s_val[warp][idx] : -FLT_MAX;
+            ci[h] = idx < n ? s_cand[warp][idx] : 0x7fffffff;
+        }
+        for (int slot = 0; slot < kTopK; ++slot) {
+            float bv = -FLT_MAX;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+                if (ci[h] != 0x7fffffff && (cv[h] > bv || (cv[h] == bv && ci[h] < bi))) {
+                    bv = cv[h];
+                    bi = ci[h];
+                }
+            const unsigned key = bi == 0x7fffffff ? 0u : float_order_key(bv);
+            const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+            const unsigned imin = __reduce_min_sync(0xffffffffu, key == kmax ? (unsigned)bi : 0xffffffffu);
+            const int owner_h = (ci[0] == (int)imin) ? 0 : 1;
+            const bool mine = (ci[0] == (int)imin) || (ci[1] == (int)imin);
+            const unsigned ob = __ballot_sync(0xffffffffu, mine);
+            const int owner = __ffs(ob) - 1;
+            const float val = __shfl_sync(0xffffffffu, mine ? cv[owner_h] : 0.0f, owner);
+            if (mine) ci[owner_h] = 0x7fffffff;
+            top_v[slot] = val;
+            top_i[slot] = (int)imin;
+        }
+    } else {
+        for (int e = 0; e < E; ++e) {
+            float val = exact_logit(a.router + (size_t)e * H, x, H, lane);
+            if (a.bias) val = __fadd_rn(val, a.bias[e]);
+            // Insert into the running top-8 (every lane keeps the same copy).
+            if (val > top_v[kTopK - 1]) {
+                int p = kTopK - 1;
+                while (p > 0 && val > top_v[p - 1]) {
+                    top_v[p] = top_v[p - 1];
+                    top_i[p] = top_i[p - 1];
+                    --p;
+                }
+                top_v[p] = val;
+                top_i[p] = e;
+            }
+        }
+    }
+    const float sl = exact_logit(a.router + (size_t)E * H, x, H, lane);
+    if (lane == 0) {
+        float den = 0.0f;
+#pragma unroll
+        for (int slot = 0; slot < kTopK; ++slot) den += expf(top_v[slot] - top_v[0]);
+        for (int slot = 0; slot < kTopK; ++slot) {
+            s.ids[t * kSlots + slot] = top_i[slot];
+            s.weights[t * kSlots + slot] = expf(top_v[slot] - top_v[0]) / den;
+        }
+        s.ids[t * kSlots + kTopK] = E;
+        s.weights[t * kSlots + kTopK] = 1.0f / (1.0f + expf(-sl));
+    }
+    if (lane < kTopK) {
+        const int e = top_i[lane];
+        atomicOr(&s.blk_mask[(size_t)(t >> 6) * E + e], 1ull << (t & 63));
+    }
+}
+
+// Single CTA: per-expert block bases and counts, offsets, the compacted
+// active groups (routed experts with tokens, then the shared expert) and the
+// GEMM column-tile table.
+__global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int T) {
+    __shared__ int s_cnt[256], s_off[257], s_aidx[256], s_tiles[257], s_tstart[257];
+    __shared__ int s_total[3];
+    const int E = s.E;
+    const int nb = (T + 63) / 64;
+    const int e = threadIdx.x;
+    int run = 0;
+    if (e < E) {
+        for (int b = 0; b < nb; ++b) {
+            s.blk_base[(size_t)b * E + e] = run;
+            run += __popcll(s.blk_mask[(size_t)b * E + e]);
+        }
+        s.counts[e] = run;
+    }
+    s_cnt[e] = e < E ? run : 0;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int off = 0, act = 0, tiles = 0;
+        for (int i = 0; i < E; ++i) {
+            s_off[i] = off;
+            off += s_cnt[i];
+            if (s_cnt[i] > 0) {
+                s_aidx[i] = act++;
+                s_tstart[i] = tiles;
+                tiles += (s_cnt[i] + kPrefillTileN - 1) / kPrefillTileN;
+            } else {
+                s_aidx[i] = -1;
+            }
+        }
+        s_off[E] = off;
+        s_tstart[E] = tiles;  // shared expert's first column tile
+        tiles += (T + kPrefillTileN - 1) / kPrefillTileN;
+        s_total[0] = act;
+        s_total[1] = tiles;
+    }
+    __syncthreads();
+    const int nrouted = s_total[0];
+    if (e < E) {
+        s.offsets[e] = s_off[e];
+        const int ai = s_aidx[e];
+        if (ai >= 0) {
+            s.active_expert[ai] = e;
+            s.tok_start[ai] = s_off[e];
+            s.tok_count[ai] = s_cnt[e];
+            const int nt = (s_cnt[e] + kPrefillTileN - 1) / kPrefillTileN;
+            for (int j = 0; j < nt; ++j) {
+                s.tile_group[s_tstart[e] + j] = ai;
+                s.tile_n0[s_tstart[e] + j] = s_off[e] + j * kPrefillTileN;
+            }
+        }
+    }
+    if (threadIdx.x == 0) {
+        s.offsets[E] = s_off[E];
+        s.active_expert[nrouted] = E;
+        s.tok_start[nrouted] = T * kTopK;
+        s.tok_count[nrouted] = T;
+        *s.n_active = nrouted + 1;
+        *s.n_tiles = s_total[1];
+    }
+    const int st = s_tstart[E], nt = (T + kPrefillTileN - 1) / kPrefillTileN;
+    for (int j = threadIdx.x; j < nt; j += blockDim.x) {
+        s.tile_group[st + j] = nrouted;
+        s.tile_n0[st + j] = T * kTopK + j * kPrefillTileN;
+    }
+}
+
+// Thread per (token, slot): position in the expert-grouped order (experts
+// ascending, tokens ascending), and the per-slot-row tables.
+__global__ void prefill_place_kernel(PrefillScratch s, int T, const float *inv_scales) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int E = s.E;
+    const float *inv_down = inv_scales + 2 * (size_t)(E + 1);
+    if (i < T * kTopK) {
+        const int t = i / kTopK, k = i - t * kTopK;
+        const int e = s.ids[t * kSlots + k];
+        const int b = t >> 6;
+        const unsigned long long m = s.blk_mask[(size_t)b * E + e];
+        const int pos = s.offsets[e] + s.blk_base[(size_t)b * E + e] + __popcll(m & ((1ull << (t & 63)) - 1ull));
+        s.perm[pos] = i;
+        s.tok_list[pos] = t;
+        s.inv_pos[i] = pos;
+        s.coef[pos] = s.weights[t * kSlots + k] * inv_down[e];
+    } else if (i < T * kSlots) {
+        const int t = i - T * kTopK;
+        const int pos = T * kTopK + t;
+        s.tok_list[pos] = t;
+        s.coef[pos] = s.weights[t * kSlots + kTopK] * inv_down[E];
+    }
+}
+
+// ------------------------------------------------------- quantisation
+
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+    uint16_t r;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+    uint16_t r;
+    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}"
+        : "=h"(r)
+        : "f"(hi), "f"(lo));
+    return r;
+}
+
+__device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
+    const uint32_t h2 = e4m3x2_to_f16x2(static_cast<uint16_t>(b));
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+}
+
+// Clear the sign of zero-magnitude E2M1 codes (eight nibbles per word).
+__device__ __forceinline__ uint32_t canonical_zero_codes(uint32_t w) {
+    const uint32_t m = w & 0x77777777u;
+    const uint32_t nz = (m | (m >> 1) | (m >> 2)) & 0x11111111u;
+    return m | (w & (nz << 3));
+}
+
+// One warp per row. Lane l quantises the 64-column chunks l, l+32, ...; a
+// chunk holds four 16-column blocks, so each lane writes whole scale words.
+// Per term: s = E4M3_RN((bamax / 6) / g); denom = s * g; code =
+// E2M1_RN(r * RN(1/denom)) (0 when denom is 0); r -= code * denom.
+template <int J>
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int src_is_f16, int rows, int cols,
+                                                            uint8_t *codes, uint32_t *sf, float *g_out,
+                                                            int rows_stride) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= rows) return;
+    const int r = warp;
+    const uint16_t *row = static_cast<const uint16_t *>(src) + (size_t)r * cols;
+    const int chunks = cols / 64;
+    auto load_chunk = [&](int ch, float (&v)[64]) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + ch * 64);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const uint4 u = __ldg(p + q);
+            const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                if (src_is_f16) {
+                    const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[h]));
+                    v[8 * q + 2 * h] = f.x;
+                    v[8 * q + 2 * h + 1] = f.y;
+                } else {
+                    v[8 * q + 2 * h] = bf16_bits_to_f32(w[h] & 0xFFFFu);
+                    v[8 * q + 2 * h + 1] = bf16_bits_to_f32(w[h] >> 16);
+                }
+            }
+        }
+    };
+    float amax = 0.0f;
+    for (int ch = lane; ch < chunks; ch += 32) {
+        float v[64];
+        load_chunk(ch, v);
+#pragma unroll
+        for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float g = amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
+    if (lane == 0) g_out[r] = g;
+    for (int ch = lane; ch < chunks; ch += 32) {
+        float v[64];
+        load_chunk(ch, v);
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+            uint32_t sword = 0;
+            uint32_t cw[8];
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                float bamax = 0.0f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(v[16 * b + i]));
+                const float target = __fdiv_rn(__fdiv_rn(bamax, 6.0f), g);
+                const uint32_t sb = f32x2_to_e4m3x2(target, 0.0f) & 0xFFu;
+                sword |= sb << (8 * b);
+                const float denom = __fmul_rn(e4m3_byte_to_f32(sb), g);
+                const float inv = denom != 0.0f ? __frcp_rn(denom) : 0.0f;
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                    uint32_t word = 0;
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const int e0 = 16 * b + 8 * p + 2 * i;
+                        const uint32_t cc = f32x2_to_e2m1x2(__fmul_rn(v[e0], inv), __fmul_rn(v[e0 + 1], inv)) & 0xFFu;
+                        word |= cc << (8 * i);
+                    }
+                    word = canonical_zero_codes(word);
+                    cw[2 * b + p] = word;
+                    // Residual for the next term.
+                    uint32_t h[4];
+                    e2m1x8_to_f16x8(word, h);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                        const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(&h[i]));
+                        const int e0 = 16 * b + 8 * p + 2 * i;
+                        v[e0] = __fsub_rn(v[e0], __fmul_rn(d.x, denom));
+                        v[e0 + 1] = __fsub_rn(v[e0 + 1], __fmul_rn(d.y, denom));
+                    }
+                }
+            }
+            const size_t prow = (size_t)j * rows_stride + r;
+            uint4 *dst = reinterpret_cast<uint4 *>(codes + prow * (cols / 2) + ch * 32);
+            dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+            dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+            sf[prow * (cols / 64) + ch] = sword;
+        }
+    }
+}
+
+// ------------------------------------------------------------- combine
+
+// out[t][h] = sum over routed slots k = 0..7 of ypart[inv_pos[t*8+k]][h],
+// then the shared slot, then the BF16 residual (the decode combine order).
+// Each thread handles 8 consecutive h.
+__global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillScratch s, int T, const uint16_t *residual,
+                                                              uint16_t *out) {
+    const int t = blockIdx.y;
+    const int H = s.H;
+    const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (h >= H) return;
+    float acc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+    auto add_row = [&](int pos) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(s.ypart + (size_t)pos * H + h));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[i]));
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+        }
+    };
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) add_row(s.inv_pos[t * kTopK + k]);
+    add_row(T * kTopK + t);
+    uint32_t o[4];
+    if (residual) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(residual + (size_t)t * H + h));
+        const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            acc[2 * i] += bf16_bits_to_f32(w[i] & 0xFFFFu);
+            acc[2 * i + 1] += bf16_bits_to_f32(w[i] >> 16);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = f32_to_bf16_bits(acc[2 * i]) | (f32_to_bf16_bits(acc[2 * i + 1]) << 16);
+    *reinterpret_cast<uint4 *>(out + (size_t)t * H + h) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__global__ void scale_atoms_kernel(uint8_t *atoms, const uint8_t *scales, size_t pitch, int rows, int k16,
+                                   int row0) {
+    const size_t n = (size_t)rows * k16;
+    const int kb64 = k16 / 4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int rl = (int)(i / k16), k = (int)(i - (size_t)rl * k16);
+        const int r = row0 + rl;
+        const size_t dst = ((size_t)(r / 128) * kb64 + k / 4) * 512 + (r % 32) * 16 + ((r % 128) / 32) * 4 + (k % 4);
+        atoms[dst] = scales[(size_t)r * pitch + k];
+    }
+}
+
+}  // namespace
+
+size_t prefill_scratch_bytes(int T, int E, int H, int I, int Jx, int Ja) {
+    PrefillScratch s{};
+    prefill_scratch_carve(s, nullptr, T, E, H, I, Jx, Ja);
+    return reinterpret_cast<size_t>(s.ypart) + (size_t)T * kSlots * H * 2 + 256;
+}
+
+void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, int I, int Jx, int Ja) {
+    size_t off = 0;
+    auto take = [&](size_t bytes) {
+        const size_t o = off;
+        off += (bytes + 1023) & ~size_t(1023);
+        return static_cast<uint8_t *>(base) + o;
+    };
+    const size_t Tz = (size_t)T, P = (size_t)T * kSlots;
+    const int R = E + 1, Rp = (R + 63) / 64 * 64, nb = (T + 63) / 64;
+    s.max_tokens = T;
+    s.E = E;
+    s.H = H;
+    s.I = I;
+    s.max_tiles = (int)(P / kPrefillTileN) + R + 1;
+    s.approx = reinterpret_cast<float *>(take(Tz * Rp * 4));
+    s.ids = reinterpret_cast<int *>(take(Tz * kSlots * 4));
+    s.weights = reinterpret_cast<float *>(take(Tz * kSlots * 4));
+    s.blk_mask = reinterpret_cast<unsigned long long *>(take((size_t)nb * E * 8));
+    s.blk_base = reinterpret_cast<int *>(take((size_t)nb * E * 4));
+    s.counts = reinterpret_cast<int *>(take((size_t)E * 4));
+    s.offsets = reinterpret_cast<int *>(take((size_t)R * 4));
+    s.n_active = reinterpret_cast<int *>(take(4));
+    s.active_expert = reinterpret_cast<int *>(take((size_t)R * 4));
+    s.tok_start = reinterpret_cast<int *>(take((size_t)R * 4));
+    s.tok_count = reinterpret_cast<int *>(take((size_t)R * 4));
+    s.n_tiles = reinterpret_cast<int *>(take(4));
+    s.tile_group = reinterpret_cast<int *>(take((size_t)s.max_tiles * 4));
+    s.tile_n0 = reinterpret_cast<int *>(take((size_t)s.max_tiles * 4));
+    s.perm = reinterpret_cast<int *>(take(Tz * kTopK * 4));
+    s.inv_pos = reinterpret_cast<int *>(take(Tz * kTopK * 4));
+    s.tok_list = reinterpret_cast<int *>(take(P * 4));
+    s.coef = reinterpret_cast<float *>(take(P * 4));
+    s.xq = take((size_t)Jx * Tz * H / 2);
+    s.xsf = reinterpret_cast<uint32_t *>(take((size_t)Jx * Tz * (H / 64) * 4));
+    s.gx = reinterpret_cast<float *>(take(Tz * 4));
+    s.act = reinterpret_cast<__half *>(take(P * I * 2));
+    s.aq = take((size_t)Ja * P * I / 2);
+    s.asf = reinterpret_cast<uint32_t *>(take((size_t)Ja * P * (I / 64) * 4));
+    s.ga = reinterpret_cast<float *>(take(P * 4));
+    s.ypart = reinterpret_cast<__half *>(take(P * H * 2));
+}
+
+cudaError_t make_prefill_weight_maps(PrefillMaps &m, uint8_t *const packed[3], int E, int H, int I) {
+    const uint64_t slots = static_cast<uint64_t>(E) + 1;
+    for (int p = 0; p < 3; ++p) {
+        const uint64_t rows = slots * (p < 2 ? I : H);
+        const uint64_t k = p < 2 ? H : I;
+        cudaError_t err = make_tensor_map_u8(&m.w[p], packed[p], k / 2, k / 2, rows, 128, kPrefillTileM,
+                                             CU_TENSOR_MAP_SWIZZLE_128B);
+        if (err != cudaSuccess) return err;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t make_prefill_act_maps(PrefillMaps &m, const PrefillScratch &s, int Jx, int Ja) {
+    const uint64_t T = s.max_tokens, P = (uint64_t)s.max_tokens * kSlots;
+    cudaError_t err = make_tensor_map_u8(&m.xq, s.xq, s.H / 2, s.H / 2, Jx * T, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (err != cudaSuccess) return err;
+    return make_tensor_map_u8(&m.aq, s.aq, s.I / 2, s.I / 2, Ja * P, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pitch, int rows, int k16, int row0,
+                               cudaStream_t stream) {
+    const size_t n = (size_t)rows * k16;
+    const int grid = (int)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096);
+    scale_atoms_kernel<<<grid, 256, 0, stream>>>(atoms, scales, pitch, rows, k16, row0);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, cudaStream_t stream) {
+    const int R = a.E + 1, Rp = (R + 63) / 64 * 64;
+    const int nb = (a.T + 63) / 64;
+    cudaError_t err = cudaMemsetAsync(s.blk_mask, 0, (size_t)nb * a.E * 8, stream);
+    if (err != cudaSuccess) return err;
+    prefill_logits_kernel<<<dim3((a.T + kLogitsTile - 1) / kLogitsTile, (R + kLogitsTile - 1) / kLogitsTile), 128, 0,
+                            stream>>>(a, s.approx, Rp);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    prefill_select_kernel<<<(a.T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    prefill_scan_kernel<<<1, 256, 0, stream>>>(s, a.T);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    const int n = a.T * kSlots;
+    prefill_place_kernel<<<(n + 255) / 256, 256, 0, stream>>>(s, a.T, a.inv_scales);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
+                                 uint32_t *sf, float *g, int rows_stride, cudaStream_t stream) {
+    if (cols % 64 != 0 || rows <= 0) return cudaErrorInvalidValue;
+    const int grid = (rows + 7) / 8;
+    switch (terms) {
+        case 1: quantize_rows_kernel<1><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
+        case 2: quantize_rows_kernel<2><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
+        case 3: quantize_rows_kernel<3><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
+        case 4: quantize_rows_kernel<4><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
+        default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out,
+                                   cudaStream_t stream) {
+    const dim3 grid((s.H / 8 + 255) / 256, T);
+    prefill_combine_kernel<<<grid, 256, 0, stream>>>(s, T, static_cast<const uint16_t *>(residual),
+                                                     static_cast<uint16_t *>(out));
+    return cudaGetLastError();
+}
+
+}  // namespace nvfp4

@@ -1,0 +1,121 @@
+// Prefill path of the NVFP4 MoE layer (token batches above the decode
+// limit), built on tcgen05 block-scaled NVFP4 MMA.
+//
+// Numerics. The expert GEMMs run kind::mxf4nvf4 (E2M1 x E2M1 with E4M3
+// scales per 16 elements, FP32 accumulation in tensor memory). Activations
+// enter as a sum of J NVFP4 "terms" per row: term 1 quantises the row, term
+// j+1 quantises what terms 1..j left over, all terms sharing the row's FP32
+// global scale g = amax/2688. J = 1 is plain NVFP4 activation quantisation;
+// every extra term cuts the activation error about elevenfold (J = 3 or 4
+// holds the layer within the BF16-grade parity tolerance). The GEMM adds the
+// J products in one accumulator (the terms are extra K).
+//
+// Launch sequence (one stream):
+//   1. prefill_logits_kernel    approximate router logits (BF16 mma.sync)
+//   2. prefill_select_kernel    exact FP32 fixed-order logits of the
+//                               candidates near the top-8 boundary, top-8,
+//                               weights, shared gate; per-64-token masks
+//   3. prefill_scan_kernel      counts, offsets, active groups, tile table
+//   4. prefill_place_kernel     dispatch permutation and per-slot tables
+//   5. quantize_rows_kernel     x -> J NVFP4 terms (per token)
+//   6. moe_gemm_gate_up_kernel  act = SiLU(gate) * up, FP16 [slot rows][I]
+//   7. quantize_rows_kernel     act -> J NVFP4 terms (per slot row)
+//   8. moe_gemm_down_kernel     y = coef * W_down act, FP16 [slot rows][H]
+//   9. prefill_combine_kernel   out = sum of nine slots (+ residual), BF16
+#pragma once
+
+#include "moe_decode.cuh"
+
+#include <cuda.h>
+
+namespace nvfp4 {
+
+constexpr int kPrefillTileN = 128;   // slot rows per GEMM column tile
+constexpr int kPrefillTileM = 128;   // weight rows per GEMM tile
+constexpr int kMaxTerms = 4;
+
+// Device scratch of the prefill path for up to `max_tokens` tokens.
+struct PrefillScratch {
+    int max_tokens;
+    int E, H, I;
+    float *approx;           // [T][Rp] approximate logits, Rp = round_up(E+1, 64)
+    int *ids;                // [T][9]
+    float *weights;          // [T][9]
+    unsigned long long *blk_mask;  // [nb][E] token bits per 64-token block
+    int *blk_base;           // [nb][E]
+    int *counts;             // [E]
+    int *offsets;            // [E+1]
+    int *n_active;           // [1]
+    int *active_expert;      // [E+1]
+    int *tok_start;          // [E+1]
+    int *tok_count;          // [E+1]
+    int *n_tiles;            // [1] column tiles
+    int *tile_group;         // [max tiles] active-group index of a column tile
+    int *tile_n0;            // [max tiles] first slot row of a column tile
+    int *perm;               // [T*8]
+    int *inv_pos;            // [T*8]
+    int *tok_list;           // [T*9] token of each slot row
+    float *coef;             // [T*9] routing weight * inverse down global scale
+    uint8_t *xq;             // [Jx][T][H/2]
+    uint32_t *xsf;           // [Jx][T][H/64]
+    float *gx;               // [T]
+    __half *act;             // [T*9][I]
+    uint8_t *aq;             // [Ja][T*9][I/2]
+    uint32_t *asf;           // [Ja][T*9][I/64]
+    float *ga;               // [T*9]
+    __half *ypart;           // [T*9][H]
+    int *error;              // device error word (shared with the decode scratch)
+    int *host_error;         // host-mapped error word or nullptr
+    int max_tiles;
+};
+
+// TMA descriptors of one prefill scratch (activation terms) and a bank's
+// weights (128-row boxes).
+struct PrefillMaps {
+    CUtensorMap w[3];        // packed weights, box {128 B, 128 rows}, 128-byte swizzle
+    CUtensorMap xq;          // [Jx*T][H/2], box {128 B, 1 row}
+    CUtensorMap aq;          // [Ja*T*9][I/2], box {128 B, 1 row}
+};
+
+struct PrefillRouteArgs {
+    const uint16_t *router;   // [(E+1)][H]
+    const uint16_t *x;        // [T][H] BF16
+    const float *bias;        // [E] or nullptr
+    const float *inv_scales;  // [3][E+1]
+    float wnorm_max;          // max over router rows of the L2 norm (host-computed bound)
+    int T, E, H;
+};
+
+struct GemmArgs {
+    const uint8_t *sfa[2];    // weight scale atoms of the A projections
+    const uint32_t *sfb;      // [J][Rb][K/64]
+    int Rb;                   // rows per term of the B tensors
+    int J;                    // activation terms
+    int K;                    // reduction length
+    int M;                    // weight rows per expert
+    int E;
+    const float *inv_scales;  // [3][E+1]
+    int proj;                 // first projection index (0 gate/up, 2 down)
+    PrefillScratch s;
+};
+
+size_t prefill_scratch_bytes(int T, int E, int H, int I, int Jx, int Ja);
+void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, int I, int Jx, int Ja);
+
+cudaError_t make_prefill_weight_maps(PrefillMaps &m, uint8_t *const packed[3], int E, int H, int I);
+cudaError_t make_prefill_act_maps(PrefillMaps &m, const PrefillScratch &s, int Jx, int Ja);
+
+// Weight scale bytes [rows][K/16] (pitched) -> the tcgen05 scale-factor atom
+// layout [rows/128][K/64][512 B]: byte (r%32)*16 + ((r%128)/32)*4 + (k/16)%4.
+cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pitch, int rows, int k16, int row0,
+                               cudaStream_t stream);
+
+cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, cudaStream_t stream);
+cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
+                                 uint32_t *sf, float *g, int rows_stride, cudaStream_t stream);
+cudaError_t launch_gemm_gate_up(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream);
+cudaError_t launch_gemm_down(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream);
+cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out,
+                                   cudaStream_t stream);
+
+}  // namespace nvfp4

@@ -156,6 +156,11 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "nvfp4_moe_route_static_scratch": (
         [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
          C.c_void_p], C.c_int),
+    "nvfp4_moe_bank_set_prefill_terms": ([C.c_void_p, C.c_int, C.c_int], C.c_int),
+    "nvfp4_moe_bank_reserve_prefill": ([C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_quantize_rows_enqueue": (
+        [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
+        C.c_int),
 }
 
 
@@ -389,6 +394,16 @@ class MoeBank:
             "nvfp4_moe_bank_set_router_bias",
         )
 
+    def set_prefill_terms(self, x_terms: int, act_terms: int) -> None:
+        """additive: NVFP4 activation terms of the prefill path (1..4 each)."""
+        self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_prefill_terms(self.handle, x_terms, act_terms),
+                            "nvfp4_moe_bank_set_prefill_terms")
+
+    def reserve_prefill(self, max_tokens: int) -> None:
+        """additive: allocate prefill working memory for calls of up to max_tokens tokens."""
+        self.runtime._check(self.runtime.lib.nvfp4_moe_bank_reserve_prefill(self.handle, max_tokens),
+                            "nvfp4_moe_bank_reserve_prefill")
+
     @property
     def resident_bytes(self) -> int:
         size = C.c_size_t(0)
@@ -590,6 +605,29 @@ class Runtime:
             "bf16_gemv_device_enqueue",
         )
         return out
+
+    def quantize_rows(self, x, terms: int):
+        """additive: split BF16/FP16 rows [rows, cols] (a CUDA tensor) into
+        `terms` NVFP4 terms on torch's current stream. Returns (codes uint8
+        [terms, rows, cols/2], scale words int32 [terms, rows, cols/64], row
+        scales float32 [rows])."""
+        import torch
+
+        if x.dim() != 2 or x.dtype not in (torch.bfloat16, torch.float16) or not x.is_cuda:
+            raise ValueError("quantize_rows expects a 2D BF16 or FP16 CUDA tensor")
+        x = x.contiguous()
+        rows, cols = x.shape
+        codes = torch.empty(terms, rows, cols // 2, dtype=torch.uint8, device=x.device)
+        words = torch.empty(terms, rows, cols // 64, dtype=torch.int32, device=x.device)
+        g = torch.empty(rows, dtype=torch.float32, device=x.device)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        self._check(
+            self.lib.nvfp4_quantize_rows_enqueue(
+                _tensor_ptr(x), 1 if x.dtype == torch.float16 else 0, rows, cols, terms, _tensor_ptr(codes),
+                _tensor_ptr(words), _tensor_ptr(g), C.c_void_p(stream)),
+            "nvfp4_quantize_rows_enqueue",
+        )
+        return codes, words, g
 
     def close(self) -> None:
         if self.handle:
