@@ -187,7 +187,8 @@ void ensure_prefill(nvfp4_moe_bank *bank, int tokens) {
     const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
     const size_t bytes = prefill_scratch_bytes(cap, E, H, I, bank->terms_x, bank->terms_act);
     check_cuda(cudaMalloc(&bank->pscratch, bytes), "cudaMalloc(MoE bank prefill scratch)");
-    check_cuda(cudaMemset(bank->pscratch, 0, bytes), "cudaMemset(MoE bank prefill scratch)");
+    check_cuda(cudaMemsetAsync(bank->pscratch, 0, bytes, rt->stream), "cudaMemsetAsync(MoE bank prefill scratch)");
+    check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(prefill scratch)");
     prefill_scratch_carve(bank->ps, bank->pscratch, cap, E, H, I, bank->terms_x, bank->terms_act);
     bank->ps.error = bank->ds.error;
     bank->ps.host_error = bank->ds.host_error;
@@ -330,10 +331,14 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
                    "cudaMemsetAsync(MoE bank inverse scales)");
         const size_t router_all = slots * static_cast<size_t>(hidden) * sizeof(uint16_t);
         check_cuda(cudaMalloc(&holder->router, router_all), "cudaMalloc(MoE bank router)");
-        check_cuda(cudaMemcpy(holder->router, router_bf16, router_bytes, cudaMemcpyHostToDevice),
+        // Host-to-device copies go through the runtime stream: a synchronous
+        // cudaMemcpy from pageable memory may return before its DMA lands and
+        // is not ordered with the (non-blocking) runtime stream.
+        check_cuda(cudaMemcpyAsync(holder->router, router_bf16, router_bytes, cudaMemcpyHostToDevice,
+                                   runtime->stream),
                    "cudaMemcpy(MoE bank router)");
-        check_cuda(cudaMemcpy(reinterpret_cast<uint8_t *>(holder->router) + router_bytes,
-                              shared_gate_bf16, shared_gate_bytes, cudaMemcpyHostToDevice),
+        check_cuda(cudaMemcpyAsync(reinterpret_cast<uint8_t *>(holder->router) + router_bytes,
+                              shared_gate_bf16, shared_gate_bytes, cudaMemcpyHostToDevice, runtime->stream),
                    "cudaMemcpy(MoE bank shared gate)");
         const size_t scratch = decode_scratch_bytes(experts, hidden, intermediate);
         check_cuda(cudaMalloc(&holder->scratch, scratch), "cudaMalloc(MoE bank scratch)");
@@ -400,13 +405,16 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection(
             b &= 0x7Fu;
             if (b == 0x7Fu) b = 0u;
         }
-        check_cuda(cudaMemcpy(bank->packed[projection] + static_cast<size_t>(expert) * pp, packed, pp,
-                              cudaMemcpyHostToDevice),
+        // Copies are ordered on the runtime stream (see nvfp4_moe_bank_create);
+        // pageable sources are staged before each call returns.
+        check_cuda(cudaMemcpyAsync(bank->packed[projection] + static_cast<size_t>(expert) * pp, packed, pp,
+                                   cudaMemcpyHostToDevice, rt->stream),
                    "cudaMemcpy(MoE bank packed upload)");
         const size_t scols = bank->cols(projection) / 16, pitch = bank->scale_pitch(projection);
-        check_cuda(cudaMemcpy2D(bank->scales[projection] + static_cast<size_t>(expert) *
-                                                               bank->scales_per_expert(projection),
-                                pitch, clean.data(), scols, scols, bank->rows(projection), cudaMemcpyHostToDevice),
+        check_cuda(cudaMemcpy2DAsync(bank->scales[projection] + static_cast<size_t>(expert) *
+                                                                    bank->scales_per_expert(projection),
+                                     pitch, clean.data(), scols, scols, bank->rows(projection),
+                                     cudaMemcpyHostToDevice, rt->stream),
                    "cudaMemcpy2D(MoE bank scale upload)");
         check_cuda(launch_scale_atoms(bank->sf_atoms[projection], bank->scales[projection], pitch,
                                       (int)bank->rows(projection), (int)scols, expert * (int)bank->rows(projection),
@@ -414,9 +422,10 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection(
                    "scale_atoms_kernel");
         const float inv = 1.0f / weight_global_scale;
         const size_t slots = static_cast<size_t>(bank->experts) + 1;
-        check_cuda(cudaMemcpy(bank->inv_scales + static_cast<size_t>(projection) * slots + expert, &inv,
-                              sizeof(float), cudaMemcpyHostToDevice),
+        check_cuda(cudaMemcpyAsync(bank->inv_scales + static_cast<size_t>(projection) * slots + expert, &inv,
+                                   sizeof(float), cudaMemcpyHostToDevice, rt->stream),
                    "cudaMemcpy(MoE bank inverse scale)");
+        check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(MoE bank upload)");
         mark_uploaded(bank, expert, projection);
         clear_last_error();
         return NVFP4_STATUS_OK;
@@ -607,9 +616,10 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_router_bias(nvfp4_moe_bank 
             if (!bank->router_bias)
                 check_cuda(cudaMalloc(&bank->router_bias, sizeof(float) * bank->experts),
                            "cudaMalloc(router bias)");
-            check_cuda(cudaMemcpy(bank->router_bias, bias, sizeof(float) * bank->experts,
-                                  cudaMemcpyHostToDevice),
+            check_cuda(cudaMemcpyAsync(bank->router_bias, bias, sizeof(float) * bank->experts,
+                                       cudaMemcpyHostToDevice, rt->stream),
                        "cudaMemcpy(router bias)");
+            check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(router bias)");
         }
         clear_last_error();
         return NVFP4_STATUS_OK;

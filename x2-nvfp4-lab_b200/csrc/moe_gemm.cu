@@ -46,9 +46,13 @@ struct GemmCfg {
     static constexpr int kStage = kA + kB + kSfa + kSfb;
     static constexpr uint32_t kTx = kA + kB + kSfa;       // bytes tracked by the stage's transaction count
     static constexpr int kColAcc1 = 128;
-    static constexpr int kColSfa = NA * 128;
-    static constexpr int kColSfb = kColSfa + NA * 16;
-    static constexpr int kColsUsed = kColSfb + J * 16;
+    // Scale factors get one tensor-memory region per pipeline stage: PTX
+    // orders tcgen05.cp before later MMAs but not MMAs before a later
+    // tcgen05.cp, so a region is rewritten only after the MMAs that read it
+    // have committed (the producer refills a stage after that commit).
+    static constexpr int kSfCols = NA * 16 + J * 16;        // per stage: SFA then SFB
+    static constexpr int kColSf = NA * 128;
+    static constexpr int kColsUsed = kColSf + S * kSfCols;
     static constexpr uint32_t kTmemCols = kColsUsed <= 256 ? 256u : 512u;
     static constexpr size_t kSmem = 1024 + (size_t)S * kStage + 1024;
     static_assert(kStage % 1024 == 0, "stage must keep 1024-byte tile alignment");
@@ -235,16 +239,15 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t sb = smem_base + (uint32_t)st * Cfg::kStage;
                     const uint32_t sfa = sb + Cfg::kA + Cfg::kB;
                     const uint32_t sfb = sfa + Cfg::kSfa;
+                    const uint32_t tsfa = tmem + Cfg::kColSf + (uint32_t)st * Cfg::kSfCols;
+                    const uint32_t tsfb = tsfa + NA * 16;
 #pragma unroll
                     for (int at = 0; at < 4; ++at) {
-                        tc::cp_sf_atom(tmem + Cfg::kColSfa + 4 * at, tc::smem_desc_sf(sfa + at * 512));
-                        if (NA == 2)
-                            tc::cp_sf_atom(tmem + Cfg::kColSfa + 16 + 4 * at,
-                                           tc::smem_desc_sf(sfa + kSfStage + at * 512));
+                        tc::cp_sf_atom(tsfa + 4 * at, tc::smem_desc_sf(sfa + at * 512));
+                        if (NA == 2) tc::cp_sf_atom(tsfa + 16 + 4 * at, tc::smem_desc_sf(sfa + kSfStage + at * 512));
 #pragma unroll
                         for (int j = 0; j < J; ++j)
-                            tc::cp_sf_atom(tmem + Cfg::kColSfb + 16 * j + 4 * at,
-                                           tc::smem_desc_sf(sfb + j * kSfStage + at * 512));
+                            tc::cp_sf_atom(tsfb + 16 * j + 4 * at, tc::smem_desc_sf(sfb + j * kSfStage + at * 512));
                     }
 #pragma unroll
                     for (int at = 0; at < 4; ++at) {
@@ -252,13 +255,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         for (int j = 0; j < J; ++j) {
                             const uint32_t acc = (ks | at | j) != 0 ? 1u : 0u;
                             const uint64_t bdesc = tc::smem_desc_sw128(sb + Cfg::kA + j * kTileBytes + 32 * at);
-                            tc::mma_mxf4nvf4(tmem, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc,
-                                             tmem + Cfg::kColSfa + 4 * at, tmem + Cfg::kColSfb + 16 * j + 4 * at,
-                                             acc);
+                            tc::mma_mxf4nvf4(tmem, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc, tsfa + 4 * at,
+                                             tsfb + 16 * j + 4 * at, acc);
                             if (NA == 2)
                                 tc::mma_mxf4nvf4(tmem + Cfg::kColAcc1, tc::smem_desc_sw128(sb + kTileBytes + 32 * at),
-                                                 bdesc, idesc, tmem + Cfg::kColSfa + 16 + 4 * at,
-                                                 tmem + Cfg::kColSfb + 16 * j + 4 * at, acc);
+                                                 bdesc, idesc, tsfa + 16 + 4 * at, tsfb + 16 * j + 4 * at, acc);
                         }
                     }
                     tc::commit(empty + st);
