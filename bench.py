@@ -58,6 +58,7 @@ def parse_args():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
+    p.add_argument("--no-prefill", action="store_true", help="skip the prefill legs (configs 2 and 3)")
     return p.parse_args()
 
 
@@ -76,8 +77,9 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """SM clock and throttle reasons of one GPU sampled every 200 ms through
-    NVML (read-only queries) while the timed region runs."""
+    """SM clock and throttle reasons of one GPU sampled every 20 ms through
+    NVML (read-only queries) while the timed region runs (one sample at
+    entry, so a short region still has one)."""
 
     REASONS = {
         "hw_slowdown": 0x8,
@@ -86,8 +88,9 @@ class ClockSampler:
         "sw_power_cap": 0x4,
     }
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, interval: float = 0.02):
         self.index = index
+        self.interval = interval
         self.samples: list[tuple[float, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -116,7 +119,7 @@ class ClockSampler:
                 self.samples.append((float(mhz), int(reasons)))
             except Exception:
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(self.interval)
 
     def __exit__(self, *exc):
         self._stop.set()
@@ -214,6 +217,71 @@ def run_reference(args) -> int:
 
 
 # --------------------------------------------------------------- GPU leg
+
+
+def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: int, skew: bool) -> dict:
+    """BASELINE config 2 (T=4096) / config 3 (T=8192, skewed router) on the
+    resident bank: device time per layer pass (L2 flushed before each pass,
+    outside its events), per-kernel times from the runtime trace, tensor and
+    HBM rates against the algorithmic work of one pass."""
+    import numpy as np
+    import torch
+
+    from vllm_nvfp4_cuda import synthetic
+
+    bias = synthetic.synthetic_router(E, H, seed, skew=True).router_bias.numpy() if skew else None
+    bank.set_router_bias(bias)
+    bank.reserve_prefill(T)
+    pool = [synthetic.synthetic_tokens(T, H, 7000 + 17 * T + i) for i in range(2)]
+    res = synthetic.synthetic_tokens(T, H, 9000 + T)
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for i in range(warmup):
+            flush.zero_()
+            bank.forward(pool[i % 2], residual=res, out=out, stream=stream)
+    stream.synchronize()
+    r = bank.last_routing(T)
+    counts = np.asarray(r.counts)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    rt.set_trace_enabled(True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e6))
+        for i in range(steps):
+            flush.zero_()
+            starts[i].record(stream)
+            bank.forward(pool[i % 2], residual=res, out=out, stream=stream)
+            ends[i].record(stream)
+    stream.synchronize()
+    rt.synchronize()
+    by_op: dict[str, float] = {}
+    for ev in rt.trace_events():
+        by_op[ev.operation] = by_op.get(ev.operation, 0.0) + ev.duration_ns / 1e3 / steps
+    rt.set_trace_enabled(False)
+    if skew:
+        bank.set_router_bias(None)
+    ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+    ms_pass = statistics.median(ms)
+    flops = 9.0 * 6.0 * H * I * T                     # algorithmic: 9 slots x (gate, up, down) x 2 flop/MAC
+    active = int((counts > 0).sum()) + 1
+    hbm = active * 3 * PER_PROJ_BYTES + (E + 1) * H * 2 + 3 * T * H * 2
+    gemm_us = by_op.get("moe_gate_up", 0.0) + by_op.get("moe_down", 0.0)
+    return {
+        "workload": "config3_prefill8192_skewed" if skew else "config2_prefill4096",
+        "tokens": T,
+        "tokens_per_s": round(T / (ms_pass / 1000.0), 1),
+        "ms_per_pass": round(ms_pass, 4),
+        "passes": steps,
+        "kernels_us": {k: round(v, 2) for k, v in by_op.items()},
+        "algorithmic_tflops": round(flops / (ms_pass / 1000.0) / 1e12, 1),
+        "gemm_tflops": round(flops / (gemm_us / 1e6) / 1e12, 1) if gemm_us else None,
+        "fp4_dense_nominal_tflops": 9000.0,
+        "layer_hbm_gbs": round(hbm / (ms_pass / 1000.0) / 1e9, 1),
+        "activation_terms": [4, 3],
+        "max_expert_load": int(counts.max()),
+        "mean_expert_load": round(float(counts.mean()), 1),
+    }
 
 
 def run_ours(args) -> int:
@@ -337,6 +405,11 @@ def run_ours(args) -> int:
     rt.set_trace_enabled(False)
     lat = sorted(a.elapsed_time(b) * 1000.0 for a, b in ev)
 
+    prefill = []
+    if not args.no_prefill:
+        prefill.append(prefill_leg(rt, bank, stream, flush, 4096, args.seed, 10, 3, skew=False))
+        prefill.append(prefill_leg(rt, bank, stream, flush, 8192, args.seed, 10, 3, skew=True))
+
     # End to end through the lab-style C-ABI sequence with host buffers.
     host_x = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
     host_r = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
@@ -427,7 +500,8 @@ def run_ours(args) -> int:
             },
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
-            "gpu_launches": 3 * args.steps,
+            "gpu_launches": 4 * args.steps,
+            "prefill": prefill,
             "clocks": clk,
             "cpu_baseline": cpu,
         }

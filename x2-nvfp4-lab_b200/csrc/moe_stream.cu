@@ -593,11 +593,23 @@ cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *c
     return cudaSuccess;
 }
 
+// Token-group width by the expected tokens per routed expert (T*8 slots over
+// min(E, T*8) experts): one group of 8 columns covers the typical decode
+// batch, and a narrow token area leaves room for more pipeline stages. An
+// expert with more tokens (the shared expert, skewed routing) re-streams its
+// tile once per group, mostly from L2.
+static int tokens_per_expert(int T, int E) {
+    const int slots = T * kTopK;
+    const int experts = E < slots ? E : slots;
+    return (slots + experts - 1) / experts;
+}
+
 cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, int sms, cudaStream_t stream) {
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.I / kGuRows);
-    if (T <= 8) return launch_gate_up_cfg<1, 2, 7>(m, a, items_ub, sms, stream);
-    if (T <= 16) return launch_gate_up_cfg<2, 2, 5>(m, a, items_ub, sms, stream);
+    const int tpe = tokens_per_expert(T, a.E);
+    if (tpe <= 8) return launch_gate_up_cfg<1, 2, 7>(m, a, items_ub, sms, stream);
+    if (tpe <= 16) return launch_gate_up_cfg<2, 2, 5>(m, a, items_ub, sms, stream);
     return launch_gate_up_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
 }
 
@@ -606,9 +618,10 @@ cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cud
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.H / kDnRows);
     cudaError_t err;
-    if (T <= 8)
+    const int tpe = tokens_per_expert(T, a.E);
+    if (tpe <= 8)
         err = launch_down_cfg<1, 2, 6>(m, a, items_ub, sms, stream);
-    else if (T <= 16)
+    else if (tpe <= 16)
         err = launch_down_cfg<2, 2, 4>(m, a, items_ub, sms, stream);
     else
         err = launch_down_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
