@@ -219,14 +219,13 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
         check_cuda(launch_prefill_route(ra, ps, s), "prefill routing kernels");
     });
     rt->profiled_kernel("moe_quantize", stream, [&](cudaStream_t s) {
-        check_cuda(launch_quantize_rows(x, 0, tokens, H, bank->terms_x, ps.xq, ps.xsf, ps.gx, ps.max_tokens, s),
-                   "quantize_rows_kernel(x)");
+        check_cuda(launch_quantize_x_prefill(x, tokens, ps, bank->terms_x, s), "quantize_rows_kernel(x)");
     });
     GemmArgs ga{};
     ga.sfa[0] = bank->sf_atoms[0];
     ga.sfa[1] = bank->sf_atoms[1];
     ga.sfb = ps.xsf;
-    ga.Rb = ps.max_tokens;
+    ga.Rb = ps.max_rows;
     ga.J = bank->terms_x;
     ga.K = H;
     ga.M = I;
@@ -237,17 +236,14 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
     rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
         check_cuda(launch_gemm_gate_up(bank->pmaps, ga, sms, s), "moe_gemm_kernel(gate/up)");
     });
-    const int P = tokens * kSlots;
     rt->profiled_kernel("moe_quantize", stream, [&](cudaStream_t s) {
-        check_cuda(launch_quantize_rows(ps.act, 1, P, I, bank->terms_act, ps.aq, ps.asf, ps.ga,
-                                        ps.max_tokens * kSlots, s),
-                   "quantize_rows_kernel(act)");
+        check_cuda(launch_quantize_act_prefill(ps, bank->terms_act, s), "quantize_rows_kernel(act)");
     });
     GemmArgs gd = ga;
     gd.sfa[0] = bank->sf_atoms[2];
     gd.sfa[1] = bank->sf_atoms[2];
     gd.sfb = ps.asf;
-    gd.Rb = ps.max_tokens * kSlots;
+    gd.Rb = ps.max_rows;
     gd.J = bank->terms_act;
     gd.K = I;
     gd.M = H;

@@ -5,11 +5,10 @@
 // dispatch order keeps an expert's rows together); a weight-row tile is 128
 // rows of that expert's projection(s). Warp roles:
 //   warp 0     producer: per 256-column K stage, TMA tile loads of the weight
-//              rows (128-byte swizzle), one bulk copy of their scale-factor
-//              atoms, four-row TMA gathers of the J activation-term rows, and
-//              4-byte cp.async gathers of the activation scale words straight
-//              into scale-factor atom layout; all complete on the stage's
-//              mbarrier.
+//              rows and of the J activation-term tiles (128 padded slot rows
+//              each; 128-byte swizzle) and bulk copies of the weight and
+//              activation scale-factor atoms (stored in tcgen05 atom layout);
+//              all complete on the stage's mbarrier.
 //   warp 1     MMA issuer: one thread copies the stage's scale atoms into
 //              tensor memory (tcgen05.cp 32x128b.warpx4) and issues
 //              kind::mxf4nvf4 MMAs (M 128, N 128, K 64) into FP32
@@ -17,7 +16,8 @@
 //              the producer and, after the last stage, the accumulator to
 //              the epilogue. Warp 1 also owns the tensor-memory allocation.
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator rows of their
-//              sub-partition, per-column scaling, then
+//              sub-partition (the down GEMM double-buffers its accumulator so
+//              this overlaps the next tile's MMAs), per-column scaling, then
 //              gate/up: act = SiLU(gate) * up as FP16 [slot row][I];
 //              down:    y = coef * acc as FP16 [slot row][H].
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
@@ -44,14 +44,18 @@ struct GemmCfg {
     static constexpr int kSfa = NA * kSfStage;
     static constexpr int kSfb = J * kSfStage;
     static constexpr int kStage = kA + kB + kSfa + kSfb;
-    static constexpr uint32_t kTx = kA + kB + kSfa;       // bytes tracked by the stage's transaction count
+    static constexpr uint32_t kTx = kA + kB + kSfa + kSfb;  // every byte of a stage arrives by TMA / bulk copy
+    // Down (one projection) double-buffers its accumulator so the epilogue
+    // of one tile overlaps the MMAs of the next; gate/up holds two
+    // accumulators (gate, up) in one buffer.
+    static constexpr int kNumAcc = NA == 1 ? 2 : 1;
     static constexpr int kColAcc1 = 128;
     // Scale factors get one tensor-memory region per pipeline stage: PTX
     // orders tcgen05.cp before later MMAs but not MMAs before a later
     // tcgen05.cp, so a region is rewritten only after the MMAs that read it
     // have committed (the producer refills a stage after that commit).
     static constexpr int kSfCols = NA * 16 + J * 16;        // per stage: SFA then SFB
-    static constexpr int kColSf = NA * 128;
+    static constexpr int kColSf = 256;
     static constexpr int kColsUsed = kColSf + S * kSfCols;
     static constexpr uint32_t kTmemCols = kColsUsed <= 256 ? 256u : 512u;
     static constexpr size_t kSmem = 1024 + (size_t)S * kStage + 1024;
@@ -109,9 +113,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint8_t *smem = align1024(smem_raw);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)S * Cfg::kStage);
     uint64_t *empty = full + S;
-    uint64_t *acc_full = empty + S;
-    uint64_t *acc_empty = acc_full + 1;
-    uint64_t *drain = acc_empty + 1;
+    uint64_t *acc_full = empty + S;      // [kNumAcc]
+    uint64_t *acc_empty = acc_full + 2;  // [kNumAcc]
+    uint64_t *drain = acc_empty + 2;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
     float *colscale = reinterpret_cast<float *>(tmem_slot + 4);  // [128]
@@ -121,11 +125,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < S; ++i) {
-            mbar_init(full + i, 1 + 32);  // producer lane 0 (bytes) + one cp.async arrival per producer lane
+            mbar_init(full + i, 1);  // producer lane 0 (arrive + transaction bytes)
             mbar_init(empty + i, 1);
         }
-        mbar_init(acc_full, 1);
-        mbar_init(acc_empty, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + b, 1);
+            mbar_init(acc_empty + b, 1);
+        }
         mbar_init(drain, 1);
         fence_barrier_init();
         prefetch_tensormap(&tm_a0);
@@ -154,17 +160,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
             const TileInfo ti = tile_info(s, tile, mtiles);
-            int grow[4], srow[4];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const int ig = 4 * lane + q, is = lane + 32 * q;
-                const int pg = ti.n0 + (ig < ti.nvalid ? ig : 0);
-                const int ps = ti.n0 + (is < ti.nvalid ? is : 0);
-                grow[q] = MODE == 0 ? s.tok_list[pg] : pg;
-                srow[q] = MODE == 0 ? s.tok_list[ps] : ps;
-            }
             const int arow = ti.e * a.M + ti.mt * kPrefillTileM;
             const size_t sfa_off = (size_t)(arow / kPrefillTileM) * kw * 512;
+            const int sf_blocks = s.max_rows / kPrefillTileN;
             for (int ks = 0; ks < kstages; ++ks, ++it) {
                 const int st = it % S;
                 const uint32_t ph = (it / S) & 1u;
@@ -175,6 +173,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     break;
                 }
                 uint8_t *stage = smem + (size_t)st * Cfg::kStage;
+                uint8_t *sfb = stage + Cfg::kA + Cfg::kB + Cfg::kSfa;
                 if (lane == 0) {
                     mbar_arrive_expect_tx(full + st, Cfg::kTx);
                     tma_load_2d(stage, &tm_a0, full + st, ks * 128, arow);
@@ -184,31 +183,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     if (NA == 2)
                         bulk_g2s(stage + Cfg::kA + Cfg::kB + kSfStage, a.sfa[1] + sfa_off + (size_t)ks * kSfStage,
                                  kSfStage, full + st);
-                }
-                __syncwarp();
 #pragma unroll
-                for (int j = 0; j < J; ++j) {
-                    const int rb = j * a.Rb;
-                    tma_gather4(stage + Cfg::kA + j * kTileBytes + lane * 512, &tm_b, full + st, ks * 128,
-                                rb + grow[0], rb + grow[1], rb + grow[2], rb + grow[3]);
-                }
-                uint8_t *sfb = stage + Cfg::kA + Cfg::kB + Cfg::kSfa;
-#pragma unroll
-                for (int j = 0; j < J; ++j) {
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint32_t *src = a.sfb + ((size_t)j * a.Rb + srow[q]) * kw + ks * 4;
-#pragma unroll
-                        for (int at = 0; at < 4; ++at)
-                            cp_async4(sfb + j * kSfStage + at * 512 + lane * 16 + q * 4, src + at);
+                    for (int j = 0; j < J; ++j) {
+                        // The column tile is one 128-row block of slot rows:
+                        // one TMA box of codes and one bulk copy of scale atoms
+                        // per activation term.
+                        tma_load_2d(stage + Cfg::kA + j * kTileBytes, &tm_b, full + st, ks * 128, j * a.Rb + ti.n0);
+                        bulk_g2s(sfb + j * kSfStage,
+                                 a.sfb + ((size_t)(j * sf_blocks + ti.n0 / kPrefillTileN) * kw + ks * 4) * 512,
+                                 kSfStage, full + st);
                     }
                 }
-                cp_async_arrive_noinc(full + st);
             }
         }
         if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
             // Drain: wait for the copies of the last stages issued.
-            cp_async_wait_all();
             if (lane == 0) {
                 const uint32_t first = it > (uint32_t)S ? it - S : 0u;
                 for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
@@ -222,11 +211,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             uint32_t it = 0, tcount = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tcount) {
-                if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1u, err, kSiteGemmAccEmpty)) {
+                const uint32_t buf = tcount % Cfg::kNumAcc;
+                const uint32_t use = tcount / Cfg::kNumAcc;  // uses of this buffer before this tile
+                if (use > 0 && !mbar_wait(acc_empty + buf, (use - 1) & 1u, err, kSiteGemmAccEmpty)) {
                     ok = false;
                     break;
                 }
                 tc::fence_after_sync();
+                const uint32_t dacc = tmem + buf * 128;
                 for (int ks = 0; ks < kstages; ++ks, ++it) {
                     const int st = it % S;
                     const uint32_t ph = (it / S) & 1u;
@@ -255,7 +247,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         for (int j = 0; j < J; ++j) {
                             const uint32_t acc = (ks | at | j) != 0 ? 1u : 0u;
                             const uint64_t bdesc = tc::smem_desc_sw128(sb + Cfg::kA + j * kTileBytes + 32 * at);
-                            tc::mma_mxf4nvf4(tmem, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc, tsfa + 4 * at,
+                            tc::mma_mxf4nvf4(dacc, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc, tsfa + 4 * at,
                                              tsfb + 16 * j + 4 * at, acc);
                             if (NA == 2)
                                 tc::mma_mxf4nvf4(tmem + Cfg::kColAcc1, tc::smem_desc_sw128(sb + kTileBytes + 32 * at),
@@ -265,7 +257,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     tc::commit(empty + st);
                 }
                 if (!ok) break;
-                tc::commit(acc_full);
+                tc::commit(acc_full + buf);
             }
             // Every MMA of this CTA has completed before tensor memory is freed.
             tc::commit(drain);
@@ -290,7 +282,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             // One thread waits for the accumulator and the decision is
             // shared, so every epilogue warp leaves the loop together.
-            if (et == 0) *acc_ok = mbar_wait(acc_full, tcount & 1u, err, kSiteGemmAccFull) ? 1 : 0;
+            const uint32_t buf = tcount % Cfg::kNumAcc;
+            if (et == 0)
+                *acc_ok = mbar_wait(acc_full + buf, (tcount / Cfg::kNumAcc) & 1u, err, kSiteGemmAccFull) ? 1 : 0;
             named_barrier(1, 128);
             if (!*reinterpret_cast<volatile int *>(acc_ok)) break;
             tc::fence_after_sync();
@@ -317,7 +311,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int c0 = 0; c0 < kPrefillTileN; c0 += 32) {
                     if (c0 >= ti.nvalid) break;
                     uint32_t r[32];
-                    tc::ld_32x32b_x32(lane_base + c0, r);
+                    tc::ld_32x32b_x32(lane_base + buf * 128 + c0, r);
                     tc::wait_ld();
 #pragma unroll
                     for (int n = 0; n < 32; ++n)
@@ -328,7 +322,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             }
             tc::fence_before_sync();
             named_barrier(1, 128);
-            if (et == 0) mbar_arrive(acc_empty);
+            if (et == 0) mbar_arrive(acc_empty + buf);
         }
     }
 

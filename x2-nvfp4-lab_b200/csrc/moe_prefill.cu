@@ -264,11 +264,11 @@ __global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_kernel(Prefi
     }
 }
 
-// Single CTA: per-expert block bases and counts, offsets, the compacted
-// active groups (routed experts with tokens, then the shared expert) and the
-// GEMM column-tile table.
+// Single CTA: per-expert block bases and counts, unpadded offsets (routing
+// ABI), padded group starts, the compacted active groups (routed experts
+// with tokens, then the shared expert) and the GEMM column-tile table.
 __global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int T) {
-    __shared__ int s_cnt[256], s_off[257], s_aidx[256], s_tiles[257], s_tstart[257];
+    __shared__ int s_cnt[256], s_off[257], s_aidx[256], s_tstart[257], s_pst[257];
     __shared__ int s_total[3];
     const int E = s.E;
     const int nb = (T + 63) / 64;
@@ -284,57 +284,66 @@ __global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int
     s_cnt[e] = e < E ? run : 0;
     __syncthreads();
     if (threadIdx.x == 0) {
-        int off = 0, act = 0, tiles = 0;
+        int off = 0, act = 0, tiles = 0, pad = 0;
         for (int i = 0; i < E; ++i) {
             s_off[i] = off;
+            s_pst[i] = pad;
             off += s_cnt[i];
             if (s_cnt[i] > 0) {
                 s_aidx[i] = act++;
                 s_tstart[i] = tiles;
                 tiles += (s_cnt[i] + kPrefillTileN - 1) / kPrefillTileN;
+                pad += (s_cnt[i] + kPrefillTileN - 1) / kPrefillTileN * kPrefillTileN;
             } else {
                 s_aidx[i] = -1;
             }
         }
         s_off[E] = off;
         s_tstart[E] = tiles;  // shared expert's first column tile
+        s_pst[E] = pad;
         tiles += (T + kPrefillTileN - 1) / kPrefillTileN;
+        pad += (T + kPrefillTileN - 1) / kPrefillTileN * kPrefillTileN;
         s_total[0] = act;
         s_total[1] = tiles;
+        s_total[2] = pad;
     }
     __syncthreads();
     const int nrouted = s_total[0];
     if (e < E) {
         s.offsets[e] = s_off[e];
+        s.epstart[e] = s_pst[e];
         const int ai = s_aidx[e];
         if (ai >= 0) {
             s.active_expert[ai] = e;
-            s.tok_start[ai] = s_off[e];
+            s.tok_start[ai] = s_pst[e];
             s.tok_count[ai] = s_cnt[e];
             const int nt = (s_cnt[e] + kPrefillTileN - 1) / kPrefillTileN;
             for (int j = 0; j < nt; ++j) {
                 s.tile_group[s_tstart[e] + j] = ai;
-                s.tile_n0[s_tstart[e] + j] = s_off[e] + j * kPrefillTileN;
+                s.tile_n0[s_tstart[e] + j] = s_pst[e] + j * kPrefillTileN;
             }
         }
     }
     if (threadIdx.x == 0) {
         s.offsets[E] = s_off[E];
+        s.epstart[E] = s_pst[E];
         s.active_expert[nrouted] = E;
-        s.tok_start[nrouted] = T * kTopK;
+        s.tok_start[nrouted] = s_pst[E];
         s.tok_count[nrouted] = T;
         *s.n_active = nrouted + 1;
         *s.n_tiles = s_total[1];
+        *s.rows_used = s_total[2];
     }
     const int st = s_tstart[E], nt = (T + kPrefillTileN - 1) / kPrefillTileN;
     for (int j = threadIdx.x; j < nt; j += blockDim.x) {
         s.tile_group[st + j] = nrouted;
-        s.tile_n0[st + j] = T * kTopK + j * kPrefillTileN;
+        s.tile_n0[st + j] = s_pst[E] + j * kPrefillTileN;
     }
 }
 
-// Thread per (token, slot): position in the expert-grouped order (experts
-// ascending, tokens ascending), and the per-slot-row tables.
+// Thread per (token, slot): rank among the expert's tokens (tokens
+// ascending), giving the unpadded dispatch position (routing ABI) and the
+// padded slot row used by the GEMMs.
 __global__ void prefill_place_kernel(PrefillScratch s, int T, const float *inv_scales) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     const int E = s.E;
@@ -344,16 +353,17 @@ __global__ void prefill_place_kernel(PrefillScratch s, int T, const float *inv_s
         const int e = s.ids[t * kSlots + k];
         const int b = t >> 6;
         const unsigned long long m = s.blk_mask[(size_t)b * E + e];
-        const int pos = s.offsets[e] + s.blk_base[(size_t)b * E + e] + __popcll(m & ((1ull << (t & 63)) - 1ull));
-        s.perm[pos] = i;
-        s.tok_list[pos] = t;
-        s.inv_pos[i] = pos;
-        s.coef[pos] = s.weights[t * kSlots + k] * inv_down[e];
+        const int rank = s.blk_base[(size_t)b * E + e] + __popcll(m & ((1ull << (t & 63)) - 1ull));
+        const int row = s.epstart[e] + rank;
+        s.perm[s.offsets[e] + rank] = i;
+        s.tok_list[row] = t;
+        s.inv_pos[i] = row;
+        s.coef[row] = s.weights[t * kSlots + k] * inv_down[e];
     } else if (i < T * kSlots) {
         const int t = i - T * kTopK;
-        const int pos = T * kTopK + t;
-        s.tok_list[pos] = t;
-        s.coef[pos] = s.weights[t * kSlots + kTopK] * inv_down[E];
+        const int row = s.epstart[E] + t;
+        s.tok_list[row] = t;
+        s.coef[row] = s.weights[t * kSlots + kTopK] * inv_down[E];
     }
 }
 
@@ -385,17 +395,52 @@ __device__ __forceinline__ uint32_t canonical_zero_codes(uint32_t w) {
     return m | (w & (nz << 3));
 }
 
+// Where a quantised row's scale words go.
+//   kWords: compact words [J][rows_stride][cols/64] (the standalone ABI)
+//   kTokenAtoms: row r is token r; its codes and words go to each of the
+//     token's nine padded slot rows (inv_pos, shared row), words in tcgen05
+//     scale-atom layout
+//   kRowAtoms: row r is a padded slot row; words go to its own atoms, and
+//     rows at or past *rows_used are skipped
+enum QuantMode : int { kWords = 0, kTokenAtoms = 1, kRowAtoms = 2 };
+
+struct QuantTargets {
+    uint8_t *codes;           // [J][rows_stride][cols/2]
+    uint32_t *words;          // kWords
+    uint8_t *atoms;           // [J][atom_blocks][cols/64][512]
+    float *g;                 // [rows]
+    int rows_stride;
+    int atom_blocks;
+    const int *inv_pos;       // kTokenAtoms
+    const int *shared_row0;   // kTokenAtoms: padded first row of the shared expert
+    const int *rows_used;     // kRowAtoms
+};
+
+__device__ __forceinline__ size_t atom_offset(int j, int atom_blocks, int words_per_row, int p, int word) {
+    return ((size_t)(j * atom_blocks + p / 128) * words_per_row + word) * 512 + (p % 32) * 16 + ((p % 128) / 32) * 4;
+}
+
 // One warp per row. Lane l quantises the 64-column chunks l, l+32, ...; a
 // chunk holds four 16-column blocks, so each lane writes whole scale words.
 // Per term: s = E4M3_RN((bamax / 6) / g); denom = s * g; code =
 // E2M1_RN(r * RN(1/denom)) (0 when denom is 0); r -= code * denom.
-template <int J>
+template <int J, int MODE>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int src_is_f16, int rows, int cols,
-                                                            uint8_t *codes, uint32_t *sf, float *g_out,
-                                                            int rows_stride) {
+                                                            QuantTargets q) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= rows) return;
+    if (MODE == kRowAtoms && warp >= *q.rows_used) return;
     const int r = warp;
+    uint8_t *codes = q.codes;
+    float *g_out = q.g;
+    const int rows_stride = q.rows_stride;
+    const int wpr = cols / 64;
+    int dst_rows[kSlots];
+    if (MODE == kTokenAtoms) {
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) dst_rows[k] = q.inv_pos[r * kTopK + k];
+        dst_rows[kTopK] = *q.shared_row0 + r;
+    }
     const uint16_t *row = static_cast<const uint16_t *>(src) + (size_t)r * cols;
     const int chunks = cols / 64;
     auto load_chunk = [&](int ch, float (&v)[64]) {
@@ -469,10 +514,27 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
                 }
             }
             const size_t prow = (size_t)j * rows_stride + r;
-            uint4 *dst = reinterpret_cast<uint4 *>(codes + prow * (cols / 2) + ch * 32);
-            dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-            dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
-            sf[prow * (cols / 64) + ch] = sword;
+            if (MODE != kTokenAtoms) {
+                uint4 *dst = reinterpret_cast<uint4 *>(codes + prow * (cols / 2) + ch * 32);
+                dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+                dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+            }
+            if (MODE == kWords) {
+                q.words[prow * wpr + ch] = sword;
+            } else if (MODE == kRowAtoms) {
+                *reinterpret_cast<uint32_t *>(q.atoms + atom_offset(j, q.atom_blocks, wpr, r, ch)) = sword;
+            } else {
+                // The token's codes and scales go to each of its nine slot rows.
+#pragma unroll
+                for (int k = 0; k < kSlots; ++k) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(
+                        codes + ((size_t)j * rows_stride + dst_rows[k]) * (cols / 2) + ch * 32);
+                    dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
+                    dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
+                    *reinterpret_cast<uint32_t *>(q.atoms + atom_offset(j, q.atom_blocks, wpr, dst_rows[k], ch)) =
+                        sword;
+                }
+            }
         }
     }
 }
@@ -503,7 +565,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillScratch s, 
     };
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) add_row(s.inv_pos[t * kTopK + k]);
-    add_row(T * kTopK + t);
+    add_row(s.epstart[s.E] + t);
     uint32_t o[4];
     if (residual) {
         const uint4 u = __ldg(reinterpret_cast<const uint4 *>(residual + (size_t)t * H + h));
@@ -533,10 +595,15 @@ __global__ void scale_atoms_kernel(uint8_t *atoms, const uint8_t *scales, size_t
 
 }  // namespace
 
+static int prefill_rows(int T, int E) {
+    const long long rows = (long long)T * kSlots + (long long)(E + 1) * kPrefillTileN;
+    return (int)((rows + kPrefillTileN - 1) / kPrefillTileN * kPrefillTileN);
+}
+
 size_t prefill_scratch_bytes(int T, int E, int H, int I, int Jx, int Ja) {
     PrefillScratch s{};
     prefill_scratch_carve(s, nullptr, T, E, H, I, Jx, Ja);
-    return reinterpret_cast<size_t>(s.ypart) + (size_t)T * kSlots * H * 2 + 256;
+    return reinterpret_cast<size_t>(s.ypart) + (size_t)s.max_rows * H * 2 + 1024;
 }
 
 void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, int I, int Jx, int Ja) {
@@ -546,13 +613,15 @@ void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, i
         off += (bytes + 1023) & ~size_t(1023);
         return static_cast<uint8_t *>(base) + o;
     };
-    const size_t Tz = (size_t)T, P = (size_t)T * kSlots;
+    const size_t Tz = (size_t)T;
     const int R = E + 1, Rp = (R + 63) / 64 * 64, nb = (T + 63) / 64;
+    const size_t P = (size_t)prefill_rows(T, E);
     s.max_tokens = T;
+    s.max_rows = (int)P;
     s.E = E;
     s.H = H;
     s.I = I;
-    s.max_tiles = (int)(P / kPrefillTileN) + R + 1;
+    s.max_tiles = (int)(P / kPrefillTileN);
     s.approx = reinterpret_cast<float *>(take(Tz * Rp * 4));
     s.ids = reinterpret_cast<int *>(take(Tz * kSlots * 4));
     s.weights = reinterpret_cast<float *>(take(Tz * kSlots * 4));
@@ -560,6 +629,8 @@ void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, i
     s.blk_base = reinterpret_cast<int *>(take((size_t)nb * E * 4));
     s.counts = reinterpret_cast<int *>(take((size_t)E * 4));
     s.offsets = reinterpret_cast<int *>(take((size_t)R * 4));
+    s.epstart = reinterpret_cast<int *>(take((size_t)R * 4));
+    s.rows_used = reinterpret_cast<int *>(take(4));
     s.n_active = reinterpret_cast<int *>(take(4));
     s.active_expert = reinterpret_cast<int *>(take((size_t)R * 4));
     s.tok_start = reinterpret_cast<int *>(take((size_t)R * 4));
@@ -571,12 +642,12 @@ void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, i
     s.inv_pos = reinterpret_cast<int *>(take(Tz * kTopK * 4));
     s.tok_list = reinterpret_cast<int *>(take(P * 4));
     s.coef = reinterpret_cast<float *>(take(P * 4));
-    s.xq = take((size_t)Jx * Tz * H / 2);
-    s.xsf = reinterpret_cast<uint32_t *>(take((size_t)Jx * Tz * (H / 64) * 4));
+    s.xq = take((size_t)Jx * P * H / 2);
+    s.xsf = take((size_t)Jx * P * (H / 16));
     s.gx = reinterpret_cast<float *>(take(Tz * 4));
     s.act = reinterpret_cast<__half *>(take(P * I * 2));
     s.aq = take((size_t)Ja * P * I / 2);
-    s.asf = reinterpret_cast<uint32_t *>(take((size_t)Ja * P * (I / 64) * 4));
+    s.asf = take((size_t)Ja * P * (I / 16));
     s.ga = reinterpret_cast<float *>(take(P * 4));
     s.ypart = reinterpret_cast<__half *>(take(P * H * 2));
 }
@@ -594,10 +665,11 @@ cudaError_t make_prefill_weight_maps(PrefillMaps &m, uint8_t *const packed[3], i
 }
 
 cudaError_t make_prefill_act_maps(PrefillMaps &m, const PrefillScratch &s, int Jx, int Ja) {
-    const uint64_t T = s.max_tokens, P = (uint64_t)s.max_tokens * kSlots;
-    cudaError_t err = make_tensor_map_u8(&m.xq, s.xq, s.H / 2, s.H / 2, Jx * T, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+    const uint64_t P = (uint64_t)s.max_rows;
+    cudaError_t err = make_tensor_map_u8(&m.xq, s.xq, s.H / 2, s.H / 2, Jx * P, 128, kPrefillTileN,
+                                         CU_TENSOR_MAP_SWIZZLE_128B);
     if (err != cudaSuccess) return err;
-    return make_tensor_map_u8(&m.aq, s.aq, s.I / 2, s.I / 2, Ja * P, 128, 1, CU_TENSOR_MAP_SWIZZLE_128B);
+    return make_tensor_map_u8(&m.aq, s.aq, s.I / 2, s.I / 2, Ja * P, 128, kPrefillTileN, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pitch, int rows, int k16, int row0,
@@ -628,18 +700,52 @@ cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch
     return cudaGetLastError();
 }
 
-cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
-                                 uint32_t *sf, float *g, int rows_stride, cudaStream_t stream) {
+template <int MODE>
+static cudaError_t launch_quantize_mode(const void *src, int src_is_f16, int rows, int cols, int terms,
+                                        const QuantTargets &q, cudaStream_t stream) {
     if (cols % 64 != 0 || rows <= 0) return cudaErrorInvalidValue;
     const int grid = (rows + 7) / 8;
     switch (terms) {
-        case 1: quantize_rows_kernel<1><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
-        case 2: quantize_rows_kernel<2><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
-        case 3: quantize_rows_kernel<3><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
-        case 4: quantize_rows_kernel<4><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, codes, sf, g, rows_stride); break;
+        case 1: quantize_rows_kernel<1, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
+        case 2: quantize_rows_kernel<2, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
+        case 3: quantize_rows_kernel<3, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
+        case 4: quantize_rows_kernel<4, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
+                                 uint32_t *sf, float *g, int rows_stride, cudaStream_t stream) {
+    QuantTargets q{};
+    q.codes = codes;
+    q.words = sf;
+    q.g = g;
+    q.rows_stride = rows_stride;
+    return launch_quantize_mode<kWords>(src, src_is_f16, rows, cols, terms, q, stream);
+}
+
+cudaError_t launch_quantize_x_prefill(const void *x, int T, const PrefillScratch &s, int terms, cudaStream_t stream) {
+    QuantTargets q{};
+    q.codes = s.xq;
+    q.atoms = s.xsf;
+    q.g = s.gx;
+    q.rows_stride = s.max_rows;
+    q.atom_blocks = s.max_rows / kPrefillTileN;
+    q.inv_pos = s.inv_pos;
+    q.shared_row0 = s.epstart + s.E;
+    return launch_quantize_mode<kTokenAtoms>(x, 0, T, s.H, terms, q, stream);
+}
+
+cudaError_t launch_quantize_act_prefill(const PrefillScratch &s, int terms, cudaStream_t stream) {
+    QuantTargets q{};
+    q.codes = s.aq;
+    q.atoms = s.asf;
+    q.g = s.ga;
+    q.rows_stride = s.max_rows;
+    q.atom_blocks = s.max_rows / kPrefillTileN;
+    q.rows_used = s.rows_used;
+    return launch_quantize_mode<kRowAtoms>(s.act, 1, s.max_rows, s.I, terms, q, stream);
 }
 
 cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out,

@@ -34,9 +34,16 @@ constexpr int kPrefillTileN = 128;   // slot rows per GEMM column tile
 constexpr int kPrefillTileM = 128;   // weight rows per GEMM tile
 constexpr int kMaxTerms = 4;
 
+// Slot rows of the prefill path are "padded positions": each active expert
+// group (routed experts with tokens, then the shared expert) starts on a
+// multiple of 128 rows, so every GEMM column tile is one 128-row block and
+// its activation scale factors can be stored in tcgen05 atom layout. The
+// routing ABI's dispatch permutation stays unpadded.
+//
 // Device scratch of the prefill path for up to `max_tokens` tokens.
 struct PrefillScratch {
     int max_tokens;
+    int max_rows;            // padded slot-row capacity: max_tokens*9 + (E+1)*128, rounded to 128
     int E, H, I;
     float *approx;           // [T][Rp] approximate logits, Rp = round_up(E+1, 64)
     int *ids;                // [T][9]
@@ -44,26 +51,28 @@ struct PrefillScratch {
     unsigned long long *blk_mask;  // [nb][E] token bits per 64-token block
     int *blk_base;           // [nb][E]
     int *counts;             // [E]
-    int *offsets;            // [E+1]
+    int *offsets;            // [E+1] unpadded (routing ABI)
+    int *epstart;            // [E+1] padded first row of each expert (index E = shared expert)
+    int *rows_used;          // [1] padded rows in use
     int *n_active;           // [1]
     int *active_expert;      // [E+1]
-    int *tok_start;          // [E+1]
+    int *tok_start;          // [E+1] padded first row of each active group
     int *tok_count;          // [E+1]
     int *n_tiles;            // [1] column tiles
     int *tile_group;         // [max tiles] active-group index of a column tile
     int *tile_n0;            // [max tiles] first slot row of a column tile
-    int *perm;               // [T*8]
-    int *inv_pos;            // [T*8]
-    int *tok_list;           // [T*9] token of each slot row
-    float *coef;             // [T*9] routing weight * inverse down global scale
-    uint8_t *xq;             // [Jx][T][H/2]
-    uint32_t *xsf;           // [Jx][T][H/64]
+    int *perm;               // [T*8] unpadded dispatch permutation (routing ABI)
+    int *inv_pos;            // [T*8] padded row of each (token, slot)
+    int *tok_list;           // [rows] token of each padded slot row
+    float *coef;             // [rows] routing weight * inverse down global scale
+    uint8_t *xq;             // [Jx][rows][H/2] codes of each slot row's token
+    uint8_t *xsf;            // [Jx][rows/128][H/64][512] scale atoms of the slot rows
     float *gx;               // [T]
-    __half *act;             // [T*9][I]
-    uint8_t *aq;             // [Ja][T*9][I/2]
-    uint32_t *asf;           // [Ja][T*9][I/64]
-    float *ga;               // [T*9]
-    __half *ypart;           // [T*9][H]
+    __half *act;             // [rows][I]
+    uint8_t *aq;             // [Ja][rows][I/2]
+    uint8_t *asf;            // [Ja][rows/128][I/64][512] scale atoms
+    float *ga;               // [rows]
+    __half *ypart;           // [rows][H]
     int *error;              // device error word (shared with the decode scratch)
     int *host_error;         // host-mapped error word or nullptr
     int max_tiles;
@@ -73,8 +82,8 @@ struct PrefillScratch {
 // weights (128-row boxes).
 struct PrefillMaps {
     CUtensorMap w[3];        // packed weights, box {128 B, 128 rows}, 128-byte swizzle
-    CUtensorMap xq;          // [Jx*T][H/2], box {128 B, 1 row}
-    CUtensorMap aq;          // [Ja*T*9][I/2], box {128 B, 1 row}
+    CUtensorMap xq;          // [Jx*rows][H/2], box {128 B, 128 rows}
+    CUtensorMap aq;          // [Ja*rows][I/2], box {128 B, 128 rows}
 };
 
 struct PrefillRouteArgs {
@@ -88,8 +97,8 @@ struct PrefillRouteArgs {
 
 struct GemmArgs {
     const uint8_t *sfa[2];    // weight scale atoms of the A projections
-    const uint32_t *sfb;      // [J][Rb][K/64]
-    int Rb;                   // rows per term of the B tensors
+    const uint8_t *sfb;       // [J][rows/128][K/64][512] scale atoms of the slot rows
+    int Rb;                   // rows per term of the B tensors (the padded slot-row capacity)
     int J;                    // activation terms
     int K;                    // reduction length
     int M;                    // weight rows per expert
@@ -113,6 +122,11 @@ cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pit
 cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
                                  uint32_t *sf, float *g, int rows_stride, cudaStream_t stream);
+// Prefill forms: token rows of x (codes by token, scale atoms scattered to
+// each token's nine slot rows) and slot rows of the activations (codes and
+// atoms by slot row; rows past rows_used are skipped).
+cudaError_t launch_quantize_x_prefill(const void *x, int T, const PrefillScratch &s, int terms, cudaStream_t stream);
+cudaError_t launch_quantize_act_prefill(const PrefillScratch &s, int terms, cudaStream_t stream);
 cudaError_t launch_gemm_gate_up(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream);
 cudaError_t launch_gemm_down(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream);
 cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out,

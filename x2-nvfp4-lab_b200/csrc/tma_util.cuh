@@ -96,18 +96,6 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, u
         : "memory");
 }
 
-// Four-row gather: rows r0..r3 of a 2D tensor map whose box is one row of
-// `box bytes`, starting at column x, land in consecutive box-sized slots at
-// `dst` (the tensor map's swizzle applies per destination address).
-__device__ __forceinline__ void tma_gather4(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int r0, int r1,
-                                            int r2, int r3) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-        " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
-        ::"r"(smem_u32(dst)), "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3)
-        : "memory");
-}
-
 // Contiguous global -> shared bulk copy (both addresses 16-byte aligned,
 // bytes a multiple of 16), completing on `bar`.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
