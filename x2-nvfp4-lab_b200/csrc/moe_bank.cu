@@ -215,10 +215,16 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
     ra.T = tokens;
     ra.E = E;
     ra.H = H;
-    rt->profiled_kernel("moe_route", stream, [&](cudaStream_t s) {
-        check_cuda(launch_prefill_route(ra, ps, s), "prefill routing kernels");
+    rt->profiled_kernel("moe_route_logits", stream, [&](cudaStream_t s) {
+        check_cuda(launch_prefill_route(ra, ps, 0, s), "prefill_logits_kernel");
     });
-    rt->profiled_kernel("moe_quantize", stream, [&](cudaStream_t s) {
+    rt->profiled_kernel("moe_route_select", stream, [&](cudaStream_t s) {
+        check_cuda(launch_prefill_route(ra, ps, 1, s), "prefill_select_kernel");
+    });
+    rt->profiled_kernel("moe_dispatch", stream, [&](cudaStream_t s) {
+        check_cuda(launch_prefill_route(ra, ps, 2, s), "prefill dispatch kernels");
+    });
+    rt->profiled_kernel("moe_quantize_x", stream, [&](cudaStream_t s) {
         check_cuda(launch_quantize_x_prefill(x, tokens, ps, bank->terms_x, s), "quantize_rows_kernel(x)");
     });
     GemmArgs ga{};
@@ -236,7 +242,7 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
     rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
         check_cuda(launch_gemm_gate_up(bank->pmaps, ga, sms, s), "moe_gemm_kernel(gate/up)");
     });
-    rt->profiled_kernel("moe_quantize", stream, [&](cudaStream_t s) {
+    rt->profiled_kernel("moe_quantize_act", stream, [&](cudaStream_t s) {
         check_cuda(launch_quantize_act_prefill(ps, bank->terms_act, s), "quantize_rows_kernel(act)");
     });
     GemmArgs gd = ga;

@@ -12,12 +12,14 @@ namespace {
 constexpr int kLogitsTile = 64;       // tokens x router rows per CTA of the logits kernel
 constexpr int kSelectWarps = 8;       // tokens per CTA of the select kernel
 constexpr int kMaxCandidates = 64;
-// Margin of the approximate logits: |approx - exact| <= kMarginRel * |w| * |x|.
-// Both are FP32 sums of the same exactly representable BF16 x BF16 products;
-// an FP32 sum of K terms is within K * 2^-24 * sum|p| of the exact sum, and
-// sum|p| <= |w| * |x|, so 2^-8 covers K up to 2^14 with a wide reserve for
-// the tensor core's accumulation order.
-constexpr float kMarginRel = 1.0f / 256.0f;
+// Margin of the approximate logits. Both the tensor-core logit and the exact
+// one are FP32 sums of the same exactly representable BF16 x BF16 products
+// p_k; any FP32 summation order of H terms, even with truncating adds, stays
+// within 2 * H * 2^-24 * sum|p| of the true sum, and sum|p| <= |w| * |x|.
+// delta = H * 2^-21 * |w| * |x| is twice the resulting bound on
+// |approx - exact|, so every expert of the exact top-8 has an approximate
+// logit >= (approximate 8th largest) - 2 * delta.
+constexpr float kMarginPerColumn = 1.0f / 2097152.0f;  // 2^-21
 
 __device__ __forceinline__ unsigned float_order_key(float v) {
     v = (v == 0.0f) ? 0.0f : v;
@@ -37,50 +39,68 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 // ------------------------------------------------------ approximate logits
 //
 // approx[t][e] = sum_k x[t,k] * W[e,k] with BF16 tensor-core MMAs (FP32
-// accumulation, order unspecified). Warp w of a CTA covers 16 tokens x 64
-// router rows; lane (g, c) loads columns [16c, 16c+16) of each 64-column
-// chunk for its rows, and the four k16 steps of the chunk map the MMA's
-// k-slots {2c, 2c+1, 2c+8, 2c+9} to columns 16c + 4i + {0, 1, 2, 3}, the
-// same mapping on both operands.
+// accumulation, order unspecified). A CTA covers 64 tokens x 64 router rows;
+// 64-column chunks of both are staged in shared memory (cp.async, double
+// buffered, rows padded to 144 bytes so fragment loads are conflict-free).
+// Warp w computes tokens 16w..16w+15 against all 64 rows; lane (g, c) reads
+// columns [16c, 16c+16) of its rows, and the four k16 steps of a chunk map
+// the MMA's k-slots {2c, 2c+1, 2c+8, 2c+9} to columns 16c + 4i + {0,1,2,3},
+// the same mapping on both operands.
+constexpr int kLogitsPitch = 144;
+
 __global__ void __launch_bounds__(128) prefill_logits_kernel(PrefillRouteArgs a, float *approx, int Rp) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ __align__(16) uint8_t sx[2][kLogitsTile * kLogitsPitch];
+    __shared__ __align__(16) uint8_t sw[2][kLogitsTile * kLogitsPitch];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, c = lane & 3;
     const int R = a.E + 1, H = a.H;
-    const int t0 = blockIdx.x * kLogitsTile + warp * 16;
-    const int e0 = blockIdx.y * kLogitsTile;
-    const int ta = min(t0 + g, a.T - 1), tb = min(t0 + g + 8, a.T - 1);
-    const uint16_t *xa = a.x + (size_t)ta * H + 16 * c;
-    const uint16_t *xb = a.x + (size_t)tb * H + 16 * c;
-    const uint16_t *wr[8];
-#pragma unroll
-    for (int n = 0; n < 8; ++n) wr[n] = a.router + (size_t)min(e0 + 8 * n + g, R - 1) * H + 16 * c;
+    const int t0 = blockIdx.x * kLogitsTile, e0 = blockIdx.y * kLogitsTile;
+    const int chunks = H / 64;
+    auto load = [&](int buf, int k) {
+        for (int i = tid; i < kLogitsTile * 8; i += 128) {
+            const int r = i >> 3, u = i & 7;
+            cp_async16(sx[buf] + r * kLogitsPitch + u * 16, a.x + (size_t)min(t0 + r, a.T - 1) * H + k + u * 8);
+            cp_async16(sw[buf] + r * kLogitsPitch + u * 16, a.router + (size_t)min(e0 + r, R - 1) * H + k + u * 8);
+        }
+        cp_async_commit();
+    };
     float acc[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n)
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[n][r] = 0.0f;
-    for (int k = 0; k < H; k += 64) {
-        const uint4 xa0 = __ldg(reinterpret_cast<const uint4 *>(xa + k));
-        const uint4 xa1 = __ldg(reinterpret_cast<const uint4 *>(xa + k + 8));
-        const uint4 xb0 = __ldg(reinterpret_cast<const uint4 *>(xb + k));
-        const uint4 xb1 = __ldg(reinterpret_cast<const uint4 *>(xb + k + 8));
+    load(0, 0);
+    for (int kc = 0; kc < chunks; ++kc) {
+        if (kc + 1 < chunks) {
+            load((kc + 1) & 1, (kc + 1) * 64);
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
+        }
+        __syncthreads();
+        const uint8_t *bx = sx[kc & 1], *bw = sw[kc & 1];
+        const uint4 xa0 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g) * kLogitsPitch + 32 * c);
+        const uint4 xa1 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g) * kLogitsPitch + 32 * c + 16);
+        const uint4 xb0 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g + 8) * kLogitsPitch + 32 * c);
+        const uint4 xb1 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g + 8) * kLogitsPitch + 32 * c + 16);
         const uint32_t A[8] = {xa0.x, xa0.y, xa0.z, xa0.w, xa1.x, xa1.y, xa1.z, xa1.w};
         const uint32_t B[8] = {xb0.x, xb0.y, xb0.z, xb0.w, xb1.x, xb1.y, xb1.z, xb1.w};
 #pragma unroll
         for (int n = 0; n < 8; ++n) {
-            const uint4 w0 = __ldg(reinterpret_cast<const uint4 *>(wr[n] + k));
-            const uint4 w1 = __ldg(reinterpret_cast<const uint4 *>(wr[n] + k + 8));
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(bw + (8 * n + g) * kLogitsPitch + 32 * c);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(bw + (8 * n + g) * kLogitsPitch + 32 * c + 16);
             const uint32_t W[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
             for (int i = 0; i < 4; ++i)
                 mma_bf16_16816(acc[n], A[2 * i], B[2 * i], A[2 * i + 1], B[2 * i + 1], W[2 * i], W[2 * i + 1]);
         }
+        __syncthreads();
     }
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
 #pragma unroll
         for (int r = 0; r < 4; ++r) {
-            const int t = t0 + g + (r >= 2 ? 8 : 0);
+            const int t = t0 + 16 * warp + g + (r >= 2 ? 8 : 0);
             const int e = e0 + 8 * n + 2 * c + (r & 1);
             if (t < a.T && e < R) approx[(size_t)t * Rp + e] = acc[n][r];
         }
@@ -103,6 +123,31 @@ __device__ __forceinline__ float exact_logit(const uint16_t *w, const uint16_t *
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) acc = __fadd_rn(acc, __shfl_xor_sync(0xffffffffu, acc, off));
     return acc;
+}
+
+// Four exact logits at once (independent chains, identical per-row order).
+__device__ __forceinline__ void exact_logit4(const uint16_t *router, const int (&rows)[4], const uint16_t *x, int H,
+                                             int lane, float (&out)[4]) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    for (int k = lane * 4; k < H; k += 128) {
+        const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(x + k));
+        const float x0 = bf16_bits_to_f32(xv.x & 0xFFFFu), x1 = bf16_bits_to_f32(xv.x >> 16);
+        const float x2 = bf16_bits_to_f32(xv.y & 0xFFFFu), x3 = bf16_bits_to_f32(xv.y >> 16);
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+            const uint2 wv = __ldg(reinterpret_cast<const uint2 *>(router + (size_t)rows[r] * H + k));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv.x & 0xFFFFu), x0));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv.x >> 16), x1));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv.y & 0xFFFFu), x2));
+            acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv.y >> 16), x3));
+        }
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], off));
+        out[r] = acc[r];
+    }
 }
 
 // One warp per token: approximate top-8 boundary, exact logits of every
@@ -162,7 +207,7 @@ __global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_kernel(Prefi
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-    const float delta = kMarginRel * a.wnorm_max * sqrtf(ss) * 1.0001f + 1e-30f;
+    const float delta = kMarginPerColumn * (float)H * a.wnorm_max * sqrtf(ss) * 1.0001f + 1e-30f;
     const float thresh = a8 - 2.0f * delta;
 
     // Candidate list (expert ids ascending within each lane's stride).
@@ -192,11 +237,22 @@ __global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_kernel(Prefi
         top_i[k] = 0x7fffffff;
     }
     if (!overflow) {
-        for (int i = 0; i < n; ++i) {
-            const int e = s_cand[warp][i];
-            float val = exact_logit(a.router + (size_t)e * H, x, H, lane);
-            if (a.bias) val = __fadd_rn(val, a.bias[e]);
-            if (lane == 0) s_val[warp][i] = val;
+        // Candidates four at a time; the shared-gate row rides along in the
+        // first group's spare slot when there is one.
+        for (int i0 = 0; i0 < n; i0 += 4) {
+            int rows[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) rows[r] = i0 + r < n ? s_cand[warp][i0 + r] : E;
+            float val[4];
+            exact_logit4(a.router, rows, x, H, lane, val);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                if (i0 + r < n) {
+                    float v2 = val[r];
+                    if (a.bias) v2 = __fadd_rn(v2, a.bias[rows[r]]);
+                    if (lane == 0) s_val[warp][i0 + r] = v2;
+                }
+            }
         }
         __syncwarp();
         // Top-8 of the candidates: lane holds candidates lane and lane+32.
@@ -260,84 +316,104 @@ __global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_kernel(Prefi
     }
     if (lane < kTopK) {
         const int e = top_i[lane];
-        atomicOr(&s.blk_mask[(size_t)(t >> 6) * E + e], 1ull << (t & 63));
+        atomicOr(&s.blk_mask[(size_t)e * s.mask_stride + (t >> 6)], 1ull << (t & 63));
     }
 }
 
-// Single CTA: per-expert block bases and counts, unpadded offsets (routing
-// ABI), padded group starts, the compacted active groups (routed experts
-// with tokens, then the shared expert) and the GEMM column-tile table.
+// Exclusive prefix sum over the 256 threads of a CTA; *total gets the sum.
+__device__ __forceinline__ int block_excl_scan256(int v, int *warp_sums, int *total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, inc, off);
+        if (lane >= off) inc += o;
+    }
+    if (lane == 31) warp_sums[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+        const int w = lane < 8 ? warp_sums[lane] : 0;
+        int winc = w;
+#pragma unroll
+        for (int off = 1; off < 8; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, winc, off);
+            if (lane >= off) winc += o;
+        }
+        if (lane < 8) warp_sums[8 + lane] = winc - w;
+        if (lane == 7) warp_sums[16] = winc;
+    }
+    __syncthreads();
+    const int ex = warp_sums[8 + warp] + inc - v;
+    *total = warp_sums[16];
+    __syncthreads();
+    return ex;
+}
+
+// One CTA per routed expert: rank bases of its 64-token blocks (prefix sum
+// of the block masks' popcounts) and its token count. The last CTA to finish
+// then builds the cross-expert tables: unpadded offsets (routing ABI),
+// padded group starts, the compacted active groups (routed experts with
+// tokens, then the shared expert) and the GEMM column-tile table.
 __global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int T) {
-    __shared__ int s_cnt[256], s_off[257], s_aidx[256], s_tstart[257], s_pst[257];
-    __shared__ int s_total[3];
+    __shared__ int warp_sums[17];
+    __shared__ int s_last;
     const int E = s.E;
     const int nb = (T + 63) / 64;
-    const int e = threadIdx.x;
-    int run = 0;
-    if (e < E) {
-        for (int b = 0; b < nb; ++b) {
-            s.blk_base[(size_t)b * E + e] = run;
-            run += __popcll(s.blk_mask[(size_t)b * E + e]);
-        }
-        s.counts[e] = run;
+    const int e = blockIdx.x;
+    int total = 0;
+    for (int b0 = 0; b0 < nb; b0 += 256) {
+        const int b = b0 + threadIdx.x;
+        const int c = b < nb ? __popcll(s.blk_mask[(size_t)e * s.mask_stride + b]) : 0;
+        int chunk = 0;
+        const int ex = block_excl_scan256(c, warp_sums, &chunk);
+        if (b < nb) s.blk_base[(size_t)e * s.mask_stride + b] = total + ex;
+        total += chunk;
     }
-    s_cnt[e] = e < E ? run : 0;
-    __syncthreads();
     if (threadIdx.x == 0) {
-        int off = 0, act = 0, tiles = 0, pad = 0;
-        for (int i = 0; i < E; ++i) {
-            s_off[i] = off;
-            s_pst[i] = pad;
-            off += s_cnt[i];
-            if (s_cnt[i] > 0) {
-                s_aidx[i] = act++;
-                s_tstart[i] = tiles;
-                tiles += (s_cnt[i] + kPrefillTileN - 1) / kPrefillTileN;
-                pad += (s_cnt[i] + kPrefillTileN - 1) / kPrefillTileN * kPrefillTileN;
-            } else {
-                s_aidx[i] = -1;
-            }
-        }
-        s_off[E] = off;
-        s_tstart[E] = tiles;  // shared expert's first column tile
-        s_pst[E] = pad;
-        tiles += (T + kPrefillTileN - 1) / kPrefillTileN;
-        pad += (T + kPrefillTileN - 1) / kPrefillTileN * kPrefillTileN;
-        s_total[0] = act;
-        s_total[1] = tiles;
-        s_total[2] = pad;
+        s.counts[e] = total;
+        __threadfence();
+        s_last = atomicAdd(s.ticket, 1u) == gridDim.x - 1;
     }
     __syncthreads();
-    const int nrouted = s_total[0];
-    if (e < E) {
-        s.offsets[e] = s_off[e];
-        s.epstart[e] = s_pst[e];
-        const int ai = s_aidx[e];
-        if (ai >= 0) {
-            s.active_expert[ai] = e;
-            s.tok_start[ai] = s_pst[e];
-            s.tok_count[ai] = s_cnt[e];
-            const int nt = (s_cnt[e] + kPrefillTileN - 1) / kPrefillTileN;
-            for (int j = 0; j < nt; ++j) {
-                s.tile_group[s_tstart[e] + j] = ai;
-                s.tile_n0[s_tstart[e] + j] = s_pst[e] + j * kPrefillTileN;
+    if (!s_last) return;
+    __threadfence();
+
+    const int i = threadIdx.x;
+    const int cnt = i < E ? __ldcg(s.counts + i) : 0;
+    const int ntile = (cnt + kPrefillTileN - 1) / kPrefillTileN;
+    int n_off = 0, n_act = 0, n_tiles = 0, n_pad = 0;
+    const int off = block_excl_scan256(cnt, warp_sums, &n_off);
+    const int ai = block_excl_scan256(cnt > 0 ? 1 : 0, warp_sums, &n_act);
+    const int tile0 = block_excl_scan256(ntile, warp_sums, &n_tiles);
+    const int pst = block_excl_scan256(ntile * kPrefillTileN, warp_sums, &n_pad);
+    if (i < E) {
+        s.offsets[i] = off;
+        s.epstart[i] = pst;
+        if (cnt > 0) {
+            s.active_expert[ai] = i;
+            s.tok_start[ai] = pst;
+            s.tok_count[ai] = cnt;
+            for (int j = 0; j < ntile; ++j) {
+                s.tile_group[tile0 + j] = ai;
+                s.tile_n0[tile0 + j] = pst + j * kPrefillTileN;
             }
         }
     }
-    if (threadIdx.x == 0) {
-        s.offsets[E] = s_off[E];
-        s.epstart[E] = s_pst[E];
-        s.active_expert[nrouted] = E;
-        s.tok_start[nrouted] = s_pst[E];
-        s.tok_count[nrouted] = T;
-        *s.n_active = nrouted + 1;
-        *s.n_tiles = s_total[1];
-        *s.rows_used = s_total[2];
+    const int shared_tiles = (T + kPrefillTileN - 1) / kPrefillTileN;
+    for (int j = i; j < shared_tiles; j += blockDim.x) {
+        s.tile_group[n_tiles + j] = n_act;
+        s.tile_n0[n_tiles + j] = n_pad + j * kPrefillTileN;
     }
-    const int st = s_tstart[E], nt = (T + kPrefillTileN - 1) / kPrefillTileN;
-    for (int j = threadIdx.x; j < nt; j += blockDim.x) {
-        s.tile_group[st + j] = nrouted;
-        s.tile_n0[st + j] = s_pst[E] + j * kPrefillTileN;
+    if (i == 0) {
+        s.offsets[E] = n_off;
+        s.epstart[E] = n_pad;
+        s.active_expert[n_act] = E;
+        s.tok_start[n_act] = n_pad;
+        s.tok_count[n_act] = T;
+        *s.n_active = n_act + 1;
+        *s.n_tiles = n_tiles + shared_tiles;
+        *s.rows_used = n_pad + shared_tiles * kPrefillTileN;
+        *s.ticket = 0u;
     }
 }
 
@@ -352,8 +428,8 @@ __global__ void prefill_place_kernel(PrefillScratch s, int T, const float *inv_s
         const int t = i / kTopK, k = i - t * kTopK;
         const int e = s.ids[t * kSlots + k];
         const int b = t >> 6;
-        const unsigned long long m = s.blk_mask[(size_t)b * E + e];
-        const int rank = s.blk_base[(size_t)b * E + e] + __popcll(m & ((1ull << (t & 63)) - 1ull));
+        const unsigned long long m = s.blk_mask[(size_t)e * s.mask_stride + b];
+        const int rank = s.blk_base[(size_t)e * s.mask_stride + b] + __popcll(m & ((1ull << (t & 63)) - 1ull));
         const int row = s.epstart[e] + rank;
         s.perm[s.offsets[e] + rank] = i;
         s.tok_list[row] = t;
@@ -420,23 +496,28 @@ __device__ __forceinline__ size_t atom_offset(int j, int atom_blocks, int words_
     return ((size_t)(j * atom_blocks + p / 128) * words_per_row + word) * 512 + (p % 32) * 16 + ((p % 128) / 32) * 4;
 }
 
-// One warp per row. Lane l quantises the 64-column chunks l, l+32, ...; a
+// A group of 2^gs_log2 lanes per row (at most 32, so short rows share a
+// warp). Lane l of a group quantises the 64-column chunks l, l+gs, ...; a
 // chunk holds four 16-column blocks, so each lane writes whole scale words.
 // Per term: s = E4M3_RN((bamax / 6) / g); denom = s * g; code =
 // E2M1_RN(r * RN(1/denom)) (0 when denom is 0); r -= code * denom.
 template <int J, int MODE>
 __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int src_is_f16, int rows, int cols,
-                                                            QuantTargets q) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= rows) return;
-    if (MODE == kRowAtoms && warp >= *q.rows_used) return;
-    const int r = warp;
+                                                            int gs_log2, QuantTargets q) {
+    const int lane = threadIdx.x & 31;
+    const int gs = 1 << gs_log2;
+    const int lig = lane & (gs - 1);
+    const int r_raw = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 >> gs_log2) + (lane >> gs_log2);
+    bool valid = r_raw < rows;
+    if (MODE == kRowAtoms && valid && r_raw >= *q.rows_used) valid = false;
+    if (!__any_sync(0xffffffffu, valid)) return;
+    const int r = valid ? r_raw : 0;  // idle lanes still join the group reductions
     uint8_t *codes = q.codes;
     float *g_out = q.g;
     const int rows_stride = q.rows_stride;
     const int wpr = cols / 64;
     int dst_rows[kSlots];
-    if (MODE == kTokenAtoms) {
+    if (MODE == kTokenAtoms && valid) {
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) dst_rows[k] = q.inv_pos[r * kTopK + k];
         dst_rows[kTopK] = *q.shared_row0 + r;
@@ -463,17 +544,17 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
         }
     };
     float amax = 0.0f;
-    for (int ch = lane; ch < chunks; ch += 32) {
+    for (int ch = lig; ch < chunks; ch += gs) {
         float v[64];
         load_chunk(ch, v);
 #pragma unroll
         for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    for (int off = gs >> 1; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (!valid) return;
     const float g = amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
-    if (lane == 0) g_out[r] = g;
-    for (int ch = lane; ch < chunks; ch += 32) {
+    if (lig == 0) g_out[r] = g;
+    for (int ch = lig; ch < chunks; ch += gs) {
         float v[64];
         load_chunk(ch, v);
 #pragma unroll
@@ -625,8 +706,10 @@ void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, i
     s.approx = reinterpret_cast<float *>(take(Tz * Rp * 4));
     s.ids = reinterpret_cast<int *>(take(Tz * kSlots * 4));
     s.weights = reinterpret_cast<float *>(take(Tz * kSlots * 4));
+    s.mask_stride = nb;
     s.blk_mask = reinterpret_cast<unsigned long long *>(take((size_t)nb * E * 8));
     s.blk_base = reinterpret_cast<int *>(take((size_t)nb * E * 4));
+    s.ticket = reinterpret_cast<unsigned *>(take(4));
     s.counts = reinterpret_cast<int *>(take((size_t)E * 4));
     s.offsets = reinterpret_cast<int *>(take((size_t)R * 4));
     s.epstart = reinterpret_cast<int *>(take((size_t)R * 4));
@@ -680,23 +763,23 @@ cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pit
     return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, cudaStream_t stream) {
+cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, int part, cudaStream_t stream) {
     const int R = a.E + 1, Rp = (R + 63) / 64 * 64;
-    const int nb = (a.T + 63) / 64;
-    cudaError_t err = cudaMemsetAsync(s.blk_mask, 0, (size_t)nb * a.E * 8, stream);
-    if (err != cudaSuccess) return err;
-    prefill_logits_kernel<<<dim3((a.T + kLogitsTile - 1) / kLogitsTile, (R + kLogitsTile - 1) / kLogitsTile), 128, 0,
-                            stream>>>(a, s.approx, Rp);
-    err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    prefill_select_kernel<<<(a.T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
-    err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    prefill_scan_kernel<<<1, 256, 0, stream>>>(s, a.T);
-    err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    const int n = a.T * kSlots;
-    prefill_place_kernel<<<(n + 255) / 256, 256, 0, stream>>>(s, a.T, a.inv_scales);
+    cudaError_t err = cudaSuccess;
+    if (part == 0) {
+        err = cudaMemsetAsync(s.blk_mask, 0, (size_t)s.mask_stride * a.E * 8, stream);
+        if (err != cudaSuccess) return err;
+        prefill_logits_kernel<<<dim3((a.T + kLogitsTile - 1) / kLogitsTile, (R + kLogitsTile - 1) / kLogitsTile), 128,
+                                0, stream>>>(a, s.approx, Rp);
+    } else if (part == 1) {
+        prefill_select_kernel<<<(a.T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
+    } else {
+        prefill_scan_kernel<<<a.E, 256, 0, stream>>>(s, a.T);
+        err = cudaGetLastError();
+        if (err != cudaSuccess) return err;
+        const int n = a.T * kSlots;
+        prefill_place_kernel<<<(n + 255) / 256, 256, 0, stream>>>(s, a.T, a.inv_scales);
+    }
     return cudaGetLastError();
 }
 
@@ -704,12 +787,17 @@ template <int MODE>
 static cudaError_t launch_quantize_mode(const void *src, int src_is_f16, int rows, int cols, int terms,
                                         const QuantTargets &q, cudaStream_t stream) {
     if (cols % 64 != 0 || rows <= 0) return cudaErrorInvalidValue;
-    const int grid = (rows + 7) / 8;
+    // Lanes per row: the largest power of two <= min(32, cols/64).
+    const int c64 = cols / 64;
+    int gl = 0;
+    while ((2 << gl) <= (c64 < 32 ? c64 : 32)) ++gl;
+    const int rows_per_cta = 8 * (32 >> gl);
+    const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
     switch (terms) {
-        case 1: quantize_rows_kernel<1, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
-        case 2: quantize_rows_kernel<2, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
-        case 3: quantize_rows_kernel<3, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
-        case 4: quantize_rows_kernel<4, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, q); break;
+        case 1: quantize_rows_kernel<1, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
+        case 2: quantize_rows_kernel<2, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
+        case 3: quantize_rows_kernel<3, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
+        case 4: quantize_rows_kernel<4, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

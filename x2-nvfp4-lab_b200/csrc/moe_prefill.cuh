@@ -48,8 +48,10 @@ struct PrefillScratch {
     float *approx;           // [T][Rp] approximate logits, Rp = round_up(E+1, 64)
     int *ids;                // [T][9]
     float *weights;          // [T][9]
-    unsigned long long *blk_mask;  // [nb][E] token bits per 64-token block
-    int *blk_base;           // [nb][E]
+    unsigned long long *blk_mask;  // [E][mask_stride] token bits per 64-token block
+    int *blk_base;           // [E][mask_stride] rank of each block's first token within the expert
+    int mask_stride;         // 64-token blocks of max_tokens
+    unsigned *ticket;        // [1] completion counter of the dispatch scan
     int *counts;             // [E]
     int *offsets;            // [E+1] unpadded (routing ABI)
     int *epstart;            // [E+1] padded first row of each expert (index E = shared expert)
@@ -119,7 +121,8 @@ cudaError_t make_prefill_act_maps(PrefillMaps &m, const PrefillScratch &s, int J
 cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pitch, int rows, int k16, int row0,
                                cudaStream_t stream);
 
-cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, cudaStream_t stream);
+// Routing in three parts: 0 approximate logits, 1 exact selection, 2 dispatch.
+cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, int part, cudaStream_t stream);
 cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
                                  uint32_t *sf, float *g, int rows_stride, cudaStream_t stream);
 // Prefill forms: token rows of x (codes by token, scale atoms scattered to
