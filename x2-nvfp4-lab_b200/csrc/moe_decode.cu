@@ -48,6 +48,9 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     const int tt = min(kRouteTokens, a.T - t0);
     DecodeScratch &s = a.s;
     const int esz = a.x_is_f32 ? 4 : 2;
+    // Let the gate/up launch (programmatic dependent launch) get its CTAs
+    // resident now; it waits for this grid's completion before reading.
+    pdl_launch_dependents();
 
     // Router rows do not depend on the tokens: start their loads first.
     uint2 wv[kRouteChunkBatch];
@@ -193,13 +196,18 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     }
     if (threadIdx.x == 0) s.ticket[1 + blockIdx.y] = 0u;
 
-    // The last token block to finish dispatches every token.
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) s_ticket = atomicAdd(s.ticket, 1u);
-    __syncthreads();
-    if (s_ticket != gridDim.y - 1) return;
-    __threadfence();
+    // The last token block to finish dispatches every token (with a single
+    // token block this CTA is it).
+    if (gridDim.y > 1) {
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_ticket = atomicAdd(s.ticket, 1u);
+        __syncthreads();
+        if (s_ticket != gridDim.y - 1) return;
+        __threadfence();
+    } else {
+        __syncthreads();
+    }
 
     __shared__ int s_ids[kDecodeMaxTokens * kTopK];
     __shared__ float s_w[kDecodeMaxTokens * kTopK];

@@ -88,6 +88,21 @@ __device__ __forceinline__ void decode_unit(const uint4 &u, uint16_t sc, uint32_
     }
 }
 
+// Routing metadata of one work item (active expert ai, row tile mt).
+struct ItemMeta {
+    int ai, mt, e, tstart, ntok;
+};
+
+__device__ __forceinline__ ItemMeta load_item(const DecodeScratch &s, int item, int mtiles) {
+    ItemMeta m;
+    m.ai = item / mtiles;
+    m.mt = item - m.ai * mtiles;
+    m.e = s.active_expert[m.ai];
+    m.tstart = s.tok_start[m.ai];
+    m.ntok = s.tok_count[m.ai];
+    return m;
+}
+
 // ------------------------------------------------------------ gate / up
 
 template <int NT, int BOXES, int S>
@@ -138,13 +153,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr uint32_t kTx = 2 * Cfg::kPacked + 2 * Cfg::kScales;
 
     if (warp == kConsumerWarps) {
+        // Metadata is prefetched one item ahead and the token ids of a
+        // group are held in registers, so no global load sits between two
+        // stage refills.
         uint32_t it = 0;
+        ItemMeta nxt{};
+        if (blockIdx.x < items) nxt = load_item(s, blockIdx.x, mtiles);
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
-            const int ai = item / mtiles, mt = item - ai * mtiles;
-            const int y = s.active_expert[ai] * I + mt * kGuRows;
-            const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+            const ItemMeta cur = nxt;
+            if (item + (int)gridDim.x < items) nxt = load_item(s, item + gridDim.x, mtiles);
+            const int y = cur.e * I + cur.mt * kGuRows;
+            const int tstart = cur.tstart, ntok = cur.ntok;
             for (int tg = 0; tg < ntok; tg += NT * 8) {
                 const int ncols = min(NT * 8, ntok - tg);
+                const int my_tok = lane < ncols ? s.tok_list[tstart + tg + lane] : 0;
                 for (int sl = 0; sl < slices; ++sl, ++it) {
                     const int st = it % S;
                     const uint32_t ph = (it / S) & 1u;
@@ -167,13 +189,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tma_load_2d(stage + 2 * Cfg::kPacked + Cfg::kScales, &tm_us, full + st, sl * BOXES * 16, y);
                     }
                     uint8_t *tok = stage + 2 * Cfg::kPacked + 2 * Cfg::kScales;
-                    constexpr int per_row = kSK / 8;
+                    constexpr int per_row = kSK / 8;  // a multiple of 32: every lane runs the same trips
                     for (int i = lane; i < ncols * per_row; i += 32) {
                         const int j = i / per_row, kk = (i - j * per_row) * 8;
                         const int k = sl * kSK + kk;
-                        if (k < H)
-                            cp_async16(tok + tok_offset(Cfg::kTokPitch, j, kk),
-                                       s.x_f16 + (size_t)s.tok_list[tstart + tg + j] * H + k);
+                        const int t = __shfl_sync(0xffffffffu, my_tok, j);
+                        if (k < H) cp_async16(tok + tok_offset(Cfg::kTokPitch, j, kk), s.x_f16 + (size_t)t * H + k);
                     }
                     cp_async_arrive_noinc(full + st);
                 }
@@ -188,19 +209,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g = lane >> 2, c = lane & 3;
     const int r0 = mtile * 16 + g, r1 = r0 + 8;
     uint32_t it = 0;
+    ItemMeta nxt{};
+    float nx_gate = 0.0f, nx_up = 0.0f;
+    if (blockIdx.x < items) {
+        nxt = load_item(s, blockIdx.x, mtiles);
+        nx_gate = a.inv_scales[nxt.e];
+        nx_up = a.inv_scales[(E + 1) + nxt.e];
+    }
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int ai = item / mtiles, mt = item - ai * mtiles;
-        const int e = s.active_expert[ai];
-        const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
-        const float inv_gate = a.inv_scales[e];
-        const float inv_up = a.inv_scales[(E + 1) + e];
+        const ItemMeta cur = nxt;
+        const float inv_gate = nx_gate, inv_up = nx_up;
+        if (item + (int)gridDim.x < items) {
+            nxt = load_item(s, item + gridDim.x, mtiles);
+            nx_gate = a.inv_scales[nxt.e];
+            nx_up = a.inv_scales[(E + 1) + nxt.e];
+        }
+        const int mt = cur.mt;
+        const int tstart = cur.tstart, ntok = cur.ntok;
         for (int tg = 0; tg < ntok; tg += NT * 8) {
             const int ncols = min(NT * 8, ntok - tg);
-            float cg[NT][4], cu[NT][4];
+            // Two accumulators per projection (k-slot halves) halve the
+            // dependent MMA chains; they are added once per token group.
+            float cg[NT][4], cu[NT][4], cg2[NT][4], cu2[NT][4];
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) cg[n][r] = cu[n][r] = 0.0f;
+                for (int r = 0; r < 4; ++r) cg[n][r] = cu[n][r] = cg2[n][r] = cu2[n][r] = 0.0f;
 
             for (int sl = 0; sl < slices; ++sl, ++it) {
                 const int st = it % S;
@@ -251,10 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 uint4 bv = make_uint4(0u, 0u, 0u, 0u);
                                 if (have && kin) bv = lds128(tok + tok_offset(Cfg::kTokPitch, n * 8 + g, kloc + 8 * w));
                                 mma_16816(cg[n], hg0[4 * w], hg1[4 * w], hg0[4 * w + 1], hg1[4 * w + 1], bv.x, bv.y);
-                                mma_16816(cg[n], hg0[4 * w + 2], hg1[4 * w + 2], hg0[4 * w + 3], hg1[4 * w + 3], bv.z,
+                                mma_16816(cg2[n], hg0[4 * w + 2], hg1[4 * w + 2], hg0[4 * w + 3], hg1[4 * w + 3], bv.z,
                                           bv.w);
                                 mma_16816(cu[n], hu0[4 * w], hu1[4 * w], hu0[4 * w + 1], hu1[4 * w + 1], bv.x, bv.y);
-                                mma_16816(cu[n], hu0[4 * w + 2], hu1[4 * w + 2], hu0[4 * w + 3], hu1[4 * w + 3], bv.z,
+                                mma_16816(cu2[n], hu0[4 * w + 2], hu1[4 * w + 2], hu0[4 * w + 3], hu1[4 * w + 3], bv.z,
                                           bv.w);
                             }
                         }
@@ -263,6 +297,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty + st);
             }
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    cg[n][r] += cg2[n][r];
+                    cu[n][r] += cu2[n][r];
+                }
             // Fixed-order reduction of the two K halves, then SiLU(gate)*up.
             if (kh == 1) {
 #pragma unroll
@@ -343,10 +384,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (warp == kConsumerWarps) {
         uint32_t it = 0;
+        ItemMeta nxt{};
+        if (blockIdx.x < items) nxt = load_item(s, blockIdx.x, rtiles);
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
-            const int ai = item / rtiles, rt = item - ai * rtiles;
-            const int y = s.active_expert[ai] * H + rt * kDnRows;
-            const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+            const ItemMeta cur = nxt;
+            if (item + (int)gridDim.x < items) nxt = load_item(s, item + gridDim.x, rtiles);
+            const int y = cur.e * H + cur.mt * kDnRows;
+            const int tstart = cur.tstart, ntok = cur.ntok;
             for (int tg = 0; tg < ntok; tg += NT * 8) {
                 const int ncols = min(NT * 8, ntok - tg);
                 for (int sl = 0; sl < slices; ++sl, ++it) {
@@ -385,16 +429,32 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int g = lane >> 2, c = lane & 3;
     const int r0 = warp * 16 + g, r1 = r0 + 8;
     uint32_t it = 0;
+    ItemMeta nxt{};
+    if (blockIdx.x < items) nxt = load_item(s, blockIdx.x, rtiles);
     for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const int ai = item / rtiles, rt = item - ai * rtiles;
-        const int tstart = s.tok_start[ai], ntok = s.tok_count[ai];
+        const ItemMeta cur = nxt;
+        if (item + (int)gridDim.x < items) nxt = load_item(s, item + gridDim.x, rtiles);
+        const int ai = cur.ai, rt = cur.mt;
+        const int tstart = cur.tstart, ntok = cur.ntok;
         for (int tg = 0; tg < ntok; tg += NT * 8) {
             const int ncols = min(NT * 8, ntok - tg);
-            float cd[NT][4];
+            // Output scales of this lane's columns, loaded before the K loop
+            // so their latency overlaps it.
+            float coefs[NT][2];
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
-                for (int r = 0; r < 4; ++r) cd[n][r] = 0.0f;
+                for (int h = 0; h < 2; ++h) {
+                    const int col = n * 8 + 2 * c + h;
+                    coefs[n][h] = col < ncols
+                                      ? s.coef_tab[ai * kDecodeMaxTokens + s.tok_list[tstart + tg + col]]
+                                      : 0.0f;
+                }
+            float cd[NT][4], cd2[NT][4];  // two chains, added once per token group
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) cd[n][r] = cd2[n][r] = 0.0f;
             for (int sl = 0; sl < slices; ++sl, ++it) {
                 const int st = it % S;
                 const uint32_t ph = (it / S) & 1u;
@@ -429,7 +489,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                 uint4 bv = make_uint4(0u, 0u, 0u, 0u);
                                 if (have && kin) bv = lds128(tok + tok_offset(Cfg::kTokPitch, n * 8 + g, kloc + 8 * w));
                                 mma_16816(cd[n], h0[4 * w], h1[4 * w], h0[4 * w + 1], h1[4 * w + 1], bv.x, bv.y);
-                                mma_16816(cd[n], h0[4 * w + 2], h1[4 * w + 2], h0[4 * w + 3], h1[4 * w + 3], bv.z,
+                                mma_16816(cd2[n], h0[4 * w + 2], h1[4 * w + 2], h0[4 * w + 3], h1[4 * w + 3], bv.z,
                                           bv.w);
                             }
                         }
@@ -438,6 +498,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty + st);
             }
+#pragma unroll
+            for (int n = 0; n < NT; ++n)
+#pragma unroll
+                for (int r = 0; r < 4; ++r) cd[n][r] += cd2[n][r];
             // Scaled partial output of this expert for each of its tokens.
 #pragma unroll
             for (int n = 0; n < NT; ++n) {
@@ -446,10 +510,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const int col = n * 8 + 2 * c + (r & 1);
                     if (col < ncols) {
                         const int j = tg + col;
-                        const int t = s.tok_list[tstart + j];
-                        const float coef = s.coef_tab[ai * kDecodeMaxTokens + t];
                         const int row = rt * kDnRows + ((r >= 2) ? r1 : r0);
-                        s.ypart[(size_t)(tstart + j) * H + row] = coef * cd[n][r];
+                        s.ypart[(size_t)(tstart + j) * H + row] = coefs[n][r & 1] * cd[n][r];
                     }
                 }
             }
@@ -500,6 +562,15 @@ cudaError_t set_smem_once(K kernel, size_t bytes, std::atomic<uint64_t> &done) {
     return err;
 }
 
+// Resident CTAs per SM of a kernel at `smem` bytes of dynamic shared memory
+// (at least 1), so persistent grids fill every SM slot.
+template <typename K>
+int ctas_per_sm(K kernel, size_t smem) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kThreads, smem) != cudaSuccess || n < 1) return 1;
+    return n;
+}
+
 // Launch with programmatic stream serialisation: the kernel may start while
 // its predecessor drains and calls griddepcontrol.wait before reading it.
 template <typename... KArgs, typename... Args>
@@ -526,7 +597,8 @@ cudaError_t launch_gate_up_cfg(const StreamMaps &m, const GateUpArgs &a, int ite
     static std::atomic<uint64_t> done{0};
     cudaError_t err = set_smem_once(moe_gate_up_tma_kernel<NT, BOXES, S>, smem, done);
     if (err != cudaSuccess) return err;
-    const int grid = items_ub < sms ? items_ub : sms;
+    static const int per_sm = ctas_per_sm(moe_gate_up_tma_kernel<NT, BOXES, S>, smem);
+    const int grid = items_ub < sms * per_sm ? items_ub : sms * per_sm;
     const CUtensorMap &gs = BOXES == 4 ? m.scales[0] : m.scales_half[0];
     const CUtensorMap &us = BOXES == 4 ? m.scales[1] : m.scales_half[1];
     return launch_pdl(moe_gate_up_tma_kernel<NT, BOXES, S>, dim3(grid), dim3(kThreads), smem, stream, m.packed[0], gs,
@@ -540,7 +612,8 @@ cudaError_t launch_down_cfg(const StreamMaps &m, const DownArgs &a, int items_ub
     static std::atomic<uint64_t> done{0};
     cudaError_t err = set_smem_once(moe_down_tma_kernel<NT, BOXES, S>, smem, done);
     if (err != cudaSuccess) return err;
-    const int grid = items_ub < sms ? items_ub : sms;
+    static const int per_sm = ctas_per_sm(moe_down_tma_kernel<NT, BOXES, S>, smem);
+    const int grid = items_ub < sms * per_sm ? items_ub : sms * per_sm;
     return launch_pdl(moe_down_tma_kernel<NT, BOXES, S>, dim3(grid), dim3(kThreads), smem, stream, m.packed[2],
                       m.scales_half[2], a);
 }
@@ -608,7 +681,7 @@ cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, 
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.I / kGuRows);
     const int tpe = tokens_per_expert(T, a.E);
-    if (tpe <= 8) return launch_gate_up_cfg<1, 2, 7>(m, a, items_ub, sms, stream);
+    if (tpe <= 8) return launch_gate_up_cfg<1, 2, 2>(m, a, items_ub, sms, stream);
     if (tpe <= 16) return launch_gate_up_cfg<2, 2, 5>(m, a, items_ub, sms, stream);
     return launch_gate_up_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
 }
@@ -620,7 +693,7 @@ cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cud
     cudaError_t err;
     const int tpe = tokens_per_expert(T, a.E);
     if (tpe <= 8)
-        err = launch_down_cfg<1, 2, 6>(m, a, items_ub, sms, stream);
+        err = launch_down_cfg<1, 2, 2>(m, a, items_ub, sms, stream);
     else if (tpe <= 16)
         err = launch_down_cfg<2, 2, 4>(m, a, items_ub, sms, stream);
     else
