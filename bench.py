@@ -245,7 +245,6 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     counts = np.asarray(r.counts)
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    rt.set_trace_enabled(True)
     with torch.cuda.stream(stream):
         torch.cuda._sleep(int(2e6))
         for i in range(steps):
@@ -256,9 +255,10 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     stream.synchronize()
     rt.synchronize()
     by_op: dict[str, float] = {}
-    for ev in rt.trace_events():
+    traced = traced_steps(rt, stream, flush,
+                          lambda i: bank.forward(pool[i % 2], residual=res, out=out, stream=stream), steps)
+    for ev in traced:
         by_op[ev.operation] = by_op.get(ev.operation, 0.0) + ev.duration_ns / 1e3 / steps
-    rt.set_trace_enabled(False)
     if skew:
         bank.set_router_bias(None)
     ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
@@ -282,6 +282,25 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
         "max_expert_load": int(counts.max()),
         "mean_expert_load": round(float(counts.mean()), 1),
     }
+
+
+def traced_steps(rt, stream, flush, step, n: int):
+    """Run `step(i)` n times with the runtime trace on (L2 flushed before each
+    step) and return the trace events: per-kernel device durations."""
+    import torch
+
+    torch.cuda.synchronize()
+    rt.set_trace_enabled(True)
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e5) * n)
+        for i in range(n):
+            flush.zero_()
+            step(i)
+    stream.synchronize()
+    rt.synchronize()
+    events = rt.trace_events()
+    rt.set_trace_enabled(False)
+    return events
 
 
 def run_ours(args) -> int:
@@ -339,7 +358,6 @@ def run_ours(args) -> int:
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    rt.set_trace_enabled(True)
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
             # A bounded spin kernel ahead of the first event lets the host
@@ -353,8 +371,10 @@ def run_ours(args) -> int:
                 ends[i].record(stream)
         stream.synchronize()
         rt.synchronize()
-    events = rt.trace_events()
-    rt.set_trace_enabled(False)
+    # Per-kernel durations come from a second, traced pass over the same steps
+    # (tracing records an event pair around every kernel, which would also
+    # serialise the dependent launches of the timed pass).
+    events = traced_steps(rt, stream, flush, step, args.steps)
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
@@ -386,7 +406,6 @@ def run_ours(args) -> int:
     x1 = [p[:1].contiguous() for p in pool]
     o1 = torch.empty(1, H, dtype=torch.bfloat16, device="cuda")
     torch.cuda.synchronize()
-    rt.set_trace_enabled(True)
     with torch.cuda.stream(stream):
         ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(40)]
         torch.cuda._sleep(int(2e5) * 45)
@@ -399,11 +418,10 @@ def run_ours(args) -> int:
                 ev[i - 5][1].record(stream)
     stream.synchronize()
     rt.synchronize()
-    t1_ops: dict[str, list[float]] = {}
-    for evt in rt.trace_events()[-3 * 40:]:
-        t1_ops.setdefault(evt.operation, []).append(evt.duration_ns / 1e3)
-    rt.set_trace_enabled(False)
     lat = sorted(a.elapsed_time(b) * 1000.0 for a, b in ev)
+    t1_ops: dict[str, list[float]] = {}
+    for evt in traced_steps(rt, stream, flush, lambda i: bank.forward(x1[i % pool_n], out=o1, stream=stream), 20):
+        t1_ops.setdefault(evt.operation, []).append(evt.duration_ns / 1e3)
 
     prefill = []
     if not args.no_prefill:

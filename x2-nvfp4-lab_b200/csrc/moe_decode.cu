@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         s.offsets[E] = s_off[E];
         *s.n_active = nact;
     }
-    for (int i = threadIdx.x; i < nact * kDecodeMaxTokens; i += blockDim.x) s.coef_tab[i] = 0.0f;
+    // coef_tab is read only at the (active expert, token) pairs written below.
     __syncthreads();
     for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
         const int t = i / kTopK;

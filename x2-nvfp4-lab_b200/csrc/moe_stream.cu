@@ -681,6 +681,10 @@ cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, 
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.I / kGuRows);
     const int tpe = tokens_per_expert(T, a.E);
+    // With at most one item per SM (small calls) a 4-stage ring keeps a whole
+    // item's weights in flight; otherwise 2-stage rings let three CTAs share
+    // an SM.
+    if (tpe <= 8 && items_ub <= sms) return launch_gate_up_cfg<1, 2, 4>(m, a, items_ub, sms, stream);
     if (tpe <= 8) return launch_gate_up_cfg<1, 2, 2>(m, a, items_ub, sms, stream);
     if (tpe <= 16) return launch_gate_up_cfg<2, 2, 5>(m, a, items_ub, sms, stream);
     return launch_gate_up_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
