@@ -46,6 +46,12 @@ struct nvfp4_moe_bank {
     int prefill_tokens = 0;        // token capacity of pscratch
     int terms_x = 4, terms_act = 3;
     int scratch_terms_x = 0, scratch_terms_act = 0;
+    // Decode expert-GEMV variant: NVFP4_DECODE_KERNELS_TENSOR_CORE (calls of
+    // up to kDecodeTcMaxTokens tokens on shapes with prefill kernels) or
+    // NVFP4_DECODE_KERNELS_IN_REGISTER.
+    int decode_kernels = NVFP4_DECODE_KERNELS_TENSOR_CORE;
+    bool tc_ready = false;         // tc_maps built
+    DecodeTcMaps tc_maps{};
 
     ~nvfp4_moe_bank() {
         if (host_error) cudaFreeHost(host_error);
@@ -111,10 +117,16 @@ nvfp4_status check_upload_args(const nvfp4_moe_bank *bank, int expert, int proje
 // Enqueue the three decode-path kernels for `tokens` <= kDecodeMaxTokens,
 // each between a pair of profiling events (trace operations moe_route,
 // moe_gate_up, moe_down). Caller holds the runtime's queue mutex.
+bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
+    return bank->decode_kernels == NVFP4_DECODE_KERNELS_TENSOR_CORE && bank->tc_ready &&
+           tokens <= kDecodeTcMaxTokens;
+}
+
 void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const void *residual,
                     void *out, int out_f32, int tokens, cudaStream_t stream) {
     const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
     const int sms = bank->runtime->sm_count;
+    const bool tc = use_tensor_core_decode(bank, tokens);
     RouteArgs ra{};
     ra.router = bank->router;
     ra.x = x;
@@ -127,11 +139,51 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ra.e_first = 0;
     ra.e_count = E;
     ra.shared_here = 1;
+    ra.quantize_x = tc ? 1 : 0;
     ra.s = bank->ds;
     nvfp4_runtime *rt = bank->runtime;
     rt->profiled_kernel("moe_route", stream, [&](cudaStream_t s) {
         check_cuda(launch_route(ra, s), "moe_route_kernel");
     });
+
+    DownArgs da{};
+    da.down_packed = bank->packed[2];
+    da.down_scales = bank->scales[2];
+    da.residual = residual;
+    da.out = out;
+    da.out_f32 = out_f32;
+    da.shared_here = 1;
+    da.T = tokens;
+    da.E = E;
+    da.H = H;
+    da.I = I;
+    da.s = bank->ds;
+
+    if (tc) {
+        DecodeTcArgs ta{};
+        ta.inv_scales = bank->inv_scales;
+        ta.E = E;
+        ta.H = H;
+        ta.I = I;
+        ta.s = bank->ds;
+        ta.sfa[0] = bank->sf_atoms[0];
+        ta.sfa[1] = bank->sf_atoms[1];
+        ta.sfb = bank->ds.xsf_tc;
+        rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
+            check_cuda(launch_gate_up_tc(bank->pmaps.w[0], bank->pmaps.w[1], bank->tc_maps, ta, tokens, sms, s),
+                       "moe_gemv_tc_kernel(gate/up)");
+            check_cuda(launch_quantize_act_tc(bank->ds, tokens, I, s), "quantize_act_tc_kernel");
+        });
+        ta.sfa[0] = bank->sf_atoms[2];
+        ta.sfa[1] = bank->sf_atoms[2];
+        ta.sfb = bank->ds.asf_tc;
+        rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
+            check_cuda(launch_down_tc(bank->pmaps.w[2], bank->tc_maps, ta, tokens, sms, s),
+                       "moe_gemv_tc_kernel(down)");
+            check_cuda(launch_combine(da, s), "moe_combine_kernel");
+        });
+        return;
+    }
 
     GateUpArgs ga{};
     ga.gate_packed = bank->packed[0];
@@ -147,18 +199,6 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         check_cuda(launch_gate_up_tma(bank->maps, ga, tokens, sms, s), "moe_gate_up_tma_kernel");
     });
 
-    DownArgs da{};
-    da.down_packed = bank->packed[2];
-    da.down_scales = bank->scales[2];
-    da.residual = residual;
-    da.out = out;
-    da.out_f32 = out_f32;
-    da.shared_here = 1;
-    da.T = tokens;
-    da.E = E;
-    da.H = H;
-    da.I = I;
-    da.s = bank->ds;
     rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
         check_cuda(launch_down_tma(bank->maps, da, sms, s), "moe_down_tma_kernel");
     });
@@ -362,6 +402,11 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
         }
         check_cuda(make_prefill_weight_maps(holder->pmaps, holder->packed, experts, hidden, intermediate),
                    "cuTensorMapEncodeTiled(MoE bank prefill)");
+        if (prefill_supported(holder.get()) && decode_tc_supported(hidden, intermediate)) {
+            check_cuda(make_decode_tc_maps(holder->tc_maps, holder->ds, hidden, intermediate),
+                       "cuTensorMapEncodeTiled(MoE bank decode terms)");
+            holder->tc_ready = true;
+        }
         {
             // Largest routed router-row norm: bounds the approximate-logit
             // error of the prefill router (rounded up by a relative 1e-6).
@@ -664,6 +709,16 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_prefill_terms(nvfp4_moe_ban
     std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
     bank->terms_x = x_terms;
     bank->terms_act = act_terms;
+    clear_last_error();
+    return NVFP4_STATUS_OK;
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_decode_kernels(nvfp4_moe_bank *bank, int kernels) {
+    if (!bank || !bank->runtime ||
+        (kernels != NVFP4_DECODE_KERNELS_TENSOR_CORE && kernels != NVFP4_DECODE_KERNELS_IN_REGISTER))
+        return fail_invalid("decode kernels must be NVFP4_DECODE_KERNELS_TENSOR_CORE or _IN_REGISTER");
+    std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
+    bank->decode_kernels = kernels;
     clear_last_error();
     return NVFP4_STATUS_OK;
 }

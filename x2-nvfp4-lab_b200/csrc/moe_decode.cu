@@ -1,5 +1,6 @@
 // Decode-path kernels; see moe_decode.cuh for the launch sequence.
 #include "moe_decode.cuh"
+#include "quant_terms.cuh"
 #include "tma_util.cuh"
 
 #include <atomic>
@@ -74,8 +75,9 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     }
     __syncthreads();
 
-    // FP16 copy of x for the expert GEMVs (row block 0 converts its tokens).
-    if (blockIdx.x == 0) {
+    // FP16 copy of x for the in-register expert GEMVs (row block 0 converts
+    // its tokens).
+    if (blockIdx.x == 0 && !a.quantize_x) {
         for (int i = threadIdx.x; i < tt * H / 2; i += blockDim.x) {
             float2 v;
             if (a.x_is_f32) {
@@ -133,6 +135,67 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
                     if (a.bias && row < a.E) v = __fadd_rn(v, a.bias[row]);
                     s.logits[(size_t)(t0 + j) * R + row] = v;
                 }
+            }
+        }
+    }
+
+    // Tensor-core variant: row block b < tt also writes token t0 + b as four
+    // NVFP4 terms (B rows 4t + j, scale atoms, global scale), one 16-element
+    // block per thread, from the shared-memory copy of x.
+    if (a.quantize_x && (int)blockIdx.x < tt) {
+        const int jt = blockIdx.x;
+        const int t = t0 + jt;
+        const int nb = H / 16;
+        auto load_block = [&](int b, float (&v)[16]) {
+            if (a.x_is_f32) {
+                const float4 *p = reinterpret_cast<const float4 *>(route_xs + ((size_t)jt * H + 16 * b) * 4);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const float4 f = p[q];
+                    v[4 * q] = f.x;
+                    v[4 * q + 1] = f.y;
+                    v[4 * q + 2] = f.z;
+                    v[4 * q + 3] = f.w;
+                }
+            } else {
+                const uint4 *p = reinterpret_cast<const uint4 *>(route_xs + ((size_t)jt * H + 16 * b) * 2);
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const uint4 u = p[q];
+                    const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        v[8 * q + 2 * h] = bf16_bits_to_f32(w4[h] & 0xFFFFu);
+                        v[8 * q + 2 * h + 1] = bf16_bits_to_f32(w4[h] >> 16);
+                    }
+                }
+            }
+        };
+        float amax = 0.0f;
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+            float v[16];
+            load_block(b, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+        __shared__ float s_amax[kRouteRowsPerCta];
+        if (lane == 0) s_amax[warp] = amax;
+        __syncthreads();
+        amax = fmaxf(fmaxf(s_amax[0], s_amax[1]), fmaxf(s_amax[2], s_amax[3]));
+        const float g = row_global_scale(amax);
+        if (threadIdx.x == 0) s.gx_tc[t] = g;
+        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+            float v[16];
+            load_block(b, v);
+            uint32_t codes[kDecodeTcTerms][2], sc[kDecodeTcTerms];
+            quantize_block_terms<kDecodeTcTerms>(v, g, codes, sc);
+#pragma unroll
+            for (int j = 0; j < kDecodeTcTerms; ++j) {
+                const int n = kDecodeTcTerms * t + j;
+                *reinterpret_cast<uint2 *>(s.xq_tc + (size_t)n * (H / 2) + 8 * b) = make_uint2(codes[j][0], codes[j][1]);
+                s.xsf_tc[sf_atom_byte(n, b)] = static_cast<uint8_t>(sc[j]);
             }
         }
     }
@@ -307,6 +370,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         s.tok_list[pos] = t;
         const int ai = s_aidx[e];
         s.inv_pos[i] = ai >= 0 ? pos : -1;
+        s.slot_group[pos] = ai;
         if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = s_w[i] * inv_down[e];
     }
     if (a.shared_here) {
@@ -314,6 +378,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
             const int pos = T * kTopK + t;
             s.tok_list[pos] = t;
+            s.slot_group[pos] = ai;
             s.coef_tab[ai * kDecodeMaxTokens + t] = s_shared_w[t] * inv_down[E];
         }
         if (threadIdx.x == 0) {
@@ -362,9 +427,17 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
     s.coef_tab = reinterpret_cast<float *>(take((size_t)(E + 1) * T * 4));
     s.ticket = reinterpret_cast<unsigned *>(take(kRouteTickets * 4));
     s.error = reinterpret_cast<int *>(take(4));
+    s.slot_group = reinterpret_cast<int *>(take(T * kSlots * 4));
     s.act = reinterpret_cast<__half *>(take(T * kSlots * (size_t)I * 2));
     s.ypart = reinterpret_cast<float *>(take(T * kSlots * (size_t)H * 4));
     s.tile_count = reinterpret_cast<unsigned *>(take((size_t)(H / 64 + 1) * 4));
+    const size_t Ttc = kDecodeTcMaxTokens;
+    s.xq_tc = take((size_t)kDecodeTcTerms * Ttc * (H / 2));
+    s.xsf_tc = take((size_t)(H / 64) * 512);
+    s.gx_tc = reinterpret_cast<float *>(take(Ttc * 4));
+    s.aq_tc = take((size_t)kDecodeTcTerms * Ttc * kSlots * (I / 2));
+    s.asf_tc = take((size_t)(E + 1) * (I / 64) * 512);
+    s.ga_tc = reinterpret_cast<float *>(take(Ttc * kSlots * 4));
     return off;
 }
 

@@ -1,18 +1,30 @@
 // Decode-path kernels of the NVFP4 MoE layer (tokens <= kDecodeMaxTokens).
 //
-// Three launches per layer on one stream:
-//   1. moe_route_kernel        router + shared-gate logits (FP32, fixed
-//                              order), top-8 + softmax renormalisation +
-//                              sigmoid shared gate per 4-token block, then
-//                              dispatch (per-expert histogram, offsets, stable
-//                              permutation, compacted active-expert list).
-//   2. moe_gate_up_tma_kernel  gate and up NVFP4 GEMVs of every (active
-//                              expert, 32-row tile), SiLU(gate)*up fused.
-//   3. moe_down_tma_kernel     down NVFP4 GEMV of every (active expert,
-//                              64-row tile), scaled per (token, slot).
-//   4. moe_combine_kernel      sum of the nine slots + residual.
-// Launches 2-4 use programmatic dependent launch, so each one's prologue
-// (barrier init, tensor-map prefetch) overlaps its predecessor's tail.
+// Per layer call, one stream, programmatic dependent launch between kernels
+// (each one's prologue overlaps its predecessor's tail):
+//   moe_route_kernel        router + shared-gate logits (FP32, fixed order),
+//                           top-8 + softmax renormalisation + sigmoid shared
+//                           gate per 4-token block, then dispatch (per-expert
+//                           histogram, offsets, stable permutation, compacted
+//                           active-expert list).
+// then one of two expert-GEMV variants:
+//   in-register decode (any shape):
+//     moe_gate_up_tma_kernel  gate and up NVFP4 GEMVs of every (active expert,
+//                             32-row tile), E2M1/E4M3 decoded to f16 in
+//                             registers, mma.sync against f16 tokens,
+//                             SiLU(gate)*up fused;
+//     moe_down_tma_kernel     down GEMV of every (active expert, 64-row tile),
+//                             scaled per (token, slot);
+//   tensor-core (calls of up to kDecodeTcMaxTokens tokens on the shapes
+//   decode_tc_supported accepts; the routing kernel also writes x as four
+//   NVFP4 terms per token):
+//     moe_gate_up_tc_kernel   gate/up on tcgen05 block-scaled MMA; the four
+//                             terms of every token are four B rows (N), so the
+//                             weights stream once;
+//     quantize_act_tc_kernel  activations -> four terms per slot row;
+//     moe_down_tc_kernel      down, scaled per (token, slot);
+// and finally
+//   moe_combine_kernel      sum of the nine slots + residual.
 // The lab runs the same layer as seven launches (nvfp4_runtime.cpp:1943-2066:
 // router GEMV, shared-gate GEMV, top-8, gate/up, SiLU, down, reduce).
 #pragma once
@@ -27,6 +39,8 @@ constexpr int kDecodeMaxTokens = 64;
 constexpr int kTopK = 8;
 constexpr int kSlots = kTopK + 1;  // slot 8 is the shared expert
 constexpr int kRouteTickets = 1 + kDecodeMaxTokens / 4;
+constexpr int kDecodeTcMaxTokens = 32;  // tensor-core variant: 4 terms x 32 tokens = one 128-row B tile
+constexpr int kDecodeTcTerms = 4;
 
 // Device scratch of one bank for the decode path. All pointers are device
 // addresses; sizes are for kDecodeMaxTokens tokens and E routed experts.
@@ -49,9 +63,19 @@ struct DecodeScratch {
     float *coef_tab;        // [(E+1)][kDecodeMaxTokens]
     unsigned *ticket;       // [kRouteTickets] dispatch ticket, then one per 4-token block
     int *error;             // [1] device-side wait timeout flag
+    int *slot_group;        // [T*9] active-group index of each dispatch position, -1 if not computed here
     __half *act;            // [T*9][I]      SiLU(gate)*up per (token, slot)
     float *ypart;           // [T*9][H]      scaled down-projection per (token, slot)
     unsigned *tile_count;   // [H/64]        finished experts per 64-row output tile
+    // Tensor-core variant: activation terms. Row 4*t + j of a B tile is term j
+    // of token (or slot) t; scale bytes are stored in tcgen05 atom layout
+    // [K/64][512 B] per 128-row tile: byte (n%32)*16 + (n/32)*4 + (k/16)%4.
+    uint8_t *xq_tc;         // [128][H/2]               terms of x by token
+    uint8_t *xsf_tc;        // [H/64][512]              their scale atoms
+    float *gx_tc;           // [kDecodeTcMaxTokens]     global scale of each token row
+    uint8_t *aq_tc;         // [T*9*4][I/2]             terms of the activations by slot
+    uint8_t *asf_tc;        // [E+1][I/64][512]         scale atoms per active group (rows from tok_start)
+    float *ga_tc;           // [T*9]                    global scale of each slot row
     int *host_error;        // pinned host-mapped word the host reads at synchronize, or nullptr
 };
 
@@ -71,12 +95,28 @@ struct RouteArgs {
     const float *bias;        // [E] router logit bias or nullptr
     int e_first, e_count;     // locally computed routed experts
     int shared_here;          // 1 if the shared expert is computed here
+    int quantize_x;           // 1: also write x as four NVFP4 terms (tensor-core variant)
     DecodeScratch s;
 };
 
 struct GateUpArgs {
     const uint8_t *gate_packed, *gate_scales, *up_packed, *up_scales;
     const float *inv_scales;
+    int E, H, I;
+    DecodeScratch s;
+};
+
+// Tensor maps of the tensor-core variant's activation terms (128-row boxes,
+// 128-byte swizzle).
+struct DecodeTcMaps {
+    CUtensorMap xq;
+    CUtensorMap aq;
+};
+
+struct DecodeTcArgs {
+    const uint8_t *sfa[2];    // weight scale atoms: gate, up (MODE 0) or down (MODE 1)
+    const uint8_t *sfb;       // activation scale atoms (xsf_tc or asf_tc)
+    const float *inv_scales;  // [3][E+1]
     int E, H, I;
     DecodeScratch s;
 };
@@ -99,6 +139,17 @@ cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *c
                              int I);
 cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, int sms, cudaStream_t stream);
 cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream);
+cudaError_t launch_combine(const DownArgs &a, cudaStream_t stream);
+
+// Tensor-core variant (moe_decode_tc.cu): shapes it serves (H and I
+// multiples of 256, H <= 2048, I of 256 or 512).
+bool decode_tc_supported(int H, int I);
+cudaError_t make_decode_tc_maps(DecodeTcMaps &m, const DecodeScratch &s, int H, int I);
+cudaError_t launch_quantize_act_tc(const DecodeScratch &s, int T, int I, cudaStream_t stream);
+cudaError_t launch_gate_up_tc(const CUtensorMap &w_gate, const CUtensorMap &w_up, const DecodeTcMaps &m,
+                              const DecodeTcArgs &a, int T, int sms, cudaStream_t stream);
+cudaError_t launch_down_tc(const CUtensorMap &w_down, const DecodeTcMaps &m, const DecodeTcArgs &a, int T, int sms,
+                           cudaStream_t stream);
 
 // Scratch byte size for a bank of E experts, hidden H, intermediate I, and
 // the prefix of it that the routing kernel alone uses.

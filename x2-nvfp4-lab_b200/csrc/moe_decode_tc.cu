@@ -1,0 +1,692 @@
+// Tensor-core expert GEMVs of the decode path (calls of up to 32 tokens on
+// banks whose H and I are multiples of 256).
+//
+// The weights stream through tcgen05 block-scaled NVFP4 MMAs
+// (kind::mxf4nvf4, M 128, N 128, K 64, FP32 accumulators in tensor memory),
+// so no instruction of the CTA touches a weight byte: the hardware applies
+// the E4M3 block scales. The activations enter as four NVFP4 terms per row
+// sharing the row's FP32 global scale (term j+1 quantises what terms 1..j
+// left over; quant_terms.cuh: the routing kernel writes x's terms,
+// quantize_act_tc_kernel those of SiLU(gate)*up). The four terms of a row
+// are four B rows (the N dimension) rather than extra K, so every weight tile
+// is read from shared memory by one MMA and the epilogue adds the four
+// accumulator columns of a row. A B tile of 128 rows holds 32 rows x 4 terms:
+//   gate/up  B = the terms of every token of the call (one tile, resident in
+//            L2, re-read per stage); column 4t + j is term j of token t.
+//   down     B = the terms of the group's slot rows (they are consecutive in
+//            dispatch order): rows 4*tok_start .. of the activation terms.
+//
+// One persistent CTA per SM walks (active expert group, 128-row weight tile)
+// items. Warp roles as in the prefill grouped GEMM: warp 0 producer (TMA
+// tiles of the weights and of B, bulk copies of the scale-factor atoms, all
+// on the stage's mbarrier), warp 1 MMA issuer and tensor-memory owner,
+// warps 2-5 epilogue. Every mbarrier wait is bounded; on a timeout the CTA
+// records the error, drains its copies and MMAs in flight, frees its tensor
+// memory and exits.
+#include "moe_decode.cuh"
+#include "quant_terms.cuh"
+#include "tcgen05_util.cuh"
+#include "tma_util.cuh"
+
+#include <atomic>
+
+namespace nvfp4 {
+
+namespace {
+
+constexpr int kTcThreads = 192;
+constexpr int kTile = 128;                     // weight rows per item, B rows per tile
+constexpr int kTileBytes = kTile * 128;        // 128 rows x 128 bytes (256 FP4 columns)
+constexpr int kSfStage = 4 * 512;              // four 64-column scale atoms
+constexpr int kStageK = 256;
+
+__device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
+    return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
+}
+
+__device__ __forceinline__ __half f32_to_f16_sat(float v) {
+    uint16_t h;
+    asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(h) : "f"(v));
+    return __ushort_as_half(h);
+}
+
+// Bounded wait that ignores the shared error word (used to drain copies in
+// flight after a failure).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t *bar, uint32_t parity) {
+    const unsigned long long t0 = global_ns();
+    for (uint32_t i = 0;; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) return false;
+    }
+}
+
+__device__ __forceinline__ void report(const DecodeScratch &s) {
+    const int code = *reinterpret_cast<volatile int *>(s.error);
+    if (s.host_error) *reinterpret_cast<volatile int *>(s.host_error) = code != 0 ? code : kErrWaitTimeout;
+}
+
+struct Item {
+    int ai, e, mt, tstart, ntok;
+};
+
+__device__ __forceinline__ Item load_item(const DecodeScratch &s, int item, int mtiles) {
+    Item it;
+    it.ai = item / mtiles;
+    it.mt = item - it.ai * mtiles;
+    it.e = s.active_expert[it.ai];
+    it.tstart = s.tok_start[it.ai];
+    it.ntok = min(s.tok_count[it.ai], kDecodeTcMaxTokens);
+    return it;
+}
+
+// ------------------------------------------------------------- gate / up
+//
+// Items (active group, 128 rows of I) in a strided order; every item reads
+// the same B tile (the terms of every token), so x's scale factors are
+// copied into tensor memory once per CTA. Per 256-column stage: TMA of the
+// gate and up tiles and of the B slice, bulk copies of the gate and up scale
+// atoms; the MMA thread copies the eight weight atoms and issues eight MMAs.
+constexpr int kGuS = 4;
+constexpr int kGuStage = 3 * kTileBytes + 2 * kSfStage;   // A gate, A up, B, SFA gate, SFA up
+constexpr int kSfbMax = 32 * 512;                         // x scale atoms for H <= 2048
+constexpr int kGuColSfa = 256;                             // + st * 32 (gate 16, up 16)
+constexpr int kGuColSfb = kGuColSfa + kGuS * 32;           // + 4 per 64 columns of H
+constexpr size_t kGuSmem = 1024 + (size_t)kGuS * kGuStage + kSfbMax + 1024;
+static_assert(kGuColSfb + 128 <= 512, "tensor memory overflow");
+static_assert(kGuSmem <= 232448, "shared memory overflow");
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    moe_gate_up_tc_kernel(const __grid_constant__ CUtensorMap tm_g, const __grid_constant__ CUtensorMap tm_u,
+                          const __grid_constant__ CUtensorMap tm_b, DecodeTcArgs a) {
+    constexpr int S = kGuS;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint8_t *sfb_stage = smem + (size_t)S * kGuStage;
+    uint64_t *full = reinterpret_cast<uint64_t *>(sfb_stage + kSfbMax);
+    uint64_t *empty = full + S;
+    uint64_t *acc_full = empty + S;
+    uint64_t *acc_empty = acc_full + 1;
+    uint64_t *sfb_full = acc_empty + 1;
+    uint64_t *drain = sfb_full + 1;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
+    int *col_tok = reinterpret_cast<int *>(tmem_slot + 4);       // [2][32] token of each group row
+    float *col_scale = reinterpret_cast<float *>(col_tok + 64);  // [2][32] its global scale
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const DecodeScratch &s = a.s;
+    int *err = s.error;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(acc_full, 1);
+        mbar_init(acc_empty, 1);
+        mbar_init(sfb_full, 1);
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm_g);
+        prefetch_tensormap(&tm_u);
+        prefetch_tensormap(&tm_b);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // routing tables and x's terms are read from here on
+    pdl_launch_dependents();
+
+    const int mtiles = a.I / kTile;
+    const int total = *s.n_active * mtiles;
+    const int kstages = a.H / kStageK;
+    const int kw = a.H / 64;
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        uint32_t it = 0;
+        bool ok = true;
+        if (lane == 0 && (int)blockIdx.x < total) {
+            mbar_arrive_expect_tx(sfb_full, kw * 512);
+            bulk_g2s(sfb_stage, a.sfb, kw * 512, sfb_full);
+        }
+        for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+            const Item ti = load_item(s, item, mtiles);
+            const int arow = ti.e * a.I + ti.mt * kTile;
+            const size_t sfa_off = (size_t)(arow / kTile) * kw * 512;
+            for (int ks = 0; ks < kstages; ++ks, ++it) {
+                const int st = it % S;
+                const uint32_t ph = (it / S) & 1u;
+                int okw = 1;
+                if (lane == 0) okw = mbar_wait(empty + st, ph ^ 1u, err, kSiteGemmEmpty) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, okw, 0)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *stage = smem + (size_t)st * kGuStage;
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(full + st, kGuStage);
+                    tma_load_2d(stage, &tm_g, full + st, ks * 128, arow);
+                    tma_load_2d(stage + kTileBytes, &tm_u, full + st, ks * 128, arow);
+                    tma_load_2d(stage + 2 * kTileBytes, &tm_b, full + st, ks * 128, 0);
+                    bulk_g2s(stage + 3 * kTileBytes, a.sfa[0] + sfa_off + (size_t)ks * kSfStage, kSfStage, full + st);
+                    bulk_g2s(stage + 3 * kTileBytes + kSfStage, a.sfa[1] + sfa_off + (size_t)ks * kSfStage, kSfStage,
+                             full + st);
+                }
+            }
+        }
+        if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
+            // Drain the copies still in flight before the CTA exits.
+            if (lane == 0) {
+                if ((int)blockIdx.x < total) mbar_wait_drain(sfb_full, 0);
+                const uint32_t first = it > (uint32_t)S ? it - S : 0u;
+                for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_mxf4nvf4(kTile);
+            const uint32_t smem_base = smem_u32(smem);
+            uint32_t it = 0, tcount = 0;
+            bool ok = true;
+            if ((int)blockIdx.x < total) {
+                ok = mbar_wait(sfb_full, 0, err, kSiteGemmFull);
+                tc::fence_after_sync();
+                tc::fence_proxy_async_smem();
+                const uint32_t sfb_base = smem_u32(sfb_stage);
+                for (int at = 0; ok && at < kw; ++at)
+                    tc::cp_sf_atom(tmem + kGuColSfb + 4 * at, tc::smem_desc_sf(sfb_base + at * 512));
+            }
+            for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++tcount) {
+                if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1u, err, kSiteGemmAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                for (int ks = 0; ks < kstages; ++ks, ++it) {
+                    const int st = it % S;
+                    const uint32_t ph = (it / S) & 1u;
+                    if (!mbar_wait(full + st, ph, err, kSiteGemmFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    tc::fence_proxy_async_smem();
+                    const uint32_t sb = smem_base + (uint32_t)st * kGuStage;
+                    const uint32_t sfa = sb + 3 * kTileBytes;
+                    const uint32_t tsfa = tmem + kGuColSfa + (uint32_t)st * 32;
+#pragma unroll
+                    for (int at = 0; at < 4; ++at) {
+                        tc::cp_sf_atom(tsfa + 4 * at, tc::smem_desc_sf(sfa + at * 512));
+                        tc::cp_sf_atom(tsfa + 16 + 4 * at, tc::smem_desc_sf(sfa + kSfStage + at * 512));
+                    }
+#pragma unroll
+                    for (int at = 0; at < 4; ++at) {
+                        const uint32_t acc = (ks | at) != 0 ? 1u : 0u;
+                        const uint64_t bdesc = tc::smem_desc_sw128(sb + 2 * kTileBytes + 32 * at);
+                        const uint32_t tsfb = tmem + kGuColSfb + 4 * (ks * 4 + at);
+                        tc::mma_mxf4nvf4(tmem, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc, tsfa + 4 * at, tsfb,
+                                         acc);
+                        tc::mma_mxf4nvf4(tmem + 128, tc::smem_desc_sw128(sb + kTileBytes + 32 * at), bdesc, idesc,
+                                         tsfa + 16 + 4 * at, tsfb, acc);
+                    }
+                    tc::commit(empty + st);
+                }
+                if (!ok) break;
+                tc::commit(acc_full);
+            }
+            tc::commit(drain);
+            mbar_wait_drain(drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------- epilogue
+        const int sub = warp & 3;
+        const int et = threadIdx.x - 64;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
+        uint32_t tcount = 0;
+        for (int item = blockIdx.x; item < total; item += gridDim.x, ++tcount) {
+            const Item ti = load_item(s, item, mtiles);
+            int *ctok = col_tok + 32 * (tcount & 1);
+            float *cscale = col_scale + 32 * (tcount & 1);
+            if (et < ti.ntok) {
+                const int t = s.tok_list[ti.tstart + et];
+                ctok[et] = t;
+                cscale[et] = s.gx_tc[t];
+            }
+            const float ig = a.inv_scales[ti.e], iu = a.inv_scales[(a.E + 1) + ti.e];
+            if (et == 0) *acc_ok = mbar_wait(acc_full, tcount & 1u, err, kSiteGemmAccFull) ? 1 : 0;
+            named_barrier(1, 128);
+            if (!*reinterpret_cast<volatile int *>(acc_ok)) break;
+            tc::fence_after_sync();
+            const int m = ti.mt * kTile + 32 * sub + lane;
+            // Column 4t + j of the accumulators is term j of token t. The
+            // accumulator is handed back as soon as its last columns are in
+            // registers (one batch of four tokens in the common case).
+            for (int i0 = 0; i0 < ti.ntok; i0 += 4) {
+                uint32_t rg[4][4], ru[4][4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int t = ctok[i0 + q < ti.ntok ? i0 + q : i0];
+                    tc::ld_32x32b_x4(lane_base + 4 * t, rg[q]);
+                    tc::ld_32x32b_x4(lane_base + 128 + 4 * t, ru[q]);
+                }
+                tc::wait_ld();
+                if (i0 + 4 >= ti.ntok) {
+                    tc::fence_before_sync();
+                    named_barrier(1, 128);
+                    if (et == 0) mbar_arrive(acc_empty);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int i = i0 + q;
+                    if (i < ti.ntok) {
+                        const float gs = ((__uint_as_float(rg[q][0]) + __uint_as_float(rg[q][1])) +
+                                          __uint_as_float(rg[q][2])) + __uint_as_float(rg[q][3]);
+                        const float us = ((__uint_as_float(ru[q][0]) + __uint_as_float(ru[q][1])) +
+                                          __uint_as_float(ru[q][2])) + __uint_as_float(ru[q][3]);
+                        const float cs = cscale[i];
+                        const float gate = gs * (ig * cs);
+                        const float up = us * (iu * cs);
+                        s.act[(size_t)(ti.tstart + i) * a.I + m] = f32_to_f16_sat(gate / (1.0f + expf(-gate)) * up);
+                    }
+                }
+            }
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 512);
+    }
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile int *>(err) != 0) report(s);
+}
+
+// ------------------------------------------------------------------ down
+//
+// Each CTA walks a contiguous range of (active group, 128 rows of H) items,
+// so consecutive items mostly share their group: the group's B tile (its
+// slot rows' terms over all of K = I) and scale atoms are loaded into one of
+// two B buffers and copied into tensor memory once per group. A stage is one
+// item's weight tile over all of K (KB 256-column boxes) and its scale atoms.
+template <int KB>
+struct DnCfg {
+    static constexpr int kStage = KB * kTileBytes + KB * kSfStage;
+    static constexpr int kS = KB == 1 ? 8 : 4;
+    static constexpr int kAtoms = KB * 4;                   // 64-column scale atoms over K
+    static constexpr int kColSfa = 256;                     // + st * kAtoms * 4
+    static constexpr int kColSfb = kColSfa + kS * kAtoms * 4;  // + bb * kAtoms * 4
+    static constexpr size_t kSmem = 1024 + (size_t)(kS + 2) * kStage + 1024;
+    static_assert(kColSfb + 2 * kAtoms * 4 <= 512, "tensor memory overflow");
+    static_assert(kSmem <= 232448, "shared memory overflow");
+    static_assert(kStage % 1024 == 0, "stage must keep 1024-byte tile alignment");
+};
+
+template <int KB>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    moe_down_tc_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                       DecodeTcArgs a) {
+    using Cfg = DnCfg<KB>;
+    constexpr int S = Cfg::kS;
+    constexpr int kw = Cfg::kAtoms;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint8_t *bbuf = smem + (size_t)S * Cfg::kStage;  // [2] B tile + scale atoms
+    uint64_t *full = reinterpret_cast<uint64_t *>(bbuf + 2 * Cfg::kStage);
+    uint64_t *empty = full + S;
+    uint64_t *bfull = empty + S;       // [2]
+    uint64_t *bempty = bfull + 2;      // [2]
+    uint64_t *acc_full = bempty + 2;   // [2]
+    uint64_t *acc_empty = acc_full + 2;  // [2]
+    uint64_t *drain = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
+    float *col_scale = reinterpret_cast<float *>(tmem_slot + 4);  // [2][32]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const DecodeScratch &s = a.s;
+    int *err = s.error;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(bfull + b, 1);
+            mbar_init(bempty + b, 1);
+            mbar_init(acc_full + b, 1);
+            mbar_init(acc_empty + b, 1);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm_a);
+        prefetch_tensormap(&tm_b);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // routing tables and activation terms are read from here on
+    pdl_launch_dependents();
+
+    const int mtiles = a.H / kTile;
+    const int total = *s.n_active * mtiles;
+    const int lo = (int)(((long long)total * blockIdx.x) / gridDim.x);
+    const int hi = (int)(((long long)total * (blockIdx.x + 1)) / gridDim.x);
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        uint32_t it = 0, nb = 0;
+        int prev_ai = -1;
+        bool ok = true;
+        if (lane == 0) {
+            for (int item = lo; item < hi && ok; ++item) {
+                const Item ti = load_item(s, item, mtiles);
+                if (ti.ai != prev_ai) {
+                    const uint32_t bb = nb & 1u, use = nb >> 1;
+                    if (use > 0 && !mbar_wait(bempty + bb, (use - 1) & 1u, err, kSiteGemmEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *b = bbuf + (size_t)bb * Cfg::kStage;
+                    mbar_arrive_expect_tx(bfull + bb, Cfg::kStage);
+#pragma unroll
+                    for (int box = 0; box < KB; ++box)
+                        tma_load_2d(b + box * kTileBytes, &tm_b, bfull + bb, box * 128, kDecodeTcTerms * ti.tstart);
+                    bulk_g2s(b + KB * kTileBytes, a.sfb + (size_t)ti.ai * kw * 512, kw * 512, bfull + bb);
+                    ++nb;
+                    prev_ai = ti.ai;
+                }
+                const int st = it % S;
+                const uint32_t ph = (it / S) & 1u;
+                if (!mbar_wait(empty + st, ph ^ 1u, err, kSiteGemmEmpty)) {
+                    ok = false;
+                    break;
+                }
+                uint8_t *stage = smem + (size_t)st * Cfg::kStage;
+                const int arow = ti.e * a.H + ti.mt * kTile;
+                mbar_arrive_expect_tx(full + st, Cfg::kStage);
+#pragma unroll
+                for (int box = 0; box < KB; ++box) tma_load_2d(stage + box * kTileBytes, &tm_a, full + st, box * 128, arow);
+                bulk_g2s(stage + KB * kTileBytes, a.sfa[0] + (size_t)(arow / kTile) * kw * 512, kw * 512, full + st);
+                ++it;
+            }
+            if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
+                // Drain the copies still in flight before the CTA exits.
+                const uint32_t first = it > (uint32_t)S ? it - S : 0u;
+                for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                const uint32_t bfirst = nb > 2u ? nb - 2 : 0u;
+                for (uint32_t k = bfirst; k < nb; ++k) mbar_wait_drain(bfull + (k & 1u), (k >> 1) & 1u);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_mxf4nvf4(kTile);
+            const uint32_t smem_base = smem_u32(smem);
+            const uint32_t bbuf_base = smem_u32(bbuf);
+            uint32_t it = 0, tcount = 0, nb = 0;
+            int prev_ai = -1;
+            bool ok = true;
+            for (int item = lo; item < hi && ok; ++item, ++tcount) {
+                const int ai = item / mtiles;  // items are ordered group-major
+                if (ai != prev_ai) {
+                    if (nb > 0) tc::commit(bempty + ((nb - 1) & 1u));
+                    const uint32_t bb = nb & 1u;
+                    if (!mbar_wait(bfull + bb, (nb >> 1) & 1u, err, kSiteGemmFull)) {
+                        ok = false;
+                        break;
+                    }
+                    tc::fence_after_sync();
+                    tc::fence_proxy_async_smem();
+                    const uint32_t sfb = bbuf_base + bb * Cfg::kStage + KB * kTileBytes;
+#pragma unroll
+                    for (int at = 0; at < kw; ++at)
+                        tc::cp_sf_atom(tmem + Cfg::kColSfb + bb * kw * 4 + 4 * at, tc::smem_desc_sf(sfb + at * 512));
+                    ++nb;
+                    prev_ai = ai;
+                }
+                const uint32_t bb = (nb - 1) & 1u;
+                const uint32_t buf = tcount & 1u, use = tcount >> 1;
+                if (use > 0 && !mbar_wait(acc_empty + buf, (use - 1) & 1u, err, kSiteGemmAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const int st = it % S;
+                if (!mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                tc::fence_proxy_async_smem();
+                const uint32_t sb = smem_base + (uint32_t)st * Cfg::kStage;
+                const uint32_t tsfa = tmem + Cfg::kColSfa + (uint32_t)st * kw * 4;
+                const uint32_t tsfb = tmem + Cfg::kColSfb + bb * kw * 4;
+#pragma unroll
+                for (int at = 0; at < kw; ++at)
+                    tc::cp_sf_atom(tsfa + 4 * at, tc::smem_desc_sf(sb + KB * kTileBytes + at * 512));
+                const uint32_t bsm = bbuf_base + bb * Cfg::kStage;
+#pragma unroll
+                for (int k = 0; k < kw; ++k) {
+                    const uint32_t off = (k >> 2) * kTileBytes + 32 * (k & 3);
+                    tc::mma_mxf4nvf4(tmem + buf * 128, tc::smem_desc_sw128(sb + off), tc::smem_desc_sw128(bsm + off),
+                                     idesc, tsfa + 4 * k, tsfb + 4 * k, k != 0 ? 1u : 0u);
+                }
+                tc::commit(empty + st);
+                tc::commit(acc_full + buf);
+                ++it;
+            }
+            tc::commit(drain);
+            mbar_wait_drain(drain, 0);
+        }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------- epilogue
+        const int sub = warp & 3;
+        const int et = threadIdx.x - 64;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
+        uint32_t tcount = 0;
+        for (int item = lo; item < hi; ++item, ++tcount) {
+            const Item ti = load_item(s, item, mtiles);
+            float *cscale = col_scale + 32 * (tcount & 1);
+            if (et < ti.ntok) {
+                const int p = ti.tstart + et;
+                const int t = s.tok_list[p];
+                cscale[et] = s.ga_tc[p] * s.coef_tab[ti.ai * kDecodeMaxTokens + t];
+            }
+            const uint32_t buf = tcount & 1u;
+            if (et == 0) *acc_ok = mbar_wait(acc_full + buf, (tcount >> 1) & 1u, err, kSiteGemmAccFull) ? 1 : 0;
+            named_barrier(1, 128);
+            if (!*reinterpret_cast<volatile int *>(acc_ok)) break;
+            tc::fence_after_sync();
+            const int m = ti.mt * kTile + 32 * sub + lane;
+            // Column 4i + j is term j of the group's i-th slot row.
+            for (int c0 = 0; c0 < 4 * ti.ntok; c0 += 32) {
+                uint32_t r[32];
+                tc::ld_32x32b_x32(lane_base + buf * 128 + c0, r);
+                tc::wait_ld();
+                if (c0 + 32 >= 4 * ti.ntok) {
+                    tc::fence_before_sync();
+                    named_barrier(1, 128);
+                    if (et == 0) mbar_arrive(acc_empty + buf);
+                }
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    const int i = c0 / 4 + q;
+                    if (i < ti.ntok) {
+                        const float y = ((__uint_as_float(r[4 * q]) + __uint_as_float(r[4 * q + 1])) +
+                                         __uint_as_float(r[4 * q + 2])) + __uint_as_float(r[4 * q + 3]);
+                        s.ypart[(size_t)(ti.tstart + i) * a.H + m] = y * cscale[i];
+                    }
+                }
+            }
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 512);
+    }
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile int *>(err) != 0) report(s);
+}
+
+// Activation rows -> four NVFP4 terms per dispatch position p, one warp per
+// row and one 16-element block per lane: codes to row 4p + j, scale bytes to
+// the atoms of p's active group at B row 4(p - tok_start) + j, the row's
+// global scale to ga_tc[p]. Positions of groups computed elsewhere (-1) are
+// skipped.
+__global__ void __launch_bounds__(256) quantize_act_tc_kernel(DecodeScratch s, int rows, int I) {
+    pdl_wait();  // the gate/up activations are read from here on
+    pdl_launch_dependents();
+    const int lane = threadIdx.x & 31;
+    const int p = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (p >= rows) return;
+    const int ai = s.slot_group[p];
+    if (ai < 0) return;
+    const int n0 = kDecodeTcTerms * (p - s.tok_start[ai]);
+    if (n0 < 0 || n0 + kDecodeTcTerms > kTile) return;
+    const int nb = I / 16;
+    const __half *row = s.act + (size_t)p * I;
+    auto load_block = [&](int b, float (&v)[16]) {
+        const uint4 *q = reinterpret_cast<const uint4 *>(row + 16 * b);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint4 u = q[k];
+            const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w4[h]));
+                v[8 * k + 2 * h] = f.x;
+                v[8 * k + 2 * h + 1] = f.y;
+            }
+        }
+    };
+    float amax = 0.0f;
+    for (int b = lane; b < nb; b += 32) {
+        float v[16];
+        load_block(b, v);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    const float g = row_global_scale(amax);
+    if (lane == 0) s.ga_tc[p] = g;
+    uint8_t *atoms = s.asf_tc + (size_t)ai * (I / 64) * 512;
+    for (int b = lane; b < nb; b += 32) {
+        float v[16];
+        load_block(b, v);
+        uint32_t codes[kDecodeTcTerms][2], sc[kDecodeTcTerms];
+        quantize_block_terms<kDecodeTcTerms>(v, g, codes, sc);
+#pragma unroll
+        for (int j = 0; j < kDecodeTcTerms; ++j) {
+            *reinterpret_cast<uint2 *>(s.aq_tc + ((size_t)kDecodeTcTerms * p + j) * (I / 2) + 8 * b) =
+                make_uint2(codes[j][0], codes[j][1]);
+            atoms[sf_atom_byte(n0 + j, b)] = static_cast<uint8_t>(sc[j]);
+        }
+    }
+}
+
+template <typename K>
+cudaError_t set_smem_once(K kernel, size_t bytes, std::atomic<uint64_t> &done) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load() & bit)) return cudaSuccess;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) done.fetch_or(bit);
+    return err;
+}
+
+template <typename Kern, typename... Args>
+cudaError_t launch_tc(Kern kernel, size_t smem, std::atomic<uint64_t> &done, int grid, cudaStream_t stream,
+                      Args... args) {
+    cudaError_t err = set_smem_once(kernel, smem, done);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kTcThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+int tc_grid(int T, int E, int mtiles, int sms) {
+    const int routed_ub = E < T * kTopK ? E : T * kTopK;
+    const int items_ub = (routed_ub + 1) * mtiles;
+    return items_ub < sms ? items_ub : sms;
+}
+
+}  // namespace
+
+bool decode_tc_supported(int H, int I) {
+    return H % 256 == 0 && I % 256 == 0 && H <= 32 * 64 && (I == 256 || I == 512);
+}
+
+cudaError_t make_decode_tc_maps(DecodeTcMaps &m, const DecodeScratch &s, int H, int I) {
+    if (H % 256 != 0 || I % 256 != 0) return cudaErrorInvalidValue;
+    cudaError_t err = make_tensor_map_u8(&m.xq, s.xq_tc, H / 2, H / 2, (uint64_t)kDecodeTcTerms * kDecodeTcMaxTokens,
+                                         128, kTile, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (err != cudaSuccess) return err;
+    return make_tensor_map_u8(&m.aq, s.aq_tc, I / 2, I / 2,
+                              (uint64_t)kDecodeTcTerms * kDecodeTcMaxTokens * kSlots, 128, kTile,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+cudaError_t launch_quantize_act_tc(const DecodeScratch &s, int T, int I, cudaStream_t stream) {
+    if (T < 1 || T > kDecodeTcMaxTokens || I % 256 != 0) return cudaErrorInvalidValue;
+    const int rows = T * kSlots;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((rows + 7) / 8);
+    cfg.blockDim = dim3(256);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, quantize_act_tc_kernel, s, rows, I);
+}
+
+cudaError_t launch_gate_up_tc(const CUtensorMap &w_gate, const CUtensorMap &w_up, const DecodeTcMaps &m,
+                              const DecodeTcArgs &a, int T, int sms, cudaStream_t stream) {
+    if (T < 1 || T > kDecodeTcMaxTokens || !decode_tc_supported(a.H, a.I)) return cudaErrorInvalidValue;
+    static std::atomic<uint64_t> done{0};
+    return launch_tc(moe_gate_up_tc_kernel, kGuSmem, done, tc_grid(T, a.E, a.I / kTile, sms), stream, w_gate, w_up,
+                     m.xq, a);
+}
+
+cudaError_t launch_down_tc(const CUtensorMap &w_down, const DecodeTcMaps &m, const DecodeTcArgs &a, int T, int sms,
+                           cudaStream_t stream) {
+    if (T < 1 || T > kDecodeTcMaxTokens || !decode_tc_supported(a.H, a.I)) return cudaErrorInvalidValue;
+    const int grid = tc_grid(T, a.E, a.H / kTile, sms);
+    if (a.I == 256) {
+        static std::atomic<uint64_t> done{0};
+        return launch_tc(moe_down_tc_kernel<1>, DnCfg<1>::kSmem, done, grid, stream, w_down, m.aq, a);
+    }
+    static std::atomic<uint64_t> done{0};
+    return launch_tc(moe_down_tc_kernel<2>, DnCfg<2>::kSmem, done, grid, stream, w_down, m.aq, a);
+}
+
+}  // namespace nvfp4

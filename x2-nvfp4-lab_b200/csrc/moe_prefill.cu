@@ -1,6 +1,7 @@
 // Prefill path: routing, dispatch, activation quantisation and combine
 // kernels (the tcgen05 expert GEMMs are in moe_gemm.cu).
 #include "moe_prefill.cuh"
+#include "quant_terms.cuh"
 #include "tma_util.cuh"
 
 #include <cfloat>
@@ -445,32 +446,6 @@ __global__ void prefill_place_kernel(PrefillScratch s, int T, const float *inv_s
 
 // ------------------------------------------------------- quantisation
 
-__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
-    uint16_t r;
-    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
-    return r;
-}
-
-__device__ __forceinline__ uint32_t f32x2_to_e2m1x2(float lo, float hi) {
-    uint16_t r;
-    asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u16.u8 %0, t;\n\t}"
-        : "=h"(r)
-        : "f"(hi), "f"(lo));
-    return r;
-}
-
-__device__ __forceinline__ float e4m3_byte_to_f32(uint32_t b) {
-    const uint32_t h2 = e4m3x2_to_f16x2(static_cast<uint16_t>(b));
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
-}
-
-// Clear the sign of zero-magnitude E2M1 codes (eight nibbles per word).
-__device__ __forceinline__ uint32_t canonical_zero_codes(uint32_t w) {
-    const uint32_t m = w & 0x77777777u;
-    const uint32_t nz = (m | (m >> 1) | (m >> 2)) & 0x11111111u;
-    return m | (w & (nz << 3));
-}
-
 // Where a quantised row's scale words go.
 //   kWords: compact words [J][rows_stride][cols/64] (the standalone ABI)
 //   kTokenAtoms: row r is token r; its codes and words go to each of the
@@ -502,7 +477,7 @@ __device__ __forceinline__ size_t atom_offset(int j, int atom_blocks, int words_
 // Per term: s = E4M3_RN((bamax / 6) / g); denom = s * g; code =
 // E2M1_RN(r * RN(1/denom)) (0 when denom is 0); r -= code * denom.
 template <int J, int MODE>
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int src_is_f16, int rows, int cols,
+__global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int src_kind, int rows, int cols,
                                                             int gs_log2, QuantTargets q) {
     const int lane = threadIdx.x & 31;
     const int gs = 1 << gs_log2;
@@ -510,6 +485,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
     const int r_raw = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 >> gs_log2) + (lane >> gs_log2);
     bool valid = r_raw < rows;
     if (MODE == kRowAtoms && valid && r_raw >= *q.rows_used) valid = false;
+
     if (!__any_sync(0xffffffffu, valid)) return;
     const int r = valid ? r_raw : 0;  // idle lanes still join the group reductions
     uint8_t *codes = q.codes;
@@ -522,17 +498,30 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
         for (int k = 0; k < kTopK; ++k) dst_rows[k] = q.inv_pos[r * kTopK + k];
         dst_rows[kTopK] = *q.shared_row0 + r;
     }
-    const uint16_t *row = static_cast<const uint16_t *>(src) + (size_t)r * cols;
+    const int esz = src_kind == 2 ? 4 : 2;
+    const uint8_t *row = static_cast<const uint8_t *>(src) + (size_t)r * cols * esz;
     const int chunks = cols / 64;
     auto load_chunk = [&](int ch, float (&v)[64]) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(row + ch * 64);
+        if (src_kind == 2) {
+            const float4 *p = reinterpret_cast<const float4 *>(row + (size_t)ch * 64 * 4);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+                const float4 f = __ldg(p + q);
+                v[4 * q] = f.x;
+                v[4 * q + 1] = f.y;
+                v[4 * q + 2] = f.z;
+                v[4 * q + 3] = f.w;
+            }
+            return;
+        }
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + (size_t)ch * 64 * 2);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
             const uint4 u = __ldg(p + q);
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
-                if (src_is_f16) {
+                if (src_kind == 1) {
                     const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[h]));
                     v[8 * q + 2 * h] = f.x;
                     v[8 * q + 2 * h + 1] = f.y;
@@ -784,7 +773,7 @@ cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch
 }
 
 template <int MODE>
-static cudaError_t launch_quantize_mode(const void *src, int src_is_f16, int rows, int cols, int terms,
+static cudaError_t launch_quantize_mode(const void *src, int src_kind, int rows, int cols, int terms,
                                         const QuantTargets &q, cudaStream_t stream) {
     if (cols % 64 != 0 || rows <= 0) return cudaErrorInvalidValue;
     // Lanes per row: the largest power of two <= min(32, cols/64).
@@ -794,10 +783,10 @@ static cudaError_t launch_quantize_mode(const void *src, int src_is_f16, int row
     const int rows_per_cta = 8 * (32 >> gl);
     const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
     switch (terms) {
-        case 1: quantize_rows_kernel<1, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
-        case 2: quantize_rows_kernel<2, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
-        case 3: quantize_rows_kernel<3, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
-        case 4: quantize_rows_kernel<4, MODE><<<grid, 256, 0, stream>>>(src, src_is_f16, rows, cols, gl, q); break;
+        case 1: quantize_rows_kernel<1, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
+        case 2: quantize_rows_kernel<2, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
+        case 3: quantize_rows_kernel<3, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
+        case 4: quantize_rows_kernel<4, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
         default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -703,7 +703,11 @@ cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cud
     else
         err = launch_down_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
     if (err != cudaSuccess) return err;
-    const dim3 grid((a.H + 255) / 256, T);
+    return launch_combine(a, stream);
+}
+
+cudaError_t launch_combine(const DownArgs &a, cudaStream_t stream) {
+    const dim3 grid((a.H + 255) / 256, a.T);
     return launch_pdl(moe_combine_kernel, grid, dim3(256), 0, stream, a);
 }
 

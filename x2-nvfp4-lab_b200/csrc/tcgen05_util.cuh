@@ -118,6 +118,13 @@ __device__ __forceinline__ void ld_32x32b_x32(uint32_t addr, uint32_t (&r)[32]) 
         : "r"(addr));
 }
 
+// Four consecutive accumulator columns of the warp's 32 lanes.
+__device__ __forceinline__ void ld_32x32b_x4(uint32_t addr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 }  // namespace tc

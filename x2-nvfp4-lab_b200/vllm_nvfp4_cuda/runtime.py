@@ -24,6 +24,8 @@ import numpy as np
 
 LIB_NAME = "libnvfp4_moe_cuda.so"
 NVFP4_MOE_ADD_RESIDUAL = 1
+NVFP4_DECODE_KERNELS_TENSOR_CORE = 0
+NVFP4_DECODE_KERNELS_IN_REGISTER = 1
 
 
 class Profile(C.Structure):
@@ -158,6 +160,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
          C.c_void_p], C.c_int),
     "nvfp4_moe_bank_set_prefill_terms": ([C.c_void_p, C.c_int, C.c_int], C.c_int),
     "nvfp4_moe_bank_reserve_prefill": ([C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_moe_bank_set_decode_kernels": ([C.c_void_p, C.c_int], C.c_int),
     "nvfp4_quantize_rows_enqueue": (
         [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
         C.c_int),
@@ -398,6 +401,14 @@ class MoeBank:
         """additive: NVFP4 activation terms of the prefill path (1..4 each)."""
         self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_prefill_terms(self.handle, x_terms, act_terms),
                             "nvfp4_moe_bank_set_prefill_terms")
+
+    def set_decode_kernels(self, kernels: str) -> None:
+        """additive: decode expert-GEMV variant, "tensor_core" (default) or "in_register"."""
+        code = {"tensor_core": NVFP4_DECODE_KERNELS_TENSOR_CORE, "in_register": NVFP4_DECODE_KERNELS_IN_REGISTER}
+        if kernels not in code:
+            raise ValueError(f"unknown decode kernels {kernels!r}")
+        self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_decode_kernels(self.handle, code[kernels]),
+                            "nvfp4_moe_bank_set_decode_kernels")
 
     def reserve_prefill(self, max_tokens: int) -> None:
         """additive: allocate prefill working memory for calls of up to max_tokens tokens."""
