@@ -63,7 +63,7 @@ def _check_routing(bank, ref, T):
     np.testing.assert_array_equal(r.perm, ref.perm)
 
 
-@pytest.mark.parametrize("T", [1, 3, 4, 17, 32])
+@pytest.mark.parametrize("T", [12, 17, 32])
 def test_tensor_core_decode(cuda_runtime, tc_bank, tc_host, T):
     got, xf, rf = _run(tc_bank, tc_host, T, 400 + T)
     same = moe_layer_prefill(tc_host, xf, rf, 4, 4)
@@ -74,8 +74,8 @@ def test_tensor_core_decode(cuda_runtime, tc_bank, tc_host, T):
     assert max_abs_rel(got, fp32.out) <= MAX_ABS_REL_TOL
 
 
-def test_tensor_core_decode_f32_abi(cuda_runtime, tc_bank, tc_host):
-    """The reference ABI (FP32 x, FP32 out, one token) on the tensor-core variant."""
+def test_f32_abi_one_token(cuda_runtime, tc_bank, tc_host):
+    """The reference ABI (FP32 x, FP32 out, one token): in-register variant at one token."""
     H = tc_host.hidden
     x = (synthetic_np.tokens_f32(1, H, 77) * np.float32(0.2)).astype(np.float32)
     xb = cuda_runtime.upload_buffer(np.ascontiguousarray(x[0]))
@@ -83,8 +83,6 @@ def test_tensor_core_decode_f32_abi(cuda_runtime, tc_bank, tc_host):
     tc_bank.decode_device(xb, out)
     cuda_runtime.synchronize()
     got = out.download((1, H))
-    same = moe_layer_prefill(tc_host, x, None, 4, 4)
-    assert rel_rmse(got, same.out) <= SAME_TERMS_TOL
     fp32 = moe_layer(tc_host, x)
     assert rel_rmse(got, fp32.out) <= REL_RMSE_TOL
     assert max_abs_rel(got, fp32.out) <= MAX_ABS_REL_TOL
@@ -105,7 +103,7 @@ def test_in_register_decode(cuda_runtime, tc_bank, tc_host, T):
 
 def test_variants_alternate(cuda_runtime, tc_bank, tc_host):
     """Switching variants between calls leaves no stale state behind."""
-    T = 8
+    T = 16
     outs = []
     for kind in ("tensor_core", "in_register", "tensor_core"):
         tc_bank.set_decode_kernels(kind)

@@ -117,9 +117,15 @@ nvfp4_status check_upload_args(const nvfp4_moe_bank *bank, int expert, int proje
 // Enqueue the three decode-path kernels for `tokens` <= kDecodeMaxTokens,
 // each between a pair of profiling events (trace operations moe_route,
 // moe_gate_up, moe_down). Caller holds the runtime's queue mutex.
+// Below kDecodeTcMinTokens tokens the in-register GEMVs finish first (they
+// split the few active experts into more, smaller work items); from there on
+// the tensor-core GEMVs stream the weights faster (measured on one B200,
+// E 256, H 2048, I 512: equal near 12 tokens, 124 vs 140 us at 32).
+constexpr int kDecodeTcMinTokens = 12;
+
 bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
     return bank->decode_kernels == NVFP4_DECODE_KERNELS_TENSOR_CORE && bank->tc_ready &&
-           tokens <= kDecodeTcMaxTokens;
+           tokens >= kDecodeTcMinTokens && tokens <= kDecodeTcMaxTokens;
 }
 
 void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const void *residual,
