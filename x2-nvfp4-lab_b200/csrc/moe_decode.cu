@@ -12,7 +12,6 @@ namespace {
 
 constexpr int kRouteRowsPerCta = 4;   // one warp per router row, 128 threads
 constexpr int kRouteTokens = 4;       // tokens per CTA column (independent accumulation chains)
-constexpr int kRouteChunkBatch = 16;  // router 128-column chunks loaded per round trip
 
 // Monotone map of a float to uint32 for redux.sync; -0 and +0 map alike so
 // equal logits compare equal, as in the lab's selection loop.
@@ -33,13 +32,13 @@ __device__ __forceinline__ unsigned float_order_key(float v) {
 // The order is fixed, so the oracle reproduces every logit bit for bit.
 //
 // Grid: x = blocks of 4 router rows (one warp each), y = blocks of 4 tokens.
-// Each CTA first copies its tokens (a contiguous [tt][H] range of x in the
-// caller's format) into shared memory with 16-byte cp.async, so the dot
-// products read x without further global round trips. The last CTA of a
+// Each CTA first copies its four router rows and its tokens (a contiguous
+// [tt][H] range of x in the caller's format) into shared memory with 16-byte
+// cp.async, so the dot products make no global round trip. The last CTA of a
 // token block to finish runs top-8 for those tokens (one warp per token); the
 // last token block to finish then dispatches.
 __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
-    extern __shared__ __align__(16) uint8_t route_xs[];   // [tt][H] of x, BF16 or FP32
+    extern __shared__ __align__(16) uint8_t route_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = a.E + 1;
     const int row = blockIdx.x * kRouteRowsPerCta + warp;
@@ -49,22 +48,24 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     const int tt = min(kRouteTokens, a.T - t0);
     DecodeScratch &s = a.s;
     const int esz = a.x_is_f32 ? 4 : 2;
+    uint8_t *route_xs = route_smem;                                                     // [tt][H] of x
+    uint16_t *route_w = reinterpret_cast<uint16_t *>(route_smem + (size_t)kRouteTokens * H * esz);  // [4][H]
     // Let the gate/up launch (programmatic dependent launch) get its CTAs
     // resident now; it waits for this grid's completion before reading.
     pdl_launch_dependents();
 
-    // Router rows do not depend on the tokens: start their loads first.
-    uint2 wv[kRouteChunkBatch];
-    const uint16_t *w = a.router + (size_t)min(row, R - 1) * H;
-#pragma unroll
-    for (int q = 0; q < kRouteChunkBatch; ++q)
-        if (q < chunks) wv[q] = __ldg(reinterpret_cast<const uint2 *>(w + q * 128 + lane * 4));
+    // Every global input of the dot products is requested up front: the
+    // warp's router row and the block's tokens go to shared memory by
+    // cp.async, the row's bias to a register.
+    const float bias = (a.bias && row < a.E) ? __ldg(a.bias + row) : 0.0f;
     {
+        const uint8_t *wsrc = reinterpret_cast<const uint8_t *>(a.router + (size_t)min(row, R - 1) * H);
+        uint8_t *wdst = reinterpret_cast<uint8_t *>(route_w + (size_t)warp * H);
+        for (int i = lane; i < H / 8; i += 32) cp_async16(wdst + 16 * i, wsrc + 16 * i);
         const uint8_t *src = static_cast<const uint8_t *>(a.x) + (size_t)t0 * H * esz;
         if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
             const int n16 = tt * H * esz / 16;
             for (int i = threadIdx.x; i < n16; i += blockDim.x) cp_async16(route_xs + 16 * i, src + 16 * i);
-            cp_async_wait_all();
         } else if (a.x_is_f32) {
             for (int i = threadIdx.x; i < tt * H; i += blockDim.x)
                 reinterpret_cast<float *>(route_xs)[i] = __ldg(reinterpret_cast<const float *>(src) + i);
@@ -72,6 +73,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
             for (int i = threadIdx.x; i < tt * H; i += blockDim.x)
                 reinterpret_cast<uint16_t *>(route_xs)[i] = __ldg(reinterpret_cast<const uint16_t *>(src) + i);
         }
+        cp_async_wait_all();
     }
     __syncthreads();
 
@@ -90,38 +92,35 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         }
     }
 
+    // The serial stretches of this kernel run once per layer call with cold
+    // instruction caches, where code size is time: loops that need no
+    // unrolling stay rolled (#pragma unroll 1).
     if (row < R) {
         float acc[kRouteTokens];
 #pragma unroll
         for (int j = 0; j < kRouteTokens; ++j) acc[j] = 0.0f;
-        for (int qb = 0; qb < chunks; qb += kRouteChunkBatch) {
-            if (qb > 0) {
+        const uint16_t *wr = route_w + (size_t)warp * H;
+#pragma unroll 1
+        for (int q = 0; q < chunks; ++q) {
+            const int k = q * 128 + lane * 4;
+            const uint2 wv = *reinterpret_cast<const uint2 *>(wr + k);
+            const float w0 = bf16_bits_to_f32(wv.x & 0xFFFFu), w1 = bf16_bits_to_f32(wv.x >> 16);
+            const float w2 = bf16_bits_to_f32(wv.y & 0xFFFFu), w3 = bf16_bits_to_f32(wv.y >> 16);
 #pragma unroll
-                for (int q = 0; q < kRouteChunkBatch; ++q)
-                    if (qb + q < chunks) wv[q] = __ldg(reinterpret_cast<const uint2 *>(w + (qb + q) * 128 + lane * 4));
-            }
-#pragma unroll
-            for (int q = 0; q < kRouteChunkBatch; ++q) {
-                if (qb + q >= chunks) break;
-                const int k = (qb + q) * 128 + lane * 4;
-                const float w0 = bf16_bits_to_f32(wv[q].x & 0xFFFFu), w1 = bf16_bits_to_f32(wv[q].x >> 16);
-                const float w2 = bf16_bits_to_f32(wv[q].y & 0xFFFFu), w3 = bf16_bits_to_f32(wv[q].y >> 16);
-#pragma unroll
-                for (int j = 0; j < kRouteTokens; ++j) {
-                    if (j < tt) {
-                        float4 xv;
-                        if (a.x_is_f32) {
-                            xv = *reinterpret_cast<const float4 *>(route_xs + ((size_t)j * H + k) * 4);
-                        } else {
-                            const uint2 b = *reinterpret_cast<const uint2 *>(route_xs + ((size_t)j * H + k) * 2);
-                            xv = make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
-                                             bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
-                        }
-                        acc[j] = __fadd_rn(acc[j], __fmul_rn(w0, xv.x));
-                        acc[j] = __fadd_rn(acc[j], __fmul_rn(w1, xv.y));
-                        acc[j] = __fadd_rn(acc[j], __fmul_rn(w2, xv.z));
-                        acc[j] = __fadd_rn(acc[j], __fmul_rn(w3, xv.w));
+            for (int j = 0; j < kRouteTokens; ++j) {
+                if (j < tt) {
+                    float4 xv;
+                    if (a.x_is_f32) {
+                        xv = *reinterpret_cast<const float4 *>(route_xs + ((size_t)j * H + k) * 4);
+                    } else {
+                        const uint2 b = *reinterpret_cast<const uint2 *>(route_xs + ((size_t)j * H + k) * 2);
+                        xv = make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
+                                         bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
                     }
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w0, xv.x));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w1, xv.y));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w2, xv.z));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w3, xv.w));
                 }
             }
         }
@@ -132,7 +131,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
 #pragma unroll
                 for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
                 if (lane == 0) {
-                    if (a.bias && row < a.E) v = __fadd_rn(v, a.bias[row]);
+                    if (a.bias && row < a.E) v = __fadd_rn(v, bias);
                     s.logits[(size_t)(t0 + j) * R + row] = v;
                 }
             }
@@ -189,13 +188,13 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         for (int b = threadIdx.x; b < nb; b += blockDim.x) {
             float v[16];
             load_block(b, v);
-            uint32_t codes[kDecodeTcTerms][2], sc[kDecodeTcTerms];
-            quantize_block_terms<kDecodeTcTerms>(v, g, codes, sc);
-#pragma unroll
+#pragma unroll 1
             for (int j = 0; j < kDecodeTcTerms; ++j) {
+                uint32_t c0, c1;
+                const uint32_t sc = quantize_block_term(v, g, c0, c1);
                 const int n = kDecodeTcTerms * t + j;
-                *reinterpret_cast<uint2 *>(s.xq_tc + (size_t)n * (H / 2) + 8 * b) = make_uint2(codes[j][0], codes[j][1]);
-                s.xsf_tc[sf_atom_byte(n, b)] = static_cast<uint8_t>(sc[j]);
+                *reinterpret_cast<uint2 *>(s.xq_tc + (size_t)n * (H / 2) + 8 * b) = make_uint2(c0, c1);
+                s.xsf_tc[sf_atom_byte(n, b)] = static_cast<uint8_t>(sc);
             }
         }
     }
@@ -209,6 +208,26 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     if (s_ticket != gridDim.x - 1) return;
     __threadfence();
 
+    __shared__ int s_ids[kDecodeMaxTokens * kTopK];
+    __shared__ float s_w[kDecodeMaxTokens * kTopK];
+    __shared__ float s_shared_w[kDecodeMaxTokens];
+    __shared__ int s_cnt[256];
+    __shared__ int s_off[257];
+    __shared__ int s_aidx[256];
+    __shared__ unsigned long long s_tokmask[256];
+    __shared__ float s_invd[257];
+    __shared__ int s_nrouted;
+
+    // The dispatch's per-expert coefficients need the inverse down scales:
+    // request them now, store them after top-8.
+    const float *inv_down = a.inv_scales + 2 * (size_t)R;
+    float invd[3];
+#pragma unroll
+    for (int q = 0; q < 3; ++q) {
+        const int e = threadIdx.x + 128 * q;
+        invd[q] = e < R ? __ldg(inv_down + e) : 0.0f;
+    }
+
     const int E = a.E, T = a.T;
     if (warp < tt) {
         const int t = t0 + warp;
@@ -218,10 +237,12 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
             const int e = lane + 32 * i;
             v[i] = e < E ? __ldcg(s.logits + (size_t)t * R + e) : -FLT_MAX;
         }
+        const float sl = __ldcg(s.logits + (size_t)t * R + E);
+        // Lane `slot` keeps the slot-th pick.
         unsigned taken = 0;
-        float top_v[kTopK];
-        int top_i[kTopK];
-#pragma unroll
+        float my_v = 0.0f;
+        int my_i = 0;
+#pragma unroll 1
         for (int slot = 0; slot < kTopK; ++slot) {
             // Local best: strictly greater wins, so the lowest id survives ties.
             float bv = -FLT_MAX;
@@ -240,27 +261,40 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
             const unsigned imin = __reduce_min_sync(0xffffffffu, key == kmax ? (unsigned)bi : 0xffffffffu);
             bi = (int)imin;
             bv = __shfl_sync(0xffffffffu, bv, bi & 31);
-            top_v[slot] = bv;
-            top_i[slot] = bi;
+            if (lane == slot) {
+                my_v = bv;
+                my_i = bi;
+            }
             if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         }
-        if (lane == 0) {
-            float den = 0.0f;
-#pragma unroll
-            for (int slot = 0; slot < kTopK; ++slot) den += expf(top_v[slot] - top_v[0]);
-            for (int slot = 0; slot < kTopK; ++slot) {
-                s.ids[t * kSlots + slot] = top_i[slot];
-                s.weights[t * kSlots + slot] = expf(top_v[slot] - top_v[0]) / den;
-            }
-            const float sl = __ldcg(s.logits + (size_t)t * R + E);
+        // Softmax over the eight picks relative to the largest; the
+        // denominator adds the picks in slot order.
+        const float top0 = __shfl_sync(0xffffffffu, my_v, 0);
+        const float my_e = lane < kTopK ? expf(my_v - top0) : 0.0f;
+        float den = 0.0f;
+#pragma unroll 1
+        for (int slot = 0; slot < kTopK; ++slot) den += __shfl_sync(0xffffffffu, my_e, slot);
+        if (lane < kTopK) {
+            const float w = my_e / den;
+            s.ids[t * kSlots + lane] = my_i;
+            s.weights[t * kSlots + lane] = w;
+            s_ids[t * kTopK + lane] = my_i;
+            s_w[t * kTopK + lane] = w;
+        } else if (lane == kTopK) {
+            const float w = 1.0f / (1.0f + expf(-sl));
             s.ids[t * kSlots + kTopK] = E;
-            s.weights[t * kSlots + kTopK] = 1.0f / (1.0f + expf(-sl));
+            s.weights[t * kSlots + kTopK] = w;
+            s_shared_w[t] = w;
         }
     }
+#pragma unroll
+    for (int q = 0; q < 3; ++q)
+        if (threadIdx.x + 128 * q < R) s_invd[threadIdx.x + 128 * q] = invd[q];
     if (threadIdx.x == 0) s.ticket[1 + blockIdx.y] = 0u;
 
-    // The last token block to finish dispatches every token (with a single
-    // token block this CTA is it).
+    // The last token block to finish dispatches every token. With a single
+    // token block this CTA is it and its top-8 results are already in
+    // shared memory; otherwise every block's results are read back.
     if (gridDim.y > 1) {
         __threadfence();
         __syncthreads();
@@ -268,34 +302,24 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         __syncthreads();
         if (s_ticket != gridDim.y - 1) return;
         __threadfence();
-    } else {
-        __syncthreads();
-    }
-
-    __shared__ int s_ids[kDecodeMaxTokens * kTopK];
-    __shared__ float s_w[kDecodeMaxTokens * kTopK];
-    __shared__ float s_shared_w[kDecodeMaxTokens];
-    __shared__ int s_cnt[256];
-    __shared__ int s_off[257];
-    __shared__ int s_aidx[256];
-    __shared__ unsigned long long s_tokmask[256];
-    __shared__ int s_nrouted;
-
-    const float *inv_down = a.inv_scales + 2 * (size_t)R;
-    for (int i = threadIdx.x; i < T * kSlots; i += blockDim.x) {
-        const int t = i / kSlots, slot = i - t * kSlots;
-        if (slot < kTopK) {
-            s_ids[t * kTopK + slot] = __ldcg(s.ids + i);
-            s_w[t * kTopK + slot] = __ldcg(s.weights + i);
-        } else {
-            s_shared_w[t] = __ldcg(s.weights + i);
+#pragma unroll 1
+        for (int i = threadIdx.x; i < T * kSlots; i += blockDim.x) {
+            const int t = i / kSlots, slot = i - t * kSlots;
+            if (slot < kTopK) {
+                s_ids[t * kTopK + slot] = __ldcg(s.ids + i);
+                s_w[t * kTopK + slot] = __ldcg(s.weights + i);
+            } else {
+                s_shared_w[t] = __ldcg(s.weights + i);
+            }
         }
     }
+#pragma unroll 1
     for (int e = threadIdx.x; e < 256; e += blockDim.x) {
         s_cnt[e] = 0;
         s_tokmask[e] = 0ull;
     }
     __syncthreads();
+#pragma unroll 1
     for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
         const int e = s_ids[i];
         atomicAdd(&s_cnt[e], 1);
@@ -345,6 +369,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     __syncthreads();
     const int nrouted = s_nrouted;
     const int nact = nrouted + (a.shared_here ? 1 : 0);
+#pragma unroll 1
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         s.counts[e] = s_cnt[e];
         s.offsets[e] = s_off[e];
@@ -360,7 +385,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         *s.n_active = nact;
     }
     // coef_tab is read only at the (active expert, token) pairs written below.
-    __syncthreads();
+#pragma unroll 1
     for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
         const int t = i / kTopK;
         const int e = s_ids[i];
@@ -371,15 +396,16 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         const int ai = s_aidx[e];
         s.inv_pos[i] = ai >= 0 ? pos : -1;
         s.slot_group[pos] = ai;
-        if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = s_w[i] * inv_down[e];
+        if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = s_w[i] * s_invd[e];
     }
     if (a.shared_here) {
         const int ai = nrouted;
+#pragma unroll 1
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
             const int pos = T * kTopK + t;
             s.tok_list[pos] = t;
             s.slot_group[pos] = ai;
-            s.coef_tab[ai * kDecodeMaxTokens + t] = s_shared_w[t] * inv_down[E];
+            s.coef_tab[ai * kDecodeMaxTokens + t] = s_shared_w[t] * s_invd[E];
         }
         if (threadIdx.x == 0) {
             s.active_expert[ai] = E;
@@ -444,7 +470,7 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream) {
     const int R = a.E + 1;
     const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
-    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2);
+    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2;
     if (smem > 48 * 1024) {
         // Raise the limit to all the shared memory a CTA may hold, once per
         // device (bit d of `done`).

@@ -591,13 +591,15 @@ __global__ void __launch_bounds__(256) quantize_act_tc_kernel(DecodeScratch s, i
     for (int b = lane; b < nb; b += 32) {
         float v[16];
         load_block(b, v);
-        uint32_t codes[kDecodeTcTerms][2], sc[kDecodeTcTerms];
-        quantize_block_terms<kDecodeTcTerms>(v, g, codes, sc);
-#pragma unroll
+        // Terms in a loop that is not unrolled: this kernel runs once per
+        // layer call with cold instruction caches, where code size is time.
+#pragma unroll 1
         for (int j = 0; j < kDecodeTcTerms; ++j) {
+            uint32_t c0, c1;
+            const uint32_t sc = quantize_block_term(v, g, c0, c1);
             *reinterpret_cast<uint2 *>(s.aq_tc + ((size_t)kDecodeTcTerms * p + j) * (I / 2) + 8 * b) =
-                make_uint2(codes[j][0], codes[j][1]);
-            atoms[sf_atom_byte(n0 + j, b)] = static_cast<uint8_t>(sc[j]);
+                make_uint2(c0, c1);
+            atoms[sf_atom_byte(n0 + j, b)] = static_cast<uint8_t>(sc);
         }
     }
 }

@@ -46,44 +46,39 @@ __device__ __forceinline__ float row_global_scale(float amax) {
     return amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
 }
 
-// Quantise one 16-element block (v, overwritten by the final residual) into
-// J terms: codes[j][0] holds elements 0..7 (element 2i in the low nibble of
-// byte i), codes[j][1] elements 8..15; scale[j] is the term's E4M3 byte.
-template <int J>
-__device__ __forceinline__ void quantize_block_terms(float (&v)[16], float g, uint32_t (&codes)[J][2],
-                                                     uint32_t (&scale)[J]) {
+// Quantise one 16-element block (v, overwritten by the residual) into the
+// next term: c0 holds elements 0..7 (element 2i in the low nibble of byte i),
+// c1 elements 8..15; returns the term's E4M3 scale byte.
+__device__ __forceinline__ uint32_t quantize_block_term(float (&v)[16], float g, uint32_t &c0, uint32_t &c1) {
+    float bamax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-        float bamax = 0.0f;
+    for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(v[i]));
+    const float target = __fdiv_rn(__fdiv_rn(bamax, 6.0f), g);
+    const uint32_t sb = f32x2_to_e4m3x2(target, 0.0f) & 0xFFu;
+    const float denom = __fmul_rn(e4m3_byte_to_f32(sb), g);
+    const float inv = denom != 0.0f ? __frcp_rn(denom) : 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(v[i]));
-        const float target = __fdiv_rn(__fdiv_rn(bamax, 6.0f), g);
-        const uint32_t sb = f32x2_to_e4m3x2(target, 0.0f) & 0xFFu;
-        scale[j] = sb;
-        const float denom = __fmul_rn(e4m3_byte_to_f32(sb), g);
-        const float inv = denom != 0.0f ? __frcp_rn(denom) : 0.0f;
+    for (int p = 0; p < 2; ++p) {
+        uint32_t word = 0;
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
-            uint32_t word = 0;
+        for (int i = 0; i < 4; ++i) {
+            const int e0 = 8 * p + 2 * i;
+            const uint32_t cc = f32x2_to_e2m1x2(__fmul_rn(v[e0], inv), __fmul_rn(v[e0 + 1], inv)) & 0xFFu;
+            word |= cc << (8 * i);
+        }
+        word = canonical_zero_codes(word);
+        if (p == 0) c0 = word; else c1 = word;
+        uint32_t h[4];
+        e2m1x8_to_f16x8(word, h);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int e0 = 8 * p + 2 * i;
-                const uint32_t cc = f32x2_to_e2m1x2(__fmul_rn(v[e0], inv), __fmul_rn(v[e0 + 1], inv)) & 0xFFu;
-                word |= cc << (8 * i);
-            }
-            word = canonical_zero_codes(word);
-            codes[j][p] = word;
-            uint32_t h[4];
-            e2m1x8_to_f16x8(word, h);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(&h[i]));
-                const int e0 = 8 * p + 2 * i;
-                v[e0] = __fsub_rn(v[e0], __fmul_rn(d.x, denom));
-                v[e0 + 1] = __fsub_rn(v[e0 + 1], __fmul_rn(d.y, denom));
-            }
+        for (int i = 0; i < 4; ++i) {
+            const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(&h[i]));
+            const int e0 = 8 * p + 2 * i;
+            v[e0] = __fsub_rn(v[e0], __fmul_rn(d.x, denom));
+            v[e0 + 1] = __fsub_rn(v[e0 + 1], __fmul_rn(d.y, denom));
         }
     }
+    return sb;
 }
 
 // Byte offset of B row n (< 128), 16-element block b of a tcgen05
