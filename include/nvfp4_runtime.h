@@ -290,6 +290,12 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_upload_projection_device(
 /* additive: flags for the batched forward. */
 enum {
     NVFP4_MOE_ADD_RESIDUAL = 1u << 0,
+    /* dst is FP32 [tokens, hidden] and receives this bank's partial sum: the
+     * experts of its range (nvfp4_moe_bank_set_expert_range), plus the
+     * residual when NVFP4_MOE_ADD_RESIDUAL is set. Summing the partials of
+     * banks whose ranges cover every expert once (and one of which computes
+     * the shared expert) gives the layer output. */
+    NVFP4_MOE_PARTIAL_F32 = 1u << 1,
 };
 
 /* additive: batched layer forward with BF16 I/O. x and residual are BF16
@@ -372,6 +378,30 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_set_prefill_terms(
     nvfp4_moe_bank * bank,
     int x_terms,
     int act_terms);
+
+/* additive: expert parallelism (no counterpart in the lab, which runs one
+ * device). Later forwards and decodes compute only routed experts
+ * [first, first + count) and the shared expert when shared_here is 1; routing
+ * still covers every expert (ids, counts and permutation are those of the
+ * whole layer). Only the projections of the computed experts need to be
+ * uploaded. The default is every expert and the shared expert. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_set_expert_range(
+    nvfp4_moe_bank * bank,
+    int first,
+    int count,
+    int shared_here);
+
+/* additive: out = BF16(sum + residual) over [tokens, hidden], with sum FP32
+ * (the reduced partial sums of expert-parallel banks) and residual BF16 or
+ * NULL; device pointers, enqueued on `stream` (NULL: the runtime's stream). */
+NVFP4_API nvfp4_status nvfp4_moe_finalize_bf16(
+    nvfp4_runtime * runtime,
+    const float * sum_f32,
+    const void * residual_bf16,
+    void * out_bf16,
+    int tokens,
+    int hidden,
+    void * stream);
 
 /* additive: expert-GEMV kernels of the decode path (calls of up to 64
  * tokens). TENSOR_CORE (default) streams the weights through tcgen05

@@ -298,10 +298,15 @@ class LayerResult:
     perm: np.ndarray
 
 
-def moe_layer(bank: BankHost, x: np.ndarray, residual: np.ndarray | None = None) -> LayerResult:
+def moe_layer(bank: BankHost, x: np.ndarray, residual: np.ndarray | None = None,
+              expert_range: tuple[int, int] | None = None, shared_here: bool = True) -> LayerResult:
     """Full layer: router -> top-8 -> dispatch -> routed + shared SwiGLU experts
     -> weighted combine (+ residual). x is [T, H] float32 (BF16 values are
-    passed as their float32 images)."""
+    passed as their float32 images).
+
+    With ``expert_range = (first, count)`` the output is the partial sum of an
+    expert-parallel rank: only routed experts in [first, first + count) are
+    added, the shared expert only when ``shared_here`` (routing is unchanged)."""
     x = np.asarray(x, dtype=np.float32)
     T, H = x.shape
     E = bank.experts
@@ -312,11 +317,15 @@ def moe_layer(bank: BankHost, x: np.ndarray, residual: np.ndarray | None = None)
     shared_w = sigmoid32(logits[:, E])
     counts, offsets, perm = dispatch(ids, E)
     out = np.zeros((T, H), dtype=np.float64)
+    first, count = expert_range if expert_range is not None else (0, E)
     for e in np.unique(ids):
+        if not first <= int(e) < first + count:
+            continue
         rows, slots = np.nonzero(ids == e)
         y = expert_forward(bank, int(e), x[rows])
         out[rows] += weights[rows, slots].astype(np.float64)[:, None] * y
-    out += shared_w.astype(np.float64)[:, None] * expert_forward(bank, E, x)
+    if shared_here:
+        out += shared_w.astype(np.float64)[:, None] * expert_forward(bank, E, x)
     if residual is not None:
         out += np.asarray(residual, dtype=np.float64)
     ids9 = np.concatenate([ids, np.full((T, 1), E, dtype=np.int32)], axis=1)

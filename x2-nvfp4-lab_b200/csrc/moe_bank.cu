@@ -50,6 +50,9 @@ struct nvfp4_moe_bank {
     // up to kDecodeTcMaxTokens tokens on shapes with prefill kernels) or
     // NVFP4_DECODE_KERNELS_IN_REGISTER.
     int decode_kernels = NVFP4_DECODE_KERNELS_TENSOR_CORE;
+    // Expert parallelism: routed experts [e_first, e_first + e_count) and the
+    // shared expert (when shared_here) are computed by this bank.
+    int e_first = 0, e_count = 0, shared_here = 1;
     bool tc_ready = false;         // tc_maps built
     DecodeTcMaps tc_maps{};
 
@@ -77,6 +80,16 @@ struct nvfp4_moe_bank {
     // padding bytes stay zero.
     size_t scale_pitch(int projection) const { return (cols(projection) / 16 + 15) & ~size_t(15); }
     size_t scales_per_expert(int projection) const { return rows(projection) * scale_pitch(projection); }
+    // Every projection this bank computes has been uploaded.
+    bool owned_uploaded() const {
+        const size_t slots = static_cast<size_t>(experts) + 1;
+        for (int p = 0; p < 3; ++p) {
+            for (int e = e_first; e < e_first + e_count; ++e)
+                if (!uploaded[p * slots + e]) return false;
+            if (shared_here && !uploaded[p * slots + experts]) return false;
+        }
+        return true;
+    }
 };
 
 namespace {
@@ -142,9 +155,9 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ra.H = H;
     ra.inv_scales = bank->inv_scales;
     ra.bias = bank->router_bias;
-    ra.e_first = 0;
-    ra.e_count = E;
-    ra.shared_here = 1;
+    ra.e_first = bank->e_first;
+    ra.e_count = bank->e_count;
+    ra.shared_here = bank->shared_here;
     ra.quantize_x = tc ? 1 : 0;
     ra.s = bank->ds;
     nvfp4_runtime *rt = bank->runtime;
@@ -158,7 +171,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     da.residual = residual;
     da.out = out;
     da.out_f32 = out_f32;
-    da.shared_here = 1;
+    da.shared_here = bank->shared_here;
     da.T = tokens;
     da.E = E;
     da.H = H;
@@ -246,11 +259,14 @@ void ensure_prefill(nvfp4_moe_bank *bank, int tokens) {
 }
 
 // Prefill-path launches for `tokens` <= bank->prefill_tokens (BF16 in/out).
-void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, void *out, int tokens,
+void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, void *out, int out_f32, int tokens,
                      cudaStream_t stream) {
     const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
     const int sms = bank->runtime->sm_count;
     nvfp4_runtime *rt = bank->runtime;
+    bank->ps.e_first = bank->e_first;
+    bank->ps.e_count = bank->e_count;
+    bank->ps.shared_here = bank->shared_here;
     const PrefillScratch &ps = bank->ps;
     PrefillRouteArgs ra{};
     ra.router = bank->router;
@@ -304,7 +320,7 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
         check_cuda(launch_gemm_down(bank->pmaps, gd, sms, s), "moe_gemm_kernel(down)");
     });
     rt->profiled_kernel("moe_combine", stream, [&](cudaStream_t s) {
-        check_cuda(launch_prefill_combine(ps, tokens, residual, out, s), "prefill_combine_kernel");
+        check_cuda(launch_prefill_combine(ps, tokens, residual, out, out_f32, s), "prefill_combine_kernel");
     });
 }
 
@@ -314,8 +330,9 @@ constexpr int kPrefillMaxSlice = 16384;
 // prefill path above it (in slices of at most kPrefillMaxSlice tokens), or
 // decode-path slices when the bank's shape has no prefill kernels.
 void enqueue_forward_bf16(nvfp4_moe_bank *bank, const void *x, const void *residual, void *out,
-                          int tokens, cudaStream_t stream) {
+                          int tokens, cudaStream_t stream, int out_f32 = 0) {
     const size_t row_bytes = static_cast<size_t>(bank->hidden) * 2;
+    const size_t out_row_bytes = static_cast<size_t>(bank->hidden) * (out_f32 ? 4 : 2);
     const bool prefill = tokens > kDecodeMaxTokens && prefill_supported(bank);
     const int slice = prefill ? (tokens < kPrefillMaxSlice ? tokens : kPrefillMaxSlice) : kDecodeMaxTokens;
     if (prefill) ensure_prefill(bank, slice);
@@ -323,11 +340,11 @@ void enqueue_forward_bf16(nvfp4_moe_bank *bank, const void *x, const void *resid
         const int n = tokens - t0 < slice ? tokens - t0 : slice;
         const uint8_t *xs = static_cast<const uint8_t *>(x) + t0 * row_bytes;
         const uint8_t *rs = residual ? static_cast<const uint8_t *>(residual) + t0 * row_bytes : nullptr;
-        uint8_t *os = static_cast<uint8_t *>(out) + t0 * row_bytes;
+        uint8_t *os = static_cast<uint8_t *>(out) + t0 * out_row_bytes;
         if (prefill)
-            enqueue_prefill(bank, xs, rs, os, n, stream);
+            enqueue_prefill(bank, xs, rs, os, out_f32, n, stream);
         else
-            enqueue_decode(bank, xs, 0, rs, os, 0, n, stream);
+            enqueue_decode(bank, xs, 0, rs, os, out_f32, n, stream);
     }
     bank->last_tokens = tokens;
     bank->last_path = tokens <= kDecodeMaxTokens ? 1 : (prefill && tokens <= slice ? 2 : 0);
@@ -355,6 +372,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
         auto holder = std::make_unique<nvfp4_moe_bank>();
         holder->runtime = runtime;
         holder->experts = experts;
+        holder->e_count = experts;
         holder->hidden = hidden;
         holder->intermediate = intermediate;
         const size_t slots = static_cast<size_t>(experts) + 1;
@@ -533,9 +551,8 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_decode_device_enqueue_f32(nvfp4
         x->bytes < static_cast<size_t>(bank->hidden) * sizeof(float) ||
         dst->bytes < static_cast<size_t>(bank->hidden) * sizeof(float))
         return fail_invalid("invalid MoE bank decode buffers");
-    const size_t slots = static_cast<size_t>(bank->experts) + 1;
-    if (bank->uploaded_projections != slots * 3)
-        return fail_invalid("MoE bank decode requires every routed and shared projection");
+    if (!bank->owned_uploaded())
+        return fail_invalid("MoE bank decode requires every routed and shared projection of its expert range");
     try {
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
@@ -557,18 +574,17 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(nvfp4_moe_bank
                                                                  void *dst_bf16, int tokens, int flags,
                                                                  void *stream) {
     if (!bank || !bank->runtime || !x_bf16 || !dst_bf16 || tokens <= 0 ||
-        (flags & ~static_cast<int>(NVFP4_MOE_ADD_RESIDUAL)) != 0 ||
+        (flags & ~static_cast<int>(NVFP4_MOE_ADD_RESIDUAL | NVFP4_MOE_PARTIAL_F32)) != 0 ||
         ((flags & NVFP4_MOE_ADD_RESIDUAL) && !residual_bf16))
         return fail_invalid("invalid MoE bank forward arguments");
-    const size_t slots = static_cast<size_t>(bank->experts) + 1;
-    if (bank->uploaded_projections != slots * 3)
-        return fail_invalid("MoE bank forward requires every routed and shared projection");
+    if (!bank->owned_uploaded())
+        return fail_invalid("MoE bank forward requires every routed and shared projection of its expert range");
     try {
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
         const void *res = (flags & NVFP4_MOE_ADD_RESIDUAL) ? residual_bf16 : nullptr;
         rt->profiled_call("moe_bank_forward", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
-            enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s);
+            enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s, (flags & NVFP4_MOE_PARTIAL_F32) ? 1 : 0);
         });
         clear_last_error();
         return NVFP4_STATUS_OK;
@@ -584,7 +600,8 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_device_enqueue_bf16(
         dst->runtime != bank->runtime || tokens <= 0)
         return fail_invalid("invalid MoE bank forward buffers");
     const size_t bytes = static_cast<size_t>(tokens) * bank->hidden * 2;
-    if (x->bytes < bytes || dst->bytes < bytes)
+    const size_t dst_bytes = bytes * ((flags & NVFP4_MOE_PARTIAL_F32) ? 2 : 1);
+    if (x->bytes < bytes || dst->bytes < dst_bytes)
         return fail_invalid("MoE bank forward buffer capacity is too small");
     if (flags & NVFP4_MOE_ADD_RESIDUAL) {
         if (!residual || residual->runtime != bank->runtime || residual->bytes < bytes)
@@ -715,6 +732,19 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_prefill_terms(nvfp4_moe_ban
     std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
     bank->terms_x = x_terms;
     bank->terms_act = act_terms;
+    clear_last_error();
+    return NVFP4_STATUS_OK;
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_expert_range(nvfp4_moe_bank *bank, int first, int count,
+                                                                  int shared_here) {
+    if (!bank || !bank->runtime || first < 0 || count < 1 || first + count > bank->experts ||
+        (shared_here != 0 && shared_here != 1))
+        return fail_invalid("expert range must lie within [0, experts) and hold at least one expert");
+    std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
+    bank->e_first = first;
+    bank->e_count = count;
+    bank->shared_here = shared_here;
     clear_last_error();
     return NVFP4_STATUS_OK;
 }

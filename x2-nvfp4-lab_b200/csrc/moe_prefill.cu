@@ -381,16 +381,19 @@ __global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int
 
     const int i = threadIdx.x;
     const int cnt = i < E ? __ldcg(s.counts + i) : 0;
-    const int ntile = (cnt + kPrefillTileN - 1) / kPrefillTileN;
+    // Only the experts computed here get padded rows, groups and tiles.
+    const bool own = i >= s.e_first && i < s.e_first + s.e_count;
+    const int ocnt = own ? cnt : 0;
+    const int ntile = (ocnt + kPrefillTileN - 1) / kPrefillTileN;
     int n_off = 0, n_act = 0, n_tiles = 0, n_pad = 0;
     const int off = block_excl_scan256(cnt, warp_sums, &n_off);
-    const int ai = block_excl_scan256(cnt > 0 ? 1 : 0, warp_sums, &n_act);
+    const int ai = block_excl_scan256(ocnt > 0 ? 1 : 0, warp_sums, &n_act);
     const int tile0 = block_excl_scan256(ntile, warp_sums, &n_tiles);
     const int pst = block_excl_scan256(ntile * kPrefillTileN, warp_sums, &n_pad);
     if (i < E) {
         s.offsets[i] = off;
         s.epstart[i] = pst;
-        if (cnt > 0) {
+        if (ocnt > 0) {
             s.active_expert[ai] = i;
             s.tok_start[ai] = pst;
             s.tok_count[ai] = cnt;
@@ -400,7 +403,7 @@ __global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int
             }
         }
     }
-    const int shared_tiles = (T + kPrefillTileN - 1) / kPrefillTileN;
+    const int shared_tiles = s.shared_here ? (T + kPrefillTileN - 1) / kPrefillTileN : 0;
     for (int j = i; j < shared_tiles; j += blockDim.x) {
         s.tile_group[n_tiles + j] = n_act;
         s.tile_n0[n_tiles + j] = n_pad + j * kPrefillTileN;
@@ -408,10 +411,12 @@ __global__ void __launch_bounds__(256) prefill_scan_kernel(PrefillScratch s, int
     if (i == 0) {
         s.offsets[E] = n_off;
         s.epstart[E] = n_pad;
-        s.active_expert[n_act] = E;
-        s.tok_start[n_act] = n_pad;
-        s.tok_count[n_act] = T;
-        *s.n_active = n_act + 1;
+        if (s.shared_here) {
+            s.active_expert[n_act] = E;
+            s.tok_start[n_act] = n_pad;
+            s.tok_count[n_act] = T;
+        }
+        *s.n_active = n_act + (s.shared_here ? 1 : 0);
         *s.n_tiles = n_tiles + shared_tiles;
         *s.rows_used = n_pad + shared_tiles * kPrefillTileN;
         *s.ticket = 0u;
@@ -431,12 +436,16 @@ __global__ void prefill_place_kernel(PrefillScratch s, int T, const float *inv_s
         const int b = t >> 6;
         const unsigned long long m = s.blk_mask[(size_t)e * s.mask_stride + b];
         const int rank = s.blk_base[(size_t)e * s.mask_stride + b] + __popcll(m & ((1ull << (t & 63)) - 1ull));
-        const int row = s.epstart[e] + rank;
         s.perm[s.offsets[e] + rank] = i;
+        if (e < s.e_first || e >= s.e_first + s.e_count) {
+            s.inv_pos[i] = -1;  // computed on another rank
+            return;
+        }
+        const int row = s.epstart[e] + rank;
         s.tok_list[row] = t;
         s.inv_pos[i] = row;
         s.coef[row] = s.weights[t * kSlots + k] * inv_down[e];
-    } else if (i < T * kSlots) {
+    } else if (i < T * kSlots && s.shared_here) {
         const int t = i - T * kTopK;
         const int row = s.epstart[E] + t;
         s.tok_list[row] = t;
@@ -496,7 +505,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
     if (MODE == kTokenAtoms && valid) {
 #pragma unroll
         for (int k = 0; k < kTopK; ++k) dst_rows[k] = q.inv_pos[r * kTopK + k];
-        dst_rows[kTopK] = *q.shared_row0 + r;
+        dst_rows[kTopK] = q.shared_row0 ? *q.shared_row0 + r : -1;
     }
     const int esz = src_kind == 2 ? 4 : 2;
     const uint8_t *row = static_cast<const uint8_t *>(src) + (size_t)r * cols * esz;
@@ -597,6 +606,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
                 // The token's codes and scales go to each of its nine slot rows.
 #pragma unroll
                 for (int k = 0; k < kSlots; ++k) {
+                    if (dst_rows[k] < 0) continue;  // slot computed on another rank
                     uint4 *dst = reinterpret_cast<uint4 *>(
                         codes + ((size_t)j * rows_stride + dst_rows[k]) * (cols / 2) + ch * 32);
                     dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
@@ -615,7 +625,7 @@ __global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int
 // then the shared slot, then the BF16 residual (the decode combine order).
 // Each thread handles 8 consecutive h.
 __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillScratch s, int T, const uint16_t *residual,
-                                                              uint16_t *out) {
+                                                              void *out, int out_f32) {
     const int t = blockIdx.y;
     const int H = s.H;
     const int h = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
@@ -634,8 +644,11 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillScratch s, 
         }
     };
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) add_row(s.inv_pos[t * kTopK + k]);
-    add_row(s.epstart[s.E] + t);
+    for (int k = 0; k < kTopK; ++k) {
+        const int pos = s.inv_pos[t * kTopK + k];
+        if (pos >= 0) add_row(pos);  // -1: the slot's expert is computed on another rank
+    }
+    if (s.shared_here) add_row(s.epstart[s.E] + t);
     uint32_t o[4];
     if (residual) {
         const uint4 u = __ldg(reinterpret_cast<const uint4 *>(residual + (size_t)t * H + h));
@@ -646,9 +659,15 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PrefillScratch s, 
             acc[2 * i + 1] += bf16_bits_to_f32(w[i] >> 16);
         }
     }
+    if (out_f32) {
+        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(out) + (size_t)t * H + h);
+        dst[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        return;
+    }
 #pragma unroll
     for (int i = 0; i < 4; ++i) o[i] = f32_to_bf16_bits(acc[2 * i]) | (f32_to_bf16_bits(acc[2 * i + 1]) << 16);
-    *reinterpret_cast<uint4 *>(out + (size_t)t * H + h) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4 *>(static_cast<uint16_t *>(out) + (size_t)t * H + h) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 __global__ void scale_atoms_kernel(uint8_t *atoms, const uint8_t *scales, size_t pitch, int rows, int k16,
@@ -810,7 +829,7 @@ cudaError_t launch_quantize_x_prefill(const void *x, int T, const PrefillScratch
     q.rows_stride = s.max_rows;
     q.atom_blocks = s.max_rows / kPrefillTileN;
     q.inv_pos = s.inv_pos;
-    q.shared_row0 = s.epstart + s.E;
+    q.shared_row0 = s.shared_here ? s.epstart + s.E : nullptr;
     return launch_quantize_mode<kTokenAtoms>(x, 0, T, s.H, terms, q, stream);
 }
 
@@ -825,11 +844,10 @@ cudaError_t launch_quantize_act_prefill(const PrefillScratch &s, int terms, cuda
     return launch_quantize_mode<kRowAtoms>(s.act, 1, s.max_rows, s.I, terms, q, stream);
 }
 
-cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out,
+cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out, int out_f32,
                                    cudaStream_t stream) {
     const dim3 grid((s.H / 8 + 255) / 256, T);
-    prefill_combine_kernel<<<grid, 256, 0, stream>>>(s, T, static_cast<const uint16_t *>(residual),
-                                                     static_cast<uint16_t *>(out));
+    prefill_combine_kernel<<<grid, 256, 0, stream>>>(s, T, static_cast<const uint16_t *>(residual), out, out_f32);
     return cudaGetLastError();
 }
 

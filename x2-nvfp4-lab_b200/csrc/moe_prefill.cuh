@@ -78,6 +78,10 @@ struct PrefillScratch {
     int *error;              // device error word (shared with the decode scratch)
     int *host_error;         // host-mapped error word or nullptr
     int max_tiles;
+    // Experts computed here (expert parallelism): routed [e_first,
+    // e_first + e_count) and the shared expert when shared_here. Routing and
+    // the routing ABI's counts, offsets and permutation cover every expert.
+    int e_first, e_count, shared_here;
 };
 
 // TMA descriptors of one prefill scratch (activation terms) and a bank's
@@ -132,7 +136,9 @@ cudaError_t launch_quantize_x_prefill(const void *x, int T, const PrefillScratch
 cudaError_t launch_quantize_act_prefill(const PrefillScratch &s, int terms, cudaStream_t stream);
 cudaError_t launch_gemm_gate_up(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream);
 cudaError_t launch_gemm_down(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream);
-cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out,
+// out: BF16 [T][H], or FP32 when out_f32 (a partial sum for expert
+// parallelism); residual (BF16) is added when given.
+cudaError_t launch_prefill_combine(const PrefillScratch &s, int T, const void *residual, void *out, int out_f32,
                                    cudaStream_t stream);
 
 }  // namespace nvfp4

@@ -537,12 +537,11 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(DownArgs a) {
             if (pos[k] >= 0) v += s.ypart[(size_t)pos[k] * H + h];
         if (a.shared_here) v += s.ypart[(size_t)(T * kTopK + t) * H + h];
         const size_t o = (size_t)t * H + h;
-        if (a.out_f32) {
+        if (a.residual) v += bf16_bits_to_f32(static_cast<const uint16_t *>(a.residual)[o]);
+        if (a.out_f32)
             static_cast<float *>(a.out)[o] = v;
-        } else {
-            if (a.residual) v += bf16_bits_to_f32(static_cast<const uint16_t *>(a.residual)[o]);
+        else
             static_cast<uint16_t *>(a.out)[o] = f32_to_bf16_bits(v);
-        }
     }
 }
 

@@ -24,6 +24,7 @@ import numpy as np
 
 LIB_NAME = "libnvfp4_moe_cuda.so"
 NVFP4_MOE_ADD_RESIDUAL = 1
+NVFP4_MOE_PARTIAL_F32 = 2
 NVFP4_DECODE_KERNELS_TENSOR_CORE = 0
 NVFP4_DECODE_KERNELS_IN_REGISTER = 1
 
@@ -161,6 +162,9 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "nvfp4_moe_bank_set_prefill_terms": ([C.c_void_p, C.c_int, C.c_int], C.c_int),
     "nvfp4_moe_bank_reserve_prefill": ([C.c_void_p, C.c_int], C.c_int),
     "nvfp4_moe_bank_set_decode_kernels": ([C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_moe_bank_set_expert_range": ([C.c_void_p, C.c_int, C.c_int, C.c_int], C.c_int),
+    "nvfp4_moe_finalize_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "nvfp4_quantize_rows_enqueue": (
         [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
         C.c_int),
@@ -180,6 +184,17 @@ def load_library(path: Path | None = None) -> C.CDLL:
         fn.argtypes = argtypes
         fn.restype = restype
     return lib
+
+
+# cudaStreamLegacy: the legacy default stream as an explicit handle.
+CUDA_STREAM_LEGACY = 1
+
+
+def _stream_handle(stream) -> C.c_void_p:
+    """Handle of a torch.cuda.Stream for the C ABI. torch's default stream has
+    handle 0, which the ABI would read as "the runtime's own stream" (not
+    ordered with torch's work), so it is passed as cudaStreamLegacy."""
+    return C.c_void_p(stream.cuda_stream or CUDA_STREAM_LEGACY)
 
 
 def _ptr(array: np.ndarray) -> C.c_void_p:
@@ -352,11 +367,48 @@ class MoeBank:
         self.runtime._check(
             self.runtime.lib.nvfp4_moe_bank_forward_ptr_bf16(
                 self.handle, _tensor_ptr(x), _tensor_ptr(residual) if residual is not None else None,
-                _tensor_ptr(out), x.shape[0], flags, C.c_void_p(s.cuda_stream),
+                _tensor_ptr(out), x.shape[0], flags, _stream_handle(s),
             ),
             "nvfp4_moe_bank_forward_ptr_bf16",
         )
         return out
+
+    def forward_partial(self, x, out=None, residual=None, stream=None):
+        """additive (expert parallelism): FP32 [tokens, hidden] partial sum of
+        this bank's expert range (set_expert_range), plus ``residual`` when
+        given. Summing the partials of ranks that cover every expert once
+        gives the layer output before its BF16 rounding."""
+        import torch
+
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError("x must be a CUDA bfloat16 tensor [tokens, hidden]")
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+        if out.dtype != torch.float32 or out.shape != x.shape or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 tensor shaped like x")
+        flags = NVFP4_MOE_PARTIAL_F32
+        if residual is not None:
+            if residual.shape != x.shape or residual.dtype != torch.bfloat16 or not residual.is_cuda:
+                raise ValueError("residual must match x")
+            residual = residual.contiguous()
+            flags |= NVFP4_MOE_ADD_RESIDUAL
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_forward_ptr_bf16(
+                self.handle, _tensor_ptr(x), _tensor_ptr(residual) if residual is not None else None,
+                _tensor_ptr(out), x.shape[0], flags, _stream_handle(s),
+            ),
+            "nvfp4_moe_bank_forward_ptr_bf16",
+        )
+        return out
+
+    def set_expert_range(self, first: int, count: int, shared_here: bool) -> None:
+        """additive (expert parallelism): compute routed experts [first, first + count)
+        and the shared expert when ``shared_here``."""
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_set_expert_range(self.handle, first, count, 1 if shared_here else 0),
+            "nvfp4_moe_bank_set_expert_range")
 
     def last_routing(self, max_tokens: int) -> Routing:
         """additive: routing of the most recent call (synchronises)."""
@@ -617,6 +669,28 @@ class Runtime:
         )
         return out
 
+    def finalize_bf16(self, sum_f32, residual=None, out=None, stream=None):
+        """additive (expert parallelism): BF16(sum_f32 + residual) for torch CUDA
+        tensors [tokens, hidden] (sum FP32, residual BF16 or None)."""
+        import torch
+
+        if sum_f32.dtype != torch.float32 or not sum_f32.is_cuda or sum_f32.dim() != 2:
+            raise ValueError("sum_f32 must be a CUDA float32 tensor [tokens, hidden]")
+        sum_f32 = sum_f32.contiguous()
+        if out is None:
+            out = torch.empty(sum_f32.shape, dtype=torch.bfloat16, device=sum_f32.device)
+        if residual is not None:
+            if residual.shape != sum_f32.shape or residual.dtype != torch.bfloat16:
+                raise ValueError("residual must be bfloat16 shaped like sum_f32")
+            residual = residual.contiguous()
+        s = stream if stream is not None else torch.cuda.current_stream(sum_f32.device)
+        self._check(
+            self.lib.nvfp4_moe_finalize_bf16(
+                self.handle, _tensor_ptr(sum_f32), _tensor_ptr(residual) if residual is not None else None,
+                _tensor_ptr(out), sum_f32.shape[0], sum_f32.shape[1], _stream_handle(s)),
+            "nvfp4_moe_finalize_bf16")
+        return out
+
     def quantize_rows(self, x, terms: int):
         """additive: split BF16/FP16 rows [rows, cols] (a CUDA tensor) into
         `terms` NVFP4 terms on torch's current stream. Returns (codes uint8
@@ -631,11 +705,11 @@ class Runtime:
         codes = torch.empty(terms, rows, cols // 2, dtype=torch.uint8, device=x.device)
         words = torch.empty(terms, rows, cols // 64, dtype=torch.int32, device=x.device)
         g = torch.empty(rows, dtype=torch.float32, device=x.device)
-        stream = torch.cuda.current_stream(x.device).cuda_stream
+        stream = torch.cuda.current_stream(x.device)
         self._check(
             self.lib.nvfp4_quantize_rows_enqueue(
                 _tensor_ptr(x), 1 if x.dtype == torch.float16 else 0, rows, cols, terms, _tensor_ptr(codes),
-                _tensor_ptr(words), _tensor_ptr(g), C.c_void_p(stream)),
+                _tensor_ptr(words), _tensor_ptr(g), _stream_handle(stream)),
             "nvfp4_quantize_rows_enqueue",
         )
         return codes, words, g
