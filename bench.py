@@ -88,7 +88,7 @@ class ClockSampler:
         "sw_power_cap": 0x4,
     }
 
-    def __init__(self, index: int, interval: float = 0.02):
+    def __init__(self, index: int, interval: float = 0.005):
         self.index = index
         self.interval = interval
         self.samples: list[tuple[float, int]] = []
@@ -284,6 +284,51 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     }
 
 
+def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmup: int) -> dict:
+    """Expert parallelism across the job's GPUs: rank r holds routed experts
+    [r*E/N, (r+1)*E/N) (the shared expert on rank 0), the tokens are the same
+    on every rank, each rank computes its FP32 partial sum and a NCCL
+    all-reduce adds them (vllm_nvfp4_cuda.expert_parallel). Per-call device
+    time (CUDA events on the launching stream, L2 flushed before each call,
+    max over ranks) of one layer call at batch 32, one token and 4096 tokens."""
+    import torch
+
+    from vllm_nvfp4_cuda import synthetic
+    from vllm_nvfp4_cuda.expert_parallel import ExpertParallelLayer
+
+    layer = ExpertParallelLayer(bank, finalize=lambda t: rt.finalize_bf16(t))
+    out = {"ranks": world, "experts_per_rank": layer.range.count,
+           "collective": "NCCL all_reduce of the FP32 [tokens, hidden] partial sums", "calls": {}}
+    for name, T in (("decode_batch32", 32), ("decode_one_token", 1), ("prefill4096", 4096)):
+        x = synthetic.synthetic_tokens(T, H, seed + 70)   # identical on every rank
+        r = synthetic.synthetic_tokens(T, H, seed + 71)
+        n = steps if T <= 64 else min(steps, 10)
+        with torch.cuda.stream(stream):
+            for _ in range(warmup):
+                flush.zero_()
+                layer.forward(x, r)
+        stream.synchronize()
+        pg.barrier()
+        torch.cuda.synchronize()
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+        with torch.cuda.stream(stream):
+            torch.cuda._sleep(int(2e5) * n)
+            for i in range(n):
+                flush.zero_()
+                ev[i][0].record(stream)
+                layer.forward(x, r)
+                ev[i][1].record(stream)
+        stream.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev) / n
+        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        ms = float(t.item())
+        out["calls"][name] = {"tokens": T, "us_per_call": round(ms * 1000.0, 2),
+                              "tokens_per_s": round(T / (ms / 1000.0), 1)}
+    bank.set_expert_range(0, E, True)
+    return out
+
+
 def traced_steps(rt, stream, flush, step, n: int):
     """Run `step(i)` n times with the runtime trace on (L2 flushed before each
     step) and return the trace events: per-kernel device durations."""
@@ -323,6 +368,10 @@ def run_ours(args) -> int:
     from vllm_nvfp4_cuda.runtime import Runtime
 
     T = args.tokens
+    # The library runs calls of 12 to 32 tokens on the tensor-core expert
+    # GEMVs for this shape (five launches per layer call), others in-register
+    # (four launches).
+    tc_decode = 12 <= T <= 32
     rt = Runtime()
     bank, meta = synthetic.build_bank(rt, E, H, I, args.seed)
     stream = torch.cuda.Stream()
@@ -358,19 +407,21 @@ def run_ours(args) -> int:
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(local) as clocks:
-        with torch.cuda.stream(stream):
-            # A bounded spin kernel ahead of the first event lets the host
-            # enqueue every step before the GPU reaches it, so each event
-            # pair brackets device work only.
-            torch.cuda._sleep(int(2e5) * args.steps)
-            for i in range(args.steps):
-                flush.zero_()
-                starts[i].record(stream)
-                step(i)
-                ends[i].record(stream)
-        stream.synchronize()
-        rt.synchronize()
+    # Clocks are sampled from the timed decode steps through the one-token and
+    # prefill legs (all device-busy stretches).
+    clocks = ClockSampler(local).__enter__()
+    with torch.cuda.stream(stream):
+        # A bounded spin kernel ahead of the first event lets the host
+        # enqueue every step before the GPU reaches it, so each event
+        # pair brackets device work only.
+        torch.cuda._sleep(int(2e5) * args.steps)
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step(i)
+            ends[i].record(stream)
+    stream.synchronize()
+    rt.synchronize()
     # Per-kernel durations come from a second, traced pass over the same steps
     # (tracing records an event pair around every kernel, which would also
     # serialise the dependent launches of the timed pass).
@@ -423,10 +474,15 @@ def run_ours(args) -> int:
     for evt in traced_steps(rt, stream, flush, lambda i: bank.forward(x1[i % pool_n], out=o1, stream=stream), 20):
         t1_ops.setdefault(evt.operation, []).append(evt.duration_ns / 1e3)
 
+    ep = None
+    if world > 1:
+        ep = ep_leg(rt, bank, stream, flush, pg, world, args.seed, args.steps, 3)
+
     prefill = []
     if not args.no_prefill:
         prefill.append(prefill_leg(rt, bank, stream, flush, 4096, args.seed, 10, 3, skew=False))
         prefill.append(prefill_leg(rt, bank, stream, flush, 8192, args.seed, 10, 3, skew=True))
+    clocks.__exit__(None, None, None)
 
     # End to end through the lab-style C-ABI sequence with host buffers.
     host_x = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
@@ -482,7 +538,8 @@ def run_ours(args) -> int:
             "higher_is_better": True,
             "scaling": "weak",
             "vs_baseline": None,
-            "dtype": "nvfp4 weights x f16 activations, f32 accumulate; bf16 I/O",
+            "dtype": ("nvfp4 weights x nvfp4 activations (four terms per row) on tcgen05, f32 accumulate; bf16 I/O"
+                      if tc_decode else "nvfp4 weights x f16 activations, f32 accumulate; bf16 I/O"),
             "data": "synthetic (seeded BASELINE distributions; no checkpoint on this machine)",
             "config": {
                 "workload": WORKLOAD,
@@ -518,8 +575,9 @@ def run_ours(args) -> int:
             },
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
-            "gpu_launches": 4 * args.steps,
+            "gpu_launches": (5 if tc_decode else 4) * args.steps,
             "prefill": prefill,
+            "expert_parallel": ep,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
