@@ -190,7 +190,9 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         ta.sfb = bank->ds.xsf_tc;
         rt->profiled_kernel("moe_gate_up", stream, [&](cudaStream_t s) {
             check_cuda(launch_gate_up_tc(bank->pmaps.w[0], bank->pmaps.w[1], bank->tc_maps, ta, tokens, sms, s),
-                       "moe_gemv_tc_kernel(gate/up)");
+                       "moe_gate_up_tc_kernel");
+        });
+        rt->profiled_kernel("moe_quantize_act", stream, [&](cudaStream_t s) {
             check_cuda(launch_quantize_act_tc(bank->ds, tokens, I, s), "quantize_act_tc_kernel");
         });
         ta.sfa[0] = bank->sf_atoms[2];
@@ -198,7 +200,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         ta.sfb = bank->ds.asf_tc;
         rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
             check_cuda(launch_down_tc(bank->pmaps.w[2], bank->tc_maps, ta, tokens, sms, s),
-                       "moe_gemv_tc_kernel(down)");
+                       "moe_down_tc_kernel");
             check_cuda(launch_combine(da, s), "moe_combine_kernel");
         });
         return;

@@ -391,8 +391,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         int prev_ai = -1;
         bool ok = true;
         if (lane == 0) {
+            Item ti{};
             for (int item = lo; item < hi && ok; ++item) {
-                const Item ti = load_item(s, item, mtiles);
+                // Consecutive items mostly share their group: its metadata is
+                // loaded once per group.
+                if (item / mtiles != prev_ai) {
+                    ti = load_item(s, item, mtiles);
+                } else {
+                    ti.mt = item - ti.ai * mtiles;
+                }
                 if (ti.ai != prev_ai) {
                     const uint32_t bb = nb & 1u, use = nb >> 1;
                     if (use > 0 && !mbar_wait(bempty + bb, (use - 1) & 1u, err, kSiteGemmEmpty)) {
@@ -498,15 +505,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int sub = warp & 3;
         const int et = threadIdx.x - 64;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
-        uint32_t tcount = 0;
+        uint32_t tcount = 0, gcount = 0;
+        Item ti{};
+        ti.ai = -1;
         for (int item = lo; item < hi; ++item, ++tcount) {
-            const Item ti = load_item(s, item, mtiles);
-            float *cscale = col_scale + 32 * (tcount & 1);
-            if (et < ti.ntok) {
-                const int p = ti.tstart + et;
-                const int t = s.tok_list[p];
-                cscale[et] = s.ga_tc[p] * s.coef_tab[ti.ai * kDecodeMaxTokens + t];
+            // Group metadata and the per-row scales change only with the group
+            // (double-buffered by group count: a warp still computing the
+            // previous item reads the other buffer).
+            if (item / mtiles != ti.ai) {
+                ti = load_item(s, item, mtiles);
+                ++gcount;
+                if (et < ti.ntok) {
+                    const int p = ti.tstart + et;
+                    const int t = s.tok_list[p];
+                    col_scale[32 * (gcount & 1) + et] = s.ga_tc[p] * s.coef_tab[ti.ai * kDecodeMaxTokens + t];
+                }
+            } else {
+                ti.mt = item - ti.ai * mtiles;
             }
+            const float *cscale = col_scale + 32 * (gcount & 1);
             const uint32_t buf = tcount & 1u;
             if (et == 0) *acc_ok = mbar_wait(acc_full + buf, (tcount >> 1) & 1u, err, kSiteGemmAccFull) ? 1 : 0;
             named_barrier(1, 128);
