@@ -59,6 +59,8 @@ def parse_args():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill legs (configs 2 and 3)")
+    p.add_argument("--decode-kernels", choices=["tensor_core", "in_register"], default="tensor_core",
+                   help="decode expert GEMVs (the library's default is tensor_core)")
     return p.parse_args()
 
 
@@ -371,9 +373,10 @@ def run_ours(args) -> int:
     # The library runs calls of 12 to 32 tokens on the tensor-core expert
     # GEMVs for this shape (five launches per layer call), others in-register
     # (four launches).
-    tc_decode = 12 <= T <= 32
+    tc_decode = 12 <= T <= 32 and args.decode_kernels == "tensor_core"
     rt = Runtime()
     bank, meta = synthetic.build_bank(rt, E, H, I, args.seed)
+    bank.set_decode_kernels(args.decode_kernels)
     stream = torch.cuda.Stream()
     pool_n = 16
     pool = [synthetic.synthetic_tokens(T, H, 1000 * (rank + 1) + i) for i in range(pool_n)]
