@@ -289,44 +289,62 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
 def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmup: int) -> dict:
     """Expert parallelism across the job's GPUs: rank r holds routed experts
     [r*E/N, (r+1)*E/N) (the shared expert on rank 0), the tokens are the same
-    on every rank, each rank computes its FP32 partial sum and a NCCL
-    all-reduce adds them (vllm_nvfp4_cuda.expert_parallel). Per-call device
-    time (CUDA events on the launching stream, L2 flushed before each call,
-    max over ranks) of one layer call at batch 32, one token and 4096 tokens."""
+    on every rank. Two reductions of the ranks' partial sums: NCCL all-reduce
+    of FP32 partials + finalize (every size), and the combine fused with the
+    reduction over NVLink peer memory (calls of up to 64 tokens). Per-call
+    device time (CUDA events on the launching stream, L2 flushed before each
+    call, max over ranks), and each output's relative RMSE against the
+    single-GPU bank (full expert range) on the same tokens."""
     import torch
 
     from vllm_nvfp4_cuda import synthetic
     from vllm_nvfp4_cuda.expert_parallel import ExpertParallelLayer
 
-    layer = ExpertParallelLayer(bank, finalize=lambda t: rt.finalize_bf16(t))
-    out = {"ranks": world, "experts_per_rank": layer.range.count,
-           "collective": "NCCL all_reduce of the FP32 [tokens, hidden] partial sums", "calls": {}}
-    for name, T in (("decode_batch32", 32), ("decode_one_token", 1), ("prefill4096", 4096)):
-        x = synthetic.synthetic_tokens(T, H, seed + 70)   # identical on every rank
-        r = synthetic.synthetic_tokens(T, H, seed + 71)
-        n = steps if T <= 64 else min(steps, 10)
-        with torch.cuda.stream(stream):
-            for _ in range(warmup):
-                flush.zero_()
-                layer.forward(x, r)
-        stream.synchronize()
-        pg.barrier()
-        torch.cuda.synchronize()
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
-        with torch.cuda.stream(stream):
-            torch.cuda._sleep(int(2e5) * n)
-            for i in range(n):
-                flush.zero_()
-                ev[i][0].record(stream)
-                layer.forward(x, r)
-                ev[i][1].record(stream)
-        stream.synchronize()
-        ms = sum(a.elapsed_time(b) for a, b in ev) / n
-        t = torch.tensor([ms], device="cuda", dtype=torch.float64)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        ms = float(t.item())
-        out["calls"][name] = {"tokens": T, "us_per_call": round(ms * 1000.0, 2),
-                              "tokens_per_s": round(T / (ms / 1000.0), 1)}
+    cases = (("decode_batch32", 32), ("decode_one_token", 1), ("prefill4096", 4096))
+    data = {name: (synthetic.synthetic_tokens(T, H, seed + 70), synthetic.synthetic_tokens(T, H, seed + 71))
+            for name, T in cases}
+    refs = {name: bank.forward(x, residual=r).float() for name, (x, r) in data.items()}
+    torch.cuda.synchronize()
+    finalize = lambda t: rt.finalize_bf16(t)  # noqa: E731
+    layers = {"nccl_all_reduce": ExpertParallelLayer(bank, finalize),
+              "fused_combine_p2p": ExpertParallelLayer(bank, finalize, fused_runtime=rt)}
+    out = {"ranks": world, "experts_per_rank": layers["nccl_all_reduce"].range.count,
+           "reductions": {"nccl_all_reduce": "NCCL all_reduce of the FP32 [tokens, hidden] partials + finalize",
+                          "fused_combine_p2p": "combine kernel reads every rank's partial tile over NVLink"},
+           "calls": {}}
+    for kind, layer in layers.items():
+        for name, T in cases:
+            if kind == "fused_combine_p2p" and T > 64:
+                continue
+            x, r = data[name]
+            n = steps if T <= 64 else min(steps, 10)
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    flush.zero_()
+                    y = layer.forward(x, r)
+            stream.synchronize()
+            err = float(((y.float() - refs[name]).pow(2).mean() / refs[name].pow(2).mean()).sqrt())
+            pg.barrier()
+            torch.cuda.synchronize()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
+            with torch.cuda.stream(stream):
+                torch.cuda._sleep(int(2e5) * n)
+                for i in range(n):
+                    flush.zero_()
+                    ev[i][0].record(stream)
+                    layer.forward(x, r)
+                    ev[i][1].record(stream)
+            stream.synchronize()
+            rt.synchronize()
+            ms = sum(a.elapsed_time(b) for a, b in ev) / n
+            t = torch.tensor([ms, err], device="cuda", dtype=torch.float64)
+            pg.all_reduce(t, op=pg.ReduceOp.MAX)
+            ms, err = float(t[0].item()), float(t[1].item())
+            out["calls"].setdefault(kind, {})[name] = {
+                "tokens": T, "us_per_call": round(ms * 1000.0, 2), "tokens_per_s": round(T / (ms / 1000.0), 1),
+                "rel_rmse_vs_single_gpu": float(f"{err:.3g}")}
+    layers["fused_combine_p2p"].close()
+    pg.barrier()
     bank.set_expert_range(0, E, True)
     return out
 

@@ -37,6 +37,7 @@ extern "C" {
 typedef struct nvfp4_runtime nvfp4_runtime;
 typedef struct nvfp4_moe_bank nvfp4_moe_bank;
 typedef struct nvfp4_buffer nvfp4_buffer;
+typedef struct nvfp4_ep nvfp4_ep;
 
 /* reference: nvfp4_runtime.h:33-39. Code 2 keeps its slot; on this backend it
  * reports a CUDA runtime error instead of an OpenCL one. */
@@ -390,6 +391,45 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_set_expert_range(
     int first,
     int count,
     int shared_here);
+
+/* additive: expert parallelism with the reduction fused into the combine
+ * (no counterpart in the lab, which runs one device). One context per rank
+ * (one process per GPU): nvfp4_ep_create allocates this rank's partial
+ * buffers and flags, nvfp4_ep_ipc_handle exports them (NVFP4_EP_HANDLE_BYTES
+ * bytes), every rank gathers all ranks' handles in rank order (any host
+ * collective) and passes them to nvfp4_ep_open_peers. Then
+ * nvfp4_moe_bank_forward_ep_bf16, called on every rank with the same tokens
+ * (up to max_tokens <= 64) on banks whose expert ranges cover every expert
+ * once, writes the whole layer's BF16 output on every rank: the combine adds
+ * the ranks' partial tiles over NVLink peer memory (each wait bounded; a
+ * timeout is reported by nvfp4_runtime_synchronize as INTERNAL). The
+ * residual, when flagged, is added once. Calls must alternate no further
+ * than one call ahead between ranks, which stream order on each rank
+ * guarantees. */
+#define NVFP4_EP_HANDLE_BYTES 64
+NVFP4_API nvfp4_status nvfp4_ep_create(
+    nvfp4_runtime * runtime,
+    int rank,
+    int world,
+    int max_tokens,
+    int hidden,
+    nvfp4_ep ** out_ep);
+NVFP4_API nvfp4_status nvfp4_ep_ipc_handle(
+    nvfp4_ep * ep,
+    void * handle);
+NVFP4_API nvfp4_status nvfp4_ep_open_peers(
+    nvfp4_ep * ep,
+    const void * handles);
+NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ep_bf16(
+    nvfp4_moe_bank * bank,
+    nvfp4_ep * ep,
+    const void * x_bf16,
+    const void * residual_bf16,
+    void * dst_bf16,
+    int tokens,
+    int flags,
+    void * stream);
+NVFP4_API void nvfp4_ep_destroy(nvfp4_ep * ep);
 
 /* additive: out = BF16(sum + residual) over [tokens, hidden], with sum FP32
  * (the reduced partial sums of expert-parallel banks) and residual BF16 or

@@ -95,3 +95,29 @@ def test_forward_needs_owned_projections_only(cuda_runtime, ep_host, ep_banks):
             b.forward_partial(bits_to_bf16_tensor(synthetic_np.tokens_bf16(2, H, 5)))
     finally:
         b.set_expert_range(E // 2, E // 2, False)
+
+
+def test_fused_combine_single_rank_matches_forward(cuda_runtime, ep_host, ep_banks):
+    """A one-rank context runs the fused combine without peers: the output must
+    equal the plain forward bit for bit (same additions in the same order),
+    over several calls (both buffer parities) and both decode variants."""
+    import torch
+
+    from vllm_nvfp4_cuda.runtime import EpContext
+
+    full, _, _ = ep_banks
+    ep = EpContext(cuda_runtime, 0, 1, 64, H)
+    ep.open_peers([ep.ipc_handle()])
+    try:
+        for T in (1, 16, 32, 64, 16):
+            x = bits_to_bf16_tensor(synthetic_np.tokens_bf16(T, H, 1200 + T))
+            r = bits_to_bf16_tensor(synthetic_np.tokens_bf16(T, H, 1300 + T))
+            ref = full.forward(x, residual=r)
+            got = full.forward_ep(ep, x, residual=r)
+            torch.cuda.synchronize()
+            cuda_runtime.synchronize()
+            assert torch.equal(got, ref), T
+        with pytest.raises(RuntimeError):
+            full.forward_ep(ep, bits_to_bf16_tensor(synthetic_np.tokens_bf16(65, H, 1)))
+    finally:
+        ep.close()

@@ -18,6 +18,10 @@
 
 using namespace nvfp4;
 
+namespace nvfp4 {
+bool ep_next_call(nvfp4_ep *ep, int tokens, int hidden, EpArgs *out);  // moe_ep.cu
+}
+
 struct nvfp4_moe_bank {
     nvfp4_runtime *runtime = nullptr;
     int experts = 0;
@@ -142,7 +146,7 @@ bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
 }
 
 void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const void *residual,
-                    void *out, int out_f32, int tokens, cudaStream_t stream) {
+                    void *out, int out_f32, int tokens, cudaStream_t stream, const EpArgs *ep = nullptr) {
     const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
     const int sms = bank->runtime->sm_count;
     const bool tc = use_tensor_core_decode(bank, tokens);
@@ -201,7 +205,10 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
             check_cuda(launch_down_tc(bank->pmaps.w[2], bank->tc_maps, ta, tokens, sms, s),
                        "moe_down_tc_kernel");
-            check_cuda(launch_combine(da, s), "moe_combine_kernel");
+            if (ep)
+                check_cuda(launch_combine_ep(da, *ep, s), "moe_combine_ep_kernel");
+            else
+                check_cuda(launch_combine(da, s), "moe_combine_kernel");
         });
         return;
     }
@@ -221,7 +228,8 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     });
 
     rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
-        check_cuda(launch_down_tma(bank->maps, da, sms, s), "moe_down_tma_kernel");
+        check_cuda(launch_down_tma(bank->maps, da, sms, s, ep == nullptr), "moe_down_tma_kernel");
+        if (ep) check_cuda(launch_combine_ep(da, *ep, s), "moe_combine_ep_kernel");
     });
 }
 
@@ -588,6 +596,35 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(nvfp4_moe_bank
         rt->profiled_call("moe_bank_forward", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
             enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s, (flags & NVFP4_MOE_PARTIAL_F32) ? 1 : 0);
         });
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ep_bf16(nvfp4_moe_bank *bank, nvfp4_ep *ep,
+                                                                 const void *x_bf16, const void *residual_bf16,
+                                                                 void *dst_bf16, int tokens, int flags,
+                                                                 void *stream) {
+    if (!bank || !bank->runtime || !ep || !x_bf16 || !dst_bf16 || tokens < 1 || tokens > kDecodeMaxTokens ||
+        (flags & ~static_cast<int>(NVFP4_MOE_ADD_RESIDUAL)) != 0 ||
+        ((flags & NVFP4_MOE_ADD_RESIDUAL) && !residual_bf16))
+        return fail_invalid("invalid expert-parallel forward arguments (1..64 tokens)");
+    if (!bank->owned_uploaded())
+        return fail_invalid("MoE bank forward requires every routed and shared projection of its expert range");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        EpArgs e{};
+        if (!ep_next_call(ep, tokens, bank->hidden, &e))
+            return fail_invalid("expert-parallel context not opened, or its token or hidden size does not fit");
+        const void *res = (flags & NVFP4_MOE_ADD_RESIDUAL) ? residual_bf16 : nullptr;
+        rt->profiled_call("moe_bank_forward_ep", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+            enqueue_decode(bank, x_bf16, 0, res, dst_bf16, 0, tokens, s, &e);
+        });
+        bank->last_tokens = tokens;
+        bank->last_path = 1;
         clear_last_error();
         return NVFP4_STATUS_OK;
     } catch (const std::exception &error) {

@@ -131,6 +131,23 @@ struct DownArgs {
     DecodeScratch s;
 };
 
+// Expert-parallel combine fused with the cross-rank reduction (moe_ep.cu).
+// Each rank writes its partial tile into its own buffer (mapped by every
+// peer), raises one flag per peer for that tile, waits (bounded) until every
+// peer's flag for the tile has arrived, then sums all ranks' tiles in rank
+// order, so every rank produces the same BF16 output.
+constexpr int kMaxEpRanks = 8;
+struct EpArgs {
+    float *part[kMaxEpRanks];          // each rank's partial buffer of this call's parity, [T][H] FP32
+    unsigned *flags_peer[kMaxEpRanks]; // each rank's flag array [world][tiles]
+    unsigned *flags_local;             // this rank's flag array
+    unsigned epoch;                    // call number, >= 1
+    int rank, world, tiles;
+    int *err;                          // device error word
+    int *host_err;                     // host-mapped error word or nullptr
+};
+cudaError_t launch_combine_ep(const DownArgs &a, const EpArgs &e, cudaStream_t stream);
+
 // Launch helpers (defined in moe_decode.cu).
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream);
 
@@ -138,7 +155,8 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream);
 cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *const scales[3], int E, int H,
                              int I);
 cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, int sms, cudaStream_t stream);
-cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream);
+cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream,
+                            bool with_combine = true);
 cudaError_t launch_combine(const DownArgs &a, cudaStream_t stream);
 
 // Tensor-core variant (moe_decode_tc.cu): shapes it serves (H and I

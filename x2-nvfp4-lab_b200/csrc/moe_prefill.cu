@@ -4,6 +4,7 @@
 #include "quant_terms.cuh"
 #include "tma_util.cuh"
 
+#include <atomic>
 #include <cfloat>
 
 namespace nvfp4 {
@@ -49,37 +50,44 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 // the same mapping on both operands.
 constexpr int kLogitsPitch = 144;
 
+constexpr int kLogitsStages = 4;      // cp.async ring depth (64 columns of x and of the router per stage)
+constexpr int kLogitsStageBytes = 2 * kLogitsTile * kLogitsPitch;
+
 __global__ void __launch_bounds__(128) prefill_logits_kernel(PrefillRouteArgs a, float *approx, int Rp) {
-    __shared__ __align__(16) uint8_t sx[2][kLogitsTile * kLogitsPitch];
-    __shared__ __align__(16) uint8_t sw[2][kLogitsTile * kLogitsPitch];
+    extern __shared__ __align__(16) uint8_t logits_smem[];  // [kLogitsStages][x tile | router tile]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int g = lane >> 2, c = lane & 3;
     const int R = a.E + 1, H = a.H;
     const int t0 = blockIdx.x * kLogitsTile, e0 = blockIdx.y * kLogitsTile;
     const int chunks = H / 64;
-    auto load = [&](int buf, int k) {
-        for (int i = tid; i < kLogitsTile * 8; i += 128) {
-            const int r = i >> 3, u = i & 7;
-            cp_async16(sx[buf] + r * kLogitsPitch + u * 16, a.x + (size_t)min(t0 + r, a.T - 1) * H + k + u * 8);
-            cp_async16(sw[buf] + r * kLogitsPitch + u * 16, a.router + (size_t)min(e0 + r, R - 1) * H + k + u * 8);
+    // Stage kc holds columns [64 kc, 64 kc + 64) of the CTA's 64 tokens and
+    // 64 router rows; three stages are in flight while one is multiplied.
+    auto load = [&](int kc) {
+        if (kc < chunks) {
+            uint8_t *sx = logits_smem + (size_t)(kc % kLogitsStages) * kLogitsStageBytes;
+            uint8_t *sw = sx + kLogitsTile * kLogitsPitch;
+            const int k = kc * 64;
+            for (int i = tid; i < kLogitsTile * 8; i += 128) {
+                const int r = i >> 3, u = i & 7;
+                cp_async16(sx + r * kLogitsPitch + u * 16, a.x + (size_t)min(t0 + r, a.T - 1) * H + k + u * 8);
+                cp_async16(sw + r * kLogitsPitch + u * 16, a.router + (size_t)min(e0 + r, R - 1) * H + k + u * 8);
+            }
         }
-        cp_async_commit();
+        cp_async_commit();  // an empty group past the end keeps the group count uniform
     };
     float acc[8][4];
 #pragma unroll
     for (int n = 0; n < 8; ++n)
 #pragma unroll
         for (int r = 0; r < 4; ++r) acc[n][r] = 0.0f;
-    load(0, 0);
+#pragma unroll
+    for (int kc = 0; kc < kLogitsStages - 1; ++kc) load(kc);
     for (int kc = 0; kc < chunks; ++kc) {
-        if (kc + 1 < chunks) {
-            load((kc + 1) & 1, (kc + 1) * 64);
-            cp_async_wait_group<1>();
-        } else {
-            cp_async_wait_group<0>();
-        }
+        load(kc + kLogitsStages - 1);
+        cp_async_wait_group<kLogitsStages - 1>();
         __syncthreads();
-        const uint8_t *bx = sx[kc & 1], *bw = sw[kc & 1];
+        const uint8_t *bx = logits_smem + (size_t)(kc % kLogitsStages) * kLogitsStageBytes;
+        const uint8_t *bw = bx + kLogitsTile * kLogitsPitch;
         const uint4 xa0 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g) * kLogitsPitch + 32 * c);
         const uint4 xa1 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g) * kLogitsPitch + 32 * c + 16);
         const uint4 xb0 = *reinterpret_cast<const uint4 *>(bx + (16 * warp + g + 8) * kLogitsPitch + 32 * c);
@@ -95,7 +103,7 @@ __global__ void __launch_bounds__(128) prefill_logits_kernel(PrefillRouteArgs a,
             for (int i = 0; i < 4; ++i)
                 mma_bf16_16816(acc[n], A[2 * i], B[2 * i], A[2 * i + 1], B[2 * i + 1], W[2 * i], W[2 * i + 1]);
         }
-        __syncthreads();
+        __syncthreads();  // the stage is refilled by a later iteration's load
     }
 #pragma unroll
     for (int n = 0; n < 8; ++n) {
@@ -480,140 +488,111 @@ __device__ __forceinline__ size_t atom_offset(int j, int atom_blocks, int words_
     return ((size_t)(j * atom_blocks + p / 128) * words_per_row + word) * 512 + (p % 32) * 16 + ((p % 128) / 32) * 4;
 }
 
-// A group of 2^gs_log2 lanes per row (at most 32, so short rows share a
-// warp). Lane l of a group quantises the 64-column chunks l, l+gs, ...; a
-// chunk holds four 16-column blocks, so each lane writes whole scale words.
-// Per term: s = E4M3_RN((bamax / 6) / g); denom = s * g; code =
-// E2M1_RN(r * RN(1/denom)) (0 when denom is 0); r -= code * denom.
-template <int J, int MODE>
-__global__ void __launch_bounds__(256) quantize_rows_kernel(const void *src, int src_kind, int rows, int cols,
-                                                            int gs_log2, QuantTargets q) {
-    const int lane = threadIdx.x & 31;
-    const int gs = 1 << gs_log2;
-    const int lig = lane & (gs - 1);
-    const int r_raw = ((blockIdx.x * blockDim.x + threadIdx.x) >> 5) * (32 >> gs_log2) + (lane >> gs_log2);
-    bool valid = r_raw < rows;
-    if (MODE == kRowAtoms && valid && r_raw >= *q.rows_used) valid = false;
+// One thread per 16-element block of a row (the row's threads reduce its
+// absolute maximum first), terms in a loop that is not unrolled: a lean
+// kernel keeps many rows in flight. Per term: s = E4M3_RN((bamax / 6) / g);
+// denom = s * g; code = E2M1_RN(r * RN(1/denom)) (0 when denom is 0);
+// r -= code * denom (quant_terms.cuh).
+constexpr int kQuantThreads = 256;
 
-    if (!__any_sync(0xffffffffu, valid)) return;
-    const int r = valid ? r_raw : 0;  // idle lanes still join the group reductions
-    uint8_t *codes = q.codes;
-    float *g_out = q.g;
-    const int rows_stride = q.rows_stride;
+template <int MODE>
+__global__ void __launch_bounds__(kQuantThreads) quantize_blocks_kernel(const void *src, int src_kind, int rows,
+                                                                       int cols, int terms, int row_threads,
+                                                                       QuantTargets q) {
+    __shared__ float s_warp_max[kQuantThreads / 32];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int rows_per_cta = blockDim.x / row_threads;
+    const int lr = threadIdx.x / row_threads;           // row within the CTA
+    const int tr = threadIdx.x - lr * row_threads;      // thread within the row
+    const int r = blockIdx.x * rows_per_cta + lr;
+    bool valid = r < rows;
+    if (MODE == kRowAtoms && valid && r >= *q.rows_used) valid = false;
+    const int nb = cols / 16;
     const int wpr = cols / 64;
-    int dst_rows[kSlots];
-    if (MODE == kTokenAtoms && valid) {
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) dst_rows[k] = q.inv_pos[r * kTopK + k];
-        dst_rows[kTopK] = q.shared_row0 ? *q.shared_row0 + r : -1;
-    }
     const int esz = src_kind == 2 ? 4 : 2;
-    const uint8_t *row = static_cast<const uint8_t *>(src) + (size_t)r * cols * esz;
-    const int chunks = cols / 64;
-    auto load_chunk = [&](int ch, float (&v)[64]) {
+    const uint8_t *row = static_cast<const uint8_t *>(src) + (size_t)(valid ? r : 0) * cols * esz;
+    auto load_block = [&](int b, float (&v)[16]) {
         if (src_kind == 2) {
-            const float4 *p = reinterpret_cast<const float4 *>(row + (size_t)ch * 64 * 4);
+            const float4 *p = reinterpret_cast<const float4 *>(row + (size_t)b * 64);
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-                const float4 f = __ldg(p + q);
-                v[4 * q] = f.x;
-                v[4 * q + 1] = f.y;
-                v[4 * q + 2] = f.z;
-                v[4 * q + 3] = f.w;
+            for (int i = 0; i < 4; ++i) {
+                const float4 f = __ldg(p + i);
+                v[4 * i] = f.x;
+                v[4 * i + 1] = f.y;
+                v[4 * i + 2] = f.z;
+                v[4 * i + 3] = f.w;
             }
             return;
         }
-        const uint4 *p = reinterpret_cast<const uint4 *>(row + (size_t)ch * 64 * 2);
+        const uint4 *p = reinterpret_cast<const uint4 *>(row + (size_t)b * 32);
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const uint4 u = __ldg(p + q);
+        for (int i = 0; i < 2; ++i) {
+            const uint4 u = __ldg(p + i);
             const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
             for (int h = 0; h < 4; ++h) {
                 if (src_kind == 1) {
                     const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[h]));
-                    v[8 * q + 2 * h] = f.x;
-                    v[8 * q + 2 * h + 1] = f.y;
+                    v[8 * i + 2 * h] = f.x;
+                    v[8 * i + 2 * h + 1] = f.y;
                 } else {
-                    v[8 * q + 2 * h] = bf16_bits_to_f32(w[h] & 0xFFFFu);
-                    v[8 * q + 2 * h + 1] = bf16_bits_to_f32(w[h] >> 16);
+                    v[8 * i + 2 * h] = bf16_bits_to_f32(w[h] & 0xFFFFu);
+                    v[8 * i + 2 * h + 1] = bf16_bits_to_f32(w[h] >> 16);
                 }
             }
         }
     };
+    // Row absolute maximum: the row's threads (whole warps when a row spans
+    // several; a lane group of a warp otherwise) reduce it.
     float amax = 0.0f;
-    for (int ch = lig; ch < chunks; ch += gs) {
-        float v[64];
-        load_chunk(ch, v);
+    if (valid)
+        for (int b = tr; b < nb; b += row_threads) {
+            float v[16];
+            load_block(b, v);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        }
+    const int span = row_threads < 32 ? row_threads : 32;
+    for (int off = span >> 1; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+    if (row_threads > 32) {
+        if (lane == 0) s_warp_max[warp] = amax;
+        __syncthreads();
+        const int w0 = (lr * row_threads) >> 5, nw = row_threads >> 5;
+        amax = 0.0f;
+#pragma unroll 1
+        for (int w = 0; w < nw; ++w) amax = fmaxf(amax, s_warp_max[w0 + w]);
     }
-    for (int off = gs >> 1; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     if (!valid) return;
-    const float g = amax > 0.0f ? __fdiv_rn(amax, 2688.0f) : 1.0f;
-    if (lig == 0) g_out[r] = g;
-    for (int ch = lig; ch < chunks; ch += gs) {
-        float v[64];
-        load_chunk(ch, v);
+    const float g = row_global_scale(amax);
+    if (tr == 0) q.g[r] = g;
+    int dst[kSlots];
+    int ndst = 1;
+    dst[0] = r;
+    if (MODE == kTokenAtoms) {
+        ndst = 0;
 #pragma unroll
-        for (int j = 0; j < J; ++j) {
-            uint32_t sword = 0;
-            uint32_t cw[8];
-#pragma unroll
-            for (int b = 0; b < 4; ++b) {
-                float bamax = 0.0f;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) bamax = fmaxf(bamax, fabsf(v[16 * b + i]));
-                const float target = __fdiv_rn(__fdiv_rn(bamax, 6.0f), g);
-                const uint32_t sb = f32x2_to_e4m3x2(target, 0.0f) & 0xFFu;
-                sword |= sb << (8 * b);
-                const float denom = __fmul_rn(e4m3_byte_to_f32(sb), g);
-                const float inv = denom != 0.0f ? __frcp_rn(denom) : 0.0f;
-#pragma unroll
-                for (int p = 0; p < 2; ++p) {
-                    uint32_t word = 0;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int e0 = 16 * b + 8 * p + 2 * i;
-                        const uint32_t cc = f32x2_to_e2m1x2(__fmul_rn(v[e0], inv), __fmul_rn(v[e0 + 1], inv)) & 0xFFu;
-                        word |= cc << (8 * i);
-                    }
-                    word = canonical_zero_codes(word);
-                    cw[2 * b + p] = word;
-                    // Residual for the next term.
-                    uint32_t h[4];
-                    e2m1x8_to_f16x8(word, h);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(&h[i]));
-                        const int e0 = 16 * b + 8 * p + 2 * i;
-                        v[e0] = __fsub_rn(v[e0], __fmul_rn(d.x, denom));
-                        v[e0 + 1] = __fsub_rn(v[e0 + 1], __fmul_rn(d.y, denom));
-                    }
-                }
-            }
-            const size_t prow = (size_t)j * rows_stride + r;
-            if (MODE != kTokenAtoms) {
-                uint4 *dst = reinterpret_cast<uint4 *>(codes + prow * (cols / 2) + ch * 32);
-                dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-                dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
-            }
-            if (MODE == kWords) {
-                q.words[prow * wpr + ch] = sword;
-            } else if (MODE == kRowAtoms) {
-                *reinterpret_cast<uint32_t *>(q.atoms + atom_offset(j, q.atom_blocks, wpr, r, ch)) = sword;
-            } else {
-                // The token's codes and scales go to each of its nine slot rows.
-#pragma unroll
-                for (int k = 0; k < kSlots; ++k) {
-                    if (dst_rows[k] < 0) continue;  // slot computed on another rank
-                    uint4 *dst = reinterpret_cast<uint4 *>(
-                        codes + ((size_t)j * rows_stride + dst_rows[k]) * (cols / 2) + ch * 32);
-                    dst[0] = make_uint4(cw[0], cw[1], cw[2], cw[3]);
-                    dst[1] = make_uint4(cw[4], cw[5], cw[6], cw[7]);
-                    *reinterpret_cast<uint32_t *>(q.atoms + atom_offset(j, q.atom_blocks, wpr, dst_rows[k], ch)) =
-                        sword;
-                }
+        for (int k = 0; k < kTopK; ++k) {
+            const int p = q.inv_pos[r * kTopK + k];
+            if (p >= 0) dst[ndst++] = p;  // -1: the slot is computed on another rank
+        }
+        if (q.shared_row0) dst[ndst++] = *q.shared_row0 + r;
+    }
+    for (int b = tr; b < nb; b += row_threads) {
+        float v[16];
+        load_block(b, v);
+#pragma unroll 1
+        for (int j = 0; j < terms; ++j) {
+            uint32_t c0, c1;
+            const uint8_t sc = static_cast<uint8_t>(quantize_block_term(v, g, c0, c1));
+#pragma unroll 1
+            for (int d = 0; d < ndst; ++d) {
+                const int p = dst[d];
+                const size_t prow = (size_t)j * q.rows_stride + p;
+                *reinterpret_cast<uint2 *>(q.codes + prow * (cols / 2) + (size_t)b * 8) = make_uint2(c0, c1);
+                if (MODE == kWords)
+                    reinterpret_cast<uint8_t *>(q.words)[(prow * wpr + (b >> 2)) * 4 + (b & 3)] = sc;
+                else
+                    q.atoms[atom_offset(j, q.atom_blocks, wpr, p, b >> 2) + (b & 3)] = sc;
             }
         }
     }
@@ -777,8 +756,19 @@ cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch
     if (part == 0) {
         err = cudaMemsetAsync(s.blk_mask, 0, (size_t)s.mask_stride * a.E * 8, stream);
         if (err != cudaSuccess) return err;
+        constexpr size_t smem = (size_t)kLogitsStages * kLogitsStageBytes;
+        static std::atomic<uint64_t> done{0};
+        int dev = 0;
+        err = cudaGetDevice(&dev);
+        if (err != cudaSuccess) return err;
+        const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+        if (!bit || !(done.load() & bit)) {
+            err = cudaFuncSetAttribute(prefill_logits_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            if (err != cudaSuccess) return err;
+            done.fetch_or(bit);
+        }
         prefill_logits_kernel<<<dim3((a.T + kLogitsTile - 1) / kLogitsTile, (R + kLogitsTile - 1) / kLogitsTile), 128,
-                                0, stream>>>(a, s.approx, Rp);
+                                smem, stream>>>(a, s.approx, Rp);
     } else if (part == 1) {
         prefill_select_kernel<<<(a.T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
     } else {
@@ -794,20 +784,14 @@ cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch
 template <int MODE>
 static cudaError_t launch_quantize_mode(const void *src, int src_kind, int rows, int cols, int terms,
                                         const QuantTargets &q, cudaStream_t stream) {
-    if (cols % 64 != 0 || rows <= 0) return cudaErrorInvalidValue;
-    // Lanes per row: the largest power of two <= min(32, cols/64).
-    const int c64 = cols / 64;
-    int gl = 0;
-    while ((2 << gl) <= (c64 < 32 ? c64 : 32)) ++gl;
-    const int rows_per_cta = 8 * (32 >> gl);
+    if (cols % 64 != 0 || rows <= 0 || terms < 1 || terms > kMaxTerms) return cudaErrorInvalidValue;
+    // Threads per row: one per 16-element block, a power of two up to the CTA.
+    const int nb = cols / 16;
+    int row_threads = 4;
+    while (row_threads < nb && row_threads < kQuantThreads) row_threads <<= 1;
+    const int rows_per_cta = kQuantThreads / row_threads;
     const int grid = (rows + rows_per_cta - 1) / rows_per_cta;
-    switch (terms) {
-        case 1: quantize_rows_kernel<1, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
-        case 2: quantize_rows_kernel<2, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
-        case 3: quantize_rows_kernel<3, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
-        case 4: quantize_rows_kernel<4, MODE><<<grid, 256, 0, stream>>>(src, src_kind, rows, cols, gl, q); break;
-        default: return cudaErrorInvalidValue;
-    }
+    quantize_blocks_kernel<MODE><<<grid, kQuantThreads, 0, stream>>>(src, src_kind, rows, cols, terms, row_threads, q);
     return cudaGetLastError();
 }
 

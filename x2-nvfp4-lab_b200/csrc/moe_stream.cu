@@ -689,7 +689,7 @@ cudaError_t launch_gate_up_tma(const StreamMaps &m, const GateUpArgs &a, int T, 
     return launch_gate_up_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
 }
 
-cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream) {
+cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cudaStream_t stream, bool with_combine) {
     const int T = a.T;
     const int routed_ub = a.E < T * kTopK ? a.E : T * kTopK;
     const int items_ub = (routed_ub + 1) * (a.H / kDnRows);
@@ -702,7 +702,7 @@ cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cud
     else
         err = launch_down_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
     if (err != cudaSuccess) return err;
-    return launch_combine(a, stream);
+    return with_combine ? launch_combine(a, stream) : cudaSuccess;
 }
 
 cudaError_t launch_combine(const DownArgs &a, cudaStream_t stream) {

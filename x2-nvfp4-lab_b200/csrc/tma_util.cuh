@@ -25,6 +25,7 @@ enum WaitSite : int {
     kSiteGemmFull = 32,
     kSiteGemmAccEmpty = 33,
     kSiteGemmAccFull = 34,
+    kSiteEpPeerTile = 41,   // expert-parallel combine: a peer's partial tile
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {

@@ -36,15 +36,20 @@ def expert_range(rank: int, world: int, experts: int) -> ExpertRange:
 
 
 class ExpertParallelLayer:
-    """A bank that computes one rank's expert range, plus the collective.
+    """A bank that computes one rank's expert range, plus the reduction.
 
     ``bank`` needs ``experts``, ``set_expert_range`` and ``forward_partial``
     (vllm_nvfp4_cuda.runtime.MoeBank); ``finalize`` turns the reduced FP32
     sum into the BF16 output (Runtime.finalize_bf16 on GPUs). ``group`` is a
     torch.distributed process group (None: the default group).
+
+    With ``fused_runtime`` (a Runtime; GPUs only) calls of up to 64 tokens use
+    the combine fused with the reduction over NVLink peer memory
+    (MoeBank.forward_ep); every rank's buffers are mapped by every other rank
+    through CUDA IPC handles exchanged here. Larger calls use the collective.
     """
 
-    def __init__(self, bank, finalize, group=None):
+    def __init__(self, bank, finalize, group=None, fused_runtime=None):
         import torch.distributed as dist
 
         self.bank = bank
@@ -54,6 +59,20 @@ class ExpertParallelLayer:
         self.world = dist.get_world_size(group)
         self.range = expert_range(self.rank, self.world, bank.experts)
         bank.set_expert_range(self.range.first, self.range.count, self.range.shared_here)
+        self.ep = None
+        if fused_runtime is not None:
+            from vllm_nvfp4_cuda.runtime import EpContext
+
+            self.ep = EpContext(fused_runtime, self.rank, self.world, 64, bank.hidden)
+            handles = [None] * self.world
+            dist.all_gather_object(handles, self.ep.ipc_handle(), group=group)
+            self.ep.open_peers(handles)
+            dist.barrier(group=group)
+
+    def close(self):
+        if self.ep is not None:
+            self.ep.close()
+            self.ep = None
 
     def partial(self, x, residual=None, stream=None):
         """This rank's FP32 partial sum (the residual is added on rank 0 only)."""
@@ -68,6 +87,8 @@ class ExpertParallelLayer:
         import torch
         import torch.distributed as dist
 
+        if self.ep is not None and x.shape[0] <= self.ep.max_tokens:
+            return self.bank.forward_ep(self.ep, x, residual=residual, stream=stream)
         ctx = torch.cuda.stream(stream) if stream is not None else contextlib.nullcontext()
         with ctx:
             part = self.partial(x, residual)

@@ -163,6 +163,12 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "nvfp4_moe_bank_reserve_prefill": ([C.c_void_p, C.c_int], C.c_int),
     "nvfp4_moe_bank_set_decode_kernels": ([C.c_void_p, C.c_int], C.c_int),
     "nvfp4_moe_bank_set_expert_range": ([C.c_void_p, C.c_int, C.c_int, C.c_int], C.c_int),
+    "nvfp4_ep_create": ([C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
+    "nvfp4_ep_ipc_handle": ([C.c_void_p, C.c_void_p], C.c_int),
+    "nvfp4_ep_open_peers": ([C.c_void_p, C.c_void_p], C.c_int),
+    "nvfp4_ep_destroy": ([C.c_void_p], None),
+    "nvfp4_moe_bank_forward_ep_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "nvfp4_moe_finalize_bf16": (
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "nvfp4_quantize_rows_enqueue": (
@@ -255,6 +261,37 @@ class Routing:
     weights: np.ndarray   # float32 [T, 9], slot 8 = sigmoid(shared logit)
     counts: np.ndarray    # int32 [experts]
     perm: np.ndarray      # int32 [T*8]
+
+
+class EpContext:
+    """additive: one rank's buffers for the fused expert-parallel combine
+    (nvfp4_ep_*). Exchange ``ipc_handle()`` with every rank, then call
+    ``open_peers(handles_in_rank_order)``."""
+
+    HANDLE_BYTES = 64
+
+    def __init__(self, runtime: "Runtime", rank: int, world: int, max_tokens: int, hidden: int):
+        self.runtime = runtime
+        self.rank, self.world, self.max_tokens, self.hidden = rank, world, max_tokens, hidden
+        self.handle = C.c_void_p()
+        runtime._check(runtime.lib.nvfp4_ep_create(runtime.handle, rank, world, max_tokens, hidden,
+                                                   C.byref(self.handle)), "nvfp4_ep_create")
+
+    def ipc_handle(self) -> bytes:
+        buf = C.create_string_buffer(self.HANDLE_BYTES)
+        self.runtime._check(self.runtime.lib.nvfp4_ep_ipc_handle(self.handle, buf), "nvfp4_ep_ipc_handle")
+        return buf.raw
+
+    def open_peers(self, handles: list[bytes]) -> None:
+        if len(handles) != self.world or any(len(h) != self.HANDLE_BYTES for h in handles):
+            raise ValueError("one handle per rank expected")
+        blob = C.create_string_buffer(b"".join(handles), self.HANDLE_BYTES * self.world)
+        self.runtime._check(self.runtime.lib.nvfp4_ep_open_peers(self.handle, blob), "nvfp4_ep_open_peers")
+
+    def close(self) -> None:
+        if self.handle:
+            self.runtime.lib.nvfp4_ep_destroy(self.handle)
+            self.handle = C.c_void_p()
 
 
 class MoeBank:
@@ -401,6 +438,31 @@ class MoeBank:
             ),
             "nvfp4_moe_bank_forward_ptr_bf16",
         )
+        return out
+
+    def forward_ep(self, ep: "EpContext", x, residual=None, out=None, stream=None):
+        """additive (expert parallelism, reduction fused into the combine over
+        NVLink peer memory): the whole layer's BF16 output on every rank; call
+        on every rank with the same x (at most ep.max_tokens tokens)."""
+        import torch
+
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.hidden:
+            raise ValueError("x must be a CUDA bfloat16 tensor [tokens, hidden]")
+        x = x.contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        flags = 0
+        if residual is not None:
+            if residual.shape != x.shape or residual.dtype != torch.bfloat16 or not residual.is_cuda:
+                raise ValueError("residual must match x")
+            residual = residual.contiguous()
+            flags = NVFP4_MOE_ADD_RESIDUAL
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_forward_ep_bf16(
+                self.handle, ep.handle, _tensor_ptr(x), _tensor_ptr(residual) if residual is not None else None,
+                _tensor_ptr(out), x.shape[0], flags, _stream_handle(s)),
+            "nvfp4_moe_bank_forward_ep_bf16")
         return out
 
     def set_expert_range(self, first: int, count: int, shared_here: bool) -> None:
