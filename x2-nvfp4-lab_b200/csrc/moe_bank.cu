@@ -288,7 +288,7 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
     ra.E = E;
     ra.H = H;
     rt->profiled_kernel("moe_route_logits", stream, [&](cudaStream_t s) {
-        check_cuda(launch_prefill_route(ra, ps, 0, s), "prefill_logits_kernel");
+        check_cuda(launch_prefill_route(ra, ps, 0, s, &bank->pmaps), "prefill_logits_tc_kernel");
     });
     rt->profiled_kernel("moe_route_select", stream, [&](cudaStream_t s) {
         check_cuda(launch_prefill_route(ra, ps, 1, s), "prefill_select_kernel");
@@ -436,6 +436,8 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
         }
         check_cuda(make_prefill_weight_maps(holder->pmaps, holder->packed, experts, hidden, intermediate),
                    "cuTensorMapEncodeTiled(MoE bank prefill)");
+        check_cuda(make_prefill_router_map(holder->pmaps, holder->router, experts, hidden),
+                   "cuTensorMapEncodeTiled(MoE bank router)");
         if (prefill_supported(holder.get()) && decode_tc_supported(hidden, intermediate)) {
             check_cuda(make_decode_tc_maps(holder->tc_maps, holder->ds, hidden, intermediate),
                        "cuTensorMapEncodeTiled(MoE bank decode terms)");

@@ -2,6 +2,7 @@
 // kernels (the tcgen05 expert GEMMs are in moe_gemm.cu).
 #include "moe_prefill.cuh"
 #include "quant_terms.cuh"
+#include "tcgen05_util.cuh"
 #include "tma_util.cuh"
 
 #include <atomic>
@@ -49,6 +50,129 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 // the MMA's k-slots {2c, 2c+1, 2c+8, 2c+9} to columns 16c + 4i + {0,1,2,3},
 // the same mapping on both operands.
 constexpr int kLogitsPitch = 144;
+
+// Approximate logits on tcgen05 (kind::f16, BF16 x BF16 -> FP32 in tensor
+// memory): one CTA per tile of 128 tokens x 64 router rows, all of K = H in
+// 64-column stages through a 6-deep TMA ring. Warp 0 issues the TMA loads
+// (token rows and router rows as 128-byte swizzled boxes), warp 1 the MMAs
+// (four M128 N64 K16 per stage), warps 2-5 move the accumulator to `approx`.
+// The order of the FP32 additions differs from the exact logits; the
+// candidate margin of the selection bounds any order.
+constexpr int kLtTokens = 128, kLtRows = 64, kLtStages = 6;
+constexpr int kLtStageBytes = kLtTokens * 128 + kLtRows * 128;
+constexpr size_t kLtSmem = 1024 + (size_t)kLtStages * kLtStageBytes + 256;
+
+__global__ void __launch_bounds__(192, 1)
+    prefill_logits_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                             PrefillRouteArgs a, float *approx, int Rp, int *err, int *host_err) {
+    extern __shared__ uint8_t lt_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(lt_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + (size_t)kLtStages * kLtStageBytes);
+    uint64_t *empty = full + kLtStages;
+    uint64_t *acc_full = empty + kLtStages;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+    int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t0 = blockIdx.x * kLtTokens, e0 = blockIdx.y * kLtRows;
+    const int kstages = a.H / 64;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kLtStages; ++i) {
+            mbar_init(full + i, 1);
+            mbar_init(empty + i, 1);
+        }
+        mbar_init(acc_full, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm_x);
+        prefetch_tensormap(&tm_w);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 64);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    if (warp == 0) {
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int ks = 0; ks < kstages; ++ks, ++it) {
+                const int st = it % kLtStages;
+                if (!mbar_wait(empty + st, ((it / kLtStages) & 1u) ^ 1u, err, kSiteGemmEmpty)) {
+                    // Drain the loads in flight (bounded) before the CTA exits.
+                    const uint32_t first = it > (uint32_t)kLtStages ? it - kLtStages : 0u;
+                    for (uint32_t k = first; k < it; ++k) {
+                        const unsigned long long w0 = global_ns();
+                        while (!mbar_try_wait(full + (k % kLtStages), (k / kLtStages) & 1u) &&
+                               global_ns() - w0 < kWaitLimitNs) {
+                        }
+                    }
+                    break;
+                }
+                uint8_t *stage = smem + (size_t)st * kLtStageBytes;
+                mbar_arrive_expect_tx(full + st, kLtStageBytes);
+                tma_load_2d(stage, &tm_x, full + st, ks * 128, t0);
+                tma_load_2d(stage + kLtTokens * 128, &tm_w, full + st, ks * 128, e0);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_bf16(kLtRows);
+            const uint32_t base = smem_u32(smem);
+            bool ok = true;
+            for (int ks = 0; ks < kstages && ok; ++ks) {
+                const int st = ks % kLtStages;
+                if (!mbar_wait(full + st, (ks / kLtStages) & 1u, err, kSiteGemmFull)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                const uint32_t sb = base + (uint32_t)st * kLtStageBytes;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    tc::mma_bf16(tmem, tc::smem_desc_sw128(sb + 32 * k), tc::smem_desc_sw128(sb + kLtTokens * 128 + 32 * k),
+                                 idesc, (ks | k) != 0 ? 1u : 0u);
+                tc::commit(empty + st);
+            }
+            tc::commit(acc_full);
+            // Every MMA has completed before tensor memory is freed (bounded).
+            const unsigned long long w0 = global_ns();
+            while (!mbar_try_wait(acc_full, 0) && global_ns() - w0 < kWaitLimitNs) {
+            }
+        }
+        __syncwarp();
+    } else {
+        const int sub = warp & 3;
+        if (threadIdx.x == 64) *acc_ok = mbar_wait(acc_full, 0, err, kSiteGemmAccFull) ? 1 : 0;
+        named_barrier(1, 128);
+        if (*reinterpret_cast<volatile int *>(acc_ok)) {
+            tc::fence_after_sync();
+            const int t = t0 + 32 * sub + lane;
+#pragma unroll
+            for (int c0 = 0; c0 < kLtRows; c0 += 32) {
+                uint32_t r[32];
+                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * sub) << 16) + c0, r);
+                tc::wait_ld();
+                if (t < a.T) {
+#pragma unroll
+                    for (int n = 0; n < 32; ++n) {
+                        const int e = e0 + c0 + n;
+                        if (e < a.E) approx[(size_t)t * Rp + e] = __uint_as_float(r[n]);
+                    }
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 64);
+    }
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile int *>(err) != 0 && host_err)
+        *reinterpret_cast<volatile int *>(host_err) = *reinterpret_cast<volatile int *>(err);
+}
 
 constexpr int kLogitsStages = 4;      // cp.async ring depth (64 columns of x and of the router per stage)
 constexpr int kLogitsStageBytes = 2 * kLogitsTile * kLogitsPitch;
@@ -750,12 +874,39 @@ cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pit
     return cudaGetLastError();
 }
 
-cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, int part, cudaStream_t stream) {
+cudaError_t make_prefill_router_map(PrefillMaps &m, const uint16_t *router, int E, int H) {
+    return make_tensor_map_u8(&m.router, router, (uint64_t)H * 2, (uint64_t)H * 2, (uint64_t)E + 1, 128, kLtRows,
+                              CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, int part, cudaStream_t stream,
+                                 const PrefillMaps *maps) {
     const int R = a.E + 1, Rp = (R + 63) / 64 * 64;
     cudaError_t err = cudaSuccess;
     if (part == 0) {
         err = cudaMemsetAsync(s.blk_mask, 0, (size_t)s.mask_stride * a.E * 8, stream);
         if (err != cudaSuccess) return err;
+        if (maps && a.H % 64 == 0) {
+            CUtensorMap tm_x;
+            err = make_tensor_map_u8(&tm_x, a.x, (uint64_t)a.H * 2, (uint64_t)a.H * 2, (uint64_t)a.T, 128, kLtTokens,
+                                     CU_TENSOR_MAP_SWIZZLE_128B);
+            if (err != cudaSuccess) return err;
+            static std::atomic<uint64_t> done_tc{0};
+            int dev = 0;
+            err = cudaGetDevice(&dev);
+            if (err != cudaSuccess) return err;
+            const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+            if (!bit || !(done_tc.load() & bit)) {
+                err = cudaFuncSetAttribute(prefill_logits_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)kLtSmem);
+                if (err != cudaSuccess) return err;
+                done_tc.fetch_or(bit);
+            }
+            const dim3 grid((a.T + kLtTokens - 1) / kLtTokens, (a.E + kLtRows - 1) / kLtRows);
+            prefill_logits_tc_kernel<<<grid, 192, kLtSmem, stream>>>(tm_x, maps->router, a, s.approx, Rp, s.error,
+                                                                      s.host_error);
+            return cudaGetLastError();
+        }
         constexpr size_t smem = (size_t)kLogitsStages * kLogitsStageBytes;
         static std::atomic<uint64_t> done{0};
         int dev = 0;

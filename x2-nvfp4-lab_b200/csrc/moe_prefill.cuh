@@ -90,6 +90,7 @@ struct PrefillMaps {
     CUtensorMap w[3];        // packed weights, box {128 B, 128 rows}, 128-byte swizzle
     CUtensorMap xq;          // [Jx*rows][H/2], box {128 B, 128 rows}
     CUtensorMap aq;          // [Ja*rows][I/2], box {128 B, 128 rows}
+    CUtensorMap router;      // BF16 router as bytes [(E+1)][2H], box {128 B, 64 rows}
 };
 
 struct PrefillRouteArgs {
@@ -118,6 +119,7 @@ size_t prefill_scratch_bytes(int T, int E, int H, int I, int Jx, int Ja);
 void prefill_scratch_carve(PrefillScratch &s, void *base, int T, int E, int H, int I, int Jx, int Ja);
 
 cudaError_t make_prefill_weight_maps(PrefillMaps &m, uint8_t *const packed[3], int E, int H, int I);
+cudaError_t make_prefill_router_map(PrefillMaps &m, const uint16_t *router, int E, int H);
 cudaError_t make_prefill_act_maps(PrefillMaps &m, const PrefillScratch &s, int Jx, int Ja);
 
 // Weight scale bytes [rows][K/16] (pitched) -> the tcgen05 scale-factor atom
@@ -126,7 +128,9 @@ cudaError_t launch_scale_atoms(uint8_t *atoms, const uint8_t *scales, size_t pit
                                cudaStream_t stream);
 
 // Routing in three parts: 0 approximate logits, 1 exact selection, 2 dispatch.
-cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, int part, cudaStream_t stream);
+// Part 0 runs on tcgen05 when `maps` is given (H a multiple of 64).
+cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch &s, int part, cudaStream_t stream,
+                                 const PrefillMaps *maps = nullptr);
 cudaError_t launch_quantize_rows(const void *src, int src_is_f16, int rows, int cols, int terms, uint8_t *codes,
                                  uint32_t *sf, float *g, int rows_stride, cudaStream_t stream);
 // Prefill forms: token rows of x (codes by token, scale atoms scattered to

@@ -78,6 +78,26 @@ __host__ __device__ constexpr uint32_t idesc_mxf4nvf4(uint32_t n) {
            | ((128u >> 4) << 24); // M / 16
 }
 
+// Instruction descriptor of kind::f16 with BF16 A and B, FP32 accumulation,
+// both operands K-major, M = 128 and N = `n`.
+__host__ __device__ constexpr uint32_t idesc_bf16(uint32_t n) {
+    return (1u << 4)              // D format: F32
+           | (1u << 7)            // A format: BF16
+           | (1u << 10)           // B format: BF16
+           | ((n >> 3) << 17)     // N / 8
+           | ((128u >> 4) << 24); // M / 16
+}
+
+// D[tmem d] (+)= A[smem a] * B[smem b]^T, BF16 operands (K 16 per instruction).
+__device__ __forceinline__ void mma_bf16(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}"
+        ::"r"(d), "l"(a), "l"(b), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // D[tmem d] (+)= A[smem a] * B[smem b]^T with per-16 block scales read from
 // tensor memory at `sfa` and `sfb`. Issued by one thread.
 __device__ __forceinline__ void mma_mxf4nvf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
