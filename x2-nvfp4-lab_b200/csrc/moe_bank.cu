@@ -166,7 +166,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ra.s = bank->ds;
     nvfp4_runtime *rt = bank->runtime;
     rt->profiled_kernel("moe_route", stream, [&](cudaStream_t s) {
-        check_cuda(launch_route(ra, s), "moe_route_kernel");
+        check_cuda(launch_route(ra, s, true), "moe_route_kernel");
     });
 
     DownArgs da{};

@@ -62,6 +62,10 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         const uint8_t *wsrc = reinterpret_cast<const uint8_t *>(a.router + (size_t)min(row, R - 1) * H);
         uint8_t *wdst = reinterpret_cast<uint8_t *>(route_w + (size_t)warp * H);
         for (int i = lane; i < H / 8; i += 32) cp_async16(wdst + 16 * i, wsrc + 16 * i);
+        // The router belongs to the bank; x and the scratch tables may be
+        // written or still read by the preceding launch (this kernel is a
+        // programmatic dependent launch): wait for it only now.
+        pdl_wait();
         const uint8_t *src = static_cast<const uint8_t *>(a.x) + (size_t)t0 * H * esz;
         if ((reinterpret_cast<uintptr_t>(src) & 15u) == 0) {
             const int n16 = tt * H * esz / 16;
@@ -467,7 +471,7 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
     return off;
 }
 
-cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream) {
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent) {
     const int R = a.E + 1;
     const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
     const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2;
@@ -492,8 +496,21 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream) {
             done.fetch_or(bit);
         }
     }
-    moe_route_kernel<<<grid, kRouteRowsPerCta * 32, smem, stream>>>(a);
-    return cudaGetLastError();
+    if (!dependent) {
+        moe_route_kernel<<<grid, kRouteRowsPerCta * 32, smem, stream>>>(a);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kRouteRowsPerCta * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_route_kernel, a);
 }
 
 }  // namespace nvfp4

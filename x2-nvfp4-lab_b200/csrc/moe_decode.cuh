@@ -148,8 +148,11 @@ struct EpArgs {
 };
 cudaError_t launch_combine_ep(const DownArgs &a, const EpArgs &e, cudaStream_t stream);
 
-// Launch helpers (defined in moe_decode.cu).
-cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream);
+// Launch helpers (defined in moe_decode.cu). `dependent`: a programmatic
+// dependent launch (the kernel fetches the router before it waits for the
+// preceding kernel; use it only when the preceding stream operation is a
+// kernel launch).
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent = false);
 
 // TMA-pipelined expert GEMVs (moe_stream.cu).
 cudaError_t make_stream_maps(StreamMaps &m, uint8_t *const packed[3], uint8_t *const scales[3], int E, int H,
