@@ -314,7 +314,10 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_forward_device_enqueue_bf16(
 
 /* additive: the same forward on raw device pointers, enqueued on `stream`
  * (a cudaStream_t; NULL selects the runtime's stream). For host frameworks
- * whose tensors are not nvfp4_buffer objects. */
+ * whose tensors are not nvfp4_buffer objects. The batched forwards are the
+ * serving path: they record no per-call profiling events (the lab's decode
+ * entry point does), so nvfp4_runtime_last_profile covers them only while
+ * tracing is enabled, when every kernel is timed. */
 NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(
     nvfp4_moe_bank * bank,
     const void * x_bf16,

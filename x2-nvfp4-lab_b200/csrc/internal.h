@@ -84,6 +84,14 @@ struct nvfp4_runtime {
         if (trace_enabled) profiled(operation, on_stream, launch);
         else launch(on_stream ? on_stream : stream);
     }
+    // Serving entry points (raw-pointer and expert-parallel forwards, the
+    // finalize step): no per-call event pair, which would sit between the
+    // caller's previous kernel and this call's first one; with tracing
+    // enabled every kernel still gets its own pair (profiled_kernel).
+    template <typename F>
+    void direct_call(cudaStream_t on_stream, F &&launch) {
+        launch(on_stream ? on_stream : stream);
+    }
     template <typename F>
     void profiled_call(const char *operation, cudaStream_t on_stream, F &&launch) {
         if (trace_enabled) launch(on_stream ? on_stream : stream);

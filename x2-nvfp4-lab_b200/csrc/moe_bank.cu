@@ -595,7 +595,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(nvfp4_moe_bank
         nvfp4_runtime *rt = bank->runtime;
         std::lock_guard<std::mutex> lock(rt->queue_mutex);
         const void *res = (flags & NVFP4_MOE_ADD_RESIDUAL) ? residual_bf16 : nullptr;
-        rt->profiled_call("moe_bank_forward", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+        rt->direct_call(static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
             enqueue_forward_bf16(bank, x_bf16, res, dst_bf16, tokens, s, (flags & NVFP4_MOE_PARTIAL_F32) ? 1 : 0);
         });
         clear_last_error();
@@ -622,7 +622,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ep_bf16(nvfp4_moe_bank 
         if (!ep_next_call(ep, tokens, bank->hidden, &e))
             return fail_invalid("expert-parallel context not opened, or its token or hidden size does not fit");
         const void *res = (flags & NVFP4_MOE_ADD_RESIDUAL) ? residual_bf16 : nullptr;
-        rt->profiled_call("moe_bank_forward_ep", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+        rt->direct_call(static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
             enqueue_decode(bank, x_bf16, 0, res, dst_bf16, 0, tokens, s, &e);
         });
         bank->last_tokens = tokens;

@@ -257,7 +257,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_finalize_bf16(nvfp4_runtime *runtime
         std::lock_guard<std::mutex> lock(runtime->queue_mutex);
         const size_t n4 = static_cast<size_t>(tokens) * hidden / 4;
         const int grid = static_cast<int>((n4 + 255) / 256 < 4096 ? (n4 + 255) / 256 : 4096);
-        runtime->profiled_call("moe_finalize", static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+        runtime->direct_call(static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
             finalize_bf16_kernel<<<grid, 256, 0, s>>>(sum_f32, static_cast<const uint16_t *>(residual_bf16),
                                                       static_cast<uint16_t *>(out_bf16), n4);
             check_cuda(cudaGetLastError(), "finalize_bf16_kernel");
