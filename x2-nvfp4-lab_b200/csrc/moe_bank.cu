@@ -188,6 +188,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         ta.E = E;
         ta.H = H;
         ta.I = I;
+        ta.shared_last = bank->shared_here ? 1 : 0;
         ta.s = bank->ds;
         ta.sfa[0] = bank->sf_atoms[0];
         ta.sfa[1] = bank->sf_atoms[1];

@@ -14,7 +14,10 @@
 //                             registers, mma.sync against f16 tokens,
 //                             SiLU(gate)*up fused;
 //     moe_down_tma_kernel     down GEMV of every (active expert, 64-row tile),
-//                             scaled per (token, slot);
+//                             scaled per (token, slot); in calls of up to
+//                             kFusedCombineMaxTokens tokens the CTA that
+//                             finishes an output tile's last group also
+//                             combines that tile (no combine launch);
 //   tensor-core (calls of up to kDecodeTcMaxTokens tokens on the shapes
 //   decode_tc_supported accepts; the routing kernel also writes x as four
 //   NVFP4 terms per token):
@@ -23,7 +26,7 @@
 //                             weights stream once;
 //     quantize_act_tc_kernel  activations -> four terms per slot row;
 //     moe_down_tc_kernel      down, scaled per (token, slot);
-// and finally
+// and finally (unless the down kernel combined)
 //   moe_combine_kernel      sum of the nine slots + residual.
 // The lab runs the same layer as seven launches (nvfp4_runtime.cpp:1943-2066:
 // router GEMV, shared-gate GEMV, top-8, gate/up, SiLU, down, reduce).
@@ -66,7 +69,7 @@ struct DecodeScratch {
     int *slot_group;        // [T*9] active-group index of each dispatch position, -1 if not computed here
     __half *act;            // [T*9][I]      SiLU(gate)*up per (token, slot)
     float *ypart;           // [T*9][H]      scaled down-projection per (token, slot)
-    unsigned *tile_count;   // [H/64]        finished experts per 64-row output tile
+    unsigned *tile_count;   // [H/64]        finished groups per 64-row output tile (zeroed by routing)
     // Tensor-core variant: activation terms. Row 4*t + j of a B tile is term j
     // of token (or slot) t; scale bytes are stored in tcgen05 atom layout
     // [K/64][512 B] per 128-row tile: byte (n%32)*16 + (n/32)*4 + (k/16)%4.
@@ -118,6 +121,7 @@ struct DecodeTcArgs {
     const uint8_t *sfb;       // activation scale atoms (xsf_tc or asf_tc)
     const float *inv_scales;  // [3][E+1]
     int E, H, I;
+    int shared_last;          // 1: the shared expert is computed here (always the last active group)
     DecodeScratch s;
 };
 
@@ -128,8 +132,14 @@ struct DownArgs {
     int out_f32;
     int shared_here;          // 1 if the shared expert's slot is summed here
     int T, E, H, I;
+    int fuse_combine;         // in-register down kernel: the last CTA of each output tile also combines it
     DecodeScratch s;
 };
+
+// Calls of up to this many tokens combine inside the in-register down
+// kernel (one tile of at most 16 x 64 outputs per finishing CTA); larger
+// calls launch the combine kernel.
+constexpr int kFusedCombineMaxTokens = 16;
 
 // Expert-parallel combine fused with the cross-rank reduction (moe_ep.cu).
 // Each rank writes its partial tile into its own buffer (mapped by every

@@ -143,6 +143,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int mtiles = a.I / kTile;
     const int total = *s.n_active * mtiles;
+    // Strided items over the fewest CTAs that need no more waves than the
+    // whole grid: every working CTA then walks the same number of items (or
+    // one fewer), and the weight stream of the SMs left idle goes to them
+    // instead of to a last partial wave.
+    const int waves = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int ctas = waves > 0 ? (total + waves - 1) / waves : 0;
+    const int first = (int)blockIdx.x < ctas ? (int)blockIdx.x : total;  // this CTA's first item
     const int kstages = a.H / kStageK;
     const int kw = a.H / 64;
 
@@ -150,11 +157,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ------------------------------------------------------ producer
         uint32_t it = 0;
         bool ok = true;
-        if (lane == 0 && (int)blockIdx.x < total) {
+        if (lane == 0 && (int)blockIdx.x < ctas) {
             mbar_arrive_expect_tx(sfb_full, kw * 512);
             bulk_g2s(sfb_stage, a.sfb, kw * 512, sfb_full);
         }
-        for (int item = blockIdx.x; item < total && ok; item += gridDim.x) {
+        for (int item = first; item < total && ok; item += ctas) {
             const Item ti = load_item(s, item, mtiles);
             const int arow = ti.e * a.I + ti.mt * kTile;
             const size_t sfa_off = (size_t)(arow / kTile) * kw * 512;
@@ -182,7 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
             // Drain the copies still in flight before the CTA exits.
             if (lane == 0) {
-                if ((int)blockIdx.x < total) mbar_wait_drain(sfb_full, 0);
+                if ((int)blockIdx.x < ctas) mbar_wait_drain(sfb_full, 0);
                 const uint32_t first = it > (uint32_t)S ? it - S : 0u;
                 for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
             }
@@ -194,7 +201,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t smem_base = smem_u32(smem);
             uint32_t it = 0, tcount = 0;
             bool ok = true;
-            if ((int)blockIdx.x < total) {
+            if ((int)blockIdx.x < ctas) {
                 ok = mbar_wait(sfb_full, 0, err, kSiteGemmFull);
                 tc::fence_after_sync();
                 tc::fence_proxy_async_smem();
@@ -202,7 +209,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int at = 0; ok && at < kw; ++at)
                     tc::cp_sf_atom(tmem + kGuColSfb + 4 * at, tc::smem_desc_sf(sfb_base + at * 512));
             }
-            for (int item = blockIdx.x; item < total && ok; item += gridDim.x, ++tcount) {
+            for (int item = first; item < total && ok; item += ctas, ++tcount) {
                 if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1u, err, kSiteGemmAccEmpty)) {
                     ok = false;
                     break;
@@ -250,7 +257,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int et = threadIdx.x - 64;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
         uint32_t tcount = 0;
-        for (int item = blockIdx.x; item < total; item += gridDim.x, ++tcount) {
+        for (int item = first; item < total; item += ctas, ++tcount) {
             const Item ti = load_item(s, item, mtiles);
             int *ctok = col_tok + 32 * (tcount & 1);
             float *cscale = col_scale + 32 * (tcount & 1);
@@ -311,8 +318,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // ------------------------------------------------------------------ down
 //
-// Each CTA walks a contiguous range of (active group, 128 rows of H) items,
-// so consecutive items mostly share their group: the group's B tile (its
+// Each CTA walks a contiguous range of (active group, 128 rows of H) items
+// (after at most one tile of the shared expert's group, whose tiles are
+// spread over the grid), so consecutive items mostly share their group:
+// the group's B tile (its
 // slot rows' terms over all of K = I) and scale atoms are loaded into one of
 // two B buffers and copied into tensor memory once per group. A stage is one
 // item's weight tile over all of K (KB 256-column boxes) and its scale atoms.
@@ -382,8 +391,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int mtiles = a.H / kTile;
     const int total = *s.n_active * mtiles;
-    const int lo = (int)(((long long)total * blockIdx.x) / gridDim.x);
-    const int hi = (int)(((long long)total * (blockIdx.x + 1)) / gridDim.x);
+    // Items over the fewest CTAs that need no more waves than the grid, each
+    // CTA taking the same count (or one fewer). The shared expert's group
+    // (the last, with a row for every token) has the costliest items: its
+    // tiles go one each to evenly spaced CTAs, first in their lists, and the
+    // other items split into contiguous runs around them, so consecutive
+    // items of a CTA mostly share their group.
+    const int waves = (total + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int ctas = waves > 0 ? (total + waves - 1) / waves : 0;
+    const int sh = a.shared_last && total > 0 && mtiles <= ctas ? mtiles : 0;
+    const int routed = total - sh;
+    int sh_lo = 0, sh_hi = 0, r_lo = 0, r_hi = 0;
+    if ((int)blockIdx.x < ctas) {
+        const long long b = blockIdx.x;
+        sh_lo = (int)((b * sh + ctas - 1) / ctas);
+        sh_hi = (int)(((b + 1) * sh + ctas - 1) / ctas);
+        r_lo = (int)((b * total) / ctas) - sh_lo;
+        r_hi = (int)(((b + 1) * total) / ctas) - sh_hi;
+    }
+    const int nsh = sh_hi - sh_lo;
+    const int count = nsh + (r_hi - r_lo);
+    auto item_at = [&](int j) { return j < nsh ? routed + sh_lo + j : r_lo + (j - nsh); };
 
     if (warp == 0) {
         // ------------------------------------------------------ producer
@@ -392,7 +420,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         if (lane == 0) {
             Item ti{};
-            for (int item = lo; item < hi && ok; ++item) {
+            for (int j = 0; j < count && ok; ++j) {
+                const int item = item_at(j);
                 // Consecutive items mostly share their group: its metadata is
                 // loaded once per group.
                 if (item / mtiles != prev_ai) {
@@ -447,7 +476,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t it = 0, tcount = 0, nb = 0;
             int prev_ai = -1;
             bool ok = true;
-            for (int item = lo; item < hi && ok; ++item, ++tcount) {
+            for (int j = 0; j < count && ok; ++j, ++tcount) {
+                const int item = item_at(j);
                 const int ai = item / mtiles;  // items are ordered group-major
                 if (ai != prev_ai) {
                     if (nb > 0) tc::commit(bempty + ((nb - 1) & 1u));
@@ -508,7 +538,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t tcount = 0, gcount = 0;
         Item ti{};
         ti.ai = -1;
-        for (int item = lo; item < hi; ++item, ++tcount) {
+        for (int j = 0; j < count; ++j, ++tcount) {
+            const int item = item_at(j);
             // Group metadata and the per-row scales change only with the group
             // (double-buffered by group count: a warp still computing the
             // previous item reads the other buffer).

@@ -144,6 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();  // the routing kernel's outputs are read from here on
     pdl_launch_dependents();
     const int H = a.H, I = a.I, E = a.E;
+    // Output-tile tickets of the down kernel that follows (which reads them
+    // only after this grid completes).
+    if (blockIdx.x == 0)
+        for (int i = threadIdx.x; i < H / kDnRows; i += blockDim.x) s.tile_count[i] = 0u;
     const int nact = *s.n_active;
     const int mtiles = I / kGuRows;
     const int items = nact * mtiles;
@@ -340,6 +344,45 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ down
 
+// Output rows h..h+3 (h % 4 == 0) of token t: the slot partials summed in
+// slot order, then the shared slot, then the residual (the order of
+// moe_combine_kernel, so both give the same bits). The partials come from
+// other CTAs of the running grid and are read through L2.
+__device__ __forceinline__ void combine_quad(const DownArgs &a, int t, int h) {
+    const DecodeScratch &s = a.s;
+    const int H = a.H;
+    int pos[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) pos[k] = s.inv_pos[t * kTopK + k];
+    const size_t o = (size_t)t * H + h;
+    float r[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (a.residual) {
+        const uint16_t *res = static_cast<const uint16_t *>(a.residual) + o;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r[q] = bf16_bits_to_f32(res[q]);
+    }
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int k = 0; k <= kTopK; ++k) {
+        const int p = k < kTopK ? pos[k] : (a.shared_here ? a.T * kTopK + t : -1);
+        if (p >= 0) {
+            const float4 y = __ldcg(reinterpret_cast<const float4 *>(s.ypart + (size_t)p * H + h));
+            v[0] += y.x;
+            v[1] += y.y;
+            v[2] += y.z;
+            v[3] += y.w;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (a.residual) v[q] += r[q];
+        if (a.out_f32)
+            static_cast<float *>(a.out)[o + q] = v[q];
+        else
+            static_cast<uint16_t *>(a.out)[o + q] = f32_to_bf16_bits(v[q]);
+    }
+}
+
 template <int NT, int BOXES, int S>
 struct DnCfg {
     static constexpr int kPacked = BOXES * kDnRows * kBoxBytes;
@@ -358,6 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *smem = align1024(smem_raw);
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStage);
     uint64_t *empty = full + S;
+    __shared__ int s_flag[2];  // [0] a consumer warp gave up waiting; [1] this CTA combines the current tile
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const DecodeScratch &s = a.s;
     int *err = s.error;
@@ -369,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_barrier_init();
         prefetch_tensormap(&tm_dp);
         prefetch_tensormap(&tm_ds);
+        s_flag[0] = 0;
     }
     __syncthreads();
     pdl_wait();  // routing tables and gate/up activations are read from here on
@@ -436,6 +481,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (item + (int)gridDim.x < items) nxt = load_item(s, item + gridDim.x, rtiles);
         const int ai = cur.ai, rt = cur.mt;
         const int tstart = cur.tstart, ntok = cur.ntok;
+        bool failed = false;
         for (int tg = 0; tg < ntok; tg += NT * 8) {
             const int ncols = min(NT * 8, ntok - tg);
             // Output scales of this lane's columns, loaded before the K loop
@@ -458,9 +504,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int sl = 0; sl < slices; ++sl, ++it) {
                 const int st = it % S;
                 const uint32_t ph = (it / S) & 1u;
-                if (!mbar_wait(full + st, ph, err, kSiteDownFull)) {
-                    publish_timeout(s);
-                    return;
+                if (!__all_sync(0xffffffffu, mbar_wait(full + st, ph, err, kSiteDownFull))) {
+                    failed = true;
+                    break;
                 }
                 const uint8_t *stage = smem + st * Cfg::kStage;
                 const uint8_t *sc = stage + Cfg::kPacked;
@@ -498,6 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(empty + st);
             }
+            if (failed) break;
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
@@ -516,6 +563,40 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+        if (failed) publish_timeout(s);
+        if (!a.fuse_combine) {
+            if (failed) return;
+            continue;
+        }
+        // Fused combine: publish this group's partial tile and take a ticket
+        // for output tile rt; the CTA holding the tile's last ticket (every
+        // other active group's partial is then written) sums the tile. All
+        // four consumer warps reach both barriers, a warp that gave up
+        // waiting included, and leave together.
+        if (failed && lane == 0) s_flag[0] = 1;
+        __threadfence();
+        named_barrier(1, kConsumerWarps * 32);
+        if (threadIdx.x == 0 && !s_flag[0])
+            s_flag[1] = atomicAdd(s.tile_count + rt, 1u) == (unsigned)(nact - 1) ? 1 : 0;
+        named_barrier(1, kConsumerWarps * 32);
+        if (s_flag[0]) return;
+        if (s_flag[1]) {
+            __threadfence();
+            constexpr int kQuads = kDnRows / 4;
+#pragma unroll 1
+            for (int i = threadIdx.x; i < a.T * kQuads; i += kConsumerWarps * 32)
+                combine_quad(a, i / kQuads, rt * kDnRows + (i % kQuads) * 4);
+        }
+    }
+    // No active group (an expert range that no token routes to): the output
+    // is the residual alone, one tile per CTA.
+    if (a.fuse_combine && items == 0) {
+        constexpr int kQuads = kDnRows / 4;
+#pragma unroll 1
+        for (int t0 = blockIdx.x; t0 < rtiles; t0 += gridDim.x)
+#pragma unroll 1
+            for (int i = threadIdx.x; i < a.T * kQuads; i += kConsumerWarps * 32)
+                combine_quad(a, i / kQuads, t0 * kDnRows + (i % kQuads) * 4);
     }
 }
 
@@ -695,14 +776,16 @@ cudaError_t launch_down_tma(const StreamMaps &m, const DownArgs &a, int sms, cud
     const int items_ub = (routed_ub + 1) * (a.H / kDnRows);
     cudaError_t err;
     const int tpe = tokens_per_expert(T, a.E);
+    DownArgs da = a;
+    da.fuse_combine = with_combine && T <= kFusedCombineMaxTokens ? 1 : 0;
     if (tpe <= 8)
-        err = launch_down_cfg<1, 2, 2>(m, a, items_ub, sms, stream);
+        err = launch_down_cfg<1, 2, 2>(m, da, items_ub, sms, stream);
     else if (tpe <= 16)
-        err = launch_down_cfg<2, 2, 4>(m, a, items_ub, sms, stream);
+        err = launch_down_cfg<2, 2, 4>(m, da, items_ub, sms, stream);
     else
-        err = launch_down_cfg<4, 2, 3>(m, a, items_ub, sms, stream);
+        err = launch_down_cfg<4, 2, 3>(m, da, items_ub, sms, stream);
     if (err != cudaSuccess) return err;
-    return with_combine ? launch_combine(a, stream) : cudaSuccess;
+    return with_combine && !da.fuse_combine ? launch_combine(a, stream) : cudaSuccess;
 }
 
 cudaError_t launch_combine(const DownArgs &a, cudaStream_t stream) {
