@@ -17,10 +17,13 @@
 //            dispatch order): rows 4*tok_start .. of the activation terms.
 //
 // One persistent CTA per SM walks (active expert group, 128-row weight tile)
-// items. Warp roles as in the prefill grouped GEMM: warp 0 producer (TMA
-// tiles of the weights and of B, bulk copies of the scale-factor atoms, all
-// on the stage's mbarrier), warp 1 MMA issuer and tensor-memory owner,
-// warps 2-5 epilogue. Every mbarrier wait is bounded; on a timeout the CTA
+// items. Warp roles: warp 0 producer (TMA tiles of the weights and of B,
+// bulk copies of the scale-factor atoms, all on the stage's mbarrier), warp 1
+// MMA issuer and tensor-memory owner, warps 2-5 epilogue, warps 6-9 weight
+// scale factors: each stage's atoms go from shared memory into tensor memory
+// by tcgen05.st, one 32-lane quarter per warp, so the MMA thread issues only
+// MMAs and commits (a tcgen05.cp per atom costs the issuing thread about as
+// much as an MMA). Every mbarrier wait is bounded; on a timeout the CTA
 // records the error, drains its copies and MMAs in flight, frees its tensor
 // memory and exits.
 #include "moe_decode.cuh"
@@ -34,7 +37,8 @@ namespace nvfp4 {
 
 namespace {
 
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;
+constexpr int kSfWarp0 = 6;  // first scale-factor warp
 constexpr int kTile = 128;                     // weight rows per item, B rows per tile
 constexpr int kTileBytes = kTile * 128;        // 128 rows x 128 bytes (256 FP4 columns)
 constexpr int kSfStage = 4 * 512;              // four 64-column scale atoms
@@ -108,7 +112,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *acc_empty = acc_full + 1;
     uint64_t *sfb_full = acc_empty + 1;
     uint64_t *drain = sfb_full + 1;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *sfa_full = drain + 1;  // [S] the stage's weight scale factors are in tensor memory
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfa_full + S);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
     int *col_tok = reinterpret_cast<int *>(tmem_slot + 4);       // [2][32] token of each group row
     float *col_scale = reinterpret_cast<float *>(col_tok + 64);  // [2][32] its global scale
@@ -125,6 +130,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_init(acc_empty, 1);
         mbar_init(sfb_full, 1);
         mbar_init(drain, 1);
+        for (int i = 0; i < S; ++i) mbar_init(sfa_full + i, 4);
         fence_barrier_init();
         prefetch_tensormap(&tm_g);
         prefetch_tensormap(&tm_u);
@@ -218,20 +224,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 for (int ks = 0; ks < kstages; ++ks, ++it) {
                     const int st = it % S;
                     const uint32_t ph = (it / S) & 1u;
-                    if (!mbar_wait(full + st, ph, err, kSiteGemmFull)) {
+                    if (!mbar_wait(full + st, ph, err, kSiteGemmFull) ||
+                        !mbar_wait(sfa_full + st, ph, err, kSiteGemmFull)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    tc::fence_proxy_async_smem();
                     const uint32_t sb = smem_base + (uint32_t)st * kGuStage;
-                    const uint32_t sfa = sb + 3 * kTileBytes;
                     const uint32_t tsfa = tmem + kGuColSfa + (uint32_t)st * 32;
-#pragma unroll
-                    for (int at = 0; at < 4; ++at) {
-                        tc::cp_sf_atom(tsfa + 4 * at, tc::smem_desc_sf(sfa + at * 512));
-                        tc::cp_sf_atom(tsfa + 16 + 4 * at, tc::smem_desc_sf(sfa + kSfStage + at * 512));
-                    }
 #pragma unroll
                     for (int at = 0; at < 4; ++at) {
                         const uint32_t acc = (ks | at) != 0 ? 1u : 0u;
@@ -251,6 +251,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_wait_drain(drain, 0);
         }
         __syncwarp();
+    } else if (warp >= kSfWarp0) {
+        // ------------------------------------------------- scale factors
+        // Stage st's eight weight atoms (gate 0-3, up 0-3, 512 bytes apart)
+        // into columns tsfa + 4a of this warp's lane quarter. The slot is
+        // free: the stage was refilled only after the MMAs that read the
+        // slot's previous atoms completed.
+        const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int item = first; item < total && ok; item += ctas) {
+            for (int ks = 0; ks < kstages; ++ks, ++it) {
+                const int st = it % S;
+                if (!__all_sync(0xffffffffu, mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull))) {
+                    ok = false;
+                    break;
+                }
+                tc::st_sf_atoms<8>(tmem + quarter + kGuColSfa + (uint32_t)st * 32,
+                                   smem + (size_t)st * kGuStage + 3 * kTileBytes, 512, lane);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sfa_full + st);
+            }
+        }
     } else {
         // ----------------------------------------------------- epilogue
         const int sub = warp & 3;
@@ -355,7 +379,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *acc_full = bempty + 2;   // [2]
     uint64_t *acc_empty = acc_full + 2;  // [2]
     uint64_t *drain = acc_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *sfa_full = drain + 1;      // [S] the stage's weight scale factors are in tensor memory
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfa_full + S);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
     float *col_scale = reinterpret_cast<float *>(tmem_slot + 4);  // [2][32]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -374,6 +399,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(acc_empty + b, 1);
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < S; ++i) mbar_init(sfa_full + i, 4);
         fence_barrier_init();
         prefetch_tensormap(&tm_a);
         prefetch_tensormap(&tm_b);
@@ -503,7 +529,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 tc::fence_after_sync();
                 const int st = it % S;
-                if (!mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull)) {
+                if (!mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull) ||
+                    !mbar_wait(sfa_full + st, (it / S) & 1u, err, kSiteGemmFull)) {
                     ok = false;
                     break;
                 }
@@ -512,9 +539,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 const uint32_t sb = smem_base + (uint32_t)st * Cfg::kStage;
                 const uint32_t tsfa = tmem + Cfg::kColSfa + (uint32_t)st * kw * 4;
                 const uint32_t tsfb = tmem + Cfg::kColSfb + bb * kw * 4;
-#pragma unroll
-                for (int at = 0; at < kw; ++at)
-                    tc::cp_sf_atom(tsfa + 4 * at, tc::smem_desc_sf(sb + KB * kTileBytes + at * 512));
                 const uint32_t bsm = bbuf_base + bb * Cfg::kStage;
 #pragma unroll
                 for (int k = 0; k < kw; ++k) {
@@ -530,6 +554,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_wait_drain(drain, 0);
         }
         __syncwarp();
+    } else if (warp >= kSfWarp0) {
+        // ------------------------------------------------- scale factors
+        // The item's kw weight atoms (512 bytes apart after its tile) into
+        // columns tsfa + 4a of this warp's lane quarter; the slot is free
+        // once the stage has been refilled (see gate / up).
+        const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
+        uint32_t it = 0;
+        for (int j = 0; j < count; ++j, ++it) {
+            const int st = it % S;
+            if (!__all_sync(0xffffffffu, mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull))) break;
+            tc::st_sf_atoms<kw>(tmem + quarter + Cfg::kColSfa + (uint32_t)st * kw * 4,
+                                smem + (size_t)st * Cfg::kStage + KB * kTileBytes, 512, lane);
+            tc::wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(sfa_full + st);
+        }
     } else {
         // ----------------------------------------------------- epilogue
         const int sub = warp & 3;

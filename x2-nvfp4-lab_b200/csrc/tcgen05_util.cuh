@@ -2,8 +2,9 @@
 // memory allocation, shared-memory matrix descriptors, the block-scaled
 // NVFP4 MMA (kind::mxf4nvf4, E2M1 x E2M1 with E4M3 scales per 16 elements),
 // scale-factor copies into tensor memory, commits to mbarriers and
-// tensor-memory loads for the epilogue. Every helper issues exactly one PTX
-// instruction; the caller owns ordering (fences) and elected-thread rules.
+// tensor-memory loads and stores. Every helper but st_sf_atoms issues exactly
+// one PTX instruction; the caller owns ordering (fences) and elected-thread
+// rules.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -146,6 +147,57 @@ __device__ __forceinline__ void ld_32x32b_x4(uint32_t addr, uint32_t (&r)[4]) {
 }
 
 __device__ __forceinline__ void wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Store 32 consecutive 32-bit columns of the warp's 32 lanes (register c to
+// column c of the address).
+__device__ __forceinline__ void st_32x32b_x32(uint32_t addr, const uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+        "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};"
+        :
+        : "r"(addr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+          "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+          "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+        : "memory");
+}
+
+__device__ __forceinline__ void st_32x32b_x16(uint32_t addr, const uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+        :
+        : "r"(addr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+          "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
+
+__device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Scale-factor atoms of 32 rows x 16 bytes, `n` of them from shared memory
+// at `src` (atom a at src + a * stride), written by one warp into its lane
+// quarter as the layout tcgen05.cp .32x128b.warpx4 gives: lane r, columns
+// 4a..4a+3 = bytes r*16 .. r*16+15 of atom a (every lane quarter holds the
+// same 32 rows). `taddr` carries the warp's lane quarter in bits 16+.
+template <int N>
+__device__ __forceinline__ void st_sf_atoms(uint32_t taddr, const uint8_t *src, int stride, int lane) {
+    static_assert(N == 4 || N == 8, "one 16- or 32-column store");
+    uint32_t r[4 * N];
+#pragma unroll
+    for (int a = 0; a < N; ++a) {
+        uint4 v;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(src + a * stride + lane * 16))));
+        r[4 * a] = v.x;
+        r[4 * a + 1] = v.y;
+        r[4 * a + 2] = v.z;
+        r[4 * a + 3] = v.w;
+    }
+    if constexpr (N == 8)
+        st_32x32b_x32(taddr, r);
+    else
+        st_32x32b_x16(taddr, r);
+}
 
 }  // namespace tc
 }  // namespace nvfp4
