@@ -21,6 +21,208 @@ __device__ __forceinline__ unsigned float_order_key(float v) {
     return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+// Inverse of float_order_key (zero comes back as +0).
+__device__ __forceinline__ float float_from_order_key(unsigned k) {
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+// Shared-memory tables of the selection and dispatch step (E <= 256).
+struct RouteSelectSmem {
+    int ids[kDecodeMaxTokens * kTopK];
+    float w[kDecodeMaxTokens * kTopK];
+    float shared_w[kDecodeMaxTokens];
+    int cnt[256];
+    int off[257];
+    int aidx[256];
+    unsigned long long tokmask[256];
+    float invd[257];
+    int nrouted;
+};
+
+// Top-8 of token t by one warp from its logits in global memory: lane
+// `slot` < 8 keeps the slot-th pick (largest logit first, the lowest id
+// among equal logits, as the lab's selection loop), the softmax over the
+// picks relative to the largest (denominator summed in slot order), and lane
+// 8 the shared expert's sigmoid gate. Written to the scratch (ids, weights)
+// and to the block's selection tables.
+__device__ __forceinline__ void route_top8(const RouteArgs &a, int t, int lane, RouteSelectSmem &sm) {
+    const DecodeScratch &s = a.s;
+    const int E = a.E, R = E + 1;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? __ldcg(s.logits + (size_t)t * R + e) : -FLT_MAX;
+    }
+    const float sl = __ldcg(s.logits + (size_t)t * R + E);
+    // Lane `slot` keeps the slot-th pick.
+    unsigned taken = 0;
+    float my_v = 0.0f;
+    int my_i = 0;
+#pragma unroll 1
+    for (int slot = 0; slot < kTopK; ++slot) {
+        // Local best: strictly greater wins, so the lowest id survives ties.
+        float bv = -FLT_MAX;
+        int bi = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = lane + 32 * i;
+            if (e < E && !((taken >> i) & 1u) && v[i] > bv) {
+                bv = v[i];
+                bi = e;
+            }
+        }
+        // Warp best: largest value, then the lowest id among equal values.
+        const unsigned key = float_order_key(bv);
+        const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+        const unsigned imin = __reduce_min_sync(0xffffffffu, key == kmax ? (unsigned)bi : 0xffffffffu);
+        bi = (int)imin;
+        // The pick's value from its key (equal keys are equal values; a -0
+        // comes back as +0, which leaves every later difference and exp
+        // unchanged).
+        bv = float_from_order_key(kmax);
+        if (lane == slot) {
+            my_v = bv;
+            my_i = bi;
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    }
+    // Softmax over the eight picks relative to the largest; the
+    // denominator adds the picks in slot order.
+    const float top0 = __shfl_sync(0xffffffffu, my_v, 0);
+    const float my_e = lane < kTopK ? expf(my_v - top0) : 0.0f;
+    float e8[kTopK];
+#pragma unroll
+    for (int slot = 0; slot < kTopK; ++slot) e8[slot] = __shfl_sync(0xffffffffu, my_e, slot);
+    float den = 0.0f;
+#pragma unroll
+    for (int slot = 0; slot < kTopK; ++slot) den += e8[slot];
+    if (lane < kTopK) {
+        const float w = my_e / den;
+        s.ids[t * kSlots + lane] = my_i;
+        s.weights[t * kSlots + lane] = w;
+        sm.ids[t * kTopK + lane] = my_i;
+        sm.w[t * kTopK + lane] = w;
+    } else if (lane == kTopK) {
+        const float w = 1.0f / (1.0f + expf(-sl));
+        s.ids[t * kSlots + kTopK] = E;
+        s.weights[t * kSlots + kTopK] = w;
+        sm.shared_w[t] = w;
+    }
+}
+
+// Dispatch of the call's T tokens by the whole block, from the selection
+// tables: per-expert counts and offsets, the stable permutation of (token,
+// slot) pairs by expert, the compacted list of the experts computed here
+// (routed ones in [e_first, e_first + e_count), then the shared expert when
+// shared_here) with each one's token range, and the coefficient of every
+// (group, token) pair (routing weight x inverse down global scale).
+__device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSmem &sm) {
+    const DecodeScratch &s = a.s;
+    const int E = a.E, T = a.T;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+#pragma unroll 1
+    for (int e = threadIdx.x; e < 256; e += blockDim.x) {
+        sm.cnt[e] = 0;
+        sm.tokmask[e] = 0ull;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
+        const int e = sm.ids[i];
+        atomicAdd(&sm.cnt[e], 1);
+        atomicOr(&sm.tokmask[e], 1ull << (i / kTopK));
+    }
+    __syncthreads();
+    // Exclusive scans (counts -> offsets, local non-empty -> compact index).
+    if (warp == 0) {
+        int loc[8], aloc[8];
+        int sum = 0, asum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = lane * 8 + i;
+            const int c = e < E ? sm.cnt[e] : 0;
+            const int act = (c > 0 && e >= a.e_first && e < a.e_first + a.e_count) ? 1 : 0;
+            loc[i] = sum;
+            aloc[i] = asum;
+            sum += c;
+            asum += act;
+        }
+        int inc = sum, ainc = asum;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int o = __shfl_up_sync(0xffffffffu, inc, off);
+            const int ao = __shfl_up_sync(0xffffffffu, ainc, off);
+            if (lane >= off) {
+                inc += o;
+                ainc += ao;
+            }
+        }
+        const int excl = inc - sum, aexcl = ainc - asum;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int e = lane * 8 + i;
+            if (e < E) {
+                const int c = sm.cnt[e];
+                const int act = (c > 0 && e >= a.e_first && e < a.e_first + a.e_count) ? 1 : 0;
+                sm.off[e] = excl + loc[i];
+                sm.aidx[e] = act ? aexcl + aloc[i] : -1;
+            }
+        }
+        if (lane == 31) {
+            sm.off[E] = inc;
+            sm.nrouted = ainc;
+        }
+    }
+    __syncthreads();
+    const int nrouted = sm.nrouted;
+    const int nact = nrouted + (a.shared_here ? 1 : 0);
+#pragma unroll 1
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+        s.counts[e] = sm.cnt[e];
+        s.offsets[e] = sm.off[e];
+        const int ai = sm.aidx[e];
+        if (ai >= 0) {
+            s.active_expert[ai] = e;
+            s.tok_start[ai] = sm.off[e];
+            s.tok_count[ai] = sm.cnt[e];
+        }
+    }
+    if (threadIdx.x == 0) {
+        s.offsets[E] = sm.off[E];
+        *s.n_active = nact;
+    }
+    // coef_tab is read only at the (active expert, token) pairs written below.
+#pragma unroll 1
+    for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
+        const int t = i / kTopK;
+        const int e = sm.ids[i];
+        const int rank = __popcll(sm.tokmask[e] & ((1ull << t) - 1ull));
+        const int pos = sm.off[e] + rank;
+        s.perm[pos] = i;
+        s.tok_list[pos] = t;
+        const int ai = sm.aidx[e];
+        s.inv_pos[i] = ai >= 0 ? pos : -1;
+        s.slot_group[pos] = ai;
+        if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = sm.w[i] * sm.invd[e];
+    }
+    if (a.shared_here) {
+        const int ai = nrouted;
+#pragma unroll 1
+        for (int t = threadIdx.x; t < T; t += blockDim.x) {
+            const int pos = T * kTopK + t;
+            s.tok_list[pos] = t;
+            s.slot_group[pos] = ai;
+            s.coef_tab[ai * kDecodeMaxTokens + t] = sm.shared_w[t] * sm.invd[E];
+        }
+        if (threadIdx.x == 0) {
+            s.active_expert[ai] = E;
+            s.tok_start[ai] = T * kTopK;
+            s.tok_count[ai] = T;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- routing
 //
 // Router logit of token t and row r (row E = shared gate), FP32 throughout
@@ -35,8 +237,9 @@ __device__ __forceinline__ unsigned float_order_key(float v) {
 // Each CTA first copies its four router rows and its tokens (a contiguous
 // [tt][H] range of x in the caller's format) into shared memory with 16-byte
 // cp.async, so the dot products make no global round trip. The last CTA of a
-// token block to finish runs top-8 for those tokens (one warp per token); the
-// last token block to finish then dispatches.
+// token block to finish runs top-8 for those tokens (one warp per token, so
+// the selections of different blocks run on different SMs); the last token
+// block to finish then dispatches.
 __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     extern __shared__ __align__(16) uint8_t route_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -203,27 +406,18 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         }
     }
 
-    // The last row block of this token block runs top-8 for its tokens.
+    // The last row block of this token block runs top-8 for its tokens (one
+    // warp per token); the last token block to finish then dispatches.
     __shared__ unsigned s_ticket;
+    __shared__ RouteSelectSmem sm;
     __threadfence();
     __syncthreads();
     if (threadIdx.x == 0) s_ticket = atomicAdd(s.ticket + 1 + blockIdx.y, 1u);
     __syncthreads();
     if (s_ticket != gridDim.x - 1) return;
     __threadfence();
-
-    __shared__ int s_ids[kDecodeMaxTokens * kTopK];
-    __shared__ float s_w[kDecodeMaxTokens * kTopK];
-    __shared__ float s_shared_w[kDecodeMaxTokens];
-    __shared__ int s_cnt[256];
-    __shared__ int s_off[257];
-    __shared__ int s_aidx[256];
-    __shared__ unsigned long long s_tokmask[256];
-    __shared__ float s_invd[257];
-    __shared__ int s_nrouted;
-
-    // The dispatch's per-expert coefficients need the inverse down scales:
-    // request them now, store them after top-8.
+    // The coefficients need the inverse down scales: request them now,
+    // store them after top-8.
     const float *inv_down = a.inv_scales + 2 * (size_t)R;
     float invd[3];
 #pragma unroll
@@ -231,74 +425,11 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         const int e = threadIdx.x + 128 * q;
         invd[q] = e < R ? __ldg(inv_down + e) : 0.0f;
     }
-
-    const int E = a.E, T = a.T;
-    if (warp < tt) {
-        const int t = t0 + warp;
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = lane + 32 * i;
-            v[i] = e < E ? __ldcg(s.logits + (size_t)t * R + e) : -FLT_MAX;
-        }
-        const float sl = __ldcg(s.logits + (size_t)t * R + E);
-        // Lane `slot` keeps the slot-th pick.
-        unsigned taken = 0;
-        float my_v = 0.0f;
-        int my_i = 0;
-#pragma unroll 1
-        for (int slot = 0; slot < kTopK; ++slot) {
-            // Local best: strictly greater wins, so the lowest id survives ties.
-            float bv = -FLT_MAX;
-            int bi = 0;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int e = lane + 32 * i;
-                if (e < E && !((taken >> i) & 1u) && v[i] > bv) {
-                    bv = v[i];
-                    bi = e;
-                }
-            }
-            // Warp best: largest value, then the lowest id among equal values.
-            const unsigned key = float_order_key(bv);
-            const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
-            const unsigned imin = __reduce_min_sync(0xffffffffu, key == kmax ? (unsigned)bi : 0xffffffffu);
-            bi = (int)imin;
-            bv = __shfl_sync(0xffffffffu, bv, bi & 31);
-            if (lane == slot) {
-                my_v = bv;
-                my_i = bi;
-            }
-            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        }
-        // Softmax over the eight picks relative to the largest; the
-        // denominator adds the picks in slot order.
-        const float top0 = __shfl_sync(0xffffffffu, my_v, 0);
-        const float my_e = lane < kTopK ? expf(my_v - top0) : 0.0f;
-        float den = 0.0f;
-#pragma unroll 1
-        for (int slot = 0; slot < kTopK; ++slot) den += __shfl_sync(0xffffffffu, my_e, slot);
-        if (lane < kTopK) {
-            const float w = my_e / den;
-            s.ids[t * kSlots + lane] = my_i;
-            s.weights[t * kSlots + lane] = w;
-            s_ids[t * kTopK + lane] = my_i;
-            s_w[t * kTopK + lane] = w;
-        } else if (lane == kTopK) {
-            const float w = 1.0f / (1.0f + expf(-sl));
-            s.ids[t * kSlots + kTopK] = E;
-            s.weights[t * kSlots + kTopK] = w;
-            s_shared_w[t] = w;
-        }
-    }
+    if (warp < tt) route_top8(a, t0 + warp, lane, sm);
 #pragma unroll
     for (int q = 0; q < 3; ++q)
-        if (threadIdx.x + 128 * q < R) s_invd[threadIdx.x + 128 * q] = invd[q];
+        if (threadIdx.x + 128 * q < R) sm.invd[threadIdx.x + 128 * q] = invd[q];
     if (threadIdx.x == 0) s.ticket[1 + blockIdx.y] = 0u;
-
-    // The last token block to finish dispatches every token. With a single
-    // token block this CTA is it and its top-8 results are already in
-    // shared memory; otherwise every block's results are read back.
     if (gridDim.y > 1) {
         __threadfence();
         __syncthreads();
@@ -306,118 +437,33 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         __syncthreads();
         if (s_ticket != gridDim.y - 1) return;
         __threadfence();
-#pragma unroll 1
-        for (int i = threadIdx.x; i < T * kSlots; i += blockDim.x) {
-            const int t = i / kSlots, slot = i - t * kSlots;
-            if (slot < kTopK) {
-                s_ids[t * kTopK + slot] = __ldcg(s.ids + i);
-                s_w[t * kTopK + slot] = __ldcg(s.weights + i);
-            } else {
-                s_shared_w[t] = __ldcg(s.weights + i);
+        // Every token's picks, read back with all loads in flight at once.
+        constexpr int kPer = (kDecodeMaxTokens * kSlots + 127) / 128;
+        const int n = a.T * kSlots;
+        int rid[kPer];
+        float rw[kPer];
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const int i = threadIdx.x + 128 * q;
+            rid[q] = i < n ? __ldcg(s.ids + i) : 0;
+            rw[q] = i < n ? __ldcg(s.weights + i) : 0.0f;
+        }
+#pragma unroll
+        for (int q = 0; q < kPer; ++q) {
+            const int i = threadIdx.x + 128 * q;
+            if (i < n) {
+                const int t = i / kSlots, slot = i - t * kSlots;
+                if (slot < kTopK) {
+                    sm.ids[t * kTopK + slot] = rid[q];
+                    sm.w[t * kTopK + slot] = rw[q];
+                } else {
+                    sm.shared_w[t] = rw[q];
+                }
             }
         }
+        if (threadIdx.x == 0) *s.ticket = 0u;
     }
-#pragma unroll 1
-    for (int e = threadIdx.x; e < 256; e += blockDim.x) {
-        s_cnt[e] = 0;
-        s_tokmask[e] = 0ull;
-    }
-    __syncthreads();
-#pragma unroll 1
-    for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
-        const int e = s_ids[i];
-        atomicAdd(&s_cnt[e], 1);
-        atomicOr(&s_tokmask[e], 1ull << (i / kTopK));
-    }
-    __syncthreads();
-    // Exclusive scans (counts -> offsets, local non-empty -> compact index).
-    if (warp == 0) {
-        int loc[8], aloc[8];
-        int sum = 0, asum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = lane * 8 + i;
-            const int c = e < E ? s_cnt[e] : 0;
-            const int act = (c > 0 && e >= a.e_first && e < a.e_first + a.e_count) ? 1 : 0;
-            loc[i] = sum;
-            aloc[i] = asum;
-            sum += c;
-            asum += act;
-        }
-        int inc = sum, ainc = asum;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-            const int o = __shfl_up_sync(0xffffffffu, inc, off);
-            const int ao = __shfl_up_sync(0xffffffffu, ainc, off);
-            if (lane >= off) {
-                inc += o;
-                ainc += ao;
-            }
-        }
-        const int excl = inc - sum, aexcl = ainc - asum;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const int e = lane * 8 + i;
-            if (e < E) {
-                const int c = s_cnt[e];
-                const int act = (c > 0 && e >= a.e_first && e < a.e_first + a.e_count) ? 1 : 0;
-                s_off[e] = excl + loc[i];
-                s_aidx[e] = act ? aexcl + aloc[i] : -1;
-            }
-        }
-        if (lane == 31) {
-            s_off[E] = inc;
-            s_nrouted = ainc;
-        }
-    }
-    __syncthreads();
-    const int nrouted = s_nrouted;
-    const int nact = nrouted + (a.shared_here ? 1 : 0);
-#pragma unroll 1
-    for (int e = threadIdx.x; e < E; e += blockDim.x) {
-        s.counts[e] = s_cnt[e];
-        s.offsets[e] = s_off[e];
-        const int ai = s_aidx[e];
-        if (ai >= 0) {
-            s.active_expert[ai] = e;
-            s.tok_start[ai] = s_off[e];
-            s.tok_count[ai] = s_cnt[e];
-        }
-    }
-    if (threadIdx.x == 0) {
-        s.offsets[E] = s_off[E];
-        *s.n_active = nact;
-    }
-    // coef_tab is read only at the (active expert, token) pairs written below.
-#pragma unroll 1
-    for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
-        const int t = i / kTopK;
-        const int e = s_ids[i];
-        const int rank = __popcll(s_tokmask[e] & ((1ull << t) - 1ull));
-        const int pos = s_off[e] + rank;
-        s.perm[pos] = i;
-        s.tok_list[pos] = t;
-        const int ai = s_aidx[e];
-        s.inv_pos[i] = ai >= 0 ? pos : -1;
-        s.slot_group[pos] = ai;
-        if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = s_w[i] * s_invd[e];
-    }
-    if (a.shared_here) {
-        const int ai = nrouted;
-#pragma unroll 1
-        for (int t = threadIdx.x; t < T; t += blockDim.x) {
-            const int pos = T * kTopK + t;
-            s.tok_list[pos] = t;
-            s.slot_group[pos] = ai;
-            s.coef_tab[ai * kDecodeMaxTokens + t] = s_shared_w[t] * s_invd[E];
-        }
-        if (threadIdx.x == 0) {
-            s.active_expert[ai] = E;
-            s.tok_start[ai] = T * kTopK;
-            s.tok_count[ai] = T;
-        }
-    }
-    if (threadIdx.x == 0) *s.ticket = 0u;
+    route_dispatch(a, sm);
 }
 
 }  // namespace
@@ -471,38 +517,38 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
     return off;
 }
 
-cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent) {
-    const int R = a.E + 1;
-    const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
-    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2;
-    if (smem > 48 * 1024) {
-        // Raise the limit to all the shared memory a CTA may hold, once per
-        // device (bit d of `done`).
-        static std::atomic<uint64_t> done{0};
-        int dev = 0;
-        cudaError_t err = cudaGetDevice(&dev);
-        if (err != cudaSuccess) return err;
-        const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
-        if (!bit || !(done.load() & bit)) {
-            cudaFuncAttributes fa{};
-            err = cudaFuncGetAttributes(&fa, moe_route_kernel);
-            if (err != cudaSuccess) return err;
-            int optin = 0;
-            err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-            if (err != cudaSuccess) return err;
-            err = cudaFuncSetAttribute(moe_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       optin - (int)fa.sharedSizeBytes);
-            if (err != cudaSuccess) return err;
-            done.fetch_or(bit);
-        }
-    }
+namespace {
+
+// Raise a routing kernel's dynamic shared-memory limit to all a CTA may hold,
+// once per device (bit d of `done`).
+template <typename K>
+cudaError_t route_smem_limit(K kernel, std::atomic<uint64_t> &done) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+    if (bit && (done.load() & bit)) return cudaSuccess;
+    cudaFuncAttributes fa{};
+    err = cudaFuncGetAttributes(&fa, kernel);
+    if (err != cudaSuccess) return err;
+    int optin = 0;
+    err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (err != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes);
+    if (err == cudaSuccess) done.fetch_or(bit);
+    return err;
+}
+
+template <typename... KArgs>
+cudaError_t launch_maybe_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                   bool dependent, const RouteArgs &a) {
     if (!dependent) {
-        moe_route_kernel<<<grid, kRouteRowsPerCta * 32, smem, stream>>>(a);
+        kernel<<<grid, block, smem, stream>>>(a);
         return cudaGetLastError();
     }
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
-    cfg.blockDim = dim3(kRouteRowsPerCta * 32);
+    cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
@@ -510,7 +556,21 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, moe_route_kernel, a);
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
+}  // namespace
+
+cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent) {
+    const int R = a.E + 1;
+    const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
+    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2;
+    if (smem > 48 * 1024) {
+        static std::atomic<uint64_t> done{0};
+        const cudaError_t err = route_smem_limit(moe_route_kernel, done);
+        if (err != cudaSuccess) return err;
+    }
+    return launch_maybe_dependent(moe_route_kernel, grid, dim3(kRouteRowsPerCta * 32), smem, stream, dependent, a);
 }
 
 }  // namespace nvfp4
