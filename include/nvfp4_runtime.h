@@ -449,11 +449,11 @@ NVFP4_API nvfp4_status nvfp4_moe_finalize_bf16(
 /* additive: expert-GEMV kernels of the decode path (calls of up to 64
  * tokens). TENSOR_CORE (default) streams the weights through tcgen05
  * block-scaled NVFP4 MMAs with the activations as four NVFP4 terms per row
- * (relative RMSE about 1e-4 against FP32 activations); it serves calls of 12
+ * (relative RMSE about 1e-4 against FP32 activations); it serves calls of 4
  * to 32 tokens on banks with hidden a multiple of 256 up to 2048 and
  * intermediate 256 or 512, and other calls use IN_REGISTER, which decodes
  * E2M1/E4M3 to f16 in registers and keeps the activations in f16 (faster
- * below 12 tokens). Takes effect at the next forward. */
+ * below 4 tokens). Takes effect at the next forward. */
 #define NVFP4_DECODE_KERNELS_TENSOR_CORE 0
 #define NVFP4_DECODE_KERNELS_IN_REGISTER 1
 NVFP4_API nvfp4_status nvfp4_moe_bank_set_decode_kernels(

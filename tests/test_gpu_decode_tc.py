@@ -63,7 +63,7 @@ def _check_routing(bank, ref, T):
     np.testing.assert_array_equal(r.perm, ref.perm)
 
 
-@pytest.mark.parametrize("T", [12, 17, 32])
+@pytest.mark.parametrize("T", [4, 5, 12, 17, 32])
 def test_tensor_core_decode(cuda_runtime, tc_bank, tc_host, T):
     got, xf, rf = _run(tc_bank, tc_host, T, 400 + T)
     same = moe_layer_prefill(tc_host, xf, rf, 4, 4)
@@ -88,7 +88,7 @@ def test_f32_abi_one_token(cuda_runtime, tc_bank, tc_host):
     assert max_abs_rel(got, fp32.out) <= MAX_ABS_REL_TOL
 
 
-@pytest.mark.parametrize("T", [1, 32, 48])
+@pytest.mark.parametrize("T", [1, 3, 8, 32, 48])
 def test_in_register_decode(cuda_runtime, tc_bank, tc_host, T):
     tc_bank.set_decode_kernels("in_register")
     try:

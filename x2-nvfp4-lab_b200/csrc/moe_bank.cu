@@ -136,9 +136,10 @@ nvfp4_status check_upload_args(const nvfp4_moe_bank *bank, int expert, int proje
 // moe_gate_up, moe_down). Caller holds the runtime's queue mutex.
 // Below kDecodeTcMinTokens tokens the in-register GEMVs finish first (they
 // split the few active experts into more, smaller work items); from there on
-// the tensor-core GEMVs stream the weights faster (measured on one B200,
-// E 256, H 2048, I 512: equal near 12 tokens, 124 vs 140 us at 32).
-constexpr int kDecodeTcMinTokens = 12;
+// the tensor-core GEMVs stream the weights faster (layer call on one B200,
+// E 256, H 2048, I 512, L2 flushed: 42.0 vs 43.1 us at 3 tokens, 50.2 vs
+// 49.1 at 4, 72.8 vs 61.4 at 8).
+constexpr int kDecodeTcMinTokens = 4;
 
 bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
     return bank->decode_kernels == NVFP4_DECODE_KERNELS_TENSOR_CORE && bank->tc_ready &&
