@@ -113,7 +113,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *sfb_full = acc_empty + 1;
     uint64_t *drain = sfb_full + 1;
     uint64_t *sfa_full = drain + 1;  // [S] the stage's weight scale factors are in tensor memory
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfa_full + S);
+    uint64_t *sfb_ready = sfa_full + S;  // x's scale factors are in tensor memory
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfb_ready + 1);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
     int *col_tok = reinterpret_cast<int *>(tmem_slot + 4);       // [2][32] token of each group row
     float *col_scale = reinterpret_cast<float *>(col_tok + 64);  // [2][32] its global scale
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_init(sfb_full, 1);
         mbar_init(drain, 1);
         for (int i = 0; i < S; ++i) mbar_init(sfa_full + i, 4);
+        mbar_init(sfb_ready, 4);
         fence_barrier_init();
         prefetch_tensormap(&tm_g);
         prefetch_tensormap(&tm_u);
@@ -208,12 +210,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t it = 0, tcount = 0;
             bool ok = true;
             if ((int)blockIdx.x < ctas) {
-                ok = mbar_wait(sfb_full, 0, err, kSiteGemmFull);
+                ok = mbar_wait(sfb_ready, 0, err, kSiteGemmFull);
                 tc::fence_after_sync();
-                tc::fence_proxy_async_smem();
-                const uint32_t sfb_base = smem_u32(sfb_stage);
-                for (int at = 0; ok && at < kw; ++at)
-                    tc::cp_sf_atom(tmem + kGuColSfb + 4 * at, tc::smem_desc_sf(sfb_base + at * 512));
             }
             for (int item = first; item < total && ok; item += ctas, ++tcount) {
                 if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1u, err, kSiteGemmAccEmpty)) {
@@ -260,6 +258,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
         uint32_t it = 0;
         bool ok = true;
+        // First x's kw scale atoms (every item's B, kw a multiple of 4),
+        // four per store.
+        if ((int)blockIdx.x < ctas) {
+            ok = __all_sync(0xffffffffu, mbar_wait(sfb_full, 0, err, kSiteGemmFull));
+            if (ok) {
+#pragma unroll 1
+                for (int at = 0; at < kw; at += 4)
+                    tc::st_sf_atoms<4>(tmem + quarter + kGuColSfb + 4 * at, sfb_stage + at * 512, 512, lane);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sfb_ready);
+            }
+        }
         for (int item = first; item < total && ok; item += ctas) {
             for (int ks = 0; ks < kstages; ++ks, ++it) {
                 const int st = it % S;
