@@ -59,6 +59,7 @@ def parse_args():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill legs (configs 2 and 3)")
+    p.add_argument("--no-stack", action="store_true", help="skip the 40-layer stack leg (config 4)")
     p.add_argument("--decode-kernels", choices=["tensor_core", "in_register"], default="tensor_core",
                    help="decode expert GEMVs (the library's default is tensor_core)")
     return p.parse_args()
@@ -286,6 +287,63 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     }
 
 
+def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40) -> dict:
+    """the resident decode stack of ``layers`` independently
+    seeded layers (h <- h + MoE(RMSNorm(h)), attention omitted), all banks in
+    HBM, one CUDA graph per batch size replayed per step. Device time per
+    step (CUDA events around each replay; the step's input is copied in
+    before the start event); the weights a step streams (hundreds of MB)
+    are far larger than L2, so no flush is needed. Algorithmic bytes per
+    step: for every layer its routed experts' and the shared expert's three
+    projections, the router and shared gate, and the hidden state in and out."""
+    import numpy as np
+    import torch
+
+    from vllm_nvfp4_cuda import synthetic
+    from vllm_nvfp4_cuda.stack import MoeStack
+
+    banks = [synthetic.build_bank(rt, E, H, I, seed, layer=101 + layer)[0] for layer in range(layers)]
+    stack = MoeStack(rt, banks)
+    stream = torch.cuda.Stream()
+    peak = measured_peaks().get("hbm_gbs")
+    out = {"workload": "config4_stack40", "layers": layers, "l2": "not flushed (weights per step >> L2)",
+           "launches_per_layer": "RMSNorm + the layer call's decode kernels, one CUDA graph per step"}
+    for T in (1, 64):
+        g = stack.capture(T)
+        xs = [synthetic.synthetic_tokens(T, H, 12000 + 97 * T + i) for i in range(4)]
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        with torch.cuda.stream(stream):
+            for i in range(warmup):
+                g.run(xs[i % 4])
+            for i in range(steps):
+                g.input.copy_(xs[i % 4])
+                starts[i].record(stream)
+                g.replay()
+                ends[i].record(stream)
+        stream.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in zip(starts, ends))
+        step_bytes = 0
+        for b in banks:
+            r = b.last_routing(T)
+            uniq = len(set(np.asarray(r.ids)[:, :8].reshape(-1).tolist()))
+            step_bytes += (uniq + 1) * 3 * PER_PROJ_BYTES + (E + 1) * H * 2 + 2 * T * H * 2
+        gbs = step_bytes / (ms / 1000.0) / 1e9
+        out[f"batch{T}"] = {
+            "tokens_per_s": round(T / (ms / 1000.0), 1),
+            "us_per_step": round(ms * 1000.0, 2),
+            "us_per_layer": round(ms * 1000.0 / layers, 2),
+            "algorithmic_mb_per_step": round(step_bytes / 1e6, 1),
+            "hbm_gbs": round(gbs, 1),
+            "hbm_frac_of_measured": round(gbs / peak, 4) if peak else None,
+        }
+        g.close()
+        del g
+    for b in banks:
+        b.close()
+    return out
+
+
 def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmup: int) -> dict:
     """Expert parallelism across the job's GPUs: rank r holds routed experts
     [r*E/N, (r+1)*E/N) (the shared expert on rank 0), the tokens are the same
@@ -388,10 +446,12 @@ def run_ours(args) -> int:
     from vllm_nvfp4_cuda.runtime import Runtime
 
     T = args.tokens
-    # The library runs calls of 12 to 32 tokens on the tensor-core expert
+    # The library runs calls of 4 to 32 tokens on the tensor-core expert
     # GEMVs for this shape (five launches per layer call), others in-register
-    # (four launches).
-    tc_decode = 12 <= T <= 32 and args.decode_kernels == "tensor_core"
+    # (three launches up to 16 tokens, where the down kernel combines; four
+    # above).
+    tc_decode = 4 <= T <= 32 and args.decode_kernels == "tensor_core"
+    launches = 5 if tc_decode else (3 if T <= 16 else 4)
     rt = Runtime()
     bank, meta = synthetic.build_bank(rt, E, H, I, args.seed)
     bank.set_decode_kernels(args.decode_kernels)
@@ -546,6 +606,10 @@ def run_ours(args) -> int:
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline_measure(T, args.seed)
 
+    stack = None
+    if world == 1 and not args.no_stack:
+        stack = stack_leg(rt, args.seed, 30, 3)
+
     if rank == 0:
         clk = clocks.summary()
         line = {
@@ -596,9 +660,10 @@ def run_ours(args) -> int:
             },
             "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * T * H * 2,
                     "d2h_bytes_per_step": T * H * 2},
-            "gpu_launches": (5 if tc_decode else 4) * args.steps,
+            "gpu_launches": launches * args.steps,
             "prefill": prefill,
             "expert_parallel": ep,
+            "stack": stack,
             "clocks": clk,
             "cpu_baseline": cpu,
         }

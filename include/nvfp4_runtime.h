@@ -224,6 +224,24 @@ NVFP4_API nvfp4_status nvfp4_rmsnorm_device_enqueue_bf16(
     float epsilon,
     nvfp4_buffer * dst);
 
+/* additive: the same BF16 RMSNorm on raw device pointers (x, dst BF16
+ * [rows, cols], weight BF16 [cols]), enqueued on `stream` (a cudaStream_t;
+ * NULL selects the runtime's stream): the per-layer pre-norm of a resident
+ * layer stack driven from a host framework's tensors (the lab's full-model
+ * driver, native_nvfp4/bench_moe_full_model.py:388-395, norms each layer's
+ * input before its bank). Statistic per row: FP32 fmaf partial sums of 256
+ * column-strided threads, xor butterfly per warp, warp sums in order, then
+ * rsqrtf(mean + epsilon). */
+NVFP4_API nvfp4_status nvfp4_rmsnorm_ptr_bf16(
+    nvfp4_runtime * runtime,
+    const void * x_bf16,
+    const void * weight_bf16,
+    int rows,
+    int cols,
+    float epsilon,
+    void * dst_bf16,
+    void * stream);
+
 /* ------------------------------------------------------------- MoE bank */
 
 /* reference: nvfp4_runtime.h:392-403 (implemented at

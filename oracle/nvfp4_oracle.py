@@ -437,6 +437,50 @@ def moe_layer_prefill(bank: BankHost, x: np.ndarray, residual: np.ndarray | None
 # ------------------------------------------------------------- comparisons
 
 
+def rmsnorm_bf16(x: np.ndarray, weight: np.ndarray | None = None, epsilon: float = 1e-6) -> np.ndarray:
+    """Row-wise RMSNorm of x [rows, cols] (BF16 values held in FP32), output
+    rounded to BF16 values. The lab's ``rmsnorm_f32``
+    (``native_nvfp4/kernels/nvfp4_gemv.cl:1171-1197``: sum of squares,
+    x * rsqrt(mean + epsilon) * weight) in the reduction order of the CUDA
+    kernel that serves it: 256 column-strided FP32 partial sums (fused
+    multiply-add), an xor butterfly over each warp of 32 partials (offsets
+    16, 8, 4, 2, 1), the eight warp sums added in order from 0. The CUDA
+    kernel's rsqrtf is within 2 ulp of the 1/sqrt used here."""
+    x = np.asarray(x, dtype=np.float32)
+    rows, cols = x.shape
+    w = np.ones(cols, dtype=np.float32) if weight is None else np.asarray(weight, dtype=np.float32)
+    threads = 256
+    part = np.zeros((rows, threads), dtype=np.float32)
+    for c0 in range(0, cols, threads):
+        v = x[:, c0:c0 + threads].astype(np.float64)
+        n = v.shape[1]
+        # fmaf(v, v, ss): the exact v*v + ss rounded once to FP32.
+        part[:, :n] = (v * v + part[:, :n].astype(np.float64)).astype(np.float32)
+    warps = part.reshape(rows, threads // 32, 32)
+    for off in (16, 8, 4, 2, 1):
+        idx = np.arange(32) ^ off
+        warps = (warps + warps[:, :, idx]).astype(np.float32)
+    tot = np.zeros(rows, dtype=np.float32)
+    for wi in range(threads // 32):
+        tot = (tot + warps[:, wi, 0]).astype(np.float32)
+    inv = (np.float32(1.0) / np.sqrt(tot / np.float32(cols) + np.float32(epsilon))).astype(np.float32)
+    out = ((x * inv[:, None]).astype(np.float32) * w[None, :]).astype(np.float32)
+    return bf16_bits_to_f32(bf16_bits_from_f32(out))
+
+
+def moe_stack(banks: list[BankHost], x: np.ndarray, epsilon: float = 1e-6, norm_weights=None) -> np.ndarray:
+    """Resident decode stack without attention, BF16 hidden state: per layer
+    h = BF16(h + moe_layer(RMSNorm(h))), the lab's full-model step
+    (``native_nvfp4/bench_moe_full_model.py:388-406``: ``rmsnorm_device``,
+    ``bank.decode_device``, ``add_device``) with its attention omitted."""
+    h = bf16_bits_to_f32(bf16_bits_from_f32(np.asarray(x, dtype=np.float32)))
+    for layer, bank in enumerate(banks):
+        w = None if norm_weights is None else norm_weights[layer]
+        normed = rmsnorm_bf16(h, w, epsilon)
+        h = bf16_bits_to_f32(bf16_bits_from_f32(moe_layer(bank, normed, h).out))
+    return h
+
+
 def rel_rmse(actual: np.ndarray, expected: np.ndarray) -> float:
     a = np.asarray(actual, dtype=np.float64)
     e = np.asarray(expected, dtype=np.float64)

@@ -23,9 +23,11 @@ from oracle.nvfp4_oracle import (
     expert_forward,
     max_abs_rel,
     moe_layer,
+    moe_stack,
     nvfp4_gemv,
     quantize_nvfp4,
     rel_rmse,
+    rmsnorm_bf16,
     router_logits,
     top8_route,
 )
@@ -210,3 +212,25 @@ def test_bf16_roundtrip():
     x = np.array([1.0, -2.5, 1.00390625, 3.4e38, 1e-40], dtype=np.float32)
     b = bf16_bits_from_f32(x)
     assert bf16_bits_to_f32(b)[0] == 1.0 and bf16_bits_to_f32(b)[1] == -2.5
+
+
+def test_rmsnorm_restatement():
+    """The oracle's RMSNorm (CUDA kernel's reduction order, BF16 output) is
+    the lab's x * rsqrt(mean(x^2) + eps) * w to within one BF16 rounding."""
+    rng = np.random.default_rng(5)
+    x = bf16_bits_to_f32(bf16_bits_from_f32(rng.standard_normal((4, 2048)).astype(np.float32) * 3))
+    w = bf16_bits_to_f32(bf16_bits_from_f32(rng.standard_normal(2048).astype(np.float32) * 0.5 + 1))
+    exact = x.astype(np.float64) / np.sqrt(np.mean(x.astype(np.float64) ** 2, axis=1, keepdims=True) + 1e-6) * w
+    got = rmsnorm_bf16(x, w, 1e-6)
+    assert np.all(np.abs(got - exact) <= np.abs(exact) * 2.0 ** -8 + 1e-12)
+    np.testing.assert_array_equal(bf16_bits_to_f32(bf16_bits_from_f32(got)), got)
+
+
+def test_stack_composes_layers():
+    """moe_stack is h <- BF16(h + moe_layer(RMSNorm(h))) layer by layer."""
+    banks = [synthetic_np.make_bank(8, 128, 64, 40 + i) for i in range(2)]
+    x = bf16_bits_to_f32(synthetic_np.tokens_bf16(2, 128, 3))
+    h = x
+    for b in banks:
+        h = bf16_bits_to_f32(bf16_bits_from_f32(moe_layer(b, rmsnorm_bf16(h), h).out))
+    np.testing.assert_array_equal(moe_stack(banks, x), h)

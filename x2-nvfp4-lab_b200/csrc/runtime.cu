@@ -583,6 +583,24 @@ extern "C" NVFP4_API nvfp4_status nvfp4_rmsnorm_device_enqueue_bf16(nvfp4_runtim
     return rmsnorm_enqueue(runtime, x, weight, rows, cols, epsilon, dst, true);
 }
 
+extern "C" NVFP4_API nvfp4_status nvfp4_rmsnorm_ptr_bf16(nvfp4_runtime *runtime, const void *x_bf16,
+                                                         const void *weight_bf16, int rows, int cols, float epsilon,
+                                                         void *dst_bf16, void *stream) {
+    if (!runtime || !x_bf16 || !weight_bf16 || !dst_bf16 || rows <= 0 || cols <= 0 || epsilon < 0.0f)
+        return fail_invalid("invalid RMSNorm arguments");
+    try {
+        std::lock_guard<std::mutex> lock(runtime->queue_mutex);
+        runtime->direct_call(static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {
+            rmsnorm_kernel<true><<<rows, 256, 0, s>>>(x_bf16, weight_bf16, dst_bf16, cols, epsilon);
+            check_cuda(cudaGetLastError(), "rmsnorm_kernel");
+        });
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
+}
+
 extern "C" NVFP4_API nvfp4_status nvfp4_bf16_gemv_device_enqueue(nvfp4_runtime *runtime,
                                                                  const nvfp4_buffer *weights,
                                                                  const nvfp4_buffer *x, int rows,

@@ -171,6 +171,8 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "nvfp4_moe_finalize_bf16": (
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_rmsnorm_ptr_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p], C.c_int),
     "nvfp4_quantize_rows_enqueue": (
         [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
         C.c_int),
@@ -751,6 +753,29 @@ class Runtime:
                 self.handle, _tensor_ptr(sum_f32), _tensor_ptr(residual) if residual is not None else None,
                 _tensor_ptr(out), sum_f32.shape[0], sum_f32.shape[1], _stream_handle(s)),
             "nvfp4_moe_finalize_bf16")
+        return out
+
+    def rmsnorm_bf16(self, x, weight, epsilon: float = 1e-6, out=None, stream=None):
+        """additive: BF16 RMSNorm of the rows of a CUDA bfloat16 tensor [rows, cols]
+        with a bfloat16 weight [cols] (the layer stack's pre-norm), enqueued on
+        ``stream`` (None: torch's current stream)."""
+        import torch
+
+        if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2:
+            raise ValueError("x must be a CUDA bfloat16 tensor [rows, cols]")
+        if weight.dtype != torch.bfloat16 or weight.numel() != x.shape[1]:
+            raise ValueError("weight must be bfloat16 with one entry per column")
+        x = x.contiguous()
+        weight = weight.contiguous()
+        if out is None:
+            out = torch.empty_like(x)
+        elif out.shape != x.shape or out.dtype != torch.bfloat16 or not out.is_contiguous():
+            raise ValueError("out must be a contiguous bfloat16 tensor shaped like x")
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self._check(
+            self.lib.nvfp4_rmsnorm_ptr_bf16(self.handle, _tensor_ptr(x), _tensor_ptr(weight), x.shape[0], x.shape[1],
+                                            float(epsilon), _tensor_ptr(out), _stream_handle(s)),
+            "nvfp4_rmsnorm_ptr_bf16")
         return out
 
     def quantize_rows(self, x, terms: int):
