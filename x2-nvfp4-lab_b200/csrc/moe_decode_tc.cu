@@ -657,10 +657,6 @@ __global__ void __launch_bounds__(256) quantize_act_tc_kernel(DecodeScratch s, i
     const int lane = threadIdx.x & 31;
     const int p = blockIdx.x * 8 + (threadIdx.x >> 5);
     if (p >= rows) return;
-    const int ai = s.slot_group[p];
-    if (ai < 0) return;
-    const int n0 = kDecodeTcTerms * (p - s.tok_start[ai]);
-    if (n0 < 0 || n0 + kDecodeTcTerms > kTile) return;
     const int nb = I / 16;
     const __half *row = s.act + (size_t)p * I;
     auto load_block = [&](int b, float (&v)[16]) {
@@ -677,21 +673,41 @@ __global__ void __launch_bounds__(256) quantize_act_tc_kernel(DecodeScratch s, i
             }
         }
     };
-    float amax = 0.0f;
-    for (int b = lane; b < nb; b += 32) {
-        float v[16];
-        load_block(b, v);
+    // Up to 512 columns (a block per lane) the row stays in registers from
+    // the amax pass to the term pass, and its load is issued together with
+    // the group lookup.
+    float v0[16];
+    const bool one = nb <= 32;
+    if (one) {
+        if (lane < nb) {
+            load_block(lane, v0);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            for (int i = 0; i < 16; ++i) v0[i] = 0.0f;
+        }
+    }
+    const int ai = s.slot_group[p];
+    if (ai < 0) return;
+    const int n0 = kDecodeTcTerms * (p - s.tok_start[ai]);
+    if (n0 < 0 || n0 + kDecodeTcTerms > kTile) return;
+    float amax = 0.0f;
+    if (one) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v0[i]));
+    } else {
+        for (int b = lane; b < nb; b += 32) {
+            float v[16];
+            load_block(b, v);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        }
     }
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
     const float g = row_global_scale(amax);
     if (lane == 0) s.ga_tc[p] = g;
     uint8_t *atoms = s.asf_tc + (size_t)ai * (I / 64) * 512;
-    for (int b = lane; b < nb; b += 32) {
-        float v[16];
-        load_block(b, v);
+    auto write_terms = [&](int b, float (&v)[16]) {
         // Terms in a loop that is not unrolled: this kernel runs once per
         // layer call with cold instruction caches, where code size is time.
 #pragma unroll 1
@@ -701,6 +717,15 @@ __global__ void __launch_bounds__(256) quantize_act_tc_kernel(DecodeScratch s, i
             *reinterpret_cast<uint2 *>(s.aq_tc + ((size_t)kDecodeTcTerms * p + j) * (I / 2) + 8 * b) =
                 make_uint2(c0, c1);
             atoms[sf_atom_byte(n0 + j, b)] = static_cast<uint8_t>(sc);
+        }
+    };
+    if (one) {
+        if (lane < nb) write_terms(lane, v0);
+    } else {
+        for (int b = lane; b < nb; b += 32) {
+            float v[16];
+            load_block(b, v);
+            write_terms(b, v);
         }
     }
 }
