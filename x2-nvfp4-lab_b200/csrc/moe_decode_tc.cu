@@ -114,7 +114,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *drain = sfb_full + 1;
     uint64_t *sfa_full = drain + 1;  // [S] the stage's weight scale factors are in tensor memory
     uint64_t *sfb_ready = sfa_full + S;  // x's scale factors are in tensor memory
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfb_ready + 1);
+    uint64_t *sfa_in = sfb_ready + 1;    // [S] the stage's weight scale atoms are in shared memory
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfa_in + S);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
     int *col_tok = reinterpret_cast<int *>(tmem_slot + 4);       // [2][32] token of each group row
     float *col_scale = reinterpret_cast<float *>(col_tok + 64);  // [2][32] its global scale
@@ -131,7 +132,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         mbar_init(acc_empty, 1);
         mbar_init(sfb_full, 1);
         mbar_init(drain, 1);
-        for (int i = 0; i < S; ++i) mbar_init(sfa_full + i, 4);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(sfa_full + i, 4);
+            mbar_init(sfa_in + i, 1);
+        }
         mbar_init(sfb_ready, 4);
         fence_barrier_init();
         prefetch_tensormap(&tm_g);
@@ -184,13 +188,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 uint8_t *stage = smem + (size_t)st * kGuStage;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(full + st, kGuStage);
+                    // The scale atoms first and on their own barrier: the
+                    // store warps need only them, and they land first.
+                    mbar_arrive_expect_tx(sfa_in + st, 2 * kSfStage);
+                    bulk_g2s(stage + 3 * kTileBytes, a.sfa[0] + sfa_off + (size_t)ks * kSfStage, kSfStage, sfa_in + st);
+                    bulk_g2s(stage + 3 * kTileBytes + kSfStage, a.sfa[1] + sfa_off + (size_t)ks * kSfStage, kSfStage,
+                             sfa_in + st);
+                    mbar_arrive_expect_tx(full + st, 3 * kTileBytes);
                     tma_load_2d(stage, &tm_g, full + st, ks * 128, arow);
                     tma_load_2d(stage + kTileBytes, &tm_u, full + st, ks * 128, arow);
                     tma_load_2d(stage + 2 * kTileBytes, &tm_b, full + st, ks * 128, 0);
-                    bulk_g2s(stage + 3 * kTileBytes, a.sfa[0] + sfa_off + (size_t)ks * kSfStage, kSfStage, full + st);
-                    bulk_g2s(stage + 3 * kTileBytes + kSfStage, a.sfa[1] + sfa_off + (size_t)ks * kSfStage, kSfStage,
-                             full + st);
                 }
             }
         }
@@ -199,7 +206,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             if (lane == 0) {
                 if ((int)blockIdx.x < ctas) mbar_wait_drain(sfb_full, 0);
                 const uint32_t first = it > (uint32_t)S ? it - S : 0u;
-                for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                for (uint32_t k = first; k < it; ++k) {
+                    mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                    mbar_wait_drain(sfa_in + (k % S), (k / S) & 1u);
+                }
             }
         }
     } else if (warp == 1) {
@@ -275,7 +285,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int item = first; item < total && ok; item += ctas) {
             for (int ks = 0; ks < kstages; ++ks, ++it) {
                 const int st = it % S;
-                if (!__all_sync(0xffffffffu, mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull))) {
+                if (!__all_sync(0xffffffffu, mbar_wait(sfa_in + st, (it / S) & 1u, err, kSiteGemmFull))) {
                     ok = false;
                     break;
                 }
@@ -392,7 +402,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint64_t *acc_empty = acc_full + 2;  // [2]
     uint64_t *drain = acc_empty + 2;
     uint64_t *sfa_full = drain + 1;      // [S] the stage's weight scale factors are in tensor memory
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfa_full + S);
+    uint64_t *sfa_in = sfa_full + S;     // [S] the stage's weight scale atoms are in shared memory
+    uint64_t *sfb_ready = sfa_in + S;    // [2] the B buffer's scale factors are in tensor memory
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sfb_ready + 2);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
     float *col_scale = reinterpret_cast<float *>(tmem_slot + 4);  // [2][32]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -411,7 +423,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             mbar_init(acc_empty + b, 1);
         }
         mbar_init(drain, 1);
-        for (int i = 0; i < S; ++i) mbar_init(sfa_full + i, 4);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(sfa_full + i, 4);
+            mbar_init(sfa_in + i, 1);
+        }
+        mbar_init(sfb_ready, 4);
+        mbar_init(sfb_ready + 1, 4);
         fence_barrier_init();
         prefetch_tensormap(&tm_a);
         prefetch_tensormap(&tm_b);
@@ -490,16 +507,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
                 uint8_t *stage = smem + (size_t)st * Cfg::kStage;
                 const int arow = ti.e * a.H + ti.mt * kTile;
-                mbar_arrive_expect_tx(full + st, Cfg::kStage);
+                mbar_arrive_expect_tx(sfa_in + st, kw * 512);
+                bulk_g2s(stage + KB * kTileBytes, a.sfa[0] + (size_t)(arow / kTile) * kw * 512, kw * 512, sfa_in + st);
+                mbar_arrive_expect_tx(full + st, KB * kTileBytes);
 #pragma unroll
                 for (int box = 0; box < KB; ++box) tma_load_2d(stage + box * kTileBytes, &tm_a, full + st, box * 128, arow);
-                bulk_g2s(stage + KB * kTileBytes, a.sfa[0] + (size_t)(arow / kTile) * kw * 512, kw * 512, full + st);
                 ++it;
             }
             if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
                 // Drain the copies still in flight before the CTA exits.
                 const uint32_t first = it > (uint32_t)S ? it - S : 0u;
-                for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                for (uint32_t k = first; k < it; ++k) {
+                    mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                    mbar_wait_drain(sfa_in + (k % S), (k / S) & 1u);
+                }
                 const uint32_t bfirst = nb > 2u ? nb - 2 : 0u;
                 for (uint32_t k = bfirst; k < nb; ++k) mbar_wait_drain(bfull + (k & 1u), (k >> 1) & 1u);
             }
@@ -520,16 +541,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (ai != prev_ai) {
                     if (nb > 0) tc::commit(bempty + ((nb - 1) & 1u));
                     const uint32_t bb = nb & 1u;
-                    if (!mbar_wait(bfull + bb, (nb >> 1) & 1u, err, kSiteGemmFull)) {
+                    if (!mbar_wait(bfull + bb, (nb >> 1) & 1u, err, kSiteGemmFull) ||
+                        !mbar_wait(sfb_ready + bb, (nb >> 1) & 1u, err, kSiteGemmFull)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
-                    tc::fence_proxy_async_smem();
-                    const uint32_t sfb = bbuf_base + bb * Cfg::kStage + KB * kTileBytes;
-#pragma unroll
-                    for (int at = 0; at < kw; ++at)
-                        tc::cp_sf_atom(tmem + Cfg::kColSfb + bb * kw * 4 + 4 * at, tc::smem_desc_sf(sfb + at * 512));
                     ++nb;
                     prev_ai = ai;
                 }
@@ -568,14 +585,31 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
     } else if (warp >= kSfWarp0) {
         // ------------------------------------------------- scale factors
-        // The item's kw weight atoms (512 bytes apart after its tile) into
-        // columns tsfa + 4a of this warp's lane quarter; the slot is free
-        // once the stage has been refilled (see gate / up).
+        // At a group change the group's kw B atoms (after its B tile) into
+        // columns kColSfb + bb * kw * 4 + 4a, then per item its kw weight
+        // atoms (512 bytes apart after its tile) into columns tsfa + 4a, of
+        // this warp's lane quarter. A B buffer's columns are free once the
+        // buffer has been refilled, a stage's once the stage has (see gate /
+        // up).
         const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
-        uint32_t it = 0;
+        uint32_t it = 0, nb = 0;
+        int prev_ai = -1;
         for (int j = 0; j < count; ++j, ++it) {
+            const int ai = item_at(j) / mtiles;
+            if (ai != prev_ai) {
+                const uint32_t bb = nb & 1u;
+                if (!__all_sync(0xffffffffu, mbar_wait(bfull + bb, (nb >> 1) & 1u, err, kSiteGemmFull))) break;
+                tc::st_sf_atoms<kw>(tmem + quarter + Cfg::kColSfb + bb * kw * 4,
+                                    bbuf + (size_t)bb * Cfg::kStage + KB * kTileBytes, 512, lane);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sfb_ready + bb);
+                ++nb;
+                prev_ai = ai;
+            }
             const int st = it % S;
-            if (!__all_sync(0xffffffffu, mbar_wait(full + st, (it / S) & 1u, err, kSiteGemmFull))) break;
+            if (!__all_sync(0xffffffffu, mbar_wait(sfa_in + st, (it / S) & 1u, err, kSiteGemmFull))) break;
             tc::st_sf_atoms<kw>(tmem + quarter + Cfg::kColSfa + (uint32_t)st * kw * 4,
                                 smem + (size_t)st * Cfg::kStage + KB * kTileBytes, 512, lane);
             tc::wait_st();
