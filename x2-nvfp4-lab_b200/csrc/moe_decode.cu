@@ -302,7 +302,36 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     // The serial stretches of this kernel run once per layer call with cold
     // instruction caches, where code size is time: loops that need no
     // unrolling stay rolled (#pragma unroll 1).
-    if (row < R) {
+    if (row < R && tt == 1) {
+        // One token: a single accumulation chain, loads of four chunks in
+        // flight (the same products and sums in the same order as below).
+        float acc = 0.0f;
+        const uint16_t *wr = route_w + (size_t)warp * H;
+#pragma unroll 4
+        for (int q = 0; q < chunks; ++q) {
+            const int k = q * 128 + lane * 4;
+            const uint2 wv = *reinterpret_cast<const uint2 *>(wr + k);
+            float4 xv;
+            if (a.x_is_f32) {
+                xv = *reinterpret_cast<const float4 *>(route_xs + (size_t)k * 4);
+            } else {
+                const uint2 b = *reinterpret_cast<const uint2 *>(route_xs + (size_t)k * 2);
+                xv = make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
+                                 bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
+            }
+            acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.x & 0xFFFFu), xv.x));
+            acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.x >> 16), xv.y));
+            acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.y & 0xFFFFu), xv.z));
+            acc = __fadd_rn(acc, __fmul_rn(bf16_bits_to_f32(wv.y >> 16), xv.w));
+        }
+        float v = acc;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+        if (lane == 0) {
+            if (a.bias && row < a.E) v = __fadd_rn(v, bias);
+            s.logits[(size_t)t0 * R + row] = v;
+        }
+    } else if (row < R) {
         float acc[kRouteTokens];
 #pragma unroll
         for (int j = 0; j < kRouteTokens; ++j) acc[j] = 0.0f;
