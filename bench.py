@@ -289,8 +289,9 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
 
 def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40) -> dict:
     """the resident decode stack of ``layers`` independently
-    seeded layers (h <- h + MoE(RMSNorm(h)), attention omitted), all banks in
-    HBM, one CUDA graph per batch size replayed per step. Device time per
+    seeded layers (h <- h + MoE(RMSNorm(h)), attention omitted, the RMSNorm
+    fused into each layer's forward), all banks in HBM, one CUDA graph per
+    batch size replayed per step. Device time per
     step (CUDA events around each replay; the step's input is copied in
     before the start event); the weights a step streams (hundreds of MB)
     are far larger than L2, so no flush is needed. Algorithmic bytes per
@@ -307,7 +308,8 @@ def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40) -> dict:
     stream = torch.cuda.Stream()
     peak = measured_peaks().get("hbm_gbs")
     out = {"workload": "config4_stack40", "layers": layers, "l2": "not flushed (weights per step >> L2)",
-           "launches_per_layer": "RMSNorm + the layer call's decode kernels, one CUDA graph per step"}
+           "launches_per_layer": "the layer call's decode kernels with the RMSNorm fused into routing up to 32 "
+                                 "tokens (one RMSNorm launch more above); one CUDA graph per step"}
     for T in (1, 64):
         g = stack.capture(T)
         xs = [synthetic.synthetic_tokens(T, H, 12000 + 97 * T + i) for i in range(4)]

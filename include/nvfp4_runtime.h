@@ -315,6 +315,14 @@ enum {
      * banks whose ranges cover every expert once (and one of which computes
      * the shared expert) gives the layer output. */
     NVFP4_MOE_PARTIAL_F32 = 1u << 1,
+    /* x is normalised first (RMSNorm with the bank's weight and epsilon,
+     * nvfp4_moe_bank_set_pre_norm) and the experts see the normalised rows;
+     * the residual is added as given. Up to 32 tokens the routing kernel
+     * normalises its staged copy of x; larger calls normalise each slice into
+     * the slice's dst rows first (dst must not overlap x or the residual).
+     * The bits equal those of nvfp4_rmsnorm_ptr_bf16 followed by a forward
+     * without the flag. */
+    NVFP4_MOE_PRE_NORM = 1u << 2,
 };
 
 /* additive: batched layer forward with BF16 I/O. x and residual are BF16
@@ -477,6 +485,17 @@ NVFP4_API nvfp4_status nvfp4_moe_finalize_bf16(
 NVFP4_API nvfp4_status nvfp4_moe_bank_set_decode_kernels(
     nvfp4_moe_bank * bank,
     int kernels);
+
+/* additive: the RMSNorm that forwards with NVFP4_MOE_PRE_NORM apply to x
+ * (the per-layer pre-norm of a resident layer stack, fused into the layer;
+ * the lab's full-model driver runs it as a separate rmsnorm_device call,
+ * native_nvfp4/bench_moe_full_model.py:388-395). weight_bf16 is a device
+ * pointer to BF16 [hidden], copied into the bank (NULL: ones); epsilon >= 0.
+ * Synchronises the device. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_set_pre_norm(
+    nvfp4_moe_bank * bank,
+    const void * weight_bf16,
+    float epsilon);
 
 /* additive: allocate the prefill working memory for calls of up to
  * max_tokens tokens (capped at 16384 per pass) now, so that later forwards

@@ -6,6 +6,9 @@ omitted) against the oracle's composition, and its CUDA-graph replay
   (the kernel's rsqrtf is within 2 ulp of 1/sqrt).
 * Three layers of small banks at one token (in-register GEMVs) and five
   (tensor-core GEMVs) match ``moe_stack`` at the BASELINE tolerance.
+* The fused pre-norm (NVFP4_MOE_PRE_NORM) gives the same bits as the
+  standalone RMSNorm followed by the plain forward, on the decode path and
+  on the prefill path.
 * A captured step replays to the same bits as the eager stack.
 """
 
@@ -68,6 +71,22 @@ def test_stack_matches_oracle(cuda_runtime, stack, stack_hosts, T):
     ref = moe_stack(stack_hosts, synthetic_np.bf16_bits_to_f32(xbits))
     assert rel_rmse(got, ref) <= REL_RMSE_TOL
     assert max_abs_rel(got, ref) <= MAX_ABS_REL_TOL
+
+
+@pytest.mark.parametrize("T", [1, 5, 40, 80])
+def test_fused_norm_matches_separate_norm(cuda_runtime, stack, stack_hosts, T):
+    """The RMSNorm fused into the layer (routing kernel up to 64 tokens, a
+    slice pre-pass above) gives the bits of the standalone RMSNorm + forward."""
+    import torch
+
+    from vllm_nvfp4_cuda.stack import MoeStack
+
+    unfused = MoeStack(cuda_runtime, stack.banks, fused_norm=False)
+    x = bits_to_bf16_tensor(synthetic_np.tokens_bf16(T, 512, 950 + T))
+    a = stack.forward(x)
+    b = unfused.forward(x)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b)
 
 
 def test_stack_graph_replay(cuda_runtime, stack):

@@ -107,6 +107,10 @@ struct nvfp4_buffer {
 
 namespace nvfp4 {
 
+// The BF16 RMSNorm kernel of nvfp4_rmsnorm_ptr_bf16 (runtime.cu), one CTA per row.
+cudaError_t launch_rmsnorm_bf16(const void *x, const void *weight, void *dst, int rows, int cols, float epsilon,
+                                cudaStream_t stream);
+
 inline uint64_t host_now_ns() {
     return static_cast<uint64_t>(std::chrono::duration_cast<std::chrono::nanoseconds>(
                                      std::chrono::steady_clock::now().time_since_epoch())

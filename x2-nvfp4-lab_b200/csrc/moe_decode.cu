@@ -253,6 +253,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     const int esz = a.x_is_f32 ? 4 : 2;
     uint8_t *route_xs = route_smem;                                                     // [tt][H] of x
     uint16_t *route_w = reinterpret_cast<uint16_t *>(route_smem + (size_t)kRouteTokens * H * esz);  // [4][H]
+    uint16_t *route_nw = route_w + (size_t)kRouteRowsPerCta * H;  // [H] RMSNorm weight (a.norm_w only)
     // Let the gate/up launch (programmatic dependent launch) get its CTAs
     // resident now; it waits for this grid's completion before reading.
     pdl_launch_dependents();
@@ -265,6 +266,9 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         const uint8_t *wsrc = reinterpret_cast<const uint8_t *>(a.router + (size_t)min(row, R - 1) * H);
         uint8_t *wdst = reinterpret_cast<uint8_t *>(route_w + (size_t)warp * H);
         for (int i = lane; i < H / 8; i += 32) cp_async16(wdst + 16 * i, wsrc + 16 * i);
+        if (a.norm_w)  // bank data too
+            for (int i = threadIdx.x; i < H / 8; i += blockDim.x)
+                cp_async16(reinterpret_cast<uint8_t *>(route_nw) + 16 * i, reinterpret_cast<const uint8_t *>(a.norm_w) + 16 * i);
         // The router belongs to the bank; x and the scratch tables may be
         // written or still read by the preceding launch (this kernel is a
         // programmatic dependent launch): wait for it only now.
@@ -283,6 +287,58 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         cp_async_wait_all();
     }
     __syncthreads();
+
+    // Optional RMSNorm of the staged tokens, with the bits of the standalone
+    // RMSNorm kernel (runtime.cu): per token, 256 column-strided FP32 fmaf
+    // partial sums (virtual thread v = tid and tid + 128), an xor butterfly
+    // per warp of 32 partials, the eight warp sums added in order, rsqrtf,
+    // then bf16(x * inv * w). Everything after reads the normalised copy.
+    if (a.norm_w) {
+        __shared__ float s_red[kRouteTokens][8];
+        __shared__ float s_inv[kRouteTokens];
+        uint16_t *xs = reinterpret_cast<uint16_t *>(route_xs);
+#pragma unroll 1
+        for (int j = 0; j < tt; ++j) {
+            float ssa = 0.0f, ssb = 0.0f;
+            for (int c = threadIdx.x; c < H; c += 256) {
+                const float v = bf16_bits_to_f32(xs[(size_t)j * H + c]);
+                ssa = fmaf(v, v, ssa);
+            }
+            for (int c = threadIdx.x + 128; c < H; c += 256) {
+                const float v = bf16_bits_to_f32(xs[(size_t)j * H + c]);
+                ssb = fmaf(v, v, ssb);
+            }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) {
+                ssa += __shfl_xor_sync(0xffffffffu, ssa, off);
+                ssb += __shfl_xor_sync(0xffffffffu, ssb, off);
+            }
+            if (lane == 0) {
+                s_red[j][warp] = ssa;
+                s_red[j][warp + 4] = ssb;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < tt) {
+            float tot = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 8; ++w) tot += s_red[threadIdx.x][w];
+            s_inv[threadIdx.x] = rsqrtf(tot / (float)H + a.norm_eps);
+        }
+        __syncthreads();
+        // Two columns per step, the weight from its shared copy.
+        uint32_t *xs2 = reinterpret_cast<uint32_t *>(xs);
+        const uint32_t *nw2 = reinterpret_cast<const uint32_t *>(route_nw);
+        for (int i = threadIdx.x; i < tt * H / 2; i += blockDim.x) {
+            const int j = (2 * i) / H, c2 = i - j * (H / 2);
+            const uint32_t xv = xs2[i], wv = nw2[c2];
+            const float inv = s_inv[j];
+            const uint32_t lo = f32_to_bf16_bits(bf16_bits_to_f32(xv & 0xFFFFu) * inv * bf16_bits_to_f32(wv & 0xFFFFu));
+            const uint32_t hi = f32_to_bf16_bits(bf16_bits_to_f32(xv >> 16) * inv * bf16_bits_to_f32(wv >> 16));
+            xs2[i] = lo | (hi << 16);
+        }
+        __syncthreads();
+    }
 
     // FP16 copy of x for the in-register expert GEMVs (row block 0 converts
     // its tokens).
@@ -593,7 +649,8 @@ cudaError_t launch_maybe_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 blo
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent) {
     const int R = a.E + 1;
     const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
-    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2;
+    const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2 +
+                        (a.norm_w ? (size_t)a.H * 2 : 0);
     if (smem > 48 * 1024) {
         static std::atomic<uint64_t> done{0};
         const cudaError_t err = route_smem_limit(moe_route_kernel, done);

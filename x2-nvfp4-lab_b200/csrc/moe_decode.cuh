@@ -99,6 +99,8 @@ struct RouteArgs {
     int e_first, e_count;     // locally computed routed experts
     int shared_here;          // 1 if the shared expert is computed here
     int quantize_x;           // 1: also write x as four NVFP4 terms (tensor-core variant)
+    const uint16_t *norm_w;   // BF16 [H] RMSNorm weight applied to x first, or nullptr (BF16 x only)
+    float norm_eps;
     DecodeScratch s;
 };
 

@@ -121,6 +121,13 @@ int elementwise_grid(int n, int sms) {
 }
 
 }  // namespace
+
+cudaError_t launch_rmsnorm_bf16(const void *x, const void *weight, void *dst, int rows, int cols, float epsilon,
+                                cudaStream_t stream) {
+    rmsnorm_kernel<true><<<rows, 256, 0, stream>>>(x, weight, dst, cols, epsilon);
+    return cudaGetLastError();
+}
+
 }  // namespace nvfp4
 
 using namespace nvfp4;

@@ -25,6 +25,7 @@ import numpy as np
 LIB_NAME = "libnvfp4_moe_cuda.so"
 NVFP4_MOE_ADD_RESIDUAL = 1
 NVFP4_MOE_PARTIAL_F32 = 2
+NVFP4_MOE_PRE_NORM = 4
 NVFP4_DECODE_KERNELS_TENSOR_CORE = 0
 NVFP4_DECODE_KERNELS_IN_REGISTER = 1
 
@@ -162,6 +163,7 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
     "nvfp4_moe_bank_set_prefill_terms": ([C.c_void_p, C.c_int, C.c_int], C.c_int),
     "nvfp4_moe_bank_reserve_prefill": ([C.c_void_p, C.c_int], C.c_int),
     "nvfp4_moe_bank_set_decode_kernels": ([C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_moe_bank_set_pre_norm": ([C.c_void_p, C.c_void_p, C.c_float], C.c_int),
     "nvfp4_moe_bank_set_expert_range": ([C.c_void_p, C.c_int, C.c_int, C.c_int], C.c_int),
     "nvfp4_ep_create": ([C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_void_p)], C.c_int),
     "nvfp4_ep_ipc_handle": ([C.c_void_p, C.c_void_p], C.c_int),
@@ -386,9 +388,11 @@ class MoeBank:
         )
         return out
 
-    def forward(self, x, residual=None, out=None, stream=None):
+    def forward(self, x, residual=None, out=None, stream=None, pre_norm: bool = False):
         """additive: torch BF16 [tokens, hidden] CUDA tensors; enqueued on
-        ``stream`` (a torch.cuda.Stream) or torch's current stream."""
+        ``stream`` (a torch.cuda.Stream) or torch's current stream. With
+        ``pre_norm`` x is first normalised with the weight of ``set_pre_norm``
+        (``out`` must then not share memory with x or the residual)."""
         import torch
 
         if x.dtype != torch.bfloat16 or not x.is_cuda or x.dim() != 2 or x.shape[1] != self.hidden:
@@ -396,12 +400,12 @@ class MoeBank:
         x = x.contiguous()
         if out is None:
             out = torch.empty_like(x)
-        flags = 0
+        flags = NVFP4_MOE_PRE_NORM if pre_norm else 0
         if residual is not None:
             if residual.shape != x.shape or residual.dtype != torch.bfloat16 or not residual.is_cuda:
                 raise ValueError("residual must match x")
             residual = residual.contiguous()
-            flags = NVFP4_MOE_ADD_RESIDUAL
+            flags |= NVFP4_MOE_ADD_RESIDUAL
         s = stream if stream is not None else torch.cuda.current_stream(x.device)
         self.runtime._check(
             self.runtime.lib.nvfp4_moe_bank_forward_ptr_bf16(
@@ -517,6 +521,20 @@ class MoeBank:
         """additive: NVFP4 activation terms of the prefill path (1..4 each)."""
         self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_prefill_terms(self.handle, x_terms, act_terms),
                             "nvfp4_moe_bank_set_prefill_terms")
+
+    def set_pre_norm(self, weight=None, epsilon: float = 1e-6) -> None:
+        """additive: the RMSNorm of ``forward(..., pre_norm=True)``: a CUDA
+        bfloat16 tensor [hidden] (copied into the bank) or None for ones."""
+        import torch
+
+        ptr = None
+        if weight is not None:
+            if weight.dtype != torch.bfloat16 or not weight.is_cuda or weight.numel() != self.hidden:
+                raise ValueError("weight must be a CUDA bfloat16 tensor with hidden entries")
+            weight = weight.contiguous()
+            ptr = _tensor_ptr(weight)
+        self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_pre_norm(self.handle, ptr, float(epsilon)),
+                            "nvfp4_moe_bank_set_pre_norm")
 
     def set_decode_kernels(self, kernels: str) -> None:
         """additive: decode expert-GEMV variant, "tensor_core" (default) or "in_register"."""

@@ -9,9 +9,12 @@ unless given) and the MoE layer one bank's forward with h as its residual.
 This is the lab's full-model decode step (native_nvfp4/bench_moe_full_model.py:
 366-406: per layer ``rmsnorm_device``, ``bank.decode_device``, ``add_device``)
 without its attention blocks, at the hidden-state precision of the BF16
-forward path. All layers stay resident in HBM; a step enqueues 2 x layers
-calls on one stream, and ``capture`` records them once in a CUDA graph so a
-step is a single graph launch.
+forward path. All layers stay resident in HBM. By default each layer is one
+bank forward with the RMSNorm fused in (NVFP4_MOE_PRE_NORM: the routing
+kernel normalises its staged copy of the tokens, with the same bits as the
+standalone RMSNorm); ``fused_norm=False`` runs the standalone RMSNorm before
+each layer instead. ``capture`` records a step once in a CUDA graph so a step
+is a single graph launch.
 """
 
 from __future__ import annotations
@@ -19,9 +22,10 @@ from __future__ import annotations
 
 class MoeStack:
     """``banks``: MoeBank objects of one runtime, one per layer, same hidden size.
-    ``norm_weights``: optional BF16 CUDA tensors [hidden] per layer (ones when None)."""
+    ``norm_weights``: optional BF16 CUDA tensors [hidden] per layer (ones when None).
+    With ``fused_norm`` each bank is given its layer's norm (``set_pre_norm``)."""
 
-    def __init__(self, runtime, banks, epsilon: float = 1e-6, norm_weights=None):
+    def __init__(self, runtime, banks, epsilon: float = 1e-6, norm_weights=None, fused_norm: bool = True):
         import torch
 
         self.runtime = runtime
@@ -38,6 +42,10 @@ class MoeStack:
         if len(norm_weights) != len(self.banks):
             raise ValueError("one norm weight per layer")
         self.norm_weights = [w.contiguous() for w in norm_weights]
+        self.fused_norm = bool(fused_norm)
+        if self.fused_norm:
+            for bank, w in zip(self.banks, self.norm_weights):
+                bank.set_pre_norm(w, self.epsilon)
 
     @property
     def layers(self) -> int:
@@ -48,8 +56,11 @@ class MoeStack:
         (h or scratch: the two alternate as layer input and output)."""
         a, b = h, scratch
         for bank, w in zip(self.banks, self.norm_weights):
-            self.runtime.rmsnorm_bf16(a, w, self.epsilon, out=normed, stream=stream)
-            bank.forward(normed, residual=a, out=b, stream=stream)
+            if self.fused_norm:
+                bank.forward(a, residual=a, out=b, stream=stream, pre_norm=True)
+            else:
+                self.runtime.rmsnorm_bf16(a, w, self.epsilon, out=normed, stream=stream)
+                bank.forward(normed, residual=a, out=b, stream=stream)
             a, b = b, a
         return a
 
