@@ -307,7 +307,7 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
         check_cuda(launch_prefill_route(ra, ps, 2, s), "prefill dispatch kernels");
     });
     rt->profiled_kernel("moe_quantize_x", stream, [&](cudaStream_t s) {
-        check_cuda(launch_quantize_x_prefill(x, tokens, ps, bank->terms_x, s), "quantize_rows_kernel(x)");
+        check_cuda(launch_quantize_x_prefill(x, tokens, ps, bank->terms_x, s), "quantize_blocks_kernel(x)");
     });
     GemmArgs ga{};
     ga.sfa[0] = bank->sf_atoms[0];
@@ -325,7 +325,7 @@ void enqueue_prefill(nvfp4_moe_bank *bank, const void *x, const void *residual, 
         check_cuda(launch_gemm_gate_up(bank->pmaps, ga, sms, s), "moe_gemm_kernel(gate/up)");
     });
     rt->profiled_kernel("moe_quantize_act", stream, [&](cudaStream_t s) {
-        check_cuda(launch_quantize_act_prefill(ps, bank->terms_act, s), "quantize_rows_kernel(act)");
+        check_cuda(launch_quantize_act_prefill(ps, bank->terms_act, s), "quantize_blocks_kernel(act)");
     });
     GemmArgs gd = ga;
     gd.sfa[0] = bank->sf_atoms[2];
@@ -882,7 +882,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_quantize_rows_enqueue(const void *src, i
         check_cuda(launch_quantize_rows(src, src_is_f16, rows, cols, terms, static_cast<uint8_t *>(codes),
                                         static_cast<uint32_t *>(scale_words), static_cast<float *>(row_scales), rows,
                                         static_cast<cudaStream_t>(stream)),
-                   "quantize_rows_kernel");
+                   "quantize_blocks_kernel");
         clear_last_error();
         return NVFP4_STATUS_OK;
     } catch (const std::exception &error) {

@@ -11,16 +11,19 @@
 // J products in one accumulator (the terms are extra K).
 //
 // Launch sequence (one stream):
-//   1. prefill_logits_kernel    approximate router logits (BF16 mma.sync)
+//   1. prefill_logits_tc_kernel approximate router logits (tcgen05 kind::f16,
+//                               BF16 operands; prefill_logits_kernel with
+//                               mma.sync on shapes the tcgen05 tiles skip)
 //   2. prefill_select_kernel    exact FP32 fixed-order logits of the
 //                               candidates near the top-8 boundary, top-8,
 //                               weights, shared gate; per-64-token masks
 //   3. prefill_scan_kernel      counts, offsets, active groups, tile table
 //   4. prefill_place_kernel     dispatch permutation and per-slot tables
-//   5. quantize_rows_kernel     x -> J NVFP4 terms (per token)
-//   6. moe_gemm_gate_up_kernel  act = SiLU(gate) * up, FP16 [slot rows][I]
-//   7. quantize_rows_kernel     act -> J NVFP4 terms (per slot row)
-//   8. moe_gemm_down_kernel     y = coef * W_down act, FP16 [slot rows][H]
+//   5. quantize_blocks_kernel   x -> J NVFP4 terms (per token, written to
+//                               each of its slot rows)
+//   6. moe_gemm_kernel<0,...>   act = SiLU(gate) * up, FP16 [slot rows][I]
+//   7. quantize_blocks_kernel   act -> J NVFP4 terms (per slot row)
+//   8. moe_gemm_kernel<1,...>   y = coef * W_down act, FP16 [slot rows][H]
 //   9. prefill_combine_kernel   out = sum of nine slots (+ residual), BF16
 #pragma once
 
