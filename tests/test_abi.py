@@ -83,3 +83,22 @@ def test_provider_gate(monkeypatch):
     monkeypatch.delenv("VLLM_NVFP4_CUDA", raising=False)
     ok, reason = provider_enabled()
     assert not ok and "VLLM_NVFP4_CUDA=1" in reason
+
+
+def test_custom_op_fake_kernel():
+    """register() defines torch.ops.nvfp4_moe.forward with a fake kernel, so
+    model code that calls a bank can be traced (torch.compile, graph capture
+    planning) without the library: under FakeTensorMode the op returns a
+    tensor shaped like x."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import vllm_nvfp4_cuda
+
+    vllm_nvfp4_cuda.register()
+    vllm_nvfp4_cuda.register()  # idempotent
+    op = torch.ops.nvfp4_moe.forward
+    with FakeTensorMode():
+        x = torch.empty(3, 2048, dtype=torch.bfloat16)
+        y = op(0, x, torch.empty_like(x))
+        assert y.shape == x.shape and y.dtype == x.dtype
