@@ -11,7 +11,7 @@ import socket
 import numpy as np
 import pytest
 
-from vllm_nvfp4_cuda.expert_parallel import ExpertParallelLayer, expert_range
+from vllm_nvfp4_cuda.expert_parallel import ExpertParallelLayer, TokenShardedLayer, expert_range
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
@@ -52,8 +52,14 @@ class _OracleBank:
 
         first, count, shared_here = self.range
         r = residual.numpy() if residual is not None else None
-        out = moe_layer(self.host, x.numpy(), r, expert_range=(first, count), shared_here=shared_here).out
-        return torch.from_numpy(out.astype(np.float32))
+        result = moe_layer(self.host, x.numpy(), r, expert_range=(first, count), shared_here=shared_here)
+        self.last_ids = result.ids
+        return torch.from_numpy(result.out.astype(np.float32))
+
+    def last_routing(self, tokens):
+        from types import SimpleNamespace
+
+        return SimpleNamespace(ids=self.last_ids[:tokens])
 
 
 def _worker(rank, world, port, result_path):
@@ -98,3 +104,54 @@ def test_two_rank_gloo_layer_matches_single_device(tmp_path):
     ref = moe_layer(host, x, res).out
     # Only the order of the FP32 additions differs.
     np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())
+
+
+def _rank_tokens(rank):
+    from oracle import synthetic_np
+
+    T = 0 if rank == 2 else 3 + 2 * rank
+    x = synthetic_np.bf16_bits_to_f32(synthetic_np.tokens_bf16(T, 256, 60 + rank))
+    res = synthetic_np.bf16_bits_to_f32(synthetic_np.tokens_bf16(T, 256, 80 + rank))
+    return x, res
+
+
+def _sharded_worker(rank, world, port, result_dir):
+    import torch
+    import torch.distributed as dist
+
+    from oracle import synthetic_np
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        host = synthetic_np.make_bank(16, 256, 128, 41)
+        x, res = _rank_tokens(rank)
+        layer = TokenShardedLayer(_OracleBank(host), finalize=lambda t: t)
+        out = layer.forward(torch.from_numpy(x), torch.from_numpy(res))
+        np.save(os.path.join(result_dir, f"rank{rank}.npy"), out.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_token_sharded_layer_matches_single_device(tmp_path, world):
+    """Tokens sharded over the ranks (uneven counts, one rank without tokens
+    at four ranks), experts split, rows and partials moved by all-to-alls:
+    every rank gets the single-device layer output of its own tokens."""
+    import torch.multiprocessing as mp
+
+    from oracle import synthetic_np
+    from oracle.nvfp4_oracle import moe_layer
+
+    mp.start_processes(_sharded_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world,
+                       start_method="spawn", join=True)
+    host = synthetic_np.make_bank(16, 256, 128, 41)
+    for rank in range(world):
+        got = np.load(tmp_path / f"rank{rank}.npy")
+        x, res = _rank_tokens(rank)
+        assert got.shape == x.shape
+        if x.shape[0] == 0:
+            continue
+        ref = moe_layer(host, x, res).out
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-5 * np.abs(ref).max())

@@ -9,6 +9,9 @@ all-reduce over the ranks (NCCL over NVLink on GPUs) adds the partials, and
 ``finalize_bf16`` rounds the sum to BF16. This is the batch-1 decode scheme
 of an expert-parallel layer (one exchange of [tokens, hidden] FP32 per
 layer); it serves prefill the same way, with every rank routing all tokens.
+``TokenShardedLayer`` is the other form: each rank brings its own tokens and
+all-to-alls move token rows to the ranks owning their experts and the FP32
+partials back.
 
 The lab itself runs on one device and has no counterpart of this module.
 """
@@ -94,3 +97,102 @@ class ExpertParallelLayer:
             part = self.partial(x, residual)
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
             return self.finalize(part)
+
+
+class TokenShardedLayer:
+    """Expert parallelism with the tokens sharded over the ranks (prefill and
+    batched decode), as a host-level composition of the bank forward and
+    ``torch.distributed`` all-to-alls.
+
+    Each rank brings its own tokens. The router and the shared expert are
+    replicated; rank r owns the routed experts ``expert_range(r, N, E)``.
+    Per call:
+
+    1. the rank's partial sum of its own tokens: its routed experts, the
+       shared expert and the residual (``forward_partial``), which also routes
+       them (``last_routing``);
+    2. a counts all-to-all, then a payload all-to-all of the token rows, each
+       token sent once to every other rank that owns one of its eight picks;
+    3. each rank's partial sums of the tokens it received (its routed experts
+       only; it routes them again, to the same picks);
+    4. the partials all-to-all back, then the sum at the origin in rank
+       order, and ``finalize``.
+
+    ``bank`` needs ``experts``, ``set_expert_range``, ``forward_partial`` and
+    ``last_routing`` (vllm_nvfp4_cuda.runtime.MoeBank, with the shared
+    expert and the rank's routed experts uploaded); ``finalize`` turns the
+    FP32 sum into the output (Runtime.finalize_bf16 on GPUs). Calls route
+    at most 16384 tokens per rank (the bank keeps the routing record of
+    calls that run as one pass). The device kernels are those of the bank;
+    this class only moves rows between ranks (NCCL on GPUs)."""
+
+    def __init__(self, bank, finalize, group=None):
+        import torch.distributed as dist
+
+        self.bank = bank
+        self.finalize = finalize
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.range = expert_range(self.rank, self.world, bank.experts)
+        self.per_rank = bank.experts // self.world
+
+    def _exchange(self, send, send_counts, recv_counts):
+        import torch
+        import torch.distributed as dist
+
+        out = send.new_empty((int(sum(recv_counts)),) + tuple(send.shape[1:]))
+        dist.all_to_all_single(out, send.contiguous(), output_split_sizes=list(recv_counts),
+                               input_split_sizes=list(send_counts), group=self.group)
+        return out
+
+    def forward(self, x, residual=None):
+        """Layer output of this rank's tokens ``x`` [tokens, hidden] (BF16 on
+        GPUs), with ``residual`` added; every rank must call it, with its own
+        token count (zero allowed)."""
+        import numpy as np
+        import torch
+        import torch.distributed as dist
+
+        T = x.shape[0]
+        first, count = self.range.first, self.range.count
+        # 1. Own tokens: own routed experts + shared expert + residual.
+        self.bank.set_expert_range(first, count, True)
+        if T > 0:
+            part = self.bank.forward_partial(x, residual=residual)
+            if x.is_cuda:
+                torch.cuda.current_stream(x.device).synchronize()
+            ids = np.asarray(self.bank.last_routing(T).ids)[:, :8]
+        else:
+            part = torch.zeros(x.shape, dtype=torch.float32, device=x.device)
+            ids = np.zeros((0, 8), dtype=np.int64)
+        # 2. Destinations: every other rank owning one of a token's picks.
+        owner = ids // self.per_rank
+        idx = [np.nonzero((owner == k).any(axis=1))[0] if k != self.rank else np.zeros(0, dtype=np.int64)
+               for k in range(self.world)]
+        send_counts = [len(i) for i in idx]
+        counts = torch.tensor(send_counts, dtype=torch.int64, device=x.device)
+        recv = torch.empty_like(counts)
+        dist.all_to_all_single(recv, counts, group=self.group)
+        recv_counts = recv.tolist()
+        order = torch.from_numpy(np.concatenate(idx).astype(np.int64)).to(x.device)
+        recv_x = self._exchange(x.index_select(0, order), send_counts, recv_counts)
+        # 3. Received tokens: own routed experts only.
+        self.bank.set_expert_range(first, count, False)
+        if recv_x.shape[0] > 0:
+            recv_part = self.bank.forward_partial(recv_x)
+        else:
+            recv_part = torch.zeros(recv_x.shape, dtype=torch.float32, device=x.device)
+        self.bank.set_expert_range(first, count, True)
+        # 4. Partials back; the sum in rank order at the origin.
+        back = self._exchange(recv_part, recv_counts, send_counts)
+        out = torch.zeros(part.shape, dtype=torch.float32, device=x.device)
+        start = 0
+        for k in range(self.world):
+            if k == self.rank:
+                out += part
+            elif send_counts[k]:
+                sel = torch.from_numpy(idx[k].astype(np.int64)).to(x.device)
+                out.index_add_(0, sel, back[start:start + send_counts[k]])
+            start += send_counts[k]
+        return self.finalize(out)
