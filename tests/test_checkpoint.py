@@ -107,9 +107,14 @@ def test_read_layer_compressed_tensors_single_file(tmp_path, bank_host):
 
 
 class _RecordingBank:
-    def __init__(self):
+    def __init__(self, hidden=H):
         self.uploads = {}
         self.closed = False
+        self.hidden = hidden
+        self.pre_norm = None
+
+    def set_pre_norm(self, weight, epsilon):
+        self.pre_norm = (weight, epsilon)
 
     def upload_projection(self, e, p, packed, scales, divisor):
         assert (e, p) not in self.uploads
@@ -123,9 +128,12 @@ class _RecordingRuntime:
     def __init__(self):
         self.created = None
         self.bank = _RecordingBank()
+        self.banks = []
 
     def create_moe_bank(self, router, shared_gate, intermediate):
         self.created = (router, shared_gate, intermediate)
+        self.bank = _RecordingBank()
+        self.banks.append(self.bank)
         return self.bank
 
 
@@ -178,3 +186,28 @@ def test_missing_checkpoint(tmp_path):
 
     with pytest.raises(FileNotFoundError):
         CheckpointIndex(tmp_path)
+
+
+def test_load_stack_uses_each_layers_norm(tmp_path, bank_host):
+    """load_stack: one bank per layer plus its post-attention norm weight
+    (ones for a layer without one), handed to each bank as its fused pre-norm."""
+    import torch
+    from safetensors.torch import save_file
+
+    from vllm_nvfp4_cuda.checkpoint import load_stack
+
+    t = _tensors(bank_host, 0, "compressed-tensors")
+    t1 = _tensors(bank_host, 1, "compressed-tensors")
+    del t1["model.language_model.layers.1.post_attention_layernorm.weight"]
+    t.update({k: v.clone() for k, v in t1.items()})  # safetensors refuses shared storage
+    save_file(t, str(tmp_path / "model.safetensors"))
+    rt = _RecordingRuntime()
+    stack = load_stack(rt, tmp_path, [0, 1], epsilon=1e-5, device="cpu")
+    assert stack.layers == 2 and stack.fused_norm and stack.banks == rt.banks
+    w0, eps0 = rt.banks[0].pre_norm
+    w1, eps1 = rt.banks[1].pre_norm
+    assert eps0 == eps1 == 1e-5
+    np.testing.assert_array_equal(w0.view(torch.int16).numpy().view(np.uint16),
+                                  synthetic_np.bf16_bits_from_f32(np.linspace(0.5, 1.5, H, dtype=np.float32)))
+    assert (w1.float() == 1.0).all()
+    assert all(len(b.uploads) == (E + 1) * 3 for b in rt.banks)

@@ -255,3 +255,28 @@ def load_bank(runtime, model_dir, layer: int):
         raise
     return bank, {"experts": experts, "hidden": hidden, "intermediate": intermediate,
                   "conventions": sorted(conventions), "payload_bytes": payload[0]}
+
+
+def load_stack(runtime, model_dir, layers, epsilon: float = 1e-6, device: str = "cuda"):
+    """A resident layer stack (vllm_nvfp4_cuda.stack.MoeStack) of checkpoint
+    layers: each layer's bank (``load_bank``) and its pre-MoE RMSNorm weight
+    (``post_attention_layernorm.weight``; ones where the checkpoint has
+    none), fused into each layer's forward."""
+    import torch
+
+    from .stack import MoeStack
+
+    banks, norms = [], []
+    try:
+        for layer in layers:
+            bank, info = load_bank(runtime, model_dir, layer)
+            banks.append(bank)
+            bits = read_norm_weight(model_dir, layer)
+            if bits is None:
+                bits = np.full(info["hidden"], 0x3F80, dtype=np.uint16)  # BF16 1.0
+            norms.append(torch.from_numpy(bits.view(np.int16).copy()).view(torch.bfloat16).to(device))
+        return MoeStack(runtime, banks, epsilon=epsilon, norm_weights=norms)
+    except Exception:
+        for bank in banks:
+            bank.close()
+        raise
