@@ -21,7 +21,8 @@ outside that step's CUDA-event pair.
 --gpus N (under torchrun) runs N independent replicas, one bank per GPU and
 a distinct token stream per rank (weak scaling, no collective).
 --impl reference times the lab's CPU path (the C restatement) for the same
-workload and prints its own JSON line.
+workload, W untimed batches and then exactly K timed ones, each a batch of
+--tokens tokens on all host cores, and prints its own JSON line.
 """
 
 from __future__ import annotations
@@ -143,10 +144,12 @@ class ClockSampler:
 # --------------------------------------------------------------- CPU leg
 
 
-def cpu_baseline_measure(tokens: int, seed: int, min_seconds: float = 10.0, max_steps: int = 200) -> dict:
+def cpu_baseline_measure(tokens: int, seed: int, min_seconds: float = 10.0, max_steps: int = 200,
+                         steps: int | None = None, warmup: int = 1) -> dict:
     """Time the C restatement of the lab's CPU path (oracle/cpu_moe.c) on a
-    full-size synthetic bank: batches of `tokens` tokens until at least
-    `min_seconds` of CPU work (at least 2 batches, at most `max_steps`)."""
+    full-size synthetic bank: after `warmup` untimed batches, either exactly
+    `steps` batches of `tokens` tokens or, when `steps` is None, batches until
+    at least `min_seconds` of CPU work (at least 2, at most `max_steps`)."""
     import numpy as np
 
     from oracle import cpu_oracle, synthetic_np
@@ -169,15 +172,18 @@ def cpu_baseline_measure(tokens: int, seed: int, min_seconds: float = 10.0, max_
     router = np.ascontiguousarray(np.concatenate(
         [meta.router_bf16.numpy().view(np.uint16), meta.shared_gate_bf16.numpy().view(np.uint16)[None]]))
     dense = cpu_oracle.DenseBank(E, H, I, packed, scales, inv, router, None)
-    x = synthetic_np.tokens_f32(tokens, H, seed + 998)
-    dense.forward(x[:1], threads=threads)  # warm
+    warm = synthetic_np.tokens_f32(tokens, H, seed + 998)
+    for _ in range(max(1, warmup)):
+        dense.forward(warm, threads=threads)
     xs = [synthetic_np.tokens_f32(tokens, H, seed + s) for s in range(8)]
-    steps = 0
+    done = 0
     t0 = time.perf_counter()
-    while steps < max_steps and (steps < 2 or time.perf_counter() - t0 < min_seconds):
-        dense.forward(xs[steps % len(xs)], threads=threads)
-        steps += 1
+    while (done < steps) if steps is not None else (
+            done < max_steps and (done < 2 or time.perf_counter() - t0 < min_seconds)):
+        dense.forward(xs[done % len(xs)], threads=threads)
+        done += 1
     dt = time.perf_counter() - t0
+    steps = done
     return {
         "value": round(tokens * steps / dt, 3),
         "unit": UNIT,
@@ -193,8 +199,8 @@ def run_reference(args) -> int:
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    cpu = cpu_baseline_measure(args.tokens, args.seed, min_seconds=min(20.0, 2.0 * max(1, args.steps)))
-    steps = int(cpu["sample"].split()[0])
+    steps, warmup = max(1, args.steps), max(1, args.warmup)
+    cpu = cpu_baseline_measure(args.tokens, args.seed, steps=steps, warmup=warmup)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -202,7 +208,7 @@ def run_reference(args) -> int:
         "unit": UNIT,
         "n_gpus": args.gpus,
         "steps": steps,
-        "warmup": 1,
+        "warmup": warmup,
         "ms_per_step": round(1000.0 * args.tokens / cpu["value"], 3),
         "higher_is_better": True,
         "scaling": "weak",
