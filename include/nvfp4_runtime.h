@@ -38,6 +38,8 @@ typedef struct nvfp4_runtime nvfp4_runtime;
 typedef struct nvfp4_moe_bank nvfp4_moe_bank;
 typedef struct nvfp4_buffer nvfp4_buffer;
 typedef struct nvfp4_ep nvfp4_ep;
+/* reference: nvfp4_runtime.h:22 (dense NVFP4 weight matrix). */
+typedef struct nvfp4_matrix nvfp4_matrix;
 
 /* reference: nvfp4_runtime.h:33-39. Code 2 keeps its slot; on this backend it
  * reports a CUDA runtime error instead of an OpenCL one. */
@@ -49,6 +51,16 @@ typedef enum nvfp4_status {
     NVFP4_STATUS_IO_ERROR = 3,
     NVFP4_STATUS_INTERNAL_ERROR = 4,
 } nvfp4_status;
+
+/* reference: nvfp4_runtime.h:41-46. The linear entry points keep the
+ * reference's rules for these kinds (TILED needs more than one vector,
+ * ROW_TILED exactly one); every kind runs the same sm_100a kernel. */
+typedef enum nvfp4_kernel_kind {
+    NVFP4_KERNEL_SCALAR = 0,
+    NVFP4_KERNEL_SUBGROUP = 1,
+    NVFP4_KERNEL_TILED = 2,
+    NVFP4_KERNEL_ROW_TILED = 3,
+} nvfp4_kernel_kind;
 
 /* reference: nvfp4_runtime.h:48-52. kernel_ns is the summed device time of
  * the operations enqueued since the previous synchronize. */
@@ -240,6 +252,76 @@ NVFP4_API nvfp4_status nvfp4_rmsnorm_ptr_bf16(
     int cols,
     float epsilon,
     void * dst_bf16,
+    void * stream);
+
+/* ------------------------------------------------------- dense NVFP4 linear
+ * dst[v, r] = sum_c E2M1(W[r, c]) * E4M3(S[r, c/16]) * x[v, c] /
+ * weight_global_scale, x FP32 [vectors, cols] and dst FP32 [vectors, rows],
+ * both row-major (the weight path of the lab's vLLM NvFp4LinearKernel
+ * provider, vllm_nvfp4_opencl/linear.py:15-70; bias stays the adapter's job).
+ * Products of weight and scale are exact; the sum is FP32. */
+
+/* reference: nvfp4_runtime.h:208-217 (nvfp4_runtime.cpp:1705-1735). The
+ * compressed-tensors representation: packed [rows, cols/2] E2M1 pairs (low
+ * nibble = even column), scales_e4m3 [rows, cols/16]; cols a multiple of 16.
+ * Copied to device memory before returning (scale bytes sanitised: sign
+ * cleared, 0x7F -> 0). This backend supports cols <= 49152. */
+NVFP4_API nvfp4_status nvfp4_matrix_upload(
+    nvfp4_runtime * runtime,
+    const uint8_t * packed,
+    size_t packed_bytes,
+    const uint8_t * scales_e4m3,
+    size_t scale_bytes,
+    int rows,
+    int cols,
+    float weight_global_scale,
+    nvfp4_matrix ** out_matrix);
+
+/* reference: nvfp4_runtime.h:238 (nvfp4_runtime.cpp:2106-2108). Drains the
+ * runtime stream first. */
+NVFP4_API void nvfp4_matrix_destroy(nvfp4_matrix * matrix);
+
+/* reference: nvfp4_runtime.h:240-248 (nvfp4_runtime.cpp:2110-2183).
+ * Synchronous, host x and dst; last_profile gets the upload, kernel and
+ * download times. */
+NVFP4_API nvfp4_status nvfp4_linear_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_matrix * matrix,
+    const float * x,
+    int vectors,
+    float * dst,
+    nvfp4_kernel_kind kernel_kind);
+
+/* reference: nvfp4_runtime.h:250-256 (nvfp4_runtime.cpp:2185-2231).
+ * Device buffers; waits for the kernel; last_profile.kernel_ns. */
+NVFP4_API nvfp4_status nvfp4_linear_device_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_matrix * matrix,
+    const nvfp4_buffer * x,
+    int vectors,
+    nvfp4_buffer * dst,
+    nvfp4_kernel_kind kernel_kind);
+
+/* reference: nvfp4_runtime.h:258-264 (nvfp4_runtime.cpp:2233-2270).
+ * Enqueued on the runtime stream. */
+NVFP4_API nvfp4_status nvfp4_linear_device_enqueue_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_matrix * matrix,
+    const nvfp4_buffer * x,
+    int vectors,
+    nvfp4_buffer * dst,
+    nvfp4_kernel_kind kernel_kind);
+
+/* additive: the same linear on raw device pointers (x FP32 [vectors, cols],
+ * dst FP32 [vectors, rows]) enqueued on `stream` (a cudaStream_t; NULL
+ * selects the runtime's stream): the path of the torch-facing provider,
+ * whose activations are already device tensors. */
+NVFP4_API nvfp4_status nvfp4_linear_ptr_f32(
+    nvfp4_runtime * runtime,
+    const nvfp4_matrix * matrix,
+    const float * x,
+    int vectors,
+    float * dst,
     void * stream);
 
 /* ------------------------------------------------------------- MoE bank */

@@ -1,0 +1,216 @@
+"""Dense NVFP4 linear (the lab's nvfp4_matrix / nvfp4_linear_* entry points and
+its vLLM NvFp4LinearKernel provider).
+
+CPU: the provider's contract with a fake runtime (what it uploads, how it
+reshapes, casts and adds the bias) and its registration. GPU (sm_100a): every
+linear entry point against the oracle's restatement of the lab's CPU GEMV
+(``nvfp4_gemv``, pinned to the lab's golden vectors), at the lab's own GEMV
+gate (2e-5 of the output scale), including ragged shapes, several passes of
+vectors, and scale bytes outside the E4M3 value range (sign bit, 0x7F)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle.nvfp4_oracle import nvfp4_gemv
+
+GATE = 2e-5  # probe_native_nvfp4.py:294
+
+
+def _oracle(packed, scales, x, divisor):
+    return np.stack([nvfp4_gemv(packed, scales, x[v], divisor) for v in range(x.shape[0])])
+
+
+def _matrix(rows, cols, seed, full_scale_bytes=False):
+    rng = np.random.default_rng(seed)
+    packed = rng.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
+    if full_scale_bytes:
+        scales = rng.integers(0, 256, size=(rows, cols // 16), dtype=np.uint8)
+    else:
+        scales = rng.integers(0x30, 0x48, size=(rows, cols // 16), dtype=np.uint8)  # 2^-1 .. 2^2
+    return packed, scales
+
+
+# ------------------------------------------------------------------ CPU
+
+
+class _FakeRuntime:
+    def __init__(self):
+        self.uploaded = None
+        self.calls = []
+
+    def upload(self, packed, scales, divisor):
+        from vllm_nvfp4_cuda.runtime import NativeMatrix
+
+        self.uploaded = (packed, scales, divisor)
+        m = NativeMatrix.__new__(NativeMatrix)
+        m.runtime, m.handle, m.rows, m.cols, m.shared_svm = None, None, packed.shape[0], packed.shape[1] * 2, False
+        return m
+
+    def linear_tensor(self, matrix, x):
+        import torch
+
+        self.calls.append((x.dtype, tuple(x.shape)))
+        packed, scales, divisor = self.uploaded
+        flat = x.reshape(-1, matrix.cols).numpy()
+        out = _oracle(packed, scales, flat, divisor)
+        return torch.from_numpy(out).reshape(*x.shape[:-1], matrix.rows)
+
+
+def test_provider_contract_with_fake_runtime(monkeypatch):
+    import torch
+
+    import vllm_nvfp4_cuda.linear as provider
+    from vllm.model_executor.kernels.linear.nvfp4 import NvFp4LinearLayerConfig
+
+    fake = _FakeRuntime()
+    monkeypatch.setattr(provider, "get_runtime", lambda: fake)
+    monkeypatch.setattr(provider, "provider_enabled", lambda: (True, None))
+    rows, cols = 48, 64
+    packed, scales = _matrix(rows, cols, 3)
+    layer = torch.nn.Module()
+    layer.weight = torch.nn.Parameter(torch.from_numpy(packed.copy()), requires_grad=False)
+    layer.weight_scale = torch.nn.Parameter(torch.from_numpy(scales.copy()).view(torch.float8_e4m3fn),
+                                            requires_grad=False)
+    layer.weight_global_scale = torch.nn.Parameter(torch.tensor(4.0), requires_grad=False)
+    kernel = provider.CudaNvFp4LinearKernel(NvFp4LinearLayerConfig())
+    assert provider.CudaNvFp4LinearKernel.supports_a16()
+    assert provider.CudaNvFp4LinearKernel.is_supported(90)[0] is False
+    kernel.process_weights_after_loading(layer)
+    up_packed, up_scales, divisor = fake.uploaded
+    np.testing.assert_array_equal(up_packed, packed)
+    np.testing.assert_array_equal(up_scales, scales)
+    assert divisor == 0.25  # the inverse of weight_global_scale, as the lab passes it
+
+    x = torch.randn(2, 3, cols, dtype=torch.bfloat16)
+    bias = torch.randn(rows, dtype=torch.bfloat16)
+    y = kernel.apply_weights(layer, x, bias)
+    assert y.dtype == torch.bfloat16 and tuple(y.shape) == (2, 3, rows)
+    assert fake.calls == [(torch.float32, (2, 3, cols))]
+    ref = _oracle(packed, scales, x.float().reshape(-1, cols).numpy(), 0.25).reshape(2, 3, rows)
+    expect = torch.from_numpy(ref).to(torch.bfloat16) + bias
+    assert torch.equal(y, expect)
+    with pytest.raises(ValueError, match="does not match matrix width"):
+        kernel.apply_weights(layer, torch.zeros(1, cols + 16))
+
+
+def test_register_adds_cuda_linear_provider():
+    import vllm_nvfp4_cuda
+    from vllm.model_executor.kernels import linear as kl
+
+    from vllm.platforms import PlatformEnum
+
+    vllm_nvfp4_cuda.register()
+    vllm_nvfp4_cuda.register()  # idempotent
+    from vllm_nvfp4_cuda.linear import CudaNvFp4LinearKernel
+
+    assert kl._POSSIBLE_NVFP4_KERNELS[PlatformEnum.CUDA].count(CudaNvFp4LinearKernel) == 1
+
+
+def test_gemv_oracle_handles_ragged_columns():
+    """cols a multiple of 16 but not of 32: the oracle agrees with the
+    dequantise-then-matmul form (the GPU tests rely on it at such widths)."""
+    from oracle.nvfp4_oracle import dequantize
+
+    packed, scales = _matrix(7, 48, 5, full_scale_bytes=True)
+    x = np.random.default_rng(6).standard_normal(48).astype(np.float32)
+    dense = dequantize(packed, scales, 3.0).astype(np.float64) @ x.astype(np.float64)
+    got = nvfp4_gemv(packed, scales, x, 3.0)
+    np.testing.assert_allclose(got, dense, rtol=1e-5, atol=1e-5 * np.max(np.abs(dense)))
+
+
+# ------------------------------------------------------------------ GPU
+
+SHAPES = [  # (rows, cols, vectors)
+    (1000, 2048, 1),
+    (257, 528, 3),     # cols % 32 == 16: the last chunk is half padding
+    (64, 16, 2),       # one block per row
+    (33, 4096, 9),     # two passes (8 + 1 vectors)
+    (4099, 1024, 4),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rows,cols,vectors", SHAPES)
+def test_linear_matches_oracle(cuda_runtime, rows, cols, vectors):
+    packed, scales = _matrix(rows, cols, rows + cols)
+    x = np.random.default_rng(vectors).standard_normal((vectors, cols)).astype(np.float32)
+    divisor = 2.5
+    m = cuda_runtime.upload(packed, scales, divisor)
+    try:
+        got = cuda_runtime.linear(m, x)
+        ref = _oracle(packed, scales, x, divisor)
+        np.testing.assert_allclose(got, ref, rtol=GATE, atol=GATE * float(np.max(np.abs(ref))))
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+def test_linear_scale_bytes_follow_the_lab_rule(cuda_runtime):
+    packed, scales = _matrix(300, 512, 11, full_scale_bytes=True)
+    scales[:, 0] = 0x7F
+    scales[:, 1] = 0xFF
+    scales[:, 2] = 0xB8  # sign bit set: decoded as +1.0
+    x = np.random.default_rng(12).standard_normal((2, 512)).astype(np.float32)
+    m = cuda_runtime.upload(packed, scales, 1.0)
+    try:
+        got = cuda_runtime.linear(m, x)
+        ref = _oracle(packed, scales, x, 1.0)
+        np.testing.assert_allclose(got, ref, rtol=GATE, atol=GATE * float(np.max(np.abs(ref))))
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+def test_linear_entry_points_agree(cuda_runtime):
+    """Host, device-buffer, enqueued and tensor entry points run the same
+    kernel: bit-identical outputs."""
+    import torch
+
+    from vllm_nvfp4_cuda.runtime import KERNEL_SCALAR, KERNEL_TILED
+
+    rows, cols, vectors = 515, 768, 5
+    packed, scales = _matrix(rows, cols, 21)
+    x = np.random.default_rng(22).standard_normal((vectors, cols)).astype(np.float32)
+    m = cuda_runtime.upload(packed, scales, 6.0)
+    try:
+        host = cuda_runtime.linear(m, x, kernel_kind=KERNEL_TILED)
+        xb = cuda_runtime.upload_buffer(x)
+        ob = cuda_runtime.create_buffer(vectors * rows * 4)
+        cuda_runtime.linear_device(m, xb, vectors, ob, kernel_kind=KERNEL_SCALAR)
+        np.testing.assert_array_equal(ob.download((vectors, rows)), host)
+        ob2 = cuda_runtime.create_buffer(vectors * rows * 4)
+        cuda_runtime.linear_device(m, xb, vectors, ob2, kernel_kind=KERNEL_SCALAR, enqueue=True)
+        cuda_runtime.synchronize()
+        np.testing.assert_array_equal(ob2.download((vectors, rows)), host)
+        xt = torch.from_numpy(x).cuda().reshape(1, vectors, cols)
+        yt = cuda_runtime.linear_tensor(m, xt)
+        torch.cuda.synchronize()
+        assert tuple(yt.shape) == (1, vectors, rows)
+        np.testing.assert_array_equal(yt.cpu().numpy().reshape(vectors, rows), host)
+        for b in (xb, ob, ob2):
+            b.close()
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+def test_linear_argument_errors(cuda_runtime):
+    from vllm_nvfp4_cuda.runtime import KERNEL_ROW_TILED, KERNEL_TILED
+
+    packed, scales = _matrix(32, 64, 31)
+    m = cuda_runtime.upload(packed, scales, 1.0)
+    try:
+        with pytest.raises(RuntimeError, match="tiled kernel requires more than one vector"):
+            cuda_runtime.linear(m, np.zeros((1, 64), np.float32), kernel_kind=KERNEL_TILED)
+        with pytest.raises(RuntimeError, match="row-tiled kernel requires one vector"):
+            cuda_runtime.linear(m, np.zeros((2, 64), np.float32), kernel_kind=KERNEL_ROW_TILED)
+        with pytest.raises(ValueError):
+            cuda_runtime.linear(m, np.zeros((1, 32), np.float32))
+    finally:
+        m.close()
+    with pytest.raises(RuntimeError, match="at most 49152 columns"):
+        cuda_runtime.upload(np.zeros((1, 49168 // 2), np.uint8), np.zeros((1, 49168 // 16), np.uint8), 1.0)
+    with pytest.raises(RuntimeError, match="invalid native NVFP4 matrix arguments"):
+        cuda_runtime.upload(np.zeros((4, 4), np.uint8), np.zeros((4, 1), np.uint8), 0.0)

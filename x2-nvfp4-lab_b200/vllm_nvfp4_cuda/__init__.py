@@ -12,6 +12,7 @@ from __future__ import annotations
 from .runtime import (  # noqa: F401
     DeviceBuffer,
     MoeBank,
+    NativeMatrix,
     Profile,
     Routing,
     Runtime,
@@ -26,20 +27,32 @@ _registered = False
 
 
 def register() -> None:
-    """Register the provider in every vLLM process, idempotently. Registers
-    the ``nvfp4_moe::forward`` torch custom op used by model code to call a
-    resident bank."""
+    """Register the provider in every vLLM process, idempotently: the
+    ``nvfp4_moe::forward`` torch custom op used by model code to call a
+    resident bank and, when vLLM is installed, the dense NVFP4 linear provider
+    (``CudaNvFp4LinearKernel``) for the CUDA platform (the lab registers its
+    OpenCL provider the same way, __init__.py:8-29)."""
     global _registered
     if _registered:
         return
     from . import ops  # noqa: F401  (defines the custom op on import)
 
+    try:
+        from vllm.model_executor.kernels.linear import register_linear_kernel
+        from vllm.platforms import PlatformEnum
+    except ImportError:
+        register_linear_kernel = None
+    if register_linear_kernel is not None:
+        from .linear import CudaNvFp4LinearKernel
+
+        register_linear_kernel(CudaNvFp4LinearKernel, PlatformEnum.CUDA, kernel_type="nvfp4")
     _registered = True
 
 
 __all__ = [
     "DeviceBuffer",
     "MoeBank",
+    "NativeMatrix",
     "Profile",
     "Routing",
     "Runtime",

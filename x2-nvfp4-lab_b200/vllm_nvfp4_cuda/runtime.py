@@ -175,6 +175,15 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "nvfp4_rmsnorm_ptr_bf16": (
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p], C.c_int),
+    "nvfp4_matrix_upload": (
+        [C.c_void_p, C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_int, C.c_int, C.c_float,
+         C.POINTER(C.c_void_p)], C.c_int),
+    "nvfp4_matrix_destroy": ([C.c_void_p], None),
+    "nvfp4_linear_f32": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_linear_device_f32": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_linear_device_enqueue_f32": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int], C.c_int),
+    "nvfp4_linear_ptr_f32": ([C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p], C.c_int),
     "nvfp4_quantize_rows_enqueue": (
         [C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p],
         C.c_int),
@@ -296,6 +305,31 @@ class EpContext:
         if self.handle:
             self.runtime.lib.nvfp4_ep_destroy(self.handle)
             self.handle = C.c_void_p()
+
+
+class NativeMatrix:
+    """A dense NVFP4 weight matrix resident on the device (runtime.py:94-115)."""
+
+    def __init__(self, runtime: "Runtime", handle: C.c_void_p, rows: int, cols: int):
+        self.runtime = runtime
+        self.handle = handle
+        self.rows = rows
+        self.cols = cols
+        self.shared_svm = False  # the lab's Adreno SVM placement has no counterpart here
+
+    def close(self) -> None:
+        if self.handle:
+            self.runtime.lib.nvfp4_matrix_destroy(self.handle)
+            self.handle = C.c_void_p()
+
+    def __del__(self) -> None:
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+KERNEL_SCALAR, KERNEL_SUBGROUP, KERNEL_TILED, KERNEL_ROW_TILED = 0, 1, 2, 3
 
 
 class MoeBank:
@@ -794,6 +828,73 @@ class Runtime:
             self.lib.nvfp4_rmsnorm_ptr_bf16(self.handle, _tensor_ptr(x), _tensor_ptr(weight), x.shape[0], x.shape[1],
                                             float(epsilon), _tensor_ptr(out), _stream_handle(s)),
             "nvfp4_rmsnorm_ptr_bf16")
+        return out
+
+    def upload(self, packed: np.ndarray, scales: np.ndarray, checkpoint_global_scale: float, *,
+               shared_svm: bool | None = None) -> NativeMatrix:
+        """A dense NVFP4 matrix from the compressed-tensors representation
+        (runtime.py:927-990): packed uint8 [rows, cols/2], scales E4M3 bytes
+        [rows, cols/16], and the divisor of the dequantised weights. The lab's
+        ``shared_svm`` placement is an Adreno memory mode; device memory is
+        used whatever it says."""
+        packed = np.ascontiguousarray(packed, dtype=np.uint8)
+        scales = np.ascontiguousarray(scales).view(np.uint8)
+        if packed.ndim != 2:
+            raise ValueError("packed must be uint8 [rows, cols/2]")
+        handle = C.c_void_p()
+        self._check(
+            self.lib.nvfp4_matrix_upload(self.handle, _ptr(packed), packed.nbytes, _ptr(scales), scales.nbytes,
+                                         packed.shape[0], packed.shape[1] * 2, float(checkpoint_global_scale),
+                                         C.byref(handle)),
+            "matrix_upload",
+        )
+        return NativeMatrix(self, handle, packed.shape[0], packed.shape[1] * 2)
+
+    def linear(self, matrix: NativeMatrix, x: np.ndarray, kernel_kind: int | None = None) -> np.ndarray:
+        """Synchronous linear on host arrays (runtime.py:1095-1125): x float32
+        [vectors, cols] -> float32 [vectors, rows]."""
+        if x.ndim != 2 or x.shape[1] != matrix.cols or x.dtype != np.float32:
+            raise ValueError("x must be contiguous float32 [vectors, cols]")
+        x = np.ascontiguousarray(x)
+        out = np.empty((x.shape[0], matrix.rows), dtype=np.float32)
+        kind = kernel_kind if kernel_kind is not None else (
+            KERNEL_TILED if x.shape[0] > 1 else (KERNEL_ROW_TILED if matrix.rows <= 1024 else KERNEL_SUBGROUP))
+        self._check(
+            self.lib.nvfp4_linear_f32(self.handle, matrix.handle, _ptr(x), x.shape[0], _ptr(out), int(kind)),
+            "linear",
+        )
+        return out
+
+    def linear_device(self, matrix: NativeMatrix, x: DeviceBuffer, vectors: int, out: DeviceBuffer,
+                      kernel_kind: int = KERNEL_SUBGROUP, enqueue: bool = False) -> DeviceBuffer:
+        """Linear on device buffers: waits for the kernel, or only enqueues it
+        on the runtime stream with ``enqueue``."""
+        fn = self.lib.nvfp4_linear_device_enqueue_f32 if enqueue else self.lib.nvfp4_linear_device_f32
+        self._check(fn(self.handle, matrix.handle, x.handle, vectors, out.handle, int(kernel_kind)),
+                    "linear_device_enqueue" if enqueue else "linear_device")
+        return out
+
+    def linear_tensor(self, matrix: NativeMatrix, x, out=None, stream=None):
+        """additive: the linear on a CUDA float32 tensor [..., cols], enqueued on
+        ``stream`` (None: torch's current stream); returns float32 [..., rows]."""
+        import torch
+
+        if x.dtype != torch.float32 or not x.is_cuda or x.shape[-1] != matrix.cols:
+            raise ValueError("x must be a CUDA float32 tensor [..., cols]")
+        lead = x.shape[:-1]
+        x2 = x.reshape(-1, matrix.cols).contiguous()
+        if out is None:
+            out = torch.empty(*lead, matrix.rows, dtype=torch.float32, device=x.device)
+        elif out.dtype != torch.float32 or tuple(out.shape) != (*lead, matrix.rows) or not out.is_contiguous():
+            raise ValueError("out must be a contiguous float32 tensor [..., rows]")
+        if x2.shape[0] == 0:
+            return out
+        s = stream if stream is not None else torch.cuda.current_stream(x.device)
+        self._check(
+            self.lib.nvfp4_linear_ptr_f32(self.handle, matrix.handle, _tensor_ptr(x2), x2.shape[0],
+                                          _tensor_ptr(out), _stream_handle(s)),
+            "nvfp4_linear_ptr_f32",
+        )
         return out
 
     def quantize_rows(self, x, terms: int):
