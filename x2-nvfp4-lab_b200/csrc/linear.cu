@@ -30,6 +30,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <atomic>
 #include <limits>
 #include <memory>
 #include <mutex>
@@ -172,12 +173,18 @@ __global__ void __launch_bounds__(kLinThreads) nvfp4_linear_kernel(LinearArgs a)
 
 template <int V>
 void launch_pass(const LinearArgs &a, int sm_count, cudaStream_t stream) {
-    static std::once_flag attr_once;
-    std::call_once(attr_once, [] {
+    // The shared-memory limit is a per-device function attribute: set once on
+    // each device this process launches on.
+    static std::atomic<uint64_t> configured{0};
+    int device = 0;
+    check_cuda(cudaGetDevice(&device), "cudaGetDevice");
+    const uint64_t bit = device < 64 ? (uint64_t{1} << device) : 0;
+    if (!bit || !(configured.load(std::memory_order_acquire) & bit)) {
         check_cuda(cudaFuncSetAttribute(nvfp4_linear_kernel<V>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         static_cast<int>(kLinSmemBudget)),
                    "cudaFuncSetAttribute(nvfp4_linear_kernel)");
-    });
+        configured.fetch_or(bit, std::memory_order_acq_rel);
+    }
     const size_t smem = static_cast<size_t>(V) * a.chunks * 32 * sizeof(float);
     int per_sm = 0;
     check_cuda(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, nvfp4_linear_kernel<V>, kLinThreads, smem),
