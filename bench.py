@@ -17,6 +17,8 @@ outside that step's CUDA-event pair.
              its average CUDA-event duration, against MEASURED_PEAKS hbm_gbs
   cpu_baseline  the C restatement of the lab's CPU path (oracle/cpu_moe.c)
              on this host's cores, on a bounded sample
+  linear     the dense NVFP4 linear at the LM-head shape (248320 x 2048),
+             1 and 4 vectors: device time per call and its HBM rate
 
 --gpus N (under torchrun) runs N independent replicas, one bank per GPU and
 a distinct token stream per rank (weak scaling, no collective).
@@ -61,6 +63,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU baseline leg")
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill legs (configs 2 and 3)")
     p.add_argument("--no-stack", action="store_true", help="skip the 40-layer stack leg (config 4)")
+    p.add_argument("--no-linear", action="store_true", help="skip the dense NVFP4 linear leg (LM-head shape)")
     p.add_argument("--decode-kernels", choices=["tensor_core", "in_register"], default="tensor_core",
                    help="decode expert GEMVs (the library's default is tensor_core)")
     return p.parse_args()
@@ -352,6 +355,54 @@ def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40) -> dict:
     return out
 
 
+def linear_leg(rt, seed: int, steps: int, warmup: int, rows: int = 248320, cols: int = 2048) -> dict:
+    """The dense NVFP4 linear (the lab's nvfp4_linear entry points behind its
+    vLLM provider) at the LM-head shape, 248320 x 2048, for 1 and 4 FP32
+    vectors through the tensor entry point on a torch stream. Device time per
+    call (CUDA events, median); the 286 MB of weights a call streams are far
+    larger than L2, so no flush is needed. Algorithmic bytes per call: packed
+    codes and scales (0.5625 B per weight) plus x in and y out in FP32."""
+    import numpy as np
+    import torch
+
+    rng = np.random.default_rng(seed + 77)
+    packed = rng.integers(0, 256, size=(rows, cols // 2), dtype=np.uint8)
+    scales = rng.integers(0x30, 0x48, size=(rows, cols // 16), dtype=np.uint8)
+    m = rt.upload(packed, scales, 1.0)
+    del packed, scales
+    stream = torch.cuda.Stream()
+    peak = measured_peaks().get("hbm_gbs")
+    out = {"workload": f"lm_head_{rows}x{cols}", "l2": "not flushed (weights per call >> L2)",
+           "kernel": "nvfp4_linear_kernel", "launches_per_call": 1}
+    try:
+        for V in (1, 4):
+            x = torch.from_numpy(rng.standard_normal((V, cols)).astype(np.float32)).cuda()
+            y = torch.empty(V, rows, dtype=torch.float32, device="cuda")
+            stream.wait_stream(torch.cuda.current_stream())
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+            with torch.cuda.stream(stream):
+                for _ in range(warmup):
+                    rt.linear_tensor(m, x, out=y, stream=stream)
+                for i in range(steps):
+                    starts[i].record(stream)
+                    rt.linear_tensor(m, x, out=y, stream=stream)
+                    ends[i].record(stream)
+            stream.synchronize()
+            ms = statistics.median(a.elapsed_time(b) for a, b in zip(starts, ends))
+            nbytes = rows * cols * 9 // 16 + V * (rows + cols) * 4
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            out[f"vectors{V}"] = {
+                "us_per_call": round(ms * 1000.0, 2),
+                "algorithmic_mb": round(nbytes / 1e6, 1),
+                "hbm_gbs": round(gbs, 1),
+                "hbm_frac_of_measured": round(gbs / peak, 4) if peak else None,
+            }
+    finally:
+        m.close()
+    return out
+
+
 def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmup: int) -> dict:
     """Expert parallelism across the job's GPUs: rank r holds routed experts
     [r*E/N, (r+1)*E/N) (the shared expert on rank 0), the tokens are the same
@@ -622,6 +673,13 @@ def run_ours(args) -> int:
         except Exception as error:  # noqa: BLE001
             stack = {"workload": "config4_stack40", "error": f"{type(error).__name__}: {error}"}
 
+    linear = None
+    if world == 1 and not args.no_linear:
+        try:
+            linear = linear_leg(rt, args.seed, 30, 3)
+        except Exception as error:  # noqa: BLE001
+            linear = {"workload": "lm_head_248320x2048", "error": f"{type(error).__name__}: {error}"}
+
     if rank == 0:
         clk = clocks.summary()
         line = {
@@ -676,6 +734,7 @@ def run_ours(args) -> int:
             "prefill": prefill,
             "expert_parallel": ep,
             "stack": stack,
+            "linear": linear,
             "clocks": clk,
             "cpu_baseline": cpu,
         }
