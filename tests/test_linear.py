@@ -13,6 +13,8 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
+from oracle.nvfp4_oracle import E2M1 as _E2M1
+from oracle.nvfp4_oracle import decode_e4m3_scale as _decode_e4m3_scale
 from oracle.nvfp4_oracle import nvfp4_gemv
 
 GATE = 2e-5  # probe_native_nvfp4.py:294
@@ -118,6 +120,71 @@ def test_gemv_oracle_handles_ragged_columns():
     dense = dequantize(packed, scales, 3.0).astype(np.float64) @ x.astype(np.float64)
     got = nvfp4_gemv(packed, scales, x, 3.0)
     np.testing.assert_allclose(got, dense, rtol=1e-5, atol=1e-5 * np.max(np.abs(dense)))
+
+
+def _emulate_kernel(packed, scales, x, divisor, grid, V=4):
+    """The launch plan of nvfp4_linear_kernel<V> (csrc/linear.cu) run on the CPU:
+    the upload's pitches and scale sanitising, the rotated shared-memory slots
+    of the activations (every slot written once, nothing read unwritten), each
+    lane's chunks of each warp's two rows (16-byte packed words, two scale
+    bytes, low nibble = even column), and the row loop over the grid (every
+    output written once)."""
+    rows, half = packed.shape; cols = half * 2
+    pp = (half + 15) // 16 * 16; sp = (cols // 16 + 15) // 16 * 16
+    P = np.zeros((rows, pp), np.uint8); P[:, :half] = packed
+    S = np.zeros((rows, sp), np.uint8); s = scales & 0x7F; s[s == 0x7F] = 0; S[:, :cols // 16] = s
+    chunks = pp // 16; xcols = chunks * 32; vectors = x.shape[0]
+    def xs_index(v, col):
+        c, g, e = col >> 5, (col >> 2) & 7, col & 3
+        return (v * chunks + c) * 32 + (((g + c) & 7) << 2) + e
+    dst = np.full((vectors, rows), np.nan, np.float32)
+    for v0 in range(0, vectors, V):
+        xs = np.full(V * xcols, np.nan, np.float32); seen = set()
+        for i in range(V * xcols):
+            v, col = divmod(i, xcols); gv = v0 + v
+            idx = xs_index(v, col); assert idx not in seen and 0 <= idx < V * xcols; seen.add(idx)
+            xs[idx] = x[gv, col] if (gv < vectors and col < cols) else 0.0
+        for b in range(grid):
+            for w in range(8):
+                r0 = (b * 8 + w) * 2
+                while r0 < rows:
+                    acc = np.zeros((2, V, 32), np.float32)
+                    for lane in range(32):
+                        for c in range(lane, chunks, 32):
+                            for j in range(2):
+                                r = min(r0 + j, rows - 1)
+                                q = P[r, c * 16:c * 16 + 16]
+                                sc = _decode_e4m3_scale(S[r, c * 2:c * 2 + 2])
+                                for wi in range(4):
+                                    word = q[wi * 4:wi * 4 + 4]
+                                    s2 = sc[0] if wi < 2 else sc[1]
+                                    wv = np.empty(8, np.float32)
+                                    for k in range(4):
+                                        wv[2 * k] = _E2M1[word[k] & 15] * s2
+                                        wv[2 * k + 1] = _E2M1[word[k] >> 4] * s2
+                                    col = c * 32 + wi * 8
+                                    for v in range(V):
+                                        xv = np.array([xs[xs_index(v, col + t)] for t in range(8)], np.float32)
+                                        acc[j, v, lane] += np.float32(np.dot(wv.astype(np.float64), xv.astype(np.float64)))
+                    for j in range(2):
+                        for v in range(V):
+                            r, gv = r0 + j, v0 + v
+                            if r < rows and gv < vectors:
+                                assert np.isnan(dst[gv, r]); dst[gv, r] = acc[j, v].sum() / np.float32(divisor)
+                    r0 += grid * 8 * 2
+    return dst
+
+
+@pytest.mark.parametrize("rows,cols,vectors,grid", [(37, 48, 3, 2), (70, 1056, 5, 1), (5, 16, 1, 4)])
+def test_kernel_launch_plan_on_cpu(rows, cols, vectors, grid):
+    rng = np.random.default_rng(rows + cols)
+    packed = rng.integers(0, 256, (rows, cols // 2), dtype=np.uint8)
+    scales = rng.integers(0, 256, (rows, cols // 16), dtype=np.uint8)
+    x = rng.standard_normal((vectors, cols)).astype(np.float32)
+    got = _emulate_kernel(packed, scales, x, 2.0, grid)
+    ref = _oracle(packed, scales, x, 2.0)
+    assert not np.isnan(got).any()
+    np.testing.assert_allclose(got, ref, rtol=GATE, atol=GATE * float(np.max(np.abs(ref))))
 
 
 # ------------------------------------------------------------------ GPU
