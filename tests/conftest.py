@@ -23,6 +23,13 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs an sm_100a GPU and the built CUDA library")
 
 
+def pytest_collection_modifyitems(config, items):
+    """The MoE-bank path's tests run first and the dense NVFP4 linear's
+    (tests/test_linear.py, outside the bank path) last, so that a run with -x
+    reports the bank path in full whatever the linear's tests do."""
+    items.sort(key=lambda item: Path(str(item.fspath)).name == "test_linear.py")
+
+
 @pytest.fixture(scope="session")
 def cuda_runtime():
     """One Runtime per test session (GPU tests only). Fails loudly if the
