@@ -66,8 +66,11 @@ def test_provider_contract_with_fake_runtime(monkeypatch):
     import vllm_nvfp4_cuda.linear as provider
     from vllm.model_executor.kernels.linear.nvfp4 import NvFp4LinearLayerConfig
 
+    with pytest.raises(RuntimeError, match="requires CUDA activations"):
+        provider._require_cuda(torch.zeros(1, 16))
     fake = _FakeRuntime()
     monkeypatch.setattr(provider, "get_runtime", lambda: fake)
+    monkeypatch.setattr(provider, "_require_cuda", lambda x: None)  # the fake computes on the CPU
     monkeypatch.setattr(provider, "provider_enabled", lambda: (True, None))
     rows, cols = 48, 64
     packed, scales = _matrix(rows, cols, 3)

@@ -20,6 +20,13 @@ from .runtime import NativeMatrix, get_runtime, provider_enabled
 SM100 = 100
 
 
+def _require_cuda(x: torch.Tensor) -> None:
+    """The provider's device rule (the lab's raises the same way for
+    activations on the wrong device, linear.py:57-58)."""
+    if x.device.type != "cuda":
+        raise RuntimeError("CUDA NVFP4 currently requires CUDA activations")
+
+
 class CudaNvFp4LinearKernel(NvFp4LinearKernel):
     """Native compressed-tensors W4A16 linear on sm_100a."""
 
@@ -47,9 +54,10 @@ class CudaNvFp4LinearKernel(NvFp4LinearKernel):
         layer._cuda_nvfp4_matrix = get_runtime().upload(packed, scales, 1.0 / scale_multiplier)
 
     def apply_weights(self, layer: torch.nn.Module, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
-        """x [..., cols] -> [..., rows] in x's dtype (linear.py:51-68); the
-        runtime requires x on the CUDA device."""
+        """x [..., cols] on the CUDA device -> [..., rows] in x's dtype
+        (linear.py:51-68)."""
         matrix: NativeMatrix = layer._cuda_nvfp4_matrix
+        _require_cuda(x)
         if x.shape[-1] != matrix.cols:
             raise ValueError(f"input width {x.shape[-1]} does not match matrix width {matrix.cols}")
         x_f32 = x.detach().to(torch.float32)
