@@ -435,6 +435,27 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(
     int flags,
     void * stream);
 
+/* additive: one layer call on HOST buffers, end to end -- the sequence the
+ * lab's callers run as nvfp4_buffer_upload, the bank enqueue,
+ * nvfp4_runtime_synchronize and nvfp4_buffer_download
+ * (vllm_nvfp4_opencl/runtime.py:370-377, nvfp4_runtime.h:140-160,416-419),
+ * in one call: x (and the residual) are copied to device staging on the
+ * runtime stream, the forward is enqueued behind them, dst is copied back and
+ * the stream is synchronised once (device timeouts are reported as by
+ * nvfp4_runtime_synchronize). x_host, residual_host, dst_host: BF16
+ * [tokens, hidden] in host memory; page-locked memory (cudaHostAlloc,
+ * torch pin_memory) makes the copies asynchronous DMA, pageable memory works
+ * through the driver's staging. flags: NVFP4_MOE_ADD_RESIDUAL and
+ * NVFP4_MOE_PRE_NORM. The first call (and any larger call) allocates the
+ * device staging for 3 x tokens x hidden x 2 bytes, kept by the bank. */
+NVFP4_API nvfp4_status nvfp4_moe_bank_forward_host_bf16(
+    nvfp4_moe_bank * bank,
+    const void * x_host,
+    const void * residual_host,
+    void * dst_host,
+    int tokens,
+    int flags);
+
 /* additive: routing introspection of the most recent forward or decode.
  * Call after nvfp4_runtime_synchronize(). Any output pointer may be NULL.
  *   ids      int32 [tokens, 9]  top-8 ids by descending logit (lowest id on
@@ -631,7 +652,8 @@ NVFP4_API nvfp4_status nvfp4_quantize_rows_enqueue(
  * Every call shares the one array and it keeps the previous call's
  * contents; calls whose kernels overlap on the GPU race and must be ordered.
  * The first call on each device looks up the array's address; make it before
- * any stream capture. */
+ * any stream capture. The looked-up address is kept for the process: do not
+ * call this entry point on a device after cudaDeviceReset on it. */
 NVFP4_API nvfp4_status nvfp4_moe_route_static_scratch(
     const void * router_bf16,
     const void * x_bf16,

@@ -269,6 +269,28 @@ static void down_items(void *p, int begin, int end) {
     }
 }
 
+/* Routing only (router and shared-gate logits, top-8, weights, slot 8) for T
+ * tokens -- the checker of full-size prefill calls, whose expert products
+ * would take the scalar row kernel minutes. Only bank->experts, hidden,
+ * router and router_bias are read. ids/weights [T][9], logits [T][E+1].
+ * Returns 0 on success. */
+int nvfp4_oracle_route(const nvfp4_oracle_bank *bank, const float *x, int T, int32_t *ids_out,
+                       float *weights_out, float *logits_out, int threads) {
+    if (!bank || !x || !ids_out || !weights_out || !logits_out || T <= 0 || bank->experts < 8 ||
+        bank->experts > 256 || bank->hidden % 128 || !bank->router)
+        return 1;
+    layer_ctx c;
+    memset(&c, 0, sizeof(c));
+    c.bank = bank;
+    c.x = x;
+    c.T = T;
+    c.ids = ids_out;
+    c.weights = weights_out;
+    c.logits = logits_out;
+    parallel_for(T, threads, route_tokens, &c);
+    return 0;
+}
+
 /* Full layer for T tokens. x [T][H] FP32; residual [T][H] or NULL; out
  * [T][H]. ids/weights [T][9] and logits [T][E+1] are optional outputs.
  * Returns 0 on success. */

@@ -110,3 +110,35 @@ class DenseBank:
         if st:
             raise RuntimeError(f"CPU oracle forward failed ({st})")
         return out, ids, weights, logits
+
+
+def route(router_all_bf16: np.ndarray, x: np.ndarray, router_bias: np.ndarray | None = None,
+          threads: int | None = None):
+    """Routing of T tokens by the C restatement (nvfp4_oracle_route): the
+    same FP32 fixed-order logits and lowest-id top-8 as ``moe_layer``, fast
+    enough for the 8192-token BASELINE calls. router_all_bf16 is [(E+1), H]
+    BF16 bits with row E the shared gate; x is [T, H] float32. Returns (ids
+    [T, 9] int32, weights [T, 9] float32, logits [T, E+1] float32)."""
+    import os
+
+    router = np.ascontiguousarray(router_all_bf16, dtype=np.uint16)
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    R, H = router.shape
+    E = R - 1
+    T = x.shape[0]
+    b = _Bank()
+    b.experts, b.hidden, b.intermediate = E, H, 0
+    b.router = router.ctypes.data
+    bias = None if router_bias is None else np.ascontiguousarray(router_bias, dtype=np.float32)
+    b.router_bias = None if bias is None else bias.ctypes.data
+    ids = np.empty((T, 9), dtype=np.int32)
+    weights = np.empty((T, 9), dtype=np.float32)
+    logits = np.empty((T, R), dtype=np.float32)
+    f = lib().nvfp4_oracle_route
+    f.argtypes = [C.POINTER(_Bank), C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int]
+    f.restype = C.c_int
+    st = f(C.byref(b), x.ctypes.data, T, ids.ctypes.data, weights.ctypes.data, logits.ctypes.data,
+           threads if threads is not None else (os.cpu_count() or 1))
+    if st:
+        raise ValueError("invalid routing arguments")
+    return ids, weights, logits

@@ -24,10 +24,16 @@ def pytest_configure(config):
 
 
 def pytest_collection_modifyitems(config, items):
-    """The MoE-bank path's tests run first and the dense NVFP4 linear's
-    (tests/test_linear.py, outside the bank path) last, so that a run with -x
-    reports the bank path in full whatever the linear's tests do."""
-    items.sort(key=lambda item: Path(str(item.fspath)).name == "test_linear.py")
+    """The MoE-bank path's tests run first, then the dense NVFP4 linear's
+    (tests/test_linear.py, outside the bank path), so that a run with -x
+    reports the bank path in full whatever the linear's tests do; the
+    allocation-free entry point's test (tests/test_zz_no_alloc.py) runs after
+    every other test."""
+    def key(item):
+        name = Path(str(item.fspath)).name
+        return (name == "test_zz_no_alloc.py", name == "test_linear.py")
+
+    items.sort(key=key)
 
 
 @pytest.fixture(scope="session")

@@ -137,6 +137,28 @@ def test_router_logits_bit_exact_between_numpy_and_c_port():
     np.testing.assert_allclose(logits_np, exact.T, rtol=1e-5, atol=2e-5)
 
 
+def test_c_route_matches_numpy_oracle_with_ties_and_bias():
+    """The C routing entry (the full-size prefill checker) against
+    moe_layer's routing: logits bit for bit, ids exactly, on a skewed bank
+    with duplicated router rows and an all-zero token (every logit ties)."""
+    bank = synthetic_np.make_bank(64, 256, 128, 9, which=[], skew=True)
+    w = bf16_bits_to_f32(bank.router_bf16).copy()
+    w[7] = w[30] = w[2]
+    bank.router_bf16 = bf16_bits_from_f32(w)
+    bank.router_bias[[2, 7, 30]] = np.float32(0.5)
+    x = synthetic_np.tokens_f32(40, 256, 9)
+    x[0] = 0.0
+    ids, weights, logits = cpu_oracle.route(bank.router_all(), x, bank.router_bias, threads=3)
+    ref = router_logits(bank.router_all(), x)
+    ref[:, :64] = (ref[:, :64] + bank.router_bias).astype(np.float32)
+    np.testing.assert_array_equal(logits.view(np.uint32), ref.view(np.uint32))
+    top, tw = top8_route(ref[:, :64])
+    np.testing.assert_array_equal(ids[:, :8], top)
+    np.testing.assert_allclose(weights[:, :8], tw, rtol=2e-6, atol=1e-7)
+    assert (ids[:, 8] == 64).all()
+    assert list(ids[0, :3]) == [2, 7, 30]
+
+
 def test_c_port_layer_matches_numpy_oracle():
     bank = synthetic_np.make_bank(16, 256, 128, 5, skew=True)
     dense = cpu_oracle.DenseBank.from_host(bank)

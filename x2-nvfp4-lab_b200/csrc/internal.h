@@ -107,6 +107,11 @@ struct nvfp4_buffer {
 
 namespace nvfp4 {
 
+// After the runtime stream has drained: throws when a kernel of a bank on
+// this runtime recorded a bounded wait that ran out (its wait-site code is
+// in the message) and clears the words. Caller holds queue_mutex.
+void raise_device_timeouts(nvfp4_runtime *runtime);
+
 // The BF16 RMSNorm kernel of nvfp4_rmsnorm_ptr_bf16 (runtime.cu), one CTA per row.
 cudaError_t launch_rmsnorm_bf16(const void *x, const void *weight, void *dst, int rows, int cols, float epsilon,
                                 cudaStream_t stream);

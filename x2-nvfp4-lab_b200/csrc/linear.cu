@@ -34,6 +34,7 @@
 #include <limits>
 #include <memory>
 #include <mutex>
+#include <string>
 #include <vector>
 
 struct nvfp4_matrix {
@@ -442,6 +443,22 @@ extern "C" NVFP4_API nvfp4_status nvfp4_linear_ptr_f32(nvfp4_runtime *runtime, c
         return fail_invalid("invalid linear arguments or mismatched runtime/matrix");
     size_t in_bytes = 0, out_bytes = 0;
     if (!sizes_fit(matrix, vectors, &in_bytes, &out_bytes)) return fail_invalid("linear buffer size overflow");
+    // The kernel reads the matrix on the runtime's device: activations and
+    // outputs allocated on another GPU are rejected here rather than read
+    // across devices (host or managed memory the device can reach is left
+    // to the caller).
+    for (const void *p : {static_cast<const void *>(x), static_cast<const void *>(dst)}) {
+        cudaPointerAttributes attr{};
+        if (cudaPointerGetAttributes(&attr, p) != cudaSuccess) {
+            cudaGetLastError();
+            return fail_invalid("linear: cannot query the device of x or dst");
+        }
+        if (attr.type == cudaMemoryTypeDevice && attr.device != runtime->device) {
+            const std::string msg = "linear: x and dst must be on the matrix's device (cuda:" +
+                                    std::to_string(runtime->device) + "), got cuda:" + std::to_string(attr.device);
+            return fail_invalid(msg.c_str());
+        }
+    }
     try {
         std::lock_guard<std::mutex> lock(runtime->queue_mutex);
         runtime->direct_call(static_cast<cudaStream_t>(stream), [&](cudaStream_t s) {

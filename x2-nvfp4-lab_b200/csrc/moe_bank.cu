@@ -63,8 +63,13 @@ struct nvfp4_moe_bank {
     // stack's pre-norm): the bank's own copy of the BF16 weight [hidden].
     uint16_t *norm_w = nullptr;
     float norm_eps = 1e-6f;
+    // Device staging of nvfp4_moe_bank_forward_host_bf16: x, residual and
+    // output rows of the largest call so far.
+    uint8_t *io_stage = nullptr;
+    size_t io_stage_bytes = 0;
 
     ~nvfp4_moe_bank() {
+        if (io_stage) cudaFree(io_stage);
         if (host_error) cudaFreeHost(host_error);
         if (norm_w) cudaFree(norm_w);
         for (int p = 0; p < 3; ++p)
@@ -679,6 +684,50 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_device_enqueue_bf16(
     }
     return nvfp4_moe_bank_forward_ptr_bf16(bank, x->data, residual ? residual->data : nullptr,
                                           dst->data, tokens, flags, nullptr);
+}
+
+extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_host_bf16(nvfp4_moe_bank *bank, const void *x_host,
+                                                                  const void *residual_host, void *out_host,
+                                                                  int tokens, int flags) {
+    if (!bank || !bank->runtime || !x_host || !out_host || tokens <= 0 ||
+        (flags & ~static_cast<int>(NVFP4_MOE_ADD_RESIDUAL | NVFP4_MOE_PRE_NORM)) != 0 ||
+        ((flags & NVFP4_MOE_ADD_RESIDUAL) && !residual_host) || ((flags & NVFP4_MOE_PRE_NORM) && !bank->norm_w))
+        return fail_invalid("invalid MoE bank host forward arguments");
+    if (!bank->owned_uploaded())
+        return fail_invalid("MoE bank forward requires every routed and shared projection of its expert range");
+    try {
+        nvfp4_runtime *rt = bank->runtime;
+        std::lock_guard<std::mutex> lock(rt->queue_mutex);
+        const size_t bytes = static_cast<size_t>(tokens) * bank->hidden * 2;
+        if (bank->io_stage_bytes < 3 * bytes) {
+            // Grow once to the largest call; the old staging may still be read
+            // by queued work, so drain the stream before freeing it.
+            check_cuda(cudaStreamSynchronize(rt->stream), "cudaStreamSynchronize(host forward staging)");
+            if (bank->io_stage) check_cuda(cudaFree(bank->io_stage), "cudaFree(host forward staging)");
+            bank->io_stage = nullptr;
+            bank->io_stage_bytes = 0;
+            check_cuda(cudaMalloc(reinterpret_cast<void **>(&bank->io_stage), 3 * bytes),
+                       "cudaMalloc(host forward staging)");
+            bank->io_stage_bytes = 3 * bytes;
+        }
+        uint8_t *dx = bank->io_stage, *dr = bank->io_stage + bytes, *dout = bank->io_stage + 2 * bytes;
+        cudaStream_t s = rt->stream;
+        check_cuda(cudaMemcpyAsync(dx, x_host, bytes, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(x)");
+        const bool res = (flags & NVFP4_MOE_ADD_RESIDUAL) != 0;
+        if (res)
+            check_cuda(cudaMemcpyAsync(dr, residual_host, bytes, cudaMemcpyHostToDevice, s),
+                       "cudaMemcpyAsync(residual)");
+        rt->direct_call(s, [&](cudaStream_t ks) {
+            enqueue_forward_bf16(bank, dx, res ? dr : nullptr, dout, tokens, ks, 0, (flags & NVFP4_MOE_PRE_NORM) != 0);
+        });
+        check_cuda(cudaMemcpyAsync(out_host, dout, bytes, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync(out)");
+        check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(host forward)");
+        raise_device_timeouts(rt);
+        clear_last_error();
+        return NVFP4_STATUS_OK;
+    } catch (const std::exception &error) {
+        return fail_exception(error);
+    }
 }
 
 extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_last_routing(nvfp4_moe_bank *bank, int max_tokens,

@@ -24,7 +24,10 @@
 //
 // Set-up: the first call on each device looks up the array's device address
 // with cudaGetSymbolAddress (with that device current) and caches it. Make
-// that first call before any stream capture begins.
+// that first call before any stream capture begins. The cache assumes the
+// device's primary context lives as long as the process: after
+// cudaDeviceReset the cached address is stale, so a process that resets a
+// device must not call this entry point on it again.
 #include "internal.h"
 #include "moe_decode.cuh"
 

@@ -247,6 +247,28 @@ extern "C" NVFP4_API nvfp4_status nvfp4_runtime_last_profile(const nvfp4_runtime
     return NVFP4_STATUS_OK;
 }
 
+namespace nvfp4 {
+
+void raise_device_timeouts(nvfp4_runtime *runtime) {
+    int timed_out = 0;
+    for (auto &word : runtime->error_words) {
+        if (*word.first != 0) {
+            timed_out = *word.first;
+            *word.first = 0;
+            check_cuda(cudaMemsetAsync(word.second, 0, sizeof(int), runtime->stream),
+                       "cudaMemsetAsync(device error word)");
+        }
+    }
+    if (timed_out) {
+        check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize");
+        throw std::runtime_error(
+            "an MoE bank kernel gave up waiting on a pipeline barrier (wait site " + std::to_string(timed_out) +
+            "); outputs since the previous synchronize are invalid");
+    }
+}
+
+}  // namespace nvfp4
+
 extern "C" NVFP4_API nvfp4_status nvfp4_runtime_synchronize(nvfp4_runtime *runtime) {
     if (!runtime) return fail_invalid("runtime is required");
     try {
@@ -287,21 +309,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_runtime_synchronize(nvfp4_runtime *runti
         }
         check_cuda(first_error, "cudaEventElapsedTime(profile)");
         runtime->last_profile = {0, kernel_ns, 0};
-        int timed_out = 0;
-        for (auto &word : runtime->error_words) {
-            if (*word.first != 0) {
-                timed_out = *word.first;
-                *word.first = 0;
-                check_cuda(cudaMemsetAsync(word.second, 0, sizeof(int), runtime->stream),
-                           "cudaMemsetAsync(device error word)");
-            }
-        }
-        if (timed_out) {
-            check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize");
-            throw std::runtime_error(
-                "an MoE bank kernel gave up waiting on a pipeline barrier (wait site " + std::to_string(timed_out) +
-                "); outputs since the previous synchronize are invalid");
-        }
+        raise_device_timeouts(runtime);
         clear_last_error();
         return NVFP4_STATUS_OK;
     } catch (const std::exception &error) {

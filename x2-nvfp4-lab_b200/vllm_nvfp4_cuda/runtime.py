@@ -149,6 +149,8 @@ _SIGNATURES: dict[str, tuple[list, object]] = {
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
     "nvfp4_moe_bank_forward_ptr_bf16": (
         [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p], C.c_int),
+    "nvfp4_moe_bank_forward_host_bf16": (
+        [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int], C.c_int),
     "nvfp4_moe_bank_last_routing": (
         [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.POINTER(C.c_int)], C.c_int),
     "nvfp4_moe_bank_last_logits": ([C.c_void_p, C.c_int, C.c_void_p, C.POINTER(C.c_int)], C.c_int),
@@ -207,6 +209,16 @@ def load_library(path: Path | None = None) -> C.CDLL:
 
 # cudaStreamLegacy: the legacy default stream as an explicit handle.
 CUDA_STREAM_LEGACY = 1
+
+
+def _current_cuda_device() -> int | None:
+    """The calling thread's CUDA device, the one a runtime created on this
+    thread binds; None when torch has no CUDA."""
+    try:
+        import torch
+    except ImportError:
+        return None
+    return torch.cuda.current_device() if torch.cuda.is_available() else None
 
 
 def _stream_handle(stream) -> C.c_void_p:
@@ -316,6 +328,7 @@ class NativeMatrix:
         self.rows = rows
         self.cols = cols
         self.shared_svm = False  # the lab's Adreno SVM placement has no counterpart here
+        self.device = _current_cuda_device()  # the runtime's device at upload (None without torch CUDA)
 
     def close(self) -> None:
         if self.handle:
@@ -420,6 +433,44 @@ class MoeBank:
             ),
             "nvfp4_moe_bank_forward_device_enqueue_bf16",
         )
+        return out
+
+    def forward_host(self, x, residual=None, out=None, pre_norm: bool = False):
+        """additive: one end-to-end call on host memory (nvfp4_moe_bank_forward_host_bf16):
+        x, residual and out are CPU BF16 torch tensors [tokens, hidden] (pinned
+        for asynchronous copies) or uint16/int16 numpy arrays of BF16 bits.
+        Returns out once the result is in it."""
+        def host_ptr(a, name):
+            if a is None:
+                return None, None
+            if isinstance(a, np.ndarray):
+                if a.dtype not in (np.uint16, np.int16) or a.ndim != 2 or a.shape[1] != self.hidden \
+                        or not a.flags.c_contiguous:
+                    raise ValueError(f"{name} must be contiguous BF16 bits [tokens, hidden]")
+                return C.c_void_p(a.ctypes.data), a.shape[0]
+            import torch
+
+            if a.dtype != torch.bfloat16 or a.is_cuda or a.dim() != 2 or a.shape[1] != self.hidden \
+                    or not a.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous CPU bfloat16 tensor [tokens, hidden]")
+            return C.c_void_p(a.data_ptr()), a.shape[0]
+
+        xp, T = host_ptr(x, "x")
+        if out is None:
+            if isinstance(x, np.ndarray):
+                out = np.empty_like(x)
+            else:
+                import torch
+
+                out = torch.empty_like(x, pin_memory=x.is_pinned())
+        op, To = host_ptr(out, "out")
+        rp, Tr = host_ptr(residual, "residual")
+        if To != T or (residual is not None and Tr != T):
+            raise ValueError("x, residual and out must have the same number of tokens")
+        flags = (NVFP4_MOE_ADD_RESIDUAL if residual is not None else 0) | (NVFP4_MOE_PRE_NORM if pre_norm else 0)
+        self.runtime._check(
+            self.runtime.lib.nvfp4_moe_bank_forward_host_bf16(self.handle, xp, rp, op, T, flags),
+            "nvfp4_moe_bank_forward_host_bf16")
         return out
 
     def forward(self, x, residual=None, out=None, stream=None, pre_norm: bool = False):
@@ -881,6 +932,10 @@ class Runtime:
 
         if x.dtype != torch.float32 or not x.is_cuda or x.shape[-1] != matrix.cols:
             raise ValueError("x must be a CUDA float32 tensor [..., cols]")
+        home = getattr(matrix, "device", None)
+        for name, t in (("x", x), ("out", out)):
+            if t is not None and home is not None and t.device.index != home:
+                raise ValueError(f"{name} is on {t.device} but the matrix is resident on cuda:{home}")
         lead = x.shape[:-1]
         x2 = x.reshape(-1, matrix.cols).contiguous()
         if out is None:
