@@ -10,9 +10,10 @@ outside that step's CUDA-event pair.
 
   value      tokens/s over all ranks, device time (sum of per-step events,
              max over ranks)
-  e2e        the same metric through the lab-style C-ABI call sequence with
-             host buffers: buffer upload (pinned host -> device), bank
-             forward, runtime synchronize, buffer download, wall clock
+  e2e        the same metric end to end with host buffers, wall clock:
+             one nvfp4_moe_bank_forward_host_bf16 call per step (pinned
+             host x and residual -> device, the forward, the output back to
+             pinned host memory, one stream synchronize)
   roofline   dominant kernel (moe_gate_up): algorithmic bytes per launch /
              its average CUDA-event duration, against MEASURED_PEAKS hbm_gbs
   cpu_baseline  the C restatement of the lab's CPU path (oracle/cpu_moe.c)
@@ -624,28 +625,17 @@ def run_ours(args) -> int:
         prefill.append(prefill_leg(rt, bank, stream, flush, 8192, args.seed, 10, 3, skew=True))
     clocks.__exit__(None, None, None)
 
-    # End to end through the lab-style C-ABI sequence with host buffers.
+    # End to end through the one-call host entry point: pinned host x and
+    # residual in, the forward, the host output back, one synchronize.
     host_x = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
     host_r = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
     for i in range(pool_n):
         host_x[i].copy_(pool[i].cpu())
         host_r[i].copy_(res_pool[i].cpu())
     host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    xb = rt.create_buffer(T * H * 2)
-    rb = rt.create_buffer(T * H * 2)
-    ob = rt.create_buffer(T * H * 2)
-    hx = [h.view(torch.int16).numpy() for h in host_x]
-    hr = [h.view(torch.int16).numpy() for h in host_r]
-    ho = host_out.view(torch.int16).numpy()
-    import ctypes as C
 
     def e2e_step(i):
-        xb.upload(hx[i % pool_n])
-        rb.upload(hr[i % pool_n])
-        bank.forward_device(xb, T, ob, residual=rb)
-        rt.synchronize()
-        rt._check(rt.lib.nvfp4_buffer_download(ob.handle, 0, C.c_void_p(ho.ctypes.data), ho.nbytes),
-                  "buffer_download")
+        bank.forward_host(host_x[i % pool_n], residual=host_r[i % pool_n], out=host_out)
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -739,8 +729,6 @@ def run_ours(args) -> int:
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    for b in (xb, rb, ob):
-        b.close()
     bank.close()
     rt.close()
     if pg:

@@ -111,6 +111,36 @@ def test_forward_without_residual_and_buffers(cuda_runtime, small_bank, small_ho
     out.close()
 
 
+@pytest.mark.parametrize("T", [1, 32, 150])
+def test_forward_host_matches_device_forward(cuda_runtime, wide_bank, wide_host, T):
+    """nvfp4_moe_bank_forward_host_bf16 (host buffers in, host buffer out, one
+    call) gives the bits of the device-pointer forward: pinned torch tensors
+    and numpy arrays of BF16 bits, with and without the residual, and a
+    second, smaller call after a larger one (the staging is reused)."""
+    import torch
+
+    H = wide_host.hidden
+    xbits = synthetic_np.tokens_bf16(T, H, 1100 + T)
+    rbits = synthetic_np.tokens_bf16(T, H, 1200 + T)
+    x, r = bits_to_bf16_tensor(xbits), bits_to_bf16_tensor(rbits)
+    want = wide_bank.forward(x, residual=r)
+    want_bare = wide_bank.forward(x)
+    torch.cuda.synchronize()
+    want = want.cpu().view(torch.int16).numpy()
+    want_bare = want_bare.cpu().view(torch.int16).numpy()
+    hx = torch.from_numpy(xbits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    hr = torch.from_numpy(rbits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    got = wide_bank.forward_host(hx, residual=hr)
+    np.testing.assert_array_equal(got.view(torch.int16).numpy(), want)
+    got_np = wide_bank.forward_host(np.ascontiguousarray(xbits))
+    np.testing.assert_array_equal(got_np.view(np.int16), want_bare)
+    check_routing(wide_bank, moe_layer(wide_host, synthetic_np.bf16_bits_to_f32(xbits)), T)
+    want1 = wide_bank.forward(x[:1].contiguous(), residual=r[:1].contiguous())
+    torch.cuda.synchronize()
+    one = wide_bank.forward_host(np.ascontiguousarray(xbits[:1]), residual=np.ascontiguousarray(rbits[:1]))
+    np.testing.assert_array_equal(one.view(np.int16), want1.cpu().view(torch.int16).numpy())
+
+
 def test_forward_more_than_64_tokens(cuda_runtime, small_bank, small_host):
     import torch
 
@@ -215,15 +245,20 @@ def test_trace_profile_and_errors(cuda_runtime, small_bank, small_host):
     H = small_host.hidden
     x = rt.upload_buffer(np.zeros(H, dtype=np.float32))
     out = rt.create_buffer(H * 4)
-    rt.set_trace_enabled(True)
-    rt.set_trace_scope("moe.layer.00.experts")
-    small_bank.decode_device(x, out)
-    prof = rt.synchronize()
-    events = rt.trace_events()
-    rt.set_trace_enabled(False)
-    assert prof.kernel_ns > 0
-    assert [e.operation for e in events] == ["moe_route", "moe_gate_up", "moe_down"]
-    assert events[0].scope == "moe.layer.00.experts" and events[0].duration_ns > 0
+    # One token on a full bank: the one-token kernel; the in-register
+    # variant: routing, gate/up and down (the down kernel combines).
+    for kernels, ops in (("tensor_core", ["moe_token"]), ("in_register", ["moe_route", "moe_gate_up", "moe_down"])):
+        small_bank.set_decode_kernels(kernels)
+        rt.set_trace_enabled(True)
+        rt.set_trace_scope("moe.layer.00.experts")
+        small_bank.decode_device(x, out)
+        prof = rt.synchronize()
+        events = rt.trace_events()
+        rt.set_trace_enabled(False)
+        small_bank.set_decode_kernels("tensor_core")
+        assert prof.kernel_ns > 0
+        assert [e.operation for e in events] == ops
+        assert events[0].scope == "moe.layer.00.experts" and events[0].duration_ns > 0
     # Argument validation mirrors the lab's messages and status codes.
     with pytest.raises(RuntimeError, match=r"\(1\): invalid MoE bank decode buffers"):
         small_bank.decode_device(x, rt.create_buffer(4))

@@ -10,6 +10,7 @@
 #include "internal.h"
 #include "moe_decode.cuh"
 #include "moe_prefill.cuh"
+#include "moe_token.cuh"
 
 #include <cmath>
 #include <cstring>
@@ -67,8 +68,11 @@ struct nvfp4_moe_bank {
     // output rows of the largest call so far.
     uint8_t *io_stage = nullptr;
     size_t io_stage_bytes = 0;
+    // Barrier words of the one-token kernel (moe_token.cu), zeroed at creation.
+    unsigned *token_sync = nullptr;
 
     ~nvfp4_moe_bank() {
+        if (token_sync) cudaFree(token_sync);
         if (io_stage) cudaFree(io_stage);
         if (host_error) cudaFreeHost(host_error);
         if (norm_w) cudaFree(norm_w);
@@ -156,11 +160,50 @@ bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
            tokens >= kDecodeTcMinTokens && tokens <= kDecodeTcMaxTokens;
 }
 
+// One-token calls of a bank that computes every expert run as one persistent
+// kernel (moe_token.cu) under the default decode kernels; the in-register
+// variant keeps the three-launch path for every size.
+bool use_token_kernel(const nvfp4_moe_bank *bank, int tokens, const EpArgs *ep) {
+    return tokens == 1 && !ep && bank->token_sync && bank->decode_kernels == NVFP4_DECODE_KERNELS_TENSOR_CORE &&
+           bank->e_first == 0 && bank->e_count == bank->experts && bank->shared_here &&
+           token_supported(bank->runtime->sm_count, bank->experts, bank->hidden, bank->intermediate,
+                           static_cast<int>(bank->scale_pitch(0)), static_cast<int>(bank->scale_pitch(2)));
+}
+
 void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const void *residual,
                     void *out, int out_f32, int tokens, cudaStream_t stream, const EpArgs *ep = nullptr,
                     bool pre_norm = false) {
     const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
     const int sms = bank->runtime->sm_count;
+    nvfp4_runtime *rt = bank->runtime;
+    if (use_token_kernel(bank, tokens, ep)) {
+        TokenArgs ta{};
+        ta.router = bank->router;
+        ta.bias = bank->router_bias;
+        ta.x = x;
+        ta.x_is_f32 = x_is_f32;
+        ta.norm_w = pre_norm && !x_is_f32 ? bank->norm_w : nullptr;
+        ta.norm_eps = bank->norm_eps;
+        ta.residual = residual;
+        ta.out = out;
+        ta.out_f32 = out_f32;
+        for (int p = 0; p < 3; ++p) {
+            ta.packed[p] = bank->packed[p];
+            ta.scales[p] = bank->scales[p];
+            ta.scale_pitch[p] = static_cast<int>(bank->scale_pitch(p));
+        }
+        ta.inv_scales = bank->inv_scales;
+        ta.E = E;
+        ta.H = H;
+        ta.I = I;
+        ta.act = bank->ds.ypart;
+        ta.sync = bank->token_sync;
+        ta.s = bank->ds;
+        rt->profiled_kernel("moe_token", stream, [&](cudaStream_t s) {
+            check_cuda(launch_token(ta, sms, s), "moe_token_kernel");
+        });
+        return;
+    }
     const bool tc = use_tensor_core_decode(bank, tokens);
     RouteArgs ra{};
     ra.router = bank->router;
@@ -178,7 +221,6 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     ra.norm_w = pre_norm && !x_is_f32 ? bank->norm_w : nullptr;
     ra.norm_eps = bank->norm_eps;
     ra.s = bank->ds;
-    nvfp4_runtime *rt = bank->runtime;
     rt->profiled_kernel("moe_route", stream, [&](cudaStream_t s) {
         check_cuda(launch_route(ra, s, true), "moe_route_kernel");
     });
@@ -454,6 +496,9 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_create(nvfp4_runtime *runtime,
         check_cuda(cudaMemsetAsync(holder->scratch, 0, scratch, runtime->stream),
                    "cudaMemsetAsync(MoE bank scratch)");
         decode_scratch_carve(holder->ds, holder->scratch, experts, hidden, intermediate);
+        check_cuda(cudaMalloc(&holder->token_sync, token_sync_bytes()), "cudaMalloc(MoE bank token barriers)");
+        check_cuda(cudaMemsetAsync(holder->token_sync, 0, token_sync_bytes(), runtime->stream),
+                   "cudaMemsetAsync(MoE bank token barriers)");
         check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&holder->host_error), sizeof(int), cudaHostAllocMapped),
                    "cudaHostAlloc(MoE bank error word)");
         *holder->host_error = 0;
