@@ -21,8 +21,15 @@ outside that step's CUDA-event pair.
   linear     the dense NVFP4 linear at the LM-head shape (248320 x 2048),
              1 and 4 vectors: device time per call and its HBM rate
 
---gpus N (under torchrun) runs N independent replicas, one bank per GPU and
-a distinct token stream per rank (weak scaling, no collective).
+--gpus N (under torchrun) runs the layer expert-parallel over the N GPUs:
+rank r holds routed experts [r*256/N, (r+1)*256/N) and the shared expert on
+rank 0, every rank sees the same 32 tokens (strong scaling: the step's work
+is fixed), and the combine kernel reduces the ranks' partial tiles over
+NVLink peer memory (no NCCL call on the step's path). `value` is the 32
+tokens over the step time (max over ranks); `step_breakdown` splits the
+step into routing, expert GEMVs and the exchange. The `expert_parallel`
+object adds the one-token and 4096-token calls (NCCL all-reduce) and the
+token-sharded 4096-token prefill (NCCL all-to-all).
 --impl reference times the lab's CPU path (the C restatement) for the same
 workload, W untimed batches and then exactly K timed ones, each a batch of
 --tokens tokens on all host cores, and prints its own JSON line.
@@ -464,7 +471,51 @@ def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmu
     layers["fused_combine_p2p"].close()
     pg.barrier()
     bank.set_expert_range(0, E, True)
+    out["token_sharded_prefill4096"] = token_sharded_leg(bank, rt, pg, world, seed)
+    bank.set_expert_range(0, E, True)
     return out
+
+
+def token_sharded_leg(bank, rt, pg, world: int, seed: int, T: int = 4096, calls: int = 5) -> dict:
+    """BASELINE config 2 with the tokens sharded: rank r brings T/N tokens,
+    routes them, ships each token row once to every other rank owning one
+    of its picks (NCCL all-to-all), computes the rows it received over its
+    own experts and returns the FP32 partials (TokenShardedLayer). The
+    composition synchronises with the host (counts), so each call is timed
+    by wall clock between barriers, max over ranks; outputs are compared
+    with the single-GPU bank on the same tokens."""
+    import torch
+
+    from vllm_nvfp4_cuda import synthetic
+    from vllm_nvfp4_cuda.expert_parallel import TokenShardedLayer
+
+    rank = pg.get_rank()
+    per = T // world
+    x_all = synthetic.synthetic_tokens(T, H, seed + 80)
+    r_all = synthetic.synthetic_tokens(T, H, seed + 81)
+    ref = bank.forward(x_all, residual=r_all).float()[rank * per:(rank + 1) * per]
+    x = x_all[rank * per:(rank + 1) * per].contiguous()
+    r = r_all[rank * per:(rank + 1) * per].contiguous()
+    torch.cuda.synchronize()
+    layer = TokenShardedLayer(bank, lambda t: rt.finalize_bf16(t))
+    y = layer.forward(x, r)
+    torch.cuda.synchronize()
+    err = float(((y.float() - ref).pow(2).mean() / ref.pow(2).mean()).sqrt())
+    times = []
+    for _ in range(calls):
+        pg.barrier()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        layer.forward(x, r)
+        torch.cuda.synchronize()
+        times.append(time.perf_counter() - t0)
+    t = torch.tensor([min(times), err], device="cuda", dtype=torch.float64)
+    pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    sec, err = float(t[0].item()), float(t[1].item())
+    return {"tokens": T, "tokens_per_rank": per, "ms_per_call": round(sec * 1000.0, 3),
+            "tokens_per_s": round(T / sec, 1), "rel_rmse_vs_single_gpu": float(f"{err:.3g}"),
+            "timing": "wall clock per call between barriers (the composition syncs with the host), best of "
+                      f"{calls}, max over ranks"}
 
 
 def traced_steps(rt, stream, flush, step, n: int):
@@ -509,33 +560,51 @@ def run_ours(args) -> int:
     # The library runs calls of 4 to 32 tokens on the tensor-core expert
     # GEMVs for this shape (five launches per layer call), others in-register
     # (three launches up to 16 tokens, where the down kernel combines; four
-    # above).
+    # above). Under expert parallelism the combine is the cross-rank one.
     tc_decode = 4 <= T <= 32 and args.decode_kernels == "tensor_core"
     launches = 5 if tc_decode else (3 if T <= 16 else 4)
+    if world > 1:
+        launches = 5 if tc_decode else 3
     rt = Runtime()
     bank, meta = synthetic.build_bank(rt, E, H, I, args.seed)
     bank.set_decode_kernels(args.decode_kernels)
     stream = torch.cuda.Stream()
     pool_n = 16
-    pool = [synthetic.synthetic_tokens(T, H, 1000 * (rank + 1) + i) for i in range(pool_n)]
-    res_pool = [synthetic.synthetic_tokens(T, H, 5000 * (rank + 1) + i) for i in range(pool_n)]
+    # One GPU: the whole layer per rank. Several GPUs: expert parallelism --
+    # rank r holds routed experts [r*E/N, (r+1)*E/N) (the shared expert on
+    # rank 0), every rank sees the same 32 tokens, and the combine reduces
+    # the ranks' partial tiles over NVLink peer memory in the same kernel.
+    pool = [synthetic.synthetic_tokens(T, H, 1000 + i) for i in range(pool_n)]
+    res_pool = [synthetic.synthetic_tokens(T, H, 5000 + i) for i in range(pool_n)]
     out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
     torch.cuda.synchronize()
+    ep_layer = None
+    first, count, shared_here = 0, E, True
+    if world > 1:
+        from vllm_nvfp4_cuda.expert_parallel import ExpertParallelLayer
 
-    # Routing of every pool batch -> algorithmic bytes of each step.
+        ep_layer = ExpertParallelLayer(bank, lambda t: rt.finalize_bf16(t), fused_runtime=rt)
+        first, count, shared_here = ep_layer.range.first, ep_layer.range.count, ep_layer.range.shared_here
+
+    def step(i):
+        if ep_layer is not None:
+            ep_layer.forward(pool[i % pool_n], residual=res_pool[i % pool_n], stream=stream)
+        else:
+            bank.forward(pool[i % pool_n], residual=res_pool[i % pool_n], out=out, stream=stream)
+
+    # Routing of every pool batch -> algorithmic bytes of each step (this
+    # rank's routed experts, plus the shared expert where it is computed).
     uniq = []
     for i in range(pool_n):
         with torch.cuda.stream(stream):
-            bank.forward(pool[i], residual=res_pool[i], out=out, stream=stream)
+            step(i)
         stream.synchronize()
         r = bank.last_routing(T)
-        uniq.append(len(set(r.ids[:, :8].reshape(-1).tolist())))
-    gate_up_bytes = [(u + 1) * 2 * PER_PROJ_BYTES + T * H * 2 + T * 9 * I * 2 for u in uniq]
-    step_bytes = [(u + 1) * 3 * PER_PROJ_BYTES + (E + 1) * H * 2 + 3 * T * H * 2 for u in uniq]
-
-    def step(i):
-        bank.forward(pool[i % pool_n], residual=res_pool[i % pool_n], out=out, stream=stream)
+        ids = set(r.ids[:, :8].reshape(-1).tolist())
+        uniq.append(len([e for e in ids if first <= e < first + count]) + (1 if shared_here else 0))
+    gate_up_bytes = [u * 2 * PER_PROJ_BYTES + T * H * 2 + T * 9 * I * 2 for u in uniq]
+    step_bytes = [u * 3 * PER_PROJ_BYTES + (E + 1) * H * 2 + 3 * T * H * 2 for u in uniq]
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
@@ -576,7 +645,7 @@ def run_ours(args) -> int:
         t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         total_ms = float(t.item())
-    value = world * T * args.steps / (total_ms / 1000.0)
+    value = T * args.steps / (total_ms / 1000.0)
 
     by_op: dict[str, list[float]] = {}
     for ev in events:
@@ -593,49 +662,66 @@ def run_ours(args) -> int:
         traffic = json.loads(traffic_path.read_text()).get(f"moe_gate_up_T{T}")
     layer_bytes = sum(step_bytes[i % pool_n] for i in range(args.steps))
 
-    # T=1 latency (BASELINE config 0 target), same protocol.
+    # Per-step breakdown (traced pass, this rank): routing, expert GEMVs,
+    # and the cross-rank exchange (the fused combine) under expert parallelism.
+    breakdown = {
+        "routing_us": round(1000.0 * sum(by_op.get("moe_route", [])) / args.steps, 2),
+        "experts_us": round(1000.0 * sum(sum(by_op.get(k, [])) for k in ("moe_gate_up", "moe_quantize_act",
+                                                                      "moe_down")) / args.steps, 2),
+        "exchange_us": round(1000.0 * sum(by_op.get("moe_combine_ep", [])) / args.steps, 2),
+    }
+    if ep_layer is not None:
+        t = torch.tensor(list(breakdown.values()), device="cuda", dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        breakdown = dict(zip(breakdown, (round(float(v), 2) for v in t.tolist())))
+        breakdown["note"] = "per-rank traced kernel times, max over ranks; traced kernels each include a launch gap"
+
+    # T=1 latency (BASELINE config 0 target), same protocol, one GPU.
     lat = []
-    x1 = [p[:1].contiguous() for p in pool]
-    o1 = torch.empty(1, H, dtype=torch.bfloat16, device="cuda")
-    torch.cuda.synchronize()
-    with torch.cuda.stream(stream):
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(40)]
-        torch.cuda._sleep(int(2e5) * 45)
-        for i in range(45):
-            flush.zero_()
-            if i >= 5:
-                ev[i - 5][0].record(stream)
-            bank.forward(x1[i % pool_n], out=o1, stream=stream)
-            if i >= 5:
-                ev[i - 5][1].record(stream)
-    stream.synchronize()
-    rt.synchronize()
-    lat = sorted(a.elapsed_time(b) * 1000.0 for a, b in ev)
     t1_ops: dict[str, list[float]] = {}
-    for evt in traced_steps(rt, stream, flush, lambda i: bank.forward(x1[i % pool_n], out=o1, stream=stream), 20):
-        t1_ops.setdefault(evt.operation, []).append(evt.duration_ns / 1e3)
+    if world == 1:
+        x1 = [p[:1].contiguous() for p in pool]
+        o1 = torch.empty(1, H, dtype=torch.bfloat16, device="cuda")
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(40)]
+            torch.cuda._sleep(int(2e5) * 45)
+            for i in range(45):
+                flush.zero_()
+                if i >= 5:
+                    ev[i - 5][0].record(stream)
+                bank.forward(x1[i % pool_n], out=o1, stream=stream)
+                if i >= 5:
+                    ev[i - 5][1].record(stream)
+        stream.synchronize()
+        rt.synchronize()
+        lat = sorted(a.elapsed_time(b) * 1000.0 for a, b in ev)
+        for evt in traced_steps(rt, stream, flush, lambda i: bank.forward(x1[i % pool_n], out=o1, stream=stream),
+                                20):
+            t1_ops.setdefault(evt.operation, []).append(evt.duration_ns / 1e3)
 
-    ep = None
-    if world > 1:
-        ep = ep_leg(rt, bank, stream, flush, pg, world, args.seed, args.steps, 3)
-
-    prefill = []
-    if not args.no_prefill:
-        prefill.append(prefill_leg(rt, bank, stream, flush, 4096, args.seed, 10, 3, skew=False))
-        prefill.append(prefill_leg(rt, bank, stream, flush, 8192, args.seed, 10, 3, skew=True))
-    clocks.__exit__(None, None, None)
-
-    # End to end through the one-call host entry point: pinned host x and
-    # residual in, the forward, the host output back, one synchronize.
+    # End to end: pinned host x and residual in, the layer, the output back
+    # to pinned host memory, one synchronize per step.
     host_x = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
     host_r = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(pool_n)]
     for i in range(pool_n):
         host_x[i].copy_(pool[i].cpu())
         host_r[i].copy_(res_pool[i].cpu())
     host_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    dev_x = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    dev_r = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
 
     def e2e_step(i):
-        bank.forward_host(host_x[i % pool_n], residual=host_r[i % pool_n], out=host_out)
+        if ep_layer is None:
+            # One call of the host entry point (nvfp4_moe_bank_forward_host_bf16).
+            bank.forward_host(host_x[i % pool_n], residual=host_r[i % pool_n], out=host_out)
+            return
+        with torch.cuda.stream(stream):
+            dev_x.copy_(host_x[i % pool_n], non_blocking=True)
+            dev_r.copy_(host_r[i % pool_n], non_blocking=True)
+            y = ep_layer.forward(dev_x, residual=dev_r, stream=stream)
+            host_out.copy_(y, non_blocking=True)
+        stream.synchronize()
 
     for i in range(args.warmup):
         e2e_step(i)
@@ -649,7 +735,22 @@ def run_ours(args) -> int:
         t = torch.tensor([e2e_s], device="cuda", dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e_value = world * T * args.steps / e2e_s
+    e2e_value = T * args.steps / e2e_s
+
+    if ep_layer is not None:
+        ep_layer.close()
+        pg.barrier()
+        bank.set_expert_range(0, E, True)
+
+    ep = None
+    if world > 1:
+        ep = ep_leg(rt, bank, stream, flush, pg, world, args.seed, args.steps, 3)
+
+    prefill = []
+    if not args.no_prefill and world == 1:
+        prefill.append(prefill_leg(rt, bank, stream, flush, 4096, args.seed, 10, 3, skew=False))
+        prefill.append(prefill_leg(rt, bank, stream, flush, 8192, args.seed, 10, 3, skew=True))
+    clocks.__exit__(None, None, None)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -681,7 +782,7 @@ def run_ours(args) -> int:
             "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 5),
             "higher_is_better": True,
-            "scaling": "weak",
+            "scaling": "strong",
             "vs_baseline": None,
             "dtype": ("nvfp4 weights x nvfp4 activations (four terms per row) on tcgen05, f32 accumulate; bf16 I/O"
                       if tc_decode else "nvfp4 weights x f16 activations, f32 accumulate; bf16 I/O"),
@@ -696,15 +797,18 @@ def run_ours(args) -> int:
                 "top_k": 8,
                 "shared_expert": True,
                 "layers": 1,
-                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "parallelism": (f"ep{world}: {E // world} routed experts per GPU (shared expert on rank 0), "
+                                "the 32 tokens replicated, combine fused with the cross-rank reduction over "
+                                "NVLink peer memory" if world > 1 else "single GPU"),
                 "l2": "flushed before every step (256 MiB write) outside the per-step CUDA events",
                 "inputs": f"pool of {pool_n} distinct token batches per rank",
                 "mean_unique_routed_experts": round(float(np.mean(uniq)), 2),
             },
-            "us_per_token": round(1e6 / value * world, 4) if world == 1 else None,
+            "us_per_token": round(1e6 / value, 4),
+            "step_breakdown": breakdown,
             "layer_hbm_gbs": round(layer_bytes / (total_ms / 1000.0) / 1e9, 1),
-            "decode_t1_us": {"median": round(lat[len(lat) // 2], 3), "p10": round(lat[len(lat) // 10], 3),
-                             "p90": round(lat[(9 * len(lat)) // 10], 3)},
+            "decode_t1_us": ({"median": round(lat[len(lat) // 2], 3), "p10": round(lat[len(lat) // 10], 3),
+                              "p90": round(lat[(9 * len(lat)) // 10], 3)} if lat else None),
             "kernels_ms_avg": {k: round(sum(v) / len(v), 5) for k, v in by_op.items()},
             "decode_t1_kernels_us": {k: round(statistics.median(v), 3) for k, v in t1_ops.items()},
             "roofline": {
@@ -718,8 +822,8 @@ def run_ours(args) -> int:
                 "traffic": traffic,
                 "algorithmic_bytes_per_launch": round(gu_bytes / max(1, len(gu))),
             },
-            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * T * H * 2,
-                    "d2h_bytes_per_step": T * H * 2},
+            "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": 2 * T * H * 2 * world,
+                    "d2h_bytes_per_step": T * H * 2 * world},
             "gpu_launches": launches * args.steps,
             "prefill": prefill,
             "expert_parallel": ep,

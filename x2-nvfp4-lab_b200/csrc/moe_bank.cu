@@ -262,11 +262,12 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
             check_cuda(launch_down_tc(bank->pmaps.w[2], bank->tc_maps, ta, tokens, sms, s),
                        "moe_down_tc_kernel");
-            if (ep)
-                check_cuda(launch_combine_ep(da, *ep, s), "moe_combine_ep_kernel");
-            else
-                check_cuda(launch_combine(da, s), "moe_combine_kernel");
+            if (!ep) check_cuda(launch_combine(da, s), "moe_combine_kernel");
         });
+        if (ep)
+            rt->profiled_kernel("moe_combine_ep", stream, [&](cudaStream_t s) {
+                check_cuda(launch_combine_ep(da, *ep, s), "moe_combine_ep_kernel");
+            });
         return;
     }
 
@@ -286,8 +287,11 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
 
     rt->profiled_kernel("moe_down", stream, [&](cudaStream_t s) {
         check_cuda(launch_down_tma(bank->maps, da, sms, s, ep == nullptr), "moe_down_tma_kernel");
-        if (ep) check_cuda(launch_combine_ep(da, *ep, s), "moe_combine_ep_kernel");
     });
+    if (ep)
+        rt->profiled_kernel("moe_combine_ep", stream, [&](cudaStream_t s) {
+            check_cuda(launch_combine_ep(da, *ep, s), "moe_combine_ep_kernel");
+        });
 }
 
 bool prefill_supported(const nvfp4_moe_bank *bank) {

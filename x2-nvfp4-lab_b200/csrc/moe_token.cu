@@ -83,32 +83,39 @@ __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned *p) {
     return v;
 }
 
+__device__ __forceinline__ unsigned ld_relaxed_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void st_release_u32(unsigned *p, unsigned v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Grid-wide barrier over gridDim.x CTAs. Thread 0 reads the generation,
-// arrives on the count, and either (last to arrive) resets the count and
-// advances the generation, or waits -- bounded by kWaitLimitNs -- for the
-// generation to advance. After a failure recorded in *err (by this wait or
-// any other) the CTA still arrives but no longer waits. Returns false when
-// the CTA passed without the barrier having opened.
-__device__ bool grid_barrier(unsigned *count, unsigned *gen, int *err, int site, int *s_flag) {
+// Grid-wide barrier over gridDim.x CTAs. `g0` is the generation thread 0
+// read at kernel entry (it cannot advance before this CTA arrives). After
+// the CTA's __syncthreads, thread 0 arrives on the count with a gpu-scope
+// acquire-release add (which also publishes the CTA's earlier writes), and either --
+// last to arrive -- resets the count and advances the generation with a
+// release store, or polls the generation with acquire loads, bounded by
+// kWaitLimitNs. After a failure recorded in *err (by this wait or any other)
+// the CTA still arrives but no longer waits. Returns false when the CTA
+// passed without the barrier having opened.
+__device__ bool grid_barrier(unsigned *count, unsigned *gen, unsigned g0, int *err, int site, int *s_flag) {
     __syncthreads();
     if (threadIdx.x == 0) {
         int ok = 1;
-        const unsigned g0 = ld_acquire_u32(gen);
-        __threadfence();
-        const unsigned arrived = atomicAdd(count, 1u) + 1u;
-        if (arrived == gridDim.x) {
-            atomicExch(count, 0u);
-            __threadfence();
+        unsigned arrived;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(arrived) : "l"(count) : "memory");
+        if (arrived + 1u == gridDim.x) {
+            asm volatile("st.relaxed.gpu.global.u32 [%0], 0;" ::"l"(count) : "memory");
             st_release_u32(gen, g0 + 1u);
         } else {
             unsigned long long t0 = 0;
             for (unsigned i = 0;; ++i) {
                 if (ld_acquire_u32(gen) != g0) break;
-                if ((i & 7u) == 7u) {
+                if ((i & 63u) == 63u) {
                     if (*reinterpret_cast<volatile int *>(err) != 0) {
                         ok = 0;
                         break;
@@ -122,37 +129,51 @@ __device__ bool grid_barrier(unsigned *count, unsigned *gen, int *err, int site,
                         break;
                     }
                 }
-                __nanosleep(20);
             }
         }
-        __threadfence();
         *s_flag = ok;
     }
     __syncthreads();
     return *s_flag != 0;
 }
 
+// Two f16 products added to an FP32 accumulator with the sm_100
+// mixed-precision FMA (f16 inputs, f32 addend and result, one rounding):
+// acc = fma(a.lo, b.lo, acc); acc = fma(a.hi, b.hi, acc).
+__device__ __forceinline__ float fma2_f16_f32(uint32_t a, uint32_t b, float acc) {
+    asm("{\n\t.reg .f16 a0, a1, b0, b1;\n\t"
+        "mov.b32 {a0, a1}, %1;\n\tmov.b32 {b0, b1}, %2;\n\t"
+        "fma.rn.f32.f16 %0, a0, b0, %0;\n\tfma.rn.f32.f16 %0, a1, b1, %0;\n\t}"
+        : "+f"(acc)
+        : "r"(a), "r"(b));
+    return acc;
+}
+
 // Dot product of one 16-byte unit of a row (32 columns: two E4M3 blocks of
-// 16) with 32 FP32 activations: per block the exact f16 codes times x in
-// FP32, then times the block scale.
-__device__ __forceinline__ float unit_dot(uint4 w, uint16_t sc, const float *x, float acc) {
+// 16) with 32 activations held as 16 f16x2 words: the E2M1 codes convert
+// exactly to f16, each block's products accumulate in FP32 (two chains per
+// block), and the block sums are scaled by their E4M3 scales in FP32. The
+// E2M1 x activation products are exact, so the sums carry only the FP32
+// rounding of the additions.
+__device__ __forceinline__ float unit_dot_h(uint4 w, uint16_t sc, const uint32_t *xh, float acc) {
     const uint32_t s2 = e4m3x2_to_f16x2(sc);
     const float2 s = __half22float2(*reinterpret_cast<const __half2 *>(&s2));
     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-    float p[2] = {0.0f, 0.0f};
+    float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
         uint32_t h[4];
         e2m1x8_to_f16x8(words[j], h);
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&h[m]));
-            p[j >> 1] = fmaf(f.x, x[8 * j + 2 * m], p[j >> 1]);
-            p[j >> 1] = fmaf(f.y, x[8 * j + 2 * m + 1], p[j >> 1]);
-        }
+        for (int m = 0; m < 4; ++m) p[j] = fma2_f16_f32(h[m], xh[4 * j + m], p[j]);
     }
-    acc = fmaf(p[0], s.x, acc);
-    return fmaf(p[1], s.y, acc);
+    acc = fmaf(p[0] + p[1], s.x, acc);
+    return fmaf(p[2] + p[3], s.y, acc);
+}
+
+__device__ __forceinline__ uint32_t f32x2_to_f16x2(float lo, float hi) {
+    const __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<const uint32_t *>(&h);
 }
 
 struct TokenLayout {
@@ -169,7 +190,7 @@ __host__ __device__ inline TokenLayout token_layout(int G, int H, int I, int gpi
     L.NH = (H + G - 1) / G;
     size_t o = 0;
     L.x_s = o;   o = align_up(o + sizeof(float) * H, 128);
-    L.act_s = o; o = align_up(o + sizeof(float) * kSlots * I, 128);
+    L.act_s = o; o = align_up(o + sizeof(__half) * kSlots * I, 128);
     L.gpk = o;   o = align_up(o + (size_t)L.NR * (H / 2), 128);
     L.upk = o;   o = align_up(o + (size_t)L.NR * (H / 2), 128);
     L.gsc = o;   o = align_up(o + (size_t)L.NR * gpitch, 128);
@@ -181,15 +202,17 @@ __host__ __device__ inline TokenLayout token_layout(int G, int H, int I, int gpi
     return L;
 }
 
-// XN: FP32 activations each lane keeps in registers for the gate/up rows
-// (H / (lanes per row)); 64 for H = 2048, 32 for H <= 1024.
+// XN: activations each lane keeps (as f16x2 words) for the gate/up rows,
+// H / (lanes per row); 64 for H = 2048, 32 for H <= 1024.
 template <int XN>
 __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a) {
     extern __shared__ __align__(128) uint8_t tsm[];
     __shared__ uint64_t bars[4];  // gate/up shared, gate/up routed, down shared, down routed
     __shared__ int s_ids[kSlots];
     __shared__ float s_w[kSlots];
+    __shared__ float s_ginv[kSlots], s_uinv[kSlots], s_coef[kSlots];  // per slot: gate, up, weight x down
     __shared__ float s_red[kTokenWarps];
+    __shared__ float s_logits[257];
     __shared__ float s_inv;
     __shared__ int s_flag;
     __shared__ int s_drain;
@@ -200,7 +223,7 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
     const int gpitch = a.scale_pitch[0], dpitch = a.scale_pitch[2];
     const TokenLayout L = token_layout(G, H, I, gpitch, dpitch);
     float *x_s = reinterpret_cast<float *>(tsm + L.x_s);
-    float *act_s = reinterpret_cast<float *>(tsm + L.act_s);
+    __half *act_s = reinterpret_cast<__half *>(tsm + L.act_s);
     uint8_t *gpk = tsm + L.gpk, *upk = tsm + L.upk, *gsc = tsm + L.gsc, *usc = tsm + L.usc;
     uint8_t *dpk = tsm + L.dpk, *dsc = tsm + L.dsc;
     float *y_s = reinterpret_cast<float *>(tsm + L.y_s);
@@ -213,40 +236,59 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
     const int h0 = (int)((long long)H * c / G), h1 = (int)((long long)H * (c + 1) / G);
     const int nh = h1 - h0;
     const int shared_u0 = max(u0, (kSlots - 1) * I);  // first pair of slot 8 in range
+    const int routed_end = min(u1, (kSlots - 1) * I);
+    const bool have_gu_shared = shared_u0 < u1, have_gu_routed = u0 < routed_end;
+    // Routed pairs split at a slot boundary into at most two segments.
+    const int mid = have_gu_routed ? min(routed_end, (u0 / I + 1) * I) : u0;
 
     const size_t gp_row = H / 2, dp_row = I / 2;
-    // Gate/up rows of pairs [v0, v1) (one slot) of expert e -> local pair index v0 - u0.
-    auto issue_gate_up = [&](int v0, int v1, int e, uint64_t *bar) {
+    auto gate_up_bytes = [&](int v0, int v1) { return (uint32_t)((v1 - v0) * 2 * (gp_row + gpitch)); };
+    const uint32_t down_slot_bytes = (uint32_t)(nh * (dp_row + dpitch));
+    // Copy `j` of gate/up pairs [v0, v1) (one slot) of expert e: j = 0/1 the
+    // gate/up codes, 2/3 their scales, into local pair index v0 - u0.
+    auto copy_gate_up = [&](int j, int v0, int v1, int e, uint64_t *bar) {
         const int r0 = v0 % I, n = v1 - v0, li = v0 - u0;
         const size_t row0 = (size_t)e * I + r0;
-        const uint32_t pk = (uint32_t)(n * gp_row), sc = (uint32_t)(n * gpitch);
-        bulk_g2s(gpk + li * gp_row, a.packed[0] + row0 * gp_row, pk, bar);
-        bulk_g2s(upk + li * gp_row, a.packed[1] + row0 * gp_row, pk, bar);
-        bulk_g2s(gsc + (size_t)li * gpitch, a.scales[0] + row0 * gpitch, sc, bar);
-        bulk_g2s(usc + (size_t)li * gpitch, a.scales[1] + row0 * gpitch, sc, bar);
+        if (j < 2)
+            bulk_g2s((j == 0 ? gpk : upk) + li * gp_row, a.packed[j] + row0 * gp_row, (uint32_t)(n * gp_row), bar);
+        else
+            bulk_g2s((j == 2 ? gsc : usc) + (size_t)li * gpitch, a.scales[j - 2] + row0 * gpitch,
+                     (uint32_t)(n * gpitch), bar);
     };
-    auto gate_up_bytes = [&](int v0, int v1) { return (uint32_t)((v1 - v0) * 2 * (gp_row + gpitch)); };
-    auto issue_down = [&](int slot, int e, uint64_t *bar) {
+    // Copy `j` (0 codes, 1 scales) of the down rows [h0, h1) of slot `slot`.
+    auto copy_down = [&](int j, int slot, int e, uint64_t *bar) {
         const size_t row0 = (size_t)e * H + h0;
-        bulk_g2s(dpk + (size_t)slot * L.NH * dp_row, a.packed[2] + row0 * dp_row, (uint32_t)(nh * dp_row), bar);
-        bulk_g2s(dsc + (size_t)slot * L.NH * dpitch, a.scales[2] + row0 * dpitch, (uint32_t)(nh * dpitch), bar);
+        if (j == 0)
+            bulk_g2s(dpk + (size_t)slot * L.NH * dp_row, a.packed[2] + row0 * dp_row, (uint32_t)(nh * dp_row), bar);
+        else
+            bulk_g2s(dsc + (size_t)slot * L.NH * dpitch, a.scales[2] + row0 * dpitch, (uint32_t)(nh * dpitch), bar);
     };
-    const uint32_t down_slot_bytes = (uint32_t)(nh * (dp_row + dpitch));
 
-    // ---- entry: barriers, the shared expert's rows, the router row --------
-    bool have_gu_shared = shared_u0 < u1, have_gu_routed = u0 < (kSlots - 1) * I && u0 < u1;
+    // ---- entry -------------------------------------------------------------
+    // Thread 0: the barrier generations (neither can advance before this CTA
+    // arrives, so plain loads whose latency hides behind the router work),
+    // the copy barriers and every expected byte count -- the routed counts do
+    // not depend on which experts are picked.
+    unsigned gen0 = 0, gen1 = 0;
     if (threadIdx.x == 0) {
+        gen0 = ld_relaxed_u32(a.sync + 32);
+        gen1 = ld_relaxed_u32(a.sync + 96);
 #pragma unroll
         for (int i = 0; i < 4; ++i) mbar_init(&bars[i], 1);
         fence_barrier_init();
-        if (have_gu_shared) {
-            mbar_arrive_expect_tx(&bars[0], gate_up_bytes(shared_u0, u1));
-            issue_gate_up(shared_u0, u1, E, &bars[0]);
-        }
+        if (have_gu_shared) mbar_arrive_expect_tx(&bars[0], gate_up_bytes(shared_u0, u1));
+        if (have_gu_routed) mbar_arrive_expect_tx(&bars[1], gate_up_bytes(u0, routed_end));
         if (nh > 0) {
             mbar_arrive_expect_tx(&bars[2], down_slot_bytes);
-            issue_down(kSlots - 1, E, &bars[2]);
+            mbar_arrive_expect_tx(&bars[3], down_slot_bytes * kTopK);
         }
+    }
+    __syncthreads();
+    // The last warp (no router row on grids of 37 or more CTAs) fetches the
+    // shared expert's rows now, before routing resolves.
+    if (warp == kTokenWarps - 1) {
+        if (have_gu_shared && lane < 4) copy_gate_up(lane, shared_u0, u1, E, &bars[0]);
+        if (nh > 0 && lane >= 4 && lane < 6) copy_down(lane - 4, kSlots - 1, E, &bars[2]);
     }
 
     // Router row of this warp (row E is the shared gate): every load in flight
@@ -313,28 +355,34 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
         }
     }
 
-    // This lane's columns of x for the gate/up rows: LR lanes per row, lane
-    // group q of RPW rows per warp pass, 16-byte units lr + LR*k.
+    // This lane's columns of x (f16x2) for the gate/up rows: LR lanes per row,
+    // lane group q of RPW rows per warp pass, 16-byte units lr + LR*k.
     const int LR = H / XN, RPW = 32 / LR, q = lane / LR, lr = lane % LR;
-    float xr[XN];
+    uint32_t xh[XN / 2];
 #pragma unroll
     for (int k = 0; k < XN / 32; ++k) {
         const int unit = lr + LR * k;
 #pragma unroll
-        for (int m = 0; m < 32; ++m) xr[32 * k + m] = x_s[unit * 32 + m];
+        for (int m = 0; m < 16; ++m)
+            xh[16 * k + m] = f32x2_to_f16x2(x_s[unit * 32 + 2 * m], x_s[unit * 32 + 2 * m + 1]);
     }
 
-    grid_barrier(a.sync, a.sync + 32, err, kSiteTokenLogits, &s_flag);
+    grid_barrier(a.sync, a.sync + 32, gen0, err, kSiteTokenLogits, &s_flag);
 
-    // ---- top-8 (every CTA) ---------------------------------------------------
-    if (warp == 0) {
+    // ---- top-8, in every warp ------------------------------------------------
+    // The CTA reads the logits from L2 once (one request per line), then each
+    // warp selects the same eight experts from shared memory (largest first,
+    // lowest id on ties, -0 == +0) and issues its share of the routed rows'
+    // copies at once.
+    for (int e = threadIdx.x; e < R; e += kTokenThreads) s_logits[e] = __ldcg(a.s.logits + e);
+    __syncthreads();
+    {
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane + 32 * i;
-            v[i] = e < E ? __ldcg(a.s.logits + e) : -FLT_MAX;
+            v[i] = e < E ? s_logits[e] : -FLT_MAX;
         }
-        const float sl = __ldcg(a.s.logits + E);
         unsigned taken = 0;
         float my_v = 0.0f;
         int my_i = 0;
@@ -361,35 +409,62 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
             }
             if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         }
-        const float top0 = __shfl_sync(0xffffffffu, my_v, 0);
-        const float my_e = lane < kTopK ? expf(my_v - top0) : 0.0f;
-        float den = 0.0f;
+        // Routed copies: 8 gate/up (two segments x four arrays) and 16 down
+        // (eight slots x codes/scales), three per warp, lane 0 issuing; the
+        // expert of each comes from the lane that holds its slot.
 #pragma unroll
-        for (int slot = 0; slot < kTopK; ++slot) den += __shfl_sync(0xffffffffu, my_e, slot);
-        // Dispatch order of the eight picks (ids ascending), for the record.
-        int rank_in = 0;
-#pragma unroll
-        for (int slot = 0; slot < kTopK; ++slot) rank_in += __shfl_sync(0xffffffffu, my_i, slot) < my_i;
-        if (lane < kTopK) {
-            const float w = my_e / den;
-            s_ids[lane] = my_i;
-            s_w[lane] = w;
-            if (c == 0) {
-                a.s.ids[lane] = my_i;
-                a.s.weights[lane] = w;
-                a.s.perm[rank_in] = lane;
+        for (int t = 0; t < 3; ++t) {
+            const int j = 3 * warp + t;
+            const int seg = j >> 2;
+            const int v0 = seg == 0 ? u0 : mid, v1 = seg == 0 ? mid : routed_end;
+            const int src = j < 8 ? (v1 > v0 ? (v0 / I) & 7 : 0) : ((j - 8) >> 1) & 7;
+            const int e = __shfl_sync(0xffffffffu, my_i, src);
+            if (lane == 0) {
+                if (j < 8) {
+                    if (have_gu_routed && v1 > v0) copy_gate_up(j & 3, v0, v1, e, &bars[1]);
+                } else if (nh > 0) {
+                    copy_down((j - 8) & 1, (j - 8) >> 1, e, &bars[3]);
+                }
             }
-        } else if (lane == kTopK) {
-            const float w = 1.0f / (1.0f + expf(-sl));
-            s_ids[kTopK] = E;
-            s_w[kTopK] = w;
-            if (c == 0) {
-                a.s.ids[kTopK] = E;
-                a.s.weights[kTopK] = w;
+        }
+        if (warp == 0) {
+            const float sl = s_logits[E];
+            const float top0 = __shfl_sync(0xffffffffu, my_v, 0);
+            const float my_e = lane < kTopK ? expf(my_v - top0) : 0.0f;
+            float den = 0.0f;
+#pragma unroll
+            for (int slot = 0; slot < kTopK; ++slot) den += __shfl_sync(0xffffffffu, my_e, slot);
+            // Dispatch order of the eight picks (ids ascending), for the record.
+            int rank_in = 0;
+#pragma unroll
+            for (int slot = 0; slot < kTopK; ++slot) rank_in += __shfl_sync(0xffffffffu, my_i, slot) < my_i;
+            if (lane < kTopK) {
+                const float w = my_e / den;
+                s_ids[lane] = my_i;
+                s_w[lane] = w;
+                if (c == 0) {
+                    a.s.ids[lane] = my_i;
+                    a.s.weights[lane] = w;
+                    a.s.perm[rank_in] = lane;
+                }
+            } else if (lane == kTopK) {
+                const float w = 1.0f / (1.0f + expf(-sl));
+                s_ids[kTopK] = E;
+                s_w[kTopK] = w;
+                if (c == 0) {
+                    a.s.ids[kTopK] = E;
+                    a.s.weights[kTopK] = w;
+                }
             }
         }
     }
     __syncthreads();
+    if (threadIdx.x < kSlots) {
+        const int e = s_ids[threadIdx.x];
+        s_ginv[threadIdx.x] = __ldg(a.inv_scales + e);
+        s_uinv[threadIdx.x] = __ldg(a.inv_scales + R + e);
+        s_coef[threadIdx.x] = s_w[threadIdx.x] * __ldg(a.inv_scales + 2 * R + e);
+    }
     if (c == 0)
         for (int e = threadIdx.x; e < E; e += kTokenThreads) {
             int n = 0;
@@ -397,40 +472,30 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
             for (int slot = 0; slot < kTopK; ++slot) n += s_ids[slot] == e;
             a.s.counts[e] = n;
         }
-
-    // ---- routed rows: issue every copy at once ---------------------------------
-    if (threadIdx.x == 0) {
-        if (have_gu_routed) {
-            const int end = min(u1, (kSlots - 1) * I);
-            uint32_t bytes = 0;
-            for (int v0 = u0; v0 < end;) {
-                const int v1 = min(end, (v0 / I + 1) * I);
-                bytes += gate_up_bytes(v0, v1);
-                v0 = v1;
-            }
-            mbar_arrive_expect_tx(&bars[1], bytes);
-            for (int v0 = u0; v0 < end;) {
-                const int v1 = min(end, (v0 / I + 1) * I);
-                issue_gate_up(v0, v1, s_ids[v0 / I], &bars[1]);
-                v0 = v1;
-            }
-        }
-        if (nh > 0) {
-            mbar_arrive_expect_tx(&bars[3], down_slot_bytes * kTopK);
-            for (int slot = 0; slot < kTopK; ++slot) issue_down(slot, s_ids[slot], &bars[3]);
-        }
-    }
+    __syncthreads();
 
     // ---- gate/up: shared-expert pairs first (already resident), then routed ----
+    // One rolled loop over the CTA's pairs in that order (pair index t:
+    // t < n_sh the shared pairs from shared_u0, then the routed ones from
+    // u0); the routed copies are waited for when a warp first reaches them.
     bool ok = true;
-    auto gate_up_range = [&](int v0, int v1) {
-        for (int base = v0 + warp * RPW; base < v1; base += kTokenWarps * RPW) {
-            const int v = base + q;
+    {
+        const int n_sh = have_gu_shared ? u1 - shared_u0 : 0;
+        const int n_all = n_sh + (have_gu_routed ? routed_end - u0 : 0);
+        if (have_gu_shared) ok = mbar_wait(&bars[0], 0, err, kSiteTokenGateUp);
+        bool routed_ready = false;
+#pragma unroll 1
+        for (int base = warp * RPW; base < n_all; base += kTokenWarps * RPW) {
+            if (have_gu_routed && base + RPW > n_sh && !routed_ready) {
+                ok = mbar_wait(&bars[1], 0, err, kSiteTokenGateUp) && ok;
+                routed_ready = true;
+            }
+            const int t = base + q;
+            const int v = t < n_sh ? shared_u0 + t : u0 + (t - n_sh);
             float g = 0.0f, u = 0.0f;
-            int slot = 0;
-            if (v < v1) {
+            const int slot = v / I;
+            if (t < n_all && ok) {
                 const int li = v - u0;
-                slot = v / I;
                 const uint8_t *gr = gpk + li * gp_row, *ur = upk + li * gp_row;
                 const uint8_t *gs = gsc + (size_t)li * gpitch, *us = usc + (size_t)li * gpitch;
 #pragma unroll
@@ -440,8 +505,8 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
                     const uint4 uw = *reinterpret_cast<const uint4 *>(ur + unit * 16);
                     const uint16_t gsv = *reinterpret_cast<const uint16_t *>(gs + unit * 2);
                     const uint16_t usv = *reinterpret_cast<const uint16_t *>(us + unit * 2);
-                    g = unit_dot(gw, gsv, xr + 32 * k, g);
-                    u = unit_dot(uw, usv, xr + 32 * k, u);
+                    g = unit_dot_h(gw, gsv, xh + 16 * k, g);
+                    u = unit_dot_h(uw, usv, xh + 16 * k, u);
                 }
             }
 #pragma unroll
@@ -449,32 +514,34 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
                 g += __shfl_xor_sync(0xffffffffu, g, off);
                 u += __shfl_xor_sync(0xffffffffu, u, off);
             }
-            if (v < v1 && lr == 0) {
-                const int e = s_ids[slot];
-                g *= __ldg(a.inv_scales + e);
-                u *= __ldg(a.inv_scales + R + e);
+            if (t < n_all && lr == 0) {
+                g *= s_ginv[slot];
+                u *= s_uinv[slot];
                 a.act[slot * I + v % I] = g / (1.0f + expf(-g)) * u;
             }
         }
-    };
-    if (have_gu_shared) {
-        ok = mbar_wait(&bars[0], 0, err, kSiteTokenGateUp);
-        if (ok) gate_up_range(shared_u0, u1);
-    }
-    if (have_gu_routed) {
-        ok = mbar_wait(&bars[1], 0, err, kSiteTokenGateUp) && ok;
-        if (ok) gate_up_range(u0, min(u1, (kSlots - 1) * I));
+        // A warp with no routed pair of its own still consumes the phase.
+        if (have_gu_routed && !routed_ready) ok = mbar_wait(&bars[1], 0, err, kSiteTokenGateUp) && ok;
     }
 
-    grid_barrier(a.sync + 64, a.sync + 96, err, kSiteTokenAct, &s_flag);
+    grid_barrier(a.sync + 64, a.sync + 96, gen1, err, kSiteTokenAct, &s_flag);
 
-    // ---- down: the act vectors (rotated 16-byte groups, conflict-free) --------
+    // ---- down: the act vectors as f16 (rotated 16-byte groups) -----------------
     {
         const int per_slot = I / 4;  // float4 per slot
         const float4 *src = reinterpret_cast<const float4 *>(a.act);
         for (int idx = threadIdx.x; idx < kSlots * per_slot; idx += kTokenThreads) {
             const int slot = idx / per_slot, f = idx - slot * per_slot, unit = f >> 3, g4 = f & 7;
-            reinterpret_cast<float4 *>(act_s + slot * I + unit * 32)[(g4 + unit) & 7] = __ldcg(src + idx);
+            const float4 t = __ldcg(src + idx);
+            // Unit (32 columns = 64 bytes of f16) holds four 16-byte groups;
+            // group g = float4 pair (2g, 2g+1), stored at position
+            // (g + unit / 2) & 3, so the 16-byte loads of eight consecutive
+            // units hit eight distinct bank groups.
+            uint2 hv;
+            hv.x = f32x2_to_f16x2(t.x, t.y);
+            hv.y = f32x2_to_f16x2(t.z, t.w);
+            uint8_t *dst = reinterpret_cast<uint8_t *>(act_s + slot * I + unit * 32);
+            *reinterpret_cast<uint2 *>(dst + (((g4 >> 1) + (unit >> 1)) & 3) * 16 + (g4 & 1) * 8) = hv;
         }
     }
     __syncthreads();
@@ -484,41 +551,49 @@ __global__ void __launch_bounds__(kTokenThreads, 1) moe_token_kernel(TokenArgs a
     }
     if (ok && nh > 0) {
         // Rows d = slot * nh + (h - h0), slot-major; each warp a contiguous
-        // range, LD lanes per row (one 16-byte unit each), RPD rows per pass.
+        // range, LD lanes per row (one 16-byte unit each), two rows per lane
+        // at a time (RPD rows per half-pass).
         const int LD = I / 32 < 32 ? I / 32 : 32, RPD = 32 / LD, qd = lane / LD, ld = lane % LD;
         const int D = kSlots * nh;
         const int d0 = D * warp / kTokenWarps, d1 = D * (warp + 1) / kTokenWarps;
-        float av[32];
-        int cur = -1;
-        for (int base = d0; base < d1; base += RPD) {
-            const int d = base + qd;
-            const int slot = d < d1 ? d / nh : cur;
-            float acc = 0.0f;
-            if (d < d1) {
-                if (slot != cur) {
-                    const float *src = act_s + slot * I + ld * 32;
+#pragma unroll 1
+        for (int base = d0; base < d1; base += 2 * RPD) {
+            float acc[2] = {0.0f, 0.0f};
+            int dd[2], slots[2];
 #pragma unroll
-                    for (int g4 = 0; g4 < 8; ++g4) {
-                        const float4 t = reinterpret_cast<const float4 *>(src)[(g4 + ld) & 7];
-                        av[4 * g4] = t.x;
-                        av[4 * g4 + 1] = t.y;
-                        av[4 * g4 + 2] = t.z;
-                        av[4 * g4 + 3] = t.w;
-                    }
-                    cur = slot;
-                }
-                const int hl = d - slot * nh;
-                const uint8_t *pr = dpk + ((size_t)slot * L.NH + hl) * dp_row;
-                const uint8_t *sr = dsc + ((size_t)slot * L.NH + hl) * dpitch;
-                acc = unit_dot(*reinterpret_cast<const uint4 *>(pr + ld * 16),
-                               *reinterpret_cast<const uint16_t *>(sr + ld * 2), av, 0.0f);
+            for (int r = 0; r < 2; ++r) {
+                dd[r] = base + qd + r * RPD;
+                slots[r] = dd[r] < d1 ? dd[r] / nh : 0;
             }
 #pragma unroll
-            for (int off = LD / 2; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-            if (d < d1 && ld == 0) {
-                const int e = s_ids[slot];
-                const float coef = s_w[slot] * __ldg(a.inv_scales + 2 * R + e);
-                y_s[slot * L.NH + (d - slot * nh)] = coef * acc;
+            for (int r = 0; r < 2; ++r) {
+                if (dd[r] < d1) {
+                    const int hl = dd[r] - slots[r] * nh;
+                    const uint8_t *ar = reinterpret_cast<const uint8_t *>(act_s + slots[r] * I + ld * 32);
+                    uint32_t av[16];
+#pragma unroll
+                    for (int g = 0; g < 4; ++g) {
+                        const uint4 t = *reinterpret_cast<const uint4 *>(ar + ((g + (ld >> 1)) & 3) * 16);
+                        av[4 * g] = t.x;
+                        av[4 * g + 1] = t.y;
+                        av[4 * g + 2] = t.z;
+                        av[4 * g + 3] = t.w;
+                    }
+                    const uint8_t *pr = dpk + ((size_t)slots[r] * L.NH + hl) * dp_row;
+                    const uint8_t *sr = dsc + ((size_t)slots[r] * L.NH + hl) * dpitch;
+                    acc[r] = unit_dot_h(*reinterpret_cast<const uint4 *>(pr + ld * 16),
+                                        *reinterpret_cast<const uint16_t *>(sr + ld * 2), av, 0.0f);
+                }
+            }
+#pragma unroll
+            for (int off = LD / 2; off >= 1; off >>= 1) {
+                acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], off);
+                acc[1] += __shfl_xor_sync(0xffffffffu, acc[1], off);
+            }
+            if (ld == 0) {
+#pragma unroll
+                for (int r = 0; r < 2; ++r)
+                    if (dd[r] < d1) y_s[slots[r] * L.NH + (dd[r] - slots[r] * nh)] = s_coef[slots[r]] * acc[r];
             }
         }
     }
@@ -591,6 +666,8 @@ size_t token_smem_bytes(int sms, int H, int I, int gate_pitch, int down_pitch) {
 
 bool token_supported(int sms, int E, int H, int I, int gate_pitch, int down_pitch) {
     if (sms < 1 || E < kTopK || E > 256) return false;
+    // A CTA's gate/up pairs span at most two slots.
+    if ((kSlots * I + sms - 1) / sms > I) return false;
     if (H % 256 != 0 || H > 2048 || I % 128 != 0 || I > 1024) return false;
     // Every warp of the grid routes at most one router row.
     if ((long long)sms * kTokenWarps < E + 1) return false;
