@@ -72,7 +72,7 @@ def parse_args():
     p.add_argument("--no-prefill", action="store_true", help="skip the prefill legs (configs 2 and 3)")
     p.add_argument("--no-stack", action="store_true", help="skip the 40-layer stack leg (config 4)")
     p.add_argument("--no-linear", action="store_true", help="skip the dense NVFP4 linear leg (LM-head shape)")
-    p.add_argument("--decode-kernels", choices=["tensor_core", "in_register"], default="tensor_core",
+    p.add_argument("--decode-kernels", choices=["tensor_core", "in_register", "fused_token"], default="tensor_core",
                    help="decode expert GEMVs (the library's default is tensor_core)")
     return p.parse_args()
 
@@ -304,7 +304,7 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     }
 
 
-def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40) -> dict:
+def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40, decode_kernels: str = "tensor_core") -> dict:
     """the resident decode stack of ``layers`` independently
     seeded layers (h <- h + MoE(RMSNorm(h)), attention omitted, the RMSNorm
     fused into each layer's forward), all banks in HBM, one CUDA graph per
@@ -321,6 +321,8 @@ def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40) -> dict:
     from vllm_nvfp4_cuda.stack import MoeStack
 
     banks = [synthetic.build_bank(rt, E, H, I, seed, layer=101 + layer)[0] for layer in range(layers)]
+    for b in banks:
+        b.set_decode_kernels(decode_kernels)
     stack = MoeStack(rt, banks)
     stream = torch.cuda.Stream()
     peak = measured_peaks().get("hbm_gbs")
@@ -760,7 +762,7 @@ def run_ours(args) -> int:
     if world == 1 and not args.no_stack:
         # The headline line is printed whatever happens to this optional leg.
         try:
-            stack = stack_leg(rt, args.seed, 30, 3)
+            stack = stack_leg(rt, args.seed, 30, 3, decode_kernels=args.decode_kernels)
         except Exception as error:  # noqa: BLE001
             stack = {"workload": "config4_stack40", "error": f"{type(error).__name__}: {error}"}
 

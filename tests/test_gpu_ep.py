@@ -100,10 +100,7 @@ def test_forward_needs_owned_projections_only(cuda_runtime, ep_host, ep_banks):
 def test_fused_combine_single_rank_matches_forward(cuda_runtime, ep_host, ep_banks):
     """A one-rank context runs the fused combine without peers: the output must
     equal the plain forward bit for bit (same additions in the same order),
-    over several calls (both buffer parities) and both decode variants. A
-    one-token plain forward of a full bank runs the one-token kernel, which
-    expert-parallel calls do not use, so at one token the plain forward is
-    taken with the in-register kernels the expert-parallel call runs."""
+    over several calls (both buffer parities) and both decode variants."""
     import torch
 
     from vllm_nvfp4_cuda.runtime import EpContext
@@ -115,12 +112,7 @@ def test_fused_combine_single_rank_matches_forward(cuda_runtime, ep_host, ep_ban
         for T in (1, 16, 32, 64, 16):
             x = bits_to_bf16_tensor(synthetic_np.tokens_bf16(T, H, 1200 + T))
             r = bits_to_bf16_tensor(synthetic_np.tokens_bf16(T, H, 1300 + T))
-            if T == 1:
-                full.set_decode_kernels("in_register")
-            try:
-                ref = full.forward(x, residual=r)
-            finally:
-                full.set_decode_kernels("tensor_core")
+            ref = full.forward(x, residual=r)
             got = full.forward_ep(ep, x, residual=r)
             torch.cuda.synchronize()
             cuda_runtime.synchronize()

@@ -245,9 +245,9 @@ def test_trace_profile_and_errors(cuda_runtime, small_bank, small_host):
     H = small_host.hidden
     x = rt.upload_buffer(np.zeros(H, dtype=np.float32))
     out = rt.create_buffer(H * 4)
-    # One token on a full bank: the one-token kernel; the in-register
-    # variant: routing, gate/up and down (the down kernel combines).
-    for kernels, ops in (("tensor_core", ["moe_token"]), ("in_register", ["moe_route", "moe_gate_up", "moe_down"])):
+    # One token: routing, gate/up and down (the down kernel combines); with
+    # the fused one-token kernel selected, that one kernel.
+    for kernels, ops in (("tensor_core", ["moe_route", "moe_gate_up", "moe_down"]), ("fused_token", ["moe_token"])):
         small_bank.set_decode_kernels(kernels)
         rt.set_trace_enabled(True)
         rt.set_trace_scope("moe.layer.00.experts")

@@ -91,7 +91,6 @@ def test_fused_norm_matches_separate_norm(cuda_runtime, stack, stack_hosts, T):
 
 @pytest.mark.parametrize("T", [1, 2])
 def test_stack_graph_replay(cuda_runtime, stack, T):
-    """T = 1 captures the one-token kernel (a cooperative launch) in the graph."""
     import torch
 
     g = stack.capture(T)

@@ -24,8 +24,9 @@ approximate logits of the prefill path may hold -0, which its candidate
 selection treats as +0.
 
 Ids, counts and the dispatch permutation are compared bit-exactly with the
-oracle, through both decode variants (T 1, 4, 32) and the prefill path
-(T 65, 200); outputs within the BASELINE bound.
+oracle, through every decode variant (T 1, 4, 32; the fused one-token
+kernel at T 1) and the prefill path (T 65, 200); outputs within the
+BASELINE bound.
 """
 
 from __future__ import annotations
@@ -133,7 +134,7 @@ def _assert_ties_present(ref, experts):
     assert whole >= (len(ids) - 2) // 3, whole
 
 
-@pytest.mark.parametrize("kernels", ["tensor_core", "in_register"])
+@pytest.mark.parametrize("kernels", ["tensor_core", "in_register", "fused_token"])
 @pytest.mark.parametrize("T", [1, 4, 32])
 def test_decode_ties(cuda_runtime, tie_bank64, tie_host64, kernels, T):
     tie_bank64.set_decode_kernels(kernels)

@@ -2,8 +2,8 @@
 persistent grid) against the oracle, through the C ABI (needs an sm_100a
 GPU).
 
-One-token calls of a bank computing every expert run this kernel by default.
-For each shape it serves (H a multiple of 256 up to 2048, I a multiple of
+One-token calls of a bank computing every expert run this kernel when the
+bank's decode kernels are "fused_token" (opt-in). For each shape it serves (H a multiple of 256 up to 2048, I a multiple of
 128 up to 1024):
 
 * router logits equal the oracle's bit for bit (same FP32 order), ids,
@@ -14,7 +14,9 @@ For each shape it serves (H a multiple of 256 up to 2048, I a multiple of
 * it agrees with the three-launch in-register path on the same token within
   the same bound;
 * the lab's FP32 entry point (nvfp4_moe_bank_decode_device_enqueue_f32) and
-  a skewed router bias take the same kernel.
+  a skewed router bias take the same kernel;
+* captured in a CUDA graph (a cooperative kernel node), replays give the
+  eager call's bits.
 """
 
 from __future__ import annotations
@@ -58,6 +60,7 @@ def _check(bank, host, T, seed, residual):
 def test_token_kernel_shapes(cuda_runtime, E, H, I, skew):
     host = synthetic_np.make_bank(E, H, I, 400 + E + H + I, skew=skew)
     bank = upload_bank(cuda_runtime, host)
+    bank.set_decode_kernels("fused_token")
     try:
         for call in range(3):
             _check(bank, host, 1, 50 + call, residual=call != 1)
@@ -67,7 +70,7 @@ def test_token_kernel_shapes(cuda_runtime, E, H, I, skew):
         try:
             other, _ = _check(bank, host, 1, 60, residual=False)
         finally:
-            bank.set_decode_kernels("tensor_core")
+            bank.set_decode_kernels("fused_token")
         assert rel_rmse(got, other) <= 2 * REL_RMSE_TOL
     finally:
         bank.close()
@@ -76,6 +79,7 @@ def test_token_kernel_shapes(cuda_runtime, E, H, I, skew):
 def test_token_kernel_reference_f32_abi(cuda_runtime):
     host = synthetic_np.make_bank(64, 1024, 256, 77)
     bank = upload_bank(cuda_runtime, host)
+    bank.set_decode_kernels("fused_token")
     rt = cuda_runtime
     try:
         for seed in (3, 4):
@@ -106,6 +110,7 @@ def test_token_kernel_full_size_many_calls(cuda_runtime):
 
     E, H, I, seed = 256, 2048, 512, 3
     bank, meta = synthetic.build_bank(cuda_runtime, E, H, I, seed)
+    bank.set_decode_kernels("fused_token")
     host = BankHost(E, H, I, meta.router_bf16.numpy().view(np.uint16), meta.shared_gate_bf16.numpy().view(np.uint16))
     try:
         for call in range(20):
@@ -127,5 +132,39 @@ def test_token_kernel_full_size_many_calls(cuda_runtime):
             got = bf16_tensor_to_f32(out)
             assert rel_rmse(got, ref.out) <= REL_RMSE_TOL, call
             assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL, call
+    finally:
+        bank.close()
+
+
+def test_token_kernel_in_cuda_graph(cuda_runtime):
+    """The one-token kernel captured in a CUDA graph (a cooperative kernel
+    node) replays to the eager call's bits, call after call."""
+    import torch
+
+    host = synthetic_np.make_bank(32, 512, 256, 88)
+    bank = upload_bank(cuda_runtime, host)
+    bank.set_decode_kernels("fused_token")
+    try:
+        xin = torch.empty(1, host.hidden, dtype=torch.bfloat16, device="cuda")
+        res = bits_to_bf16_tensor(synthetic_np.tokens_bf16(1, host.hidden, 5))
+        out = torch.empty_like(xin)
+        stream = torch.cuda.Stream()
+        stream.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(stream):
+            bank.forward(xin, residual=res, out=out, stream=stream)  # eager warm-up outside the capture
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            bank.forward(xin, residual=res, out=out, stream=stream)
+        for seed in (6, 7, 8):
+            xbits = synthetic_np.tokens_bf16(1, host.hidden, seed)
+            xin.copy_(bits_to_bf16_tensor(xbits))
+            graph.replay()
+            torch.cuda.synchronize()
+            replayed = out.clone()
+            eager = bank.forward(xin, residual=res)
+            torch.cuda.synchronize()
+            assert torch.equal(replayed, eager), seed
+        del graph
     finally:
         bank.close()

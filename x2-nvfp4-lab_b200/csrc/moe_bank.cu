@@ -52,8 +52,9 @@ struct nvfp4_moe_bank {
     int terms_x = 4, terms_act = 3;
     int scratch_terms_x = 0, scratch_terms_act = 0;
     // Decode expert-GEMV variant: NVFP4_DECODE_KERNELS_TENSOR_CORE (calls of
-    // up to kDecodeTcMaxTokens tokens on shapes with prefill kernels) or
-    // NVFP4_DECODE_KERNELS_IN_REGISTER.
+    // up to kDecodeTcMaxTokens tokens on shapes with prefill kernels),
+    // NVFP4_DECODE_KERNELS_IN_REGISTER, or NVFP4_DECODE_KERNELS_FUSED_TOKEN
+    // (tensor-core, and one-token calls as one persistent kernel).
     int decode_kernels = NVFP4_DECODE_KERNELS_TENSOR_CORE;
     // Expert parallelism: routed experts [e_first, e_first + e_count) and the
     // shared expert (when shared_here) are computed by this bank.
@@ -156,15 +157,14 @@ nvfp4_status check_upload_args(const nvfp4_moe_bank *bank, int expert, int proje
 constexpr int kDecodeTcMinTokens = 4;
 
 bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
-    return bank->decode_kernels == NVFP4_DECODE_KERNELS_TENSOR_CORE && bank->tc_ready &&
+    return bank->decode_kernels != NVFP4_DECODE_KERNELS_IN_REGISTER && bank->tc_ready &&
            tokens >= kDecodeTcMinTokens && tokens <= kDecodeTcMaxTokens;
 }
 
 // One-token calls of a bank that computes every expert run as one persistent
-// kernel (moe_token.cu) under the default decode kernels; the in-register
-// variant keeps the three-launch path for every size.
+// kernel (moe_token.cu) when the bank's decode kernels are FUSED_TOKEN.
 bool use_token_kernel(const nvfp4_moe_bank *bank, int tokens, const EpArgs *ep) {
-    return tokens == 1 && !ep && bank->token_sync && bank->decode_kernels == NVFP4_DECODE_KERNELS_TENSOR_CORE &&
+    return tokens == 1 && !ep && bank->token_sync && bank->decode_kernels == NVFP4_DECODE_KERNELS_FUSED_TOKEN &&
            bank->e_first == 0 && bank->e_count == bank->experts && bank->shared_here &&
            token_supported(bank->runtime->sm_count, bank->experts, bank->hidden, bank->intermediate,
                            static_cast<int>(bank->scale_pitch(0)), static_cast<int>(bank->scale_pitch(2)));
@@ -919,8 +919,9 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_expert_range(nvfp4_moe_bank
 
 extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_set_decode_kernels(nvfp4_moe_bank *bank, int kernels) {
     if (!bank || !bank->runtime ||
-        (kernels != NVFP4_DECODE_KERNELS_TENSOR_CORE && kernels != NVFP4_DECODE_KERNELS_IN_REGISTER))
-        return fail_invalid("decode kernels must be NVFP4_DECODE_KERNELS_TENSOR_CORE or _IN_REGISTER");
+        (kernels != NVFP4_DECODE_KERNELS_TENSOR_CORE && kernels != NVFP4_DECODE_KERNELS_IN_REGISTER &&
+         kernels != NVFP4_DECODE_KERNELS_FUSED_TOKEN))
+        return fail_invalid("decode kernels must be NVFP4_DECODE_KERNELS_TENSOR_CORE, _IN_REGISTER or _FUSED_TOKEN");
     std::lock_guard<std::mutex> lock(bank->runtime->queue_mutex);
     bank->decode_kernels = kernels;
     clear_last_error();

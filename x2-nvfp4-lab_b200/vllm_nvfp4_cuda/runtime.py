@@ -28,6 +28,7 @@ NVFP4_MOE_PARTIAL_F32 = 2
 NVFP4_MOE_PRE_NORM = 4
 NVFP4_DECODE_KERNELS_TENSOR_CORE = 0
 NVFP4_DECODE_KERNELS_IN_REGISTER = 1
+NVFP4_DECODE_KERNELS_FUSED_TOKEN = 2
 
 
 class Profile(C.Structure):
@@ -622,8 +623,10 @@ class MoeBank:
                             "nvfp4_moe_bank_set_pre_norm")
 
     def set_decode_kernels(self, kernels: str) -> None:
-        """additive: decode expert-GEMV variant, "tensor_core" (default) or "in_register"."""
-        code = {"tensor_core": NVFP4_DECODE_KERNELS_TENSOR_CORE, "in_register": NVFP4_DECODE_KERNELS_IN_REGISTER}
+        """additive: decode expert-GEMV variant, "tensor_core" (default), "in_register" or
+        "fused_token" (tensor-core, one-token calls as one persistent kernel)."""
+        code = {"tensor_core": NVFP4_DECODE_KERNELS_TENSOR_CORE, "in_register": NVFP4_DECODE_KERNELS_IN_REGISTER,
+                "fused_token": NVFP4_DECODE_KERNELS_FUSED_TOKEN}
         if kernels not in code:
             raise ValueError(f"unknown decode kernels {kernels!r}")
         self.runtime._check(self.runtime.lib.nvfp4_moe_bank_set_decode_kernels(self.handle, code[kernels]),
