@@ -660,7 +660,7 @@ def run_ours(args) -> int:
     achieved = gu_bytes / (gu_ms / 1000.0) / 1e9 if gu_ms > 0 else None
     traffic_path = ROOT / "profiles" / "traffic.json"
     traffic = None
-    if traffic_path.exists():
+    if traffic_path.exists() and world == 1:
         traffic = json.loads(traffic_path.read_text()).get(f"moe_gate_up_T{T}")
     layer_bytes = sum(step_bytes[i % pool_n] for i in range(args.steps))
 
@@ -792,7 +792,7 @@ def run_ours(args) -> int:
             "config": {
                 "workload": WORKLOAD,
                 "tokens_per_step": T,
-                "global_batch": T * world,
+                "global_batch": T,
                 "experts": E,
                 "hidden": H,
                 "intermediate": I,
@@ -803,7 +803,7 @@ def run_ours(args) -> int:
                                 "the 32 tokens replicated, combine fused with the cross-rank reduction over "
                                 "NVLink peer memory" if world > 1 else "single GPU"),
                 "l2": "flushed before every step (256 MiB write) outside the per-step CUDA events",
-                "inputs": f"pool of {pool_n} distinct token batches per rank",
+                "inputs": f"pool of {pool_n} distinct token batches (the same on every rank)",
                 "mean_unique_routed_experts": round(float(np.mean(uniq)), 2),
             },
             "us_per_token": round(1e6 / value, 4),

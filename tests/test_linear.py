@@ -217,6 +217,32 @@ def test_linear_matches_oracle(cuda_runtime, rows, cols, vectors):
 
 
 @pytest.mark.gpu
+def test_linear_activation_range(cuda_runtime):
+    """The kernel carries each FP32 activation as two FP16 halves after a
+    per-vector power-of-two scale: vectors far above and below FP16 range,
+    one mixing a few large entries with ordinary ones, and a zero vector all
+    meet the lab's gate, each relative to its own output scale."""
+    rows, cols = 200, 1024
+    packed, scales = _matrix(rows, cols, 41)
+    x = np.random.default_rng(42).standard_normal((5, cols)).astype(np.float32)
+    x[0] *= np.float32(1e6)
+    x[1] *= np.float32(1e-30)
+    x[2, :10] *= np.float32(1e5)
+    x[3] = 0.0
+    x[4] *= np.float32(3e-5)  # below FP16's smallest normal before scaling
+    m = cuda_runtime.upload(packed, scales, 2.0)
+    try:
+        got = cuda_runtime.linear(m, x)
+        ref = _oracle(packed, scales, x, 2.0)
+        for v in range(x.shape[0]):
+            scale = float(np.max(np.abs(ref[v])))
+            np.testing.assert_allclose(got[v], ref[v], rtol=GATE, atol=GATE * scale, err_msg=f"vector {v}")
+        assert not np.any(got[3])
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
 def test_linear_scale_bytes_follow_the_lab_rule(cuda_runtime):
     packed, scales = _matrix(300, 512, 11, full_scale_bytes=True)
     scales[:, 0] = 0x7F

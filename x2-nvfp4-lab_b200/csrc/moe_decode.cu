@@ -388,56 +388,68 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
             s.logits[(size_t)t0 * R + row] = v;
         }
     } else if (row < R) {
+        // Several tokens: one FP32 chain per token in the fixed order above.
+        // The loop body has no branches (missing tokens of a short block read
+        // the block's last token and are not stored), so the four chains
+        // interleave; the format branch sits outside the loop.
         float acc[kRouteTokens];
 #pragma unroll
         for (int j = 0; j < kRouteTokens; ++j) acc[j] = 0.0f;
         const uint16_t *wr = route_w + (size_t)warp * H;
-#pragma unroll 1
-        for (int q = 0; q < chunks; ++q) {
-            const int k = q * 128 + lane * 4;
-            const uint2 wv = *reinterpret_cast<const uint2 *>(wr + k);
-            const float w0 = bf16_bits_to_f32(wv.x & 0xFFFFu), w1 = bf16_bits_to_f32(wv.x >> 16);
-            const float w2 = bf16_bits_to_f32(wv.y & 0xFFFFu), w3 = bf16_bits_to_f32(wv.y >> 16);
+        int xoff[kRouteTokens];
 #pragma unroll
-            for (int j = 0; j < kRouteTokens; ++j) {
-                if (j < tt) {
-                    float4 xv;
-                    if (a.x_is_f32) {
-                        xv = *reinterpret_cast<const float4 *>(route_xs + ((size_t)j * H + k) * 4);
-                    } else {
-                        const uint2 b = *reinterpret_cast<const uint2 *>(route_xs + ((size_t)j * H + k) * 2);
-                        xv = make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
-                                         bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
-                    }
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w0, xv.x));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w1, xv.y));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w2, xv.z));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w3, xv.w));
+        for (int j = 0; j < kRouteTokens; ++j) xoff[j] = (j < tt ? j : tt - 1) * H;
+        auto dots = [&](auto load_x) {
+#pragma unroll 4
+            for (int q = 0; q < chunks; ++q) {
+                const int k = q * 128 + lane * 4;
+                const uint2 wv = *reinterpret_cast<const uint2 *>(wr + k);
+                const float w0 = bf16_bits_to_f32(wv.x & 0xFFFFu), w1 = bf16_bits_to_f32(wv.x >> 16);
+                const float w2 = bf16_bits_to_f32(wv.y & 0xFFFFu), w3 = bf16_bits_to_f32(wv.y >> 16);
+                float4 xv[kRouteTokens];
+#pragma unroll
+                for (int j = 0; j < kRouteTokens; ++j) xv[j] = load_x(xoff[j] + k);
+#pragma unroll
+                for (int j = 0; j < kRouteTokens; ++j) {
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w0, xv[j].x));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w1, xv[j].y));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w2, xv[j].z));
+                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w3, xv[j].w));
                 }
             }
+        };
+        if (a.x_is_f32) {
+            dots([&](int idx) { return *reinterpret_cast<const float4 *>(route_xs + (size_t)idx * 4); });
+        } else {
+            dots([&](int idx) {
+                const uint2 b = *reinterpret_cast<const uint2 *>(route_xs + (size_t)idx * 2);
+                return make_float4(bf16_bits_to_f32(b.x & 0xFFFFu), bf16_bits_to_f32(b.x >> 16),
+                                   bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
+            });
         }
 #pragma unroll
         for (int j = 0; j < kRouteTokens; ++j) {
-            if (j < tt) {
-                float v = acc[j];
+            float v = acc[j];
 #pragma unroll
-                for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
-                if (lane == 0) {
-                    if (a.bias && row < a.E) v = __fadd_rn(v, bias);
-                    s.logits[(size_t)(t0 + j) * R + row] = v;
-                }
+            for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+            if (lane == 0 && j < tt) {
+                if (a.bias && row < a.E) v = __fadd_rn(v, bias);
+                s.logits[(size_t)(t0 + j) * R + row] = v;
             }
         }
     }
 
-    // Tensor-core variant: row block b < tt also writes token t0 + b as four
-    // NVFP4 terms (B rows 4t + j, scale atoms, global scale), one 16-element
-    // block per thread, from the shared-memory copy of x.
-    if (a.quantize_x && (int)blockIdx.x < tt) {
-        const int jt = blockIdx.x;
-        const int t = t0 + jt;
+    // Tensor-core variant: the block's tokens are also written as four NVFP4
+    // terms (B rows 4t + j, scale atoms, global scale). The (token, 16-element
+    // block) pairs of the token block are spread over all its CTAs, one pair
+    // per thread; a CTA first reduces the amax of each token it touches (from
+    // its shared-memory copy) so every CTA derives the same global scale.
+    if (a.quantize_x) {
         const int nb = H / 16;
-        auto load_block = [&](int b, float (&v)[16]) {
+        const int total = tt * nb;
+        const int p0 = (int)((long long)total * blockIdx.x / gridDim.x);
+        const int p1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+        auto load_block = [&](int jt, int b, float (&v)[16]) {
             if (a.x_is_f32) {
                 const float4 *p = reinterpret_cast<const float4 *>(route_xs + ((size_t)jt * H + 16 * b) * 4);
 #pragma unroll
@@ -462,24 +474,35 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
                 }
             }
         };
-        float amax = 0.0f;
-        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
-            float v[16];
-            load_block(b, v);
+        __shared__ float s_gq[kRouteTokens];
+        __shared__ float s_amax[kRouteTokens][kRouteRowsPerCta];
+        const int jt0 = p1 > p0 ? p0 / nb : 0, jt1 = p1 > p0 ? (p1 - 1) / nb : -1;
+#pragma unroll 1
+        for (int jt = jt0; jt <= jt1; ++jt) {
+            float amax = 0.0f;
+            for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+                float v[16];
+                load_block(jt, b, v);
 #pragma unroll
-            for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+                for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+            }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+            if (lane == 0) s_amax[jt][warp] = amax;
         }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-        __shared__ float s_amax[kRouteRowsPerCta];
-        if (lane == 0) s_amax[warp] = amax;
         __syncthreads();
-        amax = fmaxf(fmaxf(s_amax[0], s_amax[1]), fmaxf(s_amax[2], s_amax[3]));
-        const float g = row_global_scale(amax);
-        if (threadIdx.x == 0) s.gx_tc[t] = g;
-        for (int b = threadIdx.x; b < nb; b += blockDim.x) {
+        if (threadIdx.x < kRouteTokens && (int)threadIdx.x >= jt0 && (int)threadIdx.x <= jt1) {
+            const float (&m)[kRouteRowsPerCta] = s_amax[threadIdx.x];
+            s_gq[threadIdx.x] = row_global_scale(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])));
+        }
+        __syncthreads();
+        for (int pidx = p0 + threadIdx.x; pidx < p1; pidx += blockDim.x) {
+            const int jt = pidx / nb, b = pidx - jt * nb;
+            const int t = t0 + jt;
+            const float g = s_gq[jt];
+            if (b == 0) s.gx_tc[t] = g;
             float v[16];
-            load_block(b, v);
+            load_block(jt, b, v);
 #pragma unroll 1
             for (int j = 0; j < kDecodeTcTerms; ++j) {
                 uint32_t c0, c1;
