@@ -129,9 +129,11 @@ def _emulate_kernel(packed, scales, x, divisor, grid, V=4):
     """The launch plan of nvfp4_linear_kernel<V> (csrc/linear.cu) run on the CPU:
     the upload's pitches and scale sanitising, the rotated shared-memory slots
     of the activations (every slot written once, nothing read unwritten), each
-    lane's chunks of each warp's two rows (16-byte packed words, two scale
-    bytes, low nibble = even column), and the row loop over the grid (every
-    output written once)."""
+    lane's chunks of each warp's four rows, two chunks per lane loaded
+    together (16-byte packed words, two scale bytes, low nibble = even
+    column; a chunk past the row re-reads the last one and is skipped), and
+    the row loop over the grid (every output written once)."""
+    RPW, CIF = 4, 2  # rows per warp, chunks in flight per lane (csrc/linear.cu)
     rows, half = packed.shape; cols = half * 2
     pp = (half + 15) // 16 * 16; sp = (cols // 16 + 15) // 16 * 16
     P = np.zeros((rows, pp), np.uint8); P[:, :half] = packed
@@ -149,12 +151,18 @@ def _emulate_kernel(packed, scales, x, divisor, grid, V=4):
             xs[idx] = x[gv, col] if (gv < vectors and col < cols) else 0.0
         for b in range(grid):
             for w in range(8):
-                r0 = (b * 8 + w) * 2
+                r0 = (b * 8 + w) * RPW
                 while r0 < rows:
-                    acc = np.zeros((2, V, 32), np.float32)
+                    acc = np.zeros((RPW, V, 32), np.float32)
                     for lane in range(32):
-                        for c in range(lane, chunks, 32):
-                            for j in range(2):
+                        loaded = [min(cb + 32 * u, chunks - 1) for cb in range(lane, chunks, 32 * CIF)
+                                  for u in range(CIF)]
+                        used = [cb + 32 * u for cb in range(lane, chunks, 32 * CIF) for u in range(CIF)
+                                if cb + 32 * u < chunks]
+                        assert all(0 <= c < chunks for c in loaded)
+                        assert used == list(range(lane, chunks, 32))
+                        for c in used:
+                            for j in range(RPW):
                                 r = min(r0 + j, rows - 1)
                                 q = P[r, c * 16:c * 16 + 16]
                                 sc = _decode_e4m3_scale(S[r, c * 2:c * 2 + 2])
@@ -169,12 +177,12 @@ def _emulate_kernel(packed, scales, x, divisor, grid, V=4):
                                     for v in range(V):
                                         xv = np.array([xs[xs_index(v, col + t)] for t in range(8)], np.float32)
                                         acc[j, v, lane] += np.float32(np.dot(wv.astype(np.float64), xv.astype(np.float64)))
-                    for j in range(2):
+                    for j in range(RPW):
                         for v in range(V):
                             r, gv = r0 + j, v0 + v
                             if r < rows and gv < vectors:
                                 assert np.isnan(dst[gv, r]); dst[gv, r] = acc[j, v].sum() / np.float32(divisor)
-                    r0 += grid * 8 * 2
+                    r0 += grid * 8 * RPW
     return dst
 
 

@@ -13,9 +13,11 @@
 // row, scale bytes sanitised at upload like the bank's (sign cleared, 0x7F ->
 // 0: the lab's decoding rule, nvfp4_gemv.cl:14-27).
 //
-// Kernel: a weight stream bound by HBM for a few vectors. Each warp owns two
-// rows at a time; lane l takes the 32-column chunks l, l+32, ... of both rows
-// (one 16-byte packed load and one 2-byte scale load per chunk and row). The
+// Kernel: a weight stream bound by HBM for a few vectors. Each warp owns four
+// rows at a time; lane l takes the 32-column chunks l, l+32, ... of the rows
+// (one 16-byte packed load and one 2-byte scale load per chunk and row), two
+// chunks of every row loaded before any arithmetic so that eight 16-byte
+// loads per lane are in flight. The
 // E2M1 codes and the E4M3 scales convert exactly to FP16, their product is
 // exact in FP16 (at most five significant bits, magnitude in [2^-10, 2688]),
 // and each product multiplies the FP32 activation in an FP32 FMA; the lanes'
@@ -58,7 +60,8 @@ namespace {
 
 constexpr int kLinThreads = 256;
 constexpr int kLinWarps = kLinThreads / 32;
-constexpr int kLinRowsPerWarp = 2;
+constexpr int kLinRowsPerWarp = 4;
+constexpr int kLinChunksInFlight = 2;  // 32-column chunks per lane loaded before any math
 constexpr int kLinMaxCols = 49152;
 constexpr size_t kLinSmemBudget = 200 * 1024;  // activation bytes of one pass
 
@@ -110,16 +113,32 @@ __global__ void __launch_bounds__(kLinThreads) nvfp4_linear_kernel(LinearArgs a)
 #pragma unroll
             for (int v = 0; v < V; ++v) acc[j][v] = 0.0f;
 
-        for (int c = lane; c < a.chunks; c += 32) {
-            uint4 q[kLinRowsPerWarp];
+        for (int cb = lane; cb < a.chunks; cb += 32 * kLinChunksInFlight) {
+            // Every load of the row group's chunks is issued before any math
+            // (kLinRowsPerWarp x kLinChunksInFlight 16-byte loads per lane in
+            // flight); chunks past the row re-read the row's last chunk and
+            // are not added.
+            uint4 qq[kLinChunksInFlight][kLinRowsPerWarp];
+            uint16_t ss[kLinChunksInFlight][kLinRowsPerWarp];
+#pragma unroll
+            for (int u = 0; u < kLinChunksInFlight; ++u) {
+                const size_t cc = static_cast<size_t>(min(cb + 32 * u, a.chunks - 1));
+#pragma unroll
+                for (int j = 0; j < kLinRowsPerWarp; ++j) {
+                    // A missing row re-reads the last row; its sum is not stored.
+                    const size_t r = static_cast<size_t>(min(r0 + j, a.rows - 1));
+                    qq[u][j] = ldg_stream128(a.packed + r * a.packed_pitch + cc * 16);
+                    ss[u][j] = ldg_u16(a.scales + r * a.scale_pitch + cc * 2);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kLinChunksInFlight; ++u) {
+            const int c = cb + 32 * u;
+            if (c >= a.chunks) break;
+            const uint4 *q = qq[u];
             uint32_t sc[kLinRowsPerWarp];
 #pragma unroll
-            for (int j = 0; j < kLinRowsPerWarp; ++j) {
-                // A missing second row re-reads the last row; its sum is not stored.
-                const size_t r = static_cast<size_t>(min(r0 + j, a.rows - 1));
-                q[j] = ldg_stream128(a.packed + r * a.packed_pitch + static_cast<size_t>(c) * 16);
-                sc[j] = e4m3x2_to_f16x2(ldg_u16(a.scales + r * a.scale_pitch + static_cast<size_t>(c) * 2));
-            }
+            for (int j = 0; j < kLinRowsPerWarp; ++j) sc[j] = e4m3x2_to_f16x2(ss[u][j]);
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi) {  // word wi: columns c*32 + 8*wi .. +7
                 float w[kLinRowsPerWarp][8];
@@ -155,6 +174,7 @@ __global__ void __launch_bounds__(kLinThreads) nvfp4_linear_kernel(LinearArgs a)
                         acc[j][v] = s;
                     }
                 }
+            }
             }
         }
 #pragma unroll
