@@ -9,12 +9,18 @@
 //              each; 128-byte swizzle) and bulk copies of the weight and
 //              activation scale-factor atoms (stored in tcgen05 atom layout);
 //              all complete on the stage's mbarrier.
-//   warp 1     MMA issuer: one thread copies the stage's scale atoms into
-//              tensor memory (tcgen05.cp 32x128b.warpx4) and issues
-//              kind::mxf4nvf4 MMAs (M 128, N 128, K 64) into FP32
-//              accumulators in tensor memory, then commits the stage back to
-//              the producer and, after the last stage, the accumulator to
-//              the epilogue. Warp 1 also owns the tensor-memory allocation.
+//   warp 1     MMA issuer: one thread issues kind::mxf4nvf4 MMAs (M 128,
+//              N 128, K 64) into FP32 accumulators in tensor memory once the
+//              stage's tiles have landed and its scale factors are in tensor
+//              memory, then commits the stage back to the producer and,
+//              after the last stage, the accumulator to the epilogue. Warp 1
+//              also owns the tensor-memory allocation.
+//   warps 6-9  scale factors: each stage's weight and activation scale atoms
+//              go from shared memory into that stage's tensor-memory columns
+//              by tcgen05.st, one 32-lane quarter per warp (the layout
+//              tcgen05.cp 32x128b.warpx4 would give), so the MMA thread
+//              issues no copies (a tcgen05.cp per atom costs the issuing
+//              thread about as much as an MMA).
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator rows of their
 //              sub-partition (the down GEMM double-buffers its accumulator so
 //              this overlaps the next tile's MMAs), per-column scaling, then
@@ -32,7 +38,8 @@ namespace nvfp4 {
 
 namespace {
 
-constexpr int kGemmThreads = 192;
+constexpr int kGemmThreads = 320;
+constexpr int kSfWarp0 = 6;  // first scale-factor warp
 constexpr int kTileBytes = kPrefillTileM * 128;  // 128 rows x 128 bytes (256 FP4 columns)
 constexpr int kSfStage = 4 * 512;                // four 64-column scale atoms
 constexpr int kStageK = 256;
@@ -44,7 +51,8 @@ struct GemmCfg {
     static constexpr int kSfa = NA * kSfStage;
     static constexpr int kSfb = J * kSfStage;
     static constexpr int kStage = kA + kB + kSfa + kSfb;
-    static constexpr uint32_t kTx = kA + kB + kSfa + kSfb;  // every byte of a stage arrives by TMA / bulk copy
+    static constexpr uint32_t kTxTiles = kA + kB;   // the stage's code tiles (TMA), on `full`
+    static constexpr uint32_t kTxSf = kSfa + kSfb;    // its scale atoms (bulk copies), on `sfa_in`
     // Down (one projection) double-buffers its accumulator so the epilogue
     // of one tile overlaps the MMAs of the next; gate/up holds two
     // accumulators (gate, up) in one buffer.
@@ -55,10 +63,15 @@ struct GemmCfg {
     // tcgen05.cp, so a region is rewritten only after the MMAs that read it
     // have committed (the producer refills a stage after that commit).
     static constexpr int kSfCols = NA * 16 + J * 16;        // per stage: SFA then SFB
+    // Stage blocks start on 32-column boundaries (the store warps write up
+    // to 32 columns per tcgen05.st).
+    static constexpr int kSfStride = (kSfCols + 31) & ~31;
     static constexpr int kColSf = 256;
-    static constexpr int kColsUsed = kColSf + S * kSfCols;
+    static constexpr int kColsUsed = kColSf + S * kSfStride;
     static constexpr uint32_t kTmemCols = kColsUsed <= 256 ? 256u : 512u;
-    static constexpr size_t kSmem = 1024 + (size_t)S * kStage + 1024;
+    // Alignment slack, the stages, then barriers, the tensor-memory slot and
+    // the epilogue's two column-scale buffers (2 x 128 floats).
+    static constexpr size_t kSmem = 1024 + (size_t)S * kStage + 2048;
     static_assert(kStage % 1024 == 0, "stage must keep 1024-byte tile alignment");
     static_assert(kColsUsed <= 512, "tensor memory overflow");
 };
@@ -116,9 +129,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *acc_full = empty + S;      // [kNumAcc]
     uint64_t *acc_empty = acc_full + 2;  // [kNumAcc]
     uint64_t *drain = acc_empty + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *sf_in = drain + 1;     // [S] the stage's scale atoms are in shared memory
+    uint64_t *sf_full = sf_in + S;   // [S] the stage's scale factors are in tensor memory (4 store warps)
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sf_full + S);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
-    float *colscale = reinterpret_cast<float *>(tmem_slot + 4);  // [128]
+    float *colscale2 = reinterpret_cast<float *>(tmem_slot + 4);  // [2][128], by tile parity
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const PrefillScratch &s = a.s;
     int *err = s.error;
@@ -133,6 +148,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_init(acc_empty + b, 1);
         }
         mbar_init(drain, 1);
+        for (int i = 0; i < S; ++i) {
+            mbar_init(sf_in + i, 1);
+            mbar_init(sf_full + i, 4);
+        }
         fence_barrier_init();
         prefetch_tensormap(&tm_a0);
         if (NA == 2) prefetch_tensormap(&tm_a1);
@@ -175,24 +194,27 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 uint8_t *stage = smem + (size_t)st * Cfg::kStage;
                 uint8_t *sfb = stage + Cfg::kA + Cfg::kB + Cfg::kSfa;
                 if (lane == 0) {
-                    mbar_arrive_expect_tx(full + st, Cfg::kTx);
-                    tma_load_2d(stage, &tm_a0, full + st, ks * 128, arow);
-                    if (NA == 2) tma_load_2d(stage + kTileBytes, &tm_a1, full + st, ks * 128, arow);
+                    // The scale atoms first and on their own barrier: the
+                    // store warps need only them, and they land first.
+                    mbar_arrive_expect_tx(sf_in + st, Cfg::kTxSf);
                     bulk_g2s(stage + Cfg::kA + Cfg::kB, a.sfa[0] + sfa_off + (size_t)ks * kSfStage, kSfStage,
-                             full + st);
+                             sf_in + st);
                     if (NA == 2)
                         bulk_g2s(stage + Cfg::kA + Cfg::kB + kSfStage, a.sfa[1] + sfa_off + (size_t)ks * kSfStage,
-                                 kSfStage, full + st);
+                                 kSfStage, sf_in + st);
 #pragma unroll
-                    for (int j = 0; j < J; ++j) {
-                        // The column tile is one 128-row block of slot rows:
-                        // one TMA box of codes and one bulk copy of scale atoms
-                        // per activation term.
-                        tma_load_2d(stage + Cfg::kA + j * kTileBytes, &tm_b, full + st, ks * 128, j * a.Rb + ti.n0);
+                    for (int j = 0; j < J; ++j)
                         bulk_g2s(sfb + j * kSfStage,
                                  a.sfb + ((size_t)(j * sf_blocks + ti.n0 / kPrefillTileN) * kw + ks * 4) * 512,
-                                 kSfStage, full + st);
-                    }
+                                 kSfStage, sf_in + st);
+                    mbar_arrive_expect_tx(full + st, Cfg::kTxTiles);
+                    tma_load_2d(stage, &tm_a0, full + st, ks * 128, arow);
+                    if (NA == 2) tma_load_2d(stage + kTileBytes, &tm_a1, full + st, ks * 128, arow);
+                    // The column tile is one 128-row block of slot rows: one
+                    // TMA box of codes per activation term.
+#pragma unroll
+                    for (int j = 0; j < J; ++j)
+                        tma_load_2d(stage + Cfg::kA + j * kTileBytes, &tm_b, full + st, ks * 128, j * a.Rb + ti.n0);
                 }
             }
         }
@@ -200,7 +222,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             // Drain: wait for the copies of the last stages issued.
             if (lane == 0) {
                 const uint32_t first = it > (uint32_t)S ? it - S : 0u;
-                for (uint32_t k = first; k < it; ++k) mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                for (uint32_t k = first; k < it; ++k) {
+                    mbar_wait_drain(full + (k % S), (k / S) & 1u);
+                    mbar_wait_drain(sf_in + (k % S), (k / S) & 1u);
+                }
             }
         }
     } else if (warp == 1) {
@@ -222,25 +247,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 for (int ks = 0; ks < kstages; ++ks, ++it) {
                     const int st = it % S;
                     const uint32_t ph = (it / S) & 1u;
-                    if (!mbar_wait(full + st, ph, err, kSiteGemmFull)) {
+                    if (!mbar_wait(full + st, ph, err, kSiteGemmFull) ||
+                        !mbar_wait(sf_full + st, ph, err, kSiteGemmFull)) {
                         ok = false;
                         break;
                     }
                     tc::fence_after_sync();
                     tc::fence_proxy_async_smem();
                     const uint32_t sb = smem_base + (uint32_t)st * Cfg::kStage;
-                    const uint32_t sfa = sb + Cfg::kA + Cfg::kB;
-                    const uint32_t sfb = sfa + Cfg::kSfa;
-                    const uint32_t tsfa = tmem + Cfg::kColSf + (uint32_t)st * Cfg::kSfCols;
+                    const uint32_t tsfa = tmem + Cfg::kColSf + (uint32_t)st * Cfg::kSfStride;
                     const uint32_t tsfb = tsfa + NA * 16;
-#pragma unroll
-                    for (int at = 0; at < 4; ++at) {
-                        tc::cp_sf_atom(tsfa + 4 * at, tc::smem_desc_sf(sfa + at * 512));
-                        if (NA == 2) tc::cp_sf_atom(tsfa + 16 + 4 * at, tc::smem_desc_sf(sfa + kSfStage + at * 512));
-#pragma unroll
-                        for (int j = 0; j < J; ++j)
-                            tc::cp_sf_atom(tsfb + 16 * j + 4 * at, tc::smem_desc_sf(sfb + j * kSfStage + at * 512));
-                    }
 #pragma unroll
                     for (int at = 0; at < 4; ++at) {
 #pragma unroll
@@ -264,6 +280,38 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             mbar_wait_drain(drain, 0);
         }
         __syncwarp();
+    } else if (warp >= kSfWarp0) {
+        // ------------------------------------------------- scale factors
+        // Stage st's atoms are contiguous in shared memory (the weights' NA x
+        // 4, then the activation terms' J x 4, 512 bytes apart) and go to the
+        // stage's contiguous columns tsfa.. (4 per atom) of this warp's lane
+        // quarter. The columns are free: the producer refills a stage (and
+        // so its sf_in) only after the MMAs that read its previous atoms
+        // have committed.
+        constexpr int kAtoms = (NA + J) * 4;
+        const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
+        uint32_t it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int ks = 0; ks < kstages; ++ks, ++it) {
+                const int st = it % S;
+                if (!__all_sync(0xffffffffu, mbar_wait(sf_in + st, (it / S) & 1u, err, kSiteGemmFull))) {
+                    ok = false;
+                    break;
+                }
+                const uint32_t cols = tmem + quarter + Cfg::kColSf + (uint32_t)st * Cfg::kSfStride;
+                const uint8_t *atoms = smem + (size_t)st * Cfg::kStage + Cfg::kA + Cfg::kB;
+#pragma unroll
+                for (int a8 = 0; a8 + 8 <= kAtoms; a8 += 8)
+                    tc::st_sf_atoms<8>(cols + 4 * a8, atoms + a8 * 512, 512, lane);
+                if constexpr (kAtoms % 8 == 4) tc::st_sf_atoms<4>(cols + 4 * (kAtoms - 4), atoms + (kAtoms - 4) * 512,
+                                                                  512, lane);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(sf_full + st);
+            }
+        }
     } else {
         // ----------------------------------------------------- epilogue
         const int sub = warp & 3;
@@ -272,6 +320,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         uint32_t tcount = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
             const TileInfo ti = tile_info(s, tile, mtiles);
+            // A thread can reach the next tile while a slower one still reads
+            // this tile's scales (the gate/up accumulator is released before
+            // the arithmetic): the buffers alternate by tile.
+            float *colscale = colscale2 + 128 * (tcount & 1u);
             {
                 float cs = 0.0f;
                 if (et < ti.nvalid) {
@@ -290,20 +342,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             tc::fence_after_sync();
             const int m = ti.mt * kPrefillTileM + 32 * sub + lane;
             if (MODE == 0) {
+                // SiLU(gate) * up is rounded to FP16 right away, so the fast
+                // exponential and division (a few ulp of FP32) suffice; the
+                // accumulator is handed back once its last columns are in
+                // registers, so the next tile's MMAs overlap this arithmetic.
                 const float ig = a.inv_scales[ti.e], iu = a.inv_scales[(a.E + 1) + ti.e];
-                for (int c0 = 0; c0 < kPrefillTileN; c0 += 32) {
-                    if (c0 >= ti.nvalid) break;
+                const int ncols = (ti.nvalid + 31) & ~31;
+                for (int c0 = 0; c0 < ncols; c0 += 32) {
                     uint32_t rg[32], ru[32];
                     tc::ld_32x32b_x32(lane_base + c0, rg);
                     tc::ld_32x32b_x32(lane_base + Cfg::kColAcc1 + c0, ru);
                     tc::wait_ld();
+                    if (c0 + 32 >= ncols) {
+                        tc::fence_before_sync();
+                        named_barrier(1, 128);
+                        if (et == 0) mbar_arrive(acc_empty + buf);
+                    }
 #pragma unroll
                     for (int n = 0; n < 32; ++n) {
                         if (c0 + n < ti.nvalid) {
                             const float cs = colscale[c0 + n];
                             const float gate = __uint_as_float(rg[n]) * (ig * cs);
                             const float up = __uint_as_float(ru[n]) * (iu * cs);
-                            s.act[(size_t)(ti.n0 + c0 + n) * a.M + m] = f32_to_f16_sat(gate / (1.0f + expf(-gate)) * up);
+                            s.act[(size_t)(ti.n0 + c0 + n) * a.M + m] =
+                                f32_to_f16_sat(__fdividef(gate, 1.0f + __expf(-gate)) * up);
                         }
                     }
                 }
@@ -320,9 +382,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                 f32_to_f16_sat(__uint_as_float(r[n]) * colscale[c0 + n]);
                 }
             }
-            tc::fence_before_sync();
-            named_barrier(1, 128);
-            if (et == 0) mbar_arrive(acc_empty + buf);
+            if (MODE != 0) {
+                tc::fence_before_sync();
+                named_barrier(1, 128);
+                if (et == 0) mbar_arrive(acc_empty + buf);
+            }
         }
     }
 
