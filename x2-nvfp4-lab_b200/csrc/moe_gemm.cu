@@ -9,8 +9,9 @@
 //              each; 128-byte swizzle) and bulk copies of the weight and
 //              activation scale-factor atoms (stored in tcgen05 atom layout);
 //              all complete on the stage's mbarrier.
-//   warp 1     MMA issuer: one thread issues kind::mxf4nvf4 MMAs (M 128,
-//              N 128, K 64) into FP32 accumulators in tensor memory once the
+//   warp 1     MMA issuer: one thread issues kind::mxf4nvf4 MMAs (M 128
+//              slot rows of an activation term as A, N 128 weight rows as B,
+//              K 64) into FP32 accumulators in tensor memory once the
 //              stage's tiles have landed and its scale factors are in tensor
 //              memory, then commits the stage back to the producer and,
 //              after the last stage, the accumulator to the epilogue. Warp 1
@@ -22,10 +23,12 @@
 //              issues no copies (a tcgen05.cp per atom costs the issuing
 //              thread about as much as an MMA).
 //   warps 2-5  epilogue: tcgen05.ld of the accumulator rows of their
-//              sub-partition (the down GEMM double-buffers its accumulator so
-//              this overlaps the next tile's MMAs), per-column scaling, then
+//              sub-partition (one slot row per thread; the down GEMM
+//              double-buffers its accumulator so this overlaps the next
+//              tile's MMAs), the slot row's scale, then
 //              gate/up: act = SiLU(gate) * up as FP16 [slot row][I];
-//              down:    y = coef * acc as FP16 [slot row][H].
+//              down:    y = coef * acc as FP16 [slot row][H],
+//              in 16-byte stores of consecutive outputs.
 // Every mbarrier wait is bounded; on a timeout the CTA records the error,
 // drains its copies and MMAs in flight, frees its tensor memory and exits.
 #include "moe_prefill.cuh"
@@ -70,7 +73,7 @@ struct GemmCfg {
     static constexpr int kColsUsed = kColSf + S * kSfStride;
     static constexpr uint32_t kTmemCols = kColsUsed <= 256 ? 256u : 512u;
     // Alignment slack, the stages, then barriers, the tensor-memory slot and
-    // the epilogue's two column-scale buffers (2 x 128 floats).
+    // the accumulator-ready flag.
     static constexpr size_t kSmem = 1024 + (size_t)S * kStage + 2048;
     static_assert(kStage % 1024 == 0, "stage must keep 1024-byte tile alignment");
     static_assert(kColsUsed <= 512, "tensor memory overflow");
@@ -80,10 +83,12 @@ __device__ __forceinline__ uint8_t *align1024(uint8_t *p) {
     return reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
 }
 
-__device__ __forceinline__ __half f32_to_f16_sat(float v) {
-    uint16_t h;
-    asm("cvt.rn.satfinite.f16.f32 %0, %1;" : "=h"(h) : "f"(v));
-    return __ushort_as_half(h);
+// Two FP32 values rounded to FP16 (round to nearest even, finite values
+// saturated to +-65504): `lo` in the low half (the lower address).
+__device__ __forceinline__ uint32_t pack_f16x2_sat(float lo, float hi) {
+    uint32_t d;
+    asm("cvt.rn.satfinite.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+    return d;
 }
 
 // Bounded wait that ignores the shared error word (used to drain copies in
@@ -133,7 +138,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     uint64_t *sf_full = sf_in + S;   // [S] the stage's scale factors are in tensor memory (4 store warps)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(sf_full + S);
     int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
-    float *colscale2 = reinterpret_cast<float *>(tmem_slot + 4);  // [2][128], by tile parity
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const PrefillScratch &s = a.s;
     int *err = s.error;
@@ -257,17 +261,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t sb = smem_base + (uint32_t)st * Cfg::kStage;
                     const uint32_t tsfa = tmem + Cfg::kColSf + (uint32_t)st * Cfg::kSfStride;
                     const uint32_t tsfb = tsfa + NA * 16;
+                    // The activation term is the A operand (accumulator lane =
+                    // slot row) and the weight rows are B (column = weight
+                    // row); the scale atoms of both are laid out alike, as
+                    // both sides have 128 rows.
 #pragma unroll
                     for (int at = 0; at < 4; ++at) {
 #pragma unroll
                         for (int j = 0; j < J; ++j) {
                             const uint32_t acc = (ks | at | j) != 0 ? 1u : 0u;
-                            const uint64_t bdesc = tc::smem_desc_sw128(sb + Cfg::kA + j * kTileBytes + 32 * at);
-                            tc::mma_mxf4nvf4(dacc, tc::smem_desc_sw128(sb + 32 * at), bdesc, idesc, tsfa + 4 * at,
-                                             tsfb + 16 * j + 4 * at, acc);
+                            const uint64_t xdesc = tc::smem_desc_sw128(sb + Cfg::kA + j * kTileBytes + 32 * at);
+                            tc::mma_mxf4nvf4(dacc, xdesc, tc::smem_desc_sw128(sb + 32 * at), idesc,
+                                             tsfb + 16 * j + 4 * at, tsfa + 4 * at, acc);
                             if (NA == 2)
-                                tc::mma_mxf4nvf4(tmem + Cfg::kColAcc1, tc::smem_desc_sw128(sb + kTileBytes + 32 * at),
-                                                 bdesc, idesc, tsfa + 16 + 4 * at, tsfb + 16 * j + 4 * at, acc);
+                                tc::mma_mxf4nvf4(tmem + Cfg::kColAcc1, xdesc,
+                                                 tc::smem_desc_sw128(sb + kTileBytes + 32 * at), idesc,
+                                                 tsfb + 16 * j + 4 * at, tsfa + 16 + 4 * at, acc);
                         }
                     }
                     tc::commit(empty + st);
@@ -314,78 +323,84 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         }
     } else {
         // ----------------------------------------------------- epilogue
+        // Accumulator lane = slot row of the column tile, column = weight
+        // row: each thread owns one slot row and writes its outputs as runs
+        // of 32 consecutive FP16 values (four 16-byte stores), so a tile's
+        // results leave in 16-byte pieces with no per-element branches.
         const int sub = warp & 3;
-        const int et = threadIdx.x - 64;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
+        const bool leader = threadIdx.x == 64;
         uint32_t tcount = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
             const TileInfo ti = tile_info(s, tile, mtiles);
-            // A thread can reach the next tile while a slower one still reads
-            // this tile's scales (the gate/up accumulator is released before
-            // the arithmetic): the buffers alternate by tile.
-            float *colscale = colscale2 + 128 * (tcount & 1u);
-            {
-                float cs = 0.0f;
-                if (et < ti.nvalid) {
-                    const int p = ti.n0 + et;
-                    cs = MODE == 0 ? s.gx[s.tok_list[p]] : s.coef[p] * s.ga[p];
-                }
-                colscale[et] = cs;
-            }
+            const int r = 32 * sub + lane;  // slot row within the column tile
+            const bool valid = r < ti.nvalid;
+            const int p = ti.n0 + r;
+            // The row's scale is fetched before the accumulator wait.
+            float cs = 0.0f;
+            if (valid) cs = MODE == 0 ? s.gx[s.tok_list[p]] : s.coef[p] * s.ga[p];
             // One thread waits for the accumulator and the decision is
             // shared, so every epilogue warp leaves the loop together.
             const uint32_t buf = tcount % Cfg::kNumAcc;
-            if (et == 0)
+            if (leader)
                 *acc_ok = mbar_wait(acc_full + buf, (tcount / Cfg::kNumAcc) & 1u, err, kSiteGemmAccFull) ? 1 : 0;
             named_barrier(1, 128);
             if (!*reinterpret_cast<volatile int *>(acc_ok)) break;
             tc::fence_after_sync();
-            const int m = ti.mt * kPrefillTileM + 32 * sub + lane;
+            const int m0 = ti.mt * kPrefillTileM;
             if (MODE == 0) {
                 // SiLU(gate) * up is rounded to FP16 right away, so the fast
                 // exponential and division (a few ulp of FP32) suffice; the
                 // accumulator is handed back once its last columns are in
                 // registers, so the next tile's MMAs overlap this arithmetic.
-                const float ig = a.inv_scales[ti.e], iu = a.inv_scales[(a.E + 1) + ti.e];
-                const int ncols = (ti.nvalid + 31) & ~31;
-                for (int c0 = 0; c0 < ncols; c0 += 32) {
+                const float gs = a.inv_scales[ti.e] * cs, us = a.inv_scales[(a.E + 1) + ti.e] * cs;
+                uint4 *dst = reinterpret_cast<uint4 *>(s.act + (size_t)p * a.M + m0);
+#pragma unroll 1
+                for (int c0 = 0; c0 < kPrefillTileM; c0 += 32) {
                     uint32_t rg[32], ru[32];
                     tc::ld_32x32b_x32(lane_base + c0, rg);
                     tc::ld_32x32b_x32(lane_base + Cfg::kColAcc1 + c0, ru);
                     tc::wait_ld();
-                    if (c0 + 32 >= ncols) {
+                    if (c0 + 32 == kPrefillTileM) {
                         tc::fence_before_sync();
                         named_barrier(1, 128);
-                        if (et == 0) mbar_arrive(acc_empty + buf);
+                        if (leader) mbar_arrive(acc_empty + buf);
                     }
+                    if (valid) {
+                        uint32_t h[16];
 #pragma unroll
-                    for (int n = 0; n < 32; ++n) {
-                        if (c0 + n < ti.nvalid) {
-                            const float cs = colscale[c0 + n];
-                            const float gate = __uint_as_float(rg[n]) * (ig * cs);
-                            const float up = __uint_as_float(ru[n]) * (iu * cs);
-                            s.act[(size_t)(ti.n0 + c0 + n) * a.M + m] =
-                                f32_to_f16_sat(__fdividef(gate, 1.0f + __expf(-gate)) * up);
+                        for (int q = 0; q < 16; ++q) {
+                            const float g0 = __uint_as_float(rg[2 * q]) * gs, g1 = __uint_as_float(rg[2 * q + 1]) * gs;
+                            const float u0 = __uint_as_float(ru[2 * q]) * us, u1 = __uint_as_float(ru[2 * q + 1]) * us;
+                            h[q] = pack_f16x2_sat(__fdividef(g0, 1.0f + __expf(-g0)) * u0,
+                                                  __fdividef(g1, 1.0f + __expf(-g1)) * u1);
                         }
+#pragma unroll
+                        for (int k = 0; k < 4; ++k)
+                            dst[c0 / 8 + k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
                     }
                 }
             } else {
-                for (int c0 = 0; c0 < kPrefillTileN; c0 += 32) {
-                    if (c0 >= ti.nvalid) break;
-                    uint32_t r[32];
-                    tc::ld_32x32b_x32(lane_base + buf * 128 + c0, r);
-                    tc::wait_ld();
+                // All 128 columns come into registers first, so the
+                // accumulator is released before any arithmetic.
+                uint32_t acc[kPrefillTileM];
 #pragma unroll
-                    for (int n = 0; n < 32; ++n)
-                        if (c0 + n < ti.nvalid)
-                            s.ypart[(size_t)(ti.n0 + c0 + n) * a.M + m] =
-                                f32_to_f16_sat(__uint_as_float(r[n]) * colscale[c0 + n]);
-                }
-            }
-            if (MODE != 0) {
+                for (int q = 0; q < kPrefillTileM / 32; ++q)
+                    tc::ld_32x32b_x32(lane_base + buf * 128 + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(acc + 32 * q));
+                tc::wait_ld();
                 tc::fence_before_sync();
                 named_barrier(1, 128);
-                if (et == 0) mbar_arrive(acc_empty + buf);
+                if (leader) mbar_arrive(acc_empty + buf);
+                if (valid) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(s.ypart + (size_t)p * a.M + m0);
+#pragma unroll
+                    for (int k = 0; k < kPrefillTileM / 8; ++k)
+                        dst[k] = make_uint4(
+                            pack_f16x2_sat(__uint_as_float(acc[8 * k + 0]) * cs, __uint_as_float(acc[8 * k + 1]) * cs),
+                            pack_f16x2_sat(__uint_as_float(acc[8 * k + 2]) * cs, __uint_as_float(acc[8 * k + 3]) * cs),
+                            pack_f16x2_sat(__uint_as_float(acc[8 * k + 4]) * cs, __uint_as_float(acc[8 * k + 5]) * cs),
+                            pack_f16x2_sat(__uint_as_float(acc[8 * k + 6]) * cs, __uint_as_float(acc[8 * k + 7]) * cs));
+                }
             }
         }
     }
