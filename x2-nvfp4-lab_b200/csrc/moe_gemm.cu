@@ -10,7 +10,8 @@
 //              activation scale-factor atoms (stored in tcgen05 atom layout);
 //              all complete on the stage's mbarrier.
 //   warp 1     MMA issuer: one thread issues kind::mxf4nvf4 MMAs (M 128
-//              slot rows of an activation term as A, N 128 weight rows as B,
+//              slot rows of an activation term as A, N 128 weight rows as B
+//              -- 256 for gate/up, whose gate and up rows form one operand --
 //              K 64) into FP32 accumulators in tensor memory once the
 //              stage's tiles have landed and its scale factors are in tensor
 //              memory, then commits the stage back to the producer and,
@@ -121,6 +122,27 @@ __device__ __forceinline__ TileInfo tile_info(const PrefillScratch &s, int tile,
     return t;
 }
 
+// A warp walks this CTA's tiles with the descriptions of the next 32 held
+// one per lane: lane l loads tile `first + l * stride` (all lanes' dependent
+// table loads in flight at once) and `lane_tile` hands tile k to every lane.
+__device__ __forceinline__ TileInfo batch_tiles(const PrefillScratch &s, int first, int stride, int total,
+                                                int mtiles, int lane) {
+    TileInfo t{};
+    const int tile = first + lane * stride;
+    if (tile < total) t = tile_info(s, tile, mtiles);
+    return t;
+}
+
+__device__ __forceinline__ TileInfo lane_tile(const TileInfo &mine, int k) {
+    TileInfo t;
+    t.ai = __shfl_sync(0xffffffffu, mine.ai, k);
+    t.e = __shfl_sync(0xffffffffu, mine.e, k);
+    t.n0 = __shfl_sync(0xffffffffu, mine.n0, k);
+    t.nvalid = __shfl_sync(0xffffffffu, mine.nvalid, k);
+    t.mt = __shfl_sync(0xffffffffu, mine.mt, k);
+    return t;
+}
+
 template <int MODE, int J, int S>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_a0, const __grid_constant__ CUtensorMap tm_a1,
@@ -181,8 +203,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // ------------------------------------------------------ producer
         uint32_t it = 0;
         bool ok = true;
-        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
-            const TileInfo ti = tile_info(s, tile, mtiles);
+        TileInfo mine{};
+        for (int tile = blockIdx.x, k = 0; tile < total && ok; tile += gridDim.x, k = (k + 1) & 31) {
+            if (k == 0) mine = batch_tiles(s, tile, gridDim.x, total, mtiles, lane);
+            const TileInfo ti = lane_tile(mine, k);
             const int arow = ti.e * a.M + ti.mt * kPrefillTileM;
             const size_t sfa_off = (size_t)(arow / kPrefillTileM) * kw * 512;
             const int sf_blocks = s.max_rows / kPrefillTileN;
@@ -235,7 +259,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA
         if (lane == 0) {
-            constexpr uint32_t idesc = tc::idesc_mxf4nvf4(kPrefillTileN);
+            constexpr uint32_t idesc = tc::idesc_mxf4nvf4(NA * kPrefillTileM);
             const uint32_t smem_base = smem_u32(smem);
             uint32_t it = 0, tcount = 0;
             bool ok = true;
@@ -263,8 +287,12 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const uint32_t tsfb = tsfa + NA * 16;
                     // The activation term is the A operand (accumulator lane =
                     // slot row) and the weight rows are B (column = weight
-                    // row); the scale atoms of both are laid out alike, as
-                    // both sides have 128 rows.
+                    // row). Gate/up issues one N = 256 MMA per step: the
+                    // gate tile and the up tile are consecutive in the stage,
+                    // so together they are one 256-row K-major operand, whose
+                    // accumulator columns 0-127 are gate and 128-255 up, and
+                    // whose scale factors the store warps interleave
+                    // accordingly (8 columns per 64-wide K step).
 #pragma unroll
                     for (int at = 0; at < 4; ++at) {
 #pragma unroll
@@ -272,11 +300,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                             const uint32_t acc = (ks | at | j) != 0 ? 1u : 0u;
                             const uint64_t xdesc = tc::smem_desc_sw128(sb + Cfg::kA + j * kTileBytes + 32 * at);
                             tc::mma_mxf4nvf4(dacc, xdesc, tc::smem_desc_sw128(sb + 32 * at), idesc,
-                                             tsfb + 16 * j + 4 * at, tsfa + 4 * at, acc);
-                            if (NA == 2)
-                                tc::mma_mxf4nvf4(tmem + Cfg::kColAcc1, xdesc,
-                                                 tc::smem_desc_sw128(sb + kTileBytes + 32 * at), idesc,
-                                                 tsfb + 16 * j + 4 * at, tsfa + 16 + 4 * at, acc);
+                                             tsfb + 16 * j + 4 * at, tsfa + 4 * NA * at, acc);
                         }
                     }
                     tc::commit(empty + st);
@@ -310,8 +334,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 }
                 const uint32_t cols = tmem + quarter + Cfg::kColSf + (uint32_t)st * Cfg::kSfStride;
                 const uint8_t *atoms = smem + (size_t)st * Cfg::kStage + Cfg::kA + Cfg::kB;
+                // Gate/up: the first eight atoms are the gate and up weights'
+                // (four each), interleaved per K step for the N = 256 MMA.
+                if constexpr (NA == 2) tc::st_sf_atoms<8, true>(cols, atoms, 512, lane);
 #pragma unroll
-                for (int a8 = 0; a8 + 8 <= kAtoms; a8 += 8)
+                for (int a8 = NA == 2 ? 8 : 0; a8 + 8 <= kAtoms; a8 += 8)
                     tc::st_sf_atoms<8>(cols + 4 * a8, atoms + a8 * 512, 512, lane);
                 if constexpr (kAtoms % 8 == 4) tc::st_sf_atoms<4>(cols + 4 * (kAtoms - 4), atoms + (kAtoms - 4) * 512,
                                                                   512, lane);
@@ -331,8 +358,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
         const bool leader = threadIdx.x == 64;
         uint32_t tcount = 0;
+        TileInfo mine{};
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tcount) {
-            const TileInfo ti = tile_info(s, tile, mtiles);
+            if ((tcount & 31u) == 0) mine = batch_tiles(s, tile, gridDim.x, total, mtiles, lane);
+            const TileInfo ti = lane_tile(mine, tcount & 31u);
             const int r = 32 * sub + lane;  // slot row within the column tile
             const bool valid = r < ti.nvalid;
             const int p = ti.n0 + r;
@@ -355,29 +384,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                 // registers, so the next tile's MMAs overlap this arithmetic.
                 const float gs = a.inv_scales[ti.e] * cs, us = a.inv_scales[(a.E + 1) + ti.e] * cs;
                 uint4 *dst = reinterpret_cast<uint4 *>(s.act + (size_t)p * a.M + m0);
+                // Two 64-column halves: the accumulator is released once the
+                // second half is in registers.
 #pragma unroll 1
-                for (int c0 = 0; c0 < kPrefillTileM; c0 += 32) {
-                    uint32_t rg[32], ru[32];
-                    tc::ld_32x32b_x32(lane_base + c0, rg);
-                    tc::ld_32x32b_x32(lane_base + Cfg::kColAcc1 + c0, ru);
+                for (int c0 = 0; c0 < kPrefillTileM; c0 += 64) {
+                    uint32_t rg[64], ru[64];
+                    tc::ld_32x32b_x32(lane_base + c0, *reinterpret_cast<uint32_t(*)[32]>(rg));
+                    tc::ld_32x32b_x32(lane_base + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(rg + 32));
+                    tc::ld_32x32b_x32(lane_base + Cfg::kColAcc1 + c0, *reinterpret_cast<uint32_t(*)[32]>(ru));
+                    tc::ld_32x32b_x32(lane_base + Cfg::kColAcc1 + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(ru + 32));
                     tc::wait_ld();
-                    if (c0 + 32 == kPrefillTileM) {
+                    if (c0 + 64 == kPrefillTileM) {
                         tc::fence_before_sync();
                         named_barrier(1, 128);
                         if (leader) mbar_arrive(acc_empty + buf);
                     }
                     if (valid) {
-                        uint32_t h[16];
 #pragma unroll
-                        for (int q = 0; q < 16; ++q) {
-                            const float g0 = __uint_as_float(rg[2 * q]) * gs, g1 = __uint_as_float(rg[2 * q + 1]) * gs;
-                            const float u0 = __uint_as_float(ru[2 * q]) * us, u1 = __uint_as_float(ru[2 * q + 1]) * us;
-                            h[q] = pack_f16x2_sat(__fdividef(g0, 1.0f + __expf(-g0)) * u0,
-                                                  __fdividef(g1, 1.0f + __expf(-g1)) * u1);
+                        for (int k = 0; k < 8; ++k) {
+                            uint32_t h[4];
+#pragma unroll
+                            for (int q = 0; q < 4; ++q) {
+                                const int n = 8 * k + 2 * q;
+                                const float g0 = __uint_as_float(rg[n]) * gs, g1 = __uint_as_float(rg[n + 1]) * gs;
+                                const float u0 = __uint_as_float(ru[n]) * us, u1 = __uint_as_float(ru[n + 1]) * us;
+                                h[q] = pack_f16x2_sat(__fdividef(g0, 1.0f + __expf(-g0)) * u0,
+                                                      __fdividef(g1, 1.0f + __expf(-g1)) * u1);
+                            }
+                            dst[c0 / 8 + k] = make_uint4(h[0], h[1], h[2], h[3]);
                         }
-#pragma unroll
-                        for (int k = 0; k < 4; ++k)
-                            dst[c0 / 8 + k] = make_uint4(h[4 * k], h[4 * k + 1], h[4 * k + 2], h[4 * k + 3]);
                     }
                 }
             } else {

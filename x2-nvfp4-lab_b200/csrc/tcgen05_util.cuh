@@ -178,16 +178,22 @@ __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.
 // quarter as the layout tcgen05.cp .32x128b.warpx4 gives: lane r, columns
 // 4a..4a+3 = bytes r*16 .. r*16+15 of atom a (every lane quarter holds the
 // same 32 rows). `taddr` carries the warp's lane quarter in bits 16+.
-template <int N>
+// kPairs (N == 8): the source holds two runs of four atoms (P then Q) and
+// the columns receive them interleaved, P0 Q0 P1 Q1 ..., which is the
+// scale-factor layout of one 256-row operand made of a P row block and a Q
+// row block (row r's scales in column r / 32 of each 64-wide K step).
+template <int N, bool kPairs = false>
 __device__ __forceinline__ void st_sf_atoms(uint32_t taddr, const uint8_t *src, int stride, int lane) {
     static_assert(N == 4 || N == 8, "one 16- or 32-column store");
+    static_assert(!kPairs || N == 8, "pairs interleave two runs of four");
     uint32_t r[4 * N];
 #pragma unroll
     for (int a = 0; a < N; ++a) {
+        const int from = kPairs ? (a & 1) * 4 + (a >> 1) : a;
         uint4 v;
         asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
                      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                     : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(src + a * stride + lane * 16))));
+                     : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(src + from * stride + lane * 16))));
         r[4 * a] = v.x;
         r[4 * a + 1] = v.y;
         r[4 * a + 2] = v.z;
