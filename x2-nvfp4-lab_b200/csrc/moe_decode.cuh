@@ -118,14 +118,64 @@ struct DecodeTcMaps {
     CUtensorMap aq;
 };
 
+// Where a combining kernel writes: out = residual + the nine slot partials.
+struct CombineOut {
+    const void *residual;     // BF16 [T][H] or nullptr
+    void *out;                // BF16 or FP32 [T][H]
+    int out_f32;
+    int shared_here;          // 1 if the shared expert's slot is summed here
+    int T, H;
+};
+
 struct DecodeTcArgs {
     const uint8_t *sfa[2];    // weight scale atoms: gate, up (MODE 0) or down (MODE 1)
     const uint8_t *sfb;       // activation scale atoms (xsf_tc or asf_tc)
     const float *inv_scales;  // [3][E+1]
     int E, H, I;
     int shared_last;          // 1: the shared expert is computed here (always the last active group)
+    int fuse_combine;         // down: the CTA finishing an output tile's last item also combines the tile
+    CombineOut comb;          // the combine's inputs and output (fuse_combine only)
     DecodeScratch s;
 };
+
+// Output rows h..h+3 (h % 4 == 0) of token t: the slot partials summed in
+// slot order, then the shared slot, then the residual (the order of
+// moe_combine_kernel, so every combining kernel gives the same bits). The
+// partials may come from other CTAs of the running grid and are read
+// through L2.
+__device__ __forceinline__ void combine_quad(const CombineOut &c, const DecodeScratch &s, int t, int h) {
+    const int H = c.H;
+    int pos[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) pos[k] = s.inv_pos[t * kTopK + k];
+    const size_t o = (size_t)t * H + h;
+    float r[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    if (c.residual) {
+        const uint16_t *res = static_cast<const uint16_t *>(c.residual) + o;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) r[q] = bf16_bits_to_f32(res[q]);
+    }
+    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+    for (int k = 0; k <= kTopK; ++k) {
+        const int p = k < kTopK ? pos[k] : (c.shared_here ? c.T * kTopK + t : -1);
+        if (p >= 0) {
+            const float4 y = __ldcg(reinterpret_cast<const float4 *>(s.ypart + (size_t)p * H + h));
+            v[0] += y.x;
+            v[1] += y.y;
+            v[2] += y.z;
+            v[3] += y.w;
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        if (c.residual) v[q] += r[q];
+        if (c.out_f32)
+            static_cast<float *>(c.out)[o + q] = v[q];
+        else
+            static_cast<uint16_t *>(c.out)[o + q] = f32_to_bf16_bits(v[q]);
+    }
+}
 
 struct DownArgs {
     const uint8_t *down_packed, *down_scales;

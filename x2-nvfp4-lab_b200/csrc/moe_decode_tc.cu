@@ -441,9 +441,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    pdl_wait();  // routing tables and activation terms are read from here on
-    pdl_launch_dependents();
 
+    // This grid starts only after the gate/up grid has completed (the
+    // launches between, with programmatic serialisation, trigger their
+    // dependents only after waiting for it), so the routing tables are
+    // complete here; the activation terms and their scales are read only
+    // after each role's griddepcontrol.wait.
     const int mtiles = a.H / kTile;
     const int total = *s.n_active * mtiles;
     // Items over the fewest CTAs that need no more waves than the grid, each
@@ -473,6 +476,25 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         uint32_t it = 0, nb = 0;
         int prev_ai = -1;
         bool ok = true;
+        // A weight stage (one item's tile and scale atoms) depends on no
+        // earlier kernel of the call: the first S are requested before the
+        // wait for the activations, so they stream while that completes.
+        const int pre = count < S ? count : S;
+        auto load_weights = [&](const Item &w, int st) {
+            uint8_t *stage = smem + (size_t)st * Cfg::kStage;
+            const int arow = w.e * a.H + w.mt * kTile;
+            mbar_arrive_expect_tx(sfa_in + st, kw * 512);
+            bulk_g2s(stage + KB * kTileBytes, a.sfa[0] + (size_t)(arow / kTile) * kw * 512, kw * 512, sfa_in + st);
+            mbar_arrive_expect_tx(full + st, KB * kTileBytes);
+#pragma unroll
+            for (int box = 0; box < KB; ++box) tma_load_2d(stage + box * kTileBytes, &tm_a, full + st, box * 128, arow);
+        };
+        if (lane == 0) {
+            for (int j = 0; j < pre; ++j) load_weights(load_item(s, item_at(j), mtiles), j);
+            it = (uint32_t)pre;
+        }
+        pdl_wait();
+        pdl_launch_dependents();
         if (lane == 0) {
             Item ti{};
             for (int j = 0; j < count && ok; ++j) {
@@ -499,19 +521,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     ++nb;
                     prev_ai = ti.ai;
                 }
+                if (j < pre) continue;  // its weights were requested before the wait
                 const int st = it % S;
                 const uint32_t ph = (it / S) & 1u;
                 if (!mbar_wait(empty + st, ph ^ 1u, err, kSiteGemmEmpty)) {
                     ok = false;
                     break;
                 }
-                uint8_t *stage = smem + (size_t)st * Cfg::kStage;
-                const int arow = ti.e * a.H + ti.mt * kTile;
-                mbar_arrive_expect_tx(sfa_in + st, kw * 512);
-                bulk_g2s(stage + KB * kTileBytes, a.sfa[0] + (size_t)(arow / kTile) * kw * 512, kw * 512, sfa_in + st);
-                mbar_arrive_expect_tx(full + st, KB * kTileBytes);
-#pragma unroll
-                for (int box = 0; box < KB; ++box) tma_load_2d(stage + box * kTileBytes, &tm_a, full + st, box * 128, arow);
+                load_weights(ti, st);
                 ++it;
             }
             if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
@@ -528,6 +545,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         __syncwarp();
     } else if (warp == 1) {
         // ---------------------------------------------------------- MMA
+        pdl_wait();
+        pdl_launch_dependents();
         if (lane == 0) {
             constexpr uint32_t idesc = tc::idesc_mxf4nvf4(kTile);
             const uint32_t smem_base = smem_u32(smem);
@@ -591,6 +610,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // this warp's lane quarter. A B buffer's columns are free once the
         // buffer has been refilled, a stage's once the stage has (see gate /
         // up).
+        pdl_wait();
+        pdl_launch_dependents();
         const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
         uint32_t it = 0, nb = 0;
         int prev_ai = -1;
@@ -619,6 +640,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
     } else {
         // ----------------------------------------------------- epilogue
+        pdl_wait();
+        pdl_launch_dependents();
         const int sub = warp & 3;
         const int et = threadIdx.x - 64;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);

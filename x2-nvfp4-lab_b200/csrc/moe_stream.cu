@@ -344,43 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ------------------------------------------------------------------ down
 
-// Output rows h..h+3 (h % 4 == 0) of token t: the slot partials summed in
-// slot order, then the shared slot, then the residual (the order of
-// moe_combine_kernel, so both give the same bits). The partials come from
-// other CTAs of the running grid and are read through L2.
+// Output rows h..h+3 of token t (combine_quad over the down arguments).
 __device__ __forceinline__ void combine_quad(const DownArgs &a, int t, int h) {
-    const DecodeScratch &s = a.s;
-    const int H = a.H;
-    int pos[kTopK];
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) pos[k] = s.inv_pos[t * kTopK + k];
-    const size_t o = (size_t)t * H + h;
-    float r[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    if (a.residual) {
-        const uint16_t *res = static_cast<const uint16_t *>(a.residual) + o;
-#pragma unroll
-        for (int q = 0; q < 4; ++q) r[q] = bf16_bits_to_f32(res[q]);
-    }
-    float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-    for (int k = 0; k <= kTopK; ++k) {
-        const int p = k < kTopK ? pos[k] : (a.shared_here ? a.T * kTopK + t : -1);
-        if (p >= 0) {
-            const float4 y = __ldcg(reinterpret_cast<const float4 *>(s.ypart + (size_t)p * H + h));
-            v[0] += y.x;
-            v[1] += y.y;
-            v[2] += y.z;
-            v[3] += y.w;
-        }
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        if (a.residual) v[q] += r[q];
-        if (a.out_f32)
-            static_cast<float *>(a.out)[o + q] = v[q];
-        else
-            static_cast<uint16_t *>(a.out)[o + q] = f32_to_bf16_bits(v[q]);
-    }
+    const CombineOut c{a.residual, a.out, a.out_f32, a.shared_here, a.T, a.H};
+    combine_quad(c, a.s, t, h);
 }
 
 template <int NT, int BOXES, int S>
