@@ -5,8 +5,12 @@ one Qwen3.5-MoE-shape layer (hidden 2048, 256 routed experts x intermediate
 512, top-8 + shared expert), 32 independent BF16 tokens per step, all 257
 experts resident in HBM. A step is one layer forward over one batch. Inputs
 rotate through a pool of distinct token batches (so the routed experts
-change step to step) and L2 is flushed (256 MiB write) before every step,
-outside that step's CUDA-event pair.
+change step to step) and L2 is flushed before every step, outside that
+step's CUDA-event pair: a 256 MiB write, then a 256 MiB read, so the
+write's dirty lines reach HBM before the step instead of inside it (a
+write-only flush adds ~126 MB of write-backs to the timed step, which a
+layer's own few MB of writes never cause; the line also reports the step
+under the write-only flush, `ms_per_step_write_only_flush`).
 
   value      tokens/s over all ranks, device time (sum of per-step events,
              max over ranks)
@@ -89,6 +93,27 @@ def measured_peaks() -> dict:
     if path.exists():
         return json.loads(path.read_text())
     return {}
+
+
+class L2Flush:
+    """Evicts the layer's data from L2 (126 MB) before a timed step: a
+    256 MiB write, then a 256 MiB read of another buffer, so the write's
+    dirty lines are written back here and L2 holds clean, unrelated lines
+    when the step starts (the state a layer meets after other layers'
+    weight reads). Runs on the current stream."""
+
+    def __init__(self):
+        import torch
+
+        self.w = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+        self.r = torch.ones(64 * 1024 * 1024, dtype=torch.int32, device="cuda")
+
+    def __call__(self, write_only: bool = False) -> None:
+        import torch
+
+        self.w.zero_()
+        if not write_only:
+            torch.amax(self.r)
 
 
 class ClockSampler:
@@ -258,7 +283,7 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     torch.cuda.synchronize()
     with torch.cuda.stream(stream):
         for i in range(warmup):
-            flush.zero_()
+            flush()
             bank.forward(pool[i % 2], residual=res, out=out, stream=stream)
     stream.synchronize()
     r = bank.last_routing(T)
@@ -268,7 +293,7 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
     with torch.cuda.stream(stream):
         torch.cuda._sleep(int(2e6))
         for i in range(steps):
-            flush.zero_()
+            flush()
             starts[i].record(stream)
             bank.forward(pool[i % 2], residual=res, out=out, stream=stream)
             ends[i].record(stream)
@@ -447,7 +472,7 @@ def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmu
             n = steps if T <= 64 else min(steps, 10)
             with torch.cuda.stream(stream):
                 for _ in range(warmup):
-                    flush.zero_()
+                    flush()
                     y = layer.forward(x, r)
             stream.synchronize()
             err = float(((y.float() - refs[name]).pow(2).mean() / refs[name].pow(2).mean()).sqrt())
@@ -457,7 +482,7 @@ def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmu
             with torch.cuda.stream(stream):
                 torch.cuda._sleep(int(2e5) * n)
                 for i in range(n):
-                    flush.zero_()
+                    flush()
                     ev[i][0].record(stream)
                     layer.forward(x, r)
                     ev[i][1].record(stream)
@@ -530,7 +555,7 @@ def traced_steps(rt, stream, flush, step, n: int):
     with torch.cuda.stream(stream):
         torch.cuda._sleep(int(2e5) * n)
         for i in range(n):
-            flush.zero_()
+            flush()
             step(i)
     stream.synchronize()
     rt.synchronize()
@@ -579,7 +604,7 @@ def run_ours(args) -> int:
     pool = [synthetic.synthetic_tokens(T, H, 1000 + i) for i in range(pool_n)]
     res_pool = [synthetic.synthetic_tokens(T, H, 5000 + i) for i in range(pool_n)]
     out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+    flush = L2Flush()
     torch.cuda.synchronize()
     ep_layer = None
     first, count, shared_here = 0, E, True
@@ -610,7 +635,7 @@ def run_ours(args) -> int:
 
     with torch.cuda.stream(stream):
         for i in range(args.warmup):
-            flush.zero_()
+            flush()
             step(i)
     stream.synchronize()
     if pg:
@@ -628,10 +653,23 @@ def run_ours(args) -> int:
         # pair brackets device work only.
         torch.cuda._sleep(int(2e5) * args.steps)
         for i in range(args.steps):
-            flush.zero_()
+            flush()
             starts[i].record(stream)
             step(i)
             ends[i].record(stream)
+    stream.synchronize()
+    rt.synchronize()
+    # The same steps after a write-only flush, for comparison (reported, not
+    # the headline).
+    wo_starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    wo_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(int(2e5) * args.steps)
+        for i in range(args.steps):
+            flush(write_only=True)
+            wo_starts[i].record(stream)
+            step(i)
+            wo_ends[i].record(stream)
     stream.synchronize()
     rt.synchronize()
     # Per-kernel durations come from a second, traced pass over the same steps
@@ -643,10 +681,11 @@ def run_ours(args) -> int:
     torch.cuda.synchronize()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = float(sum(step_ms))
+    wo_total_ms = float(sum(s.elapsed_time(e) for s, e in zip(wo_starts, wo_ends)))
     if pg:
-        t = torch.tensor([total_ms], device="cuda", dtype=torch.float64)
+        t = torch.tensor([total_ms, wo_total_ms], device="cuda", dtype=torch.float64)
         pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        total_ms = float(t.item())
+        total_ms, wo_total_ms = float(t[0].item()), float(t[1].item())
     value = T * args.steps / (total_ms / 1000.0)
 
     by_op: dict[str, list[float]] = {}
@@ -689,7 +728,7 @@ def run_ours(args) -> int:
             ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(40)]
             torch.cuda._sleep(int(2e5) * 45)
             for i in range(45):
-                flush.zero_()
+                flush()
                 if i >= 5:
                     ev[i - 5][0].record(stream)
                 bank.forward(x1[i % pool_n], out=o1, stream=stream)
@@ -783,6 +822,7 @@ def run_ours(args) -> int:
             "steps": args.steps,
             "warmup": args.warmup,
             "ms_per_step": round(total_ms / args.steps, 5),
+            "ms_per_step_write_only_flush": round(wo_total_ms / args.steps, 5),
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
@@ -802,7 +842,8 @@ def run_ours(args) -> int:
                 "parallelism": (f"ep{world}: {E // world} routed experts per GPU (shared expert on rank 0), "
                                 "the 32 tokens replicated, combine fused with the cross-rank reduction over "
                                 "NVLink peer memory" if world > 1 else "single GPU"),
-                "l2": "flushed before every step (256 MiB write) outside the per-step CUDA events",
+                "l2": "flushed before every step (256 MiB write, then a 256 MiB read so no dirty line is "
+                      "left) outside the per-step CUDA events",
                 "inputs": f"pool of {pool_n} distinct token batches (the same on every rank)",
                 "mean_unique_routed_experts": round(float(np.mean(uniq)), 2),
             },
