@@ -489,10 +489,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
             for (int box = 0; box < KB; ++box) tma_load_2d(stage + box * kTileBytes, &tm_a, full + st, box * 128, arow);
         };
-        if (lane == 0) {
-            for (int j = 0; j < pre; ++j) load_weights(load_item(s, item_at(j), mtiles), j);
-            it = (uint32_t)pre;
-        }
+        // Lane j requests item j's stage (the items' table reads in flight
+        // together).
+        if (lane < pre) load_weights(load_item(s, item_at(lane), mtiles), lane);
+        it = (uint32_t)pre;
         pdl_wait();
         pdl_launch_dependents();
         if (lane == 0) {
