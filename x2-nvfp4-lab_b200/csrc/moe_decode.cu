@@ -12,6 +12,7 @@ namespace {
 
 constexpr int kRouteRowsPerCta = 4;   // one warp per router row, 128 threads
 constexpr int kRouteTokens = 4;       // tokens per CTA column (independent accumulation chains)
+constexpr int kRouteQuantCtas = 4;    // per token block, writing x's NVFP4 terms (tensor-core variant)
 
 // Monotone map of a float to uint32 for redux.sync; -0 and +0 map alike so
 // equal logits compare equal, as in the lab's selection loop.
@@ -244,6 +245,11 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     extern __shared__ __align__(16) uint8_t route_smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int R = a.E + 1;
+    // CTAs past the router rows (tensor-core variant only) write the token
+    // block's NVFP4 terms and take no ticket, so the chain logits -> top-8
+    // -> dispatch never waits for the quantisation.
+    const int nrow = (R + kRouteRowsPerCta - 1) / kRouteRowsPerCta;
+    const bool quant_cta = (int)blockIdx.x >= nrow;
     const int row = blockIdx.x * kRouteRowsPerCta + warp;
     const int H = a.H;
     const int chunks = H / 128;
@@ -265,7 +271,8 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     {
         const uint8_t *wsrc = reinterpret_cast<const uint8_t *>(a.router + (size_t)min(row, R - 1) * H);
         uint8_t *wdst = reinterpret_cast<uint8_t *>(route_w + (size_t)warp * H);
-        for (int i = lane; i < H / 8; i += 32) cp_async16(wdst + 16 * i, wsrc + 16 * i);
+        if (!quant_cta)
+            for (int i = lane; i < H / 8; i += 32) cp_async16(wdst + 16 * i, wsrc + 16 * i);
         if (a.norm_w)  // bank data too
             for (int i = threadIdx.x; i < H / 8; i += blockDim.x)
                 cp_async16(reinterpret_cast<uint8_t *>(route_nw) + 16 * i, reinterpret_cast<const uint8_t *>(a.norm_w) + 16 * i);
@@ -440,15 +447,17 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     }
 
     // Tensor-core variant: the block's tokens are also written as four NVFP4
-    // terms (B rows 4t + j, scale atoms, global scale). The (token, 16-element
-    // block) pairs of the token block are spread over all its CTAs, one pair
-    // per thread; a CTA first reduces the amax of each token it touches (from
-    // its shared-memory copy) so every CTA derives the same global scale.
-    if (a.quantize_x) {
+    // terms (B rows 4t + j, scale atoms, global scale) by the block's
+    // quantiser CTAs. The (token, 16-element block) pairs are spread over
+    // them, one pair per thread; a CTA first reduces the amax of each token it
+    // touches (from its shared-memory copy) so every CTA derives the same
+    // global scale.
+    if (quant_cta) {
         const int nb = H / 16;
         const int total = tt * nb;
-        const int p0 = (int)((long long)total * blockIdx.x / gridDim.x);
-        const int p1 = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+        const int qc = (int)blockIdx.x - nrow, nq = (int)gridDim.x - nrow;
+        const int p0 = (int)((long long)total * qc / nq);
+        const int p1 = (int)((long long)total * (qc + 1) / nq);
         auto load_block = [&](int jt, int b, float (&v)[16]) {
             if (a.x_is_f32) {
                 const float4 *p = reinterpret_cast<const float4 *>(route_xs + ((size_t)jt * H + 16 * b) * 4);
@@ -514,6 +523,8 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         }
     }
 
+    if (quant_cta) return;
+
     // The last row block of this token block runs top-8 for its tokens (one
     // warp per token); the last token block to finish then dispatches.
     __shared__ unsigned s_ticket;
@@ -522,7 +533,7 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
     __syncthreads();
     if (threadIdx.x == 0) s_ticket = atomicAdd(s.ticket + 1 + blockIdx.y, 1u);
     __syncthreads();
-    if (s_ticket != gridDim.x - 1) return;
+    if (s_ticket != (unsigned)nrow - 1u) return;
     __threadfence();
     // The coefficients need the inverse down scales: request them now,
     // store them after top-8.
@@ -671,7 +682,8 @@ cudaError_t launch_maybe_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 blo
 
 cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent) {
     const int R = a.E + 1;
-    const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta, (a.T + kRouteTokens - 1) / kRouteTokens);
+    const dim3 grid((R + kRouteRowsPerCta - 1) / kRouteRowsPerCta + (a.quantize_x ? kRouteQuantCtas : 0),
+                    (a.T + kRouteTokens - 1) / kRouteTokens);
     const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2 +
                         (a.norm_w ? (size_t)a.H * 2 : 0);
     if (smem > 48 * 1024) {
