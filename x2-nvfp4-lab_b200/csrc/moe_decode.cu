@@ -686,11 +686,11 @@ cudaError_t launch_route(const RouteArgs &a, cudaStream_t stream, bool dependent
                     (a.T + kRouteTokens - 1) / kRouteTokens);
     const size_t smem = (size_t)kRouteTokens * a.H * (a.x_is_f32 ? 4 : 2) + (size_t)kRouteRowsPerCta * a.H * 2 +
                         (a.norm_w ? (size_t)a.H * 2 : 0);
-    if (smem > 48 * 1024) {
-        static std::atomic<uint64_t> done{0};
-        const cudaError_t err = route_smem_limit(moe_route_kernel, done);
-        if (err != cudaSuccess) return err;
-    }
+    // The default dynamic limit is 48 KiB less the kernel's static shared
+    // memory: raise it once per device.
+    static std::atomic<uint64_t> done{0};
+    const cudaError_t err = route_smem_limit(moe_route_kernel, done);
+    if (err != cudaSuccess) return err;
     return launch_maybe_dependent(moe_route_kernel, grid, dim3(kRouteRowsPerCta * 32), smem, stream, dependent, a);
 }
 
