@@ -304,6 +304,29 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
                           lambda i: bank.forward(pool[i % 2], residual=res, out=out, stream=stream), steps)
     for ev in traced:
         by_op[ev.operation] = by_op.get(ev.operation, 0.0) + ev.duration_ns / 1e3 / steps
+    # Cross-check on a seeded sample of 32 tokens: the same rows through the
+    # decode path (tensor-core GEMVs, four activation terms; itself tested
+    # against the FP32 oracle), compared with this pass's output rows. The
+    # hottest expert's tokens are in the sample when the load is skewed.
+    g = torch.Generator().manual_seed(seed + T)
+    r_ids = torch.as_tensor(r.ids[:, :8])
+    hot = int(np.argmax(counts))
+    hot_tokens = torch.nonzero((r_ids == hot).any(dim=1)).flatten()[:8]
+    rest = torch.randperm(T, generator=g)[:32]
+    sample = torch.unique(torch.cat([hot_tokens, rest]))[:32].to("cuda")
+    with torch.cuda.stream(stream):
+        bank.forward(pool[(steps - 1) % 2], residual=res, out=out, stream=stream)
+        ref = bank.forward(pool[(steps - 1) % 2][sample].contiguous(), residual=res[sample].contiguous(),
+                           stream=stream)
+    stream.synchronize()
+    rt.synchronize()
+    got = out[sample].float()
+    want = ref.float()
+    diff = (got - want).norm() / want.norm()
+    mar = ((got - want).abs().max() / want.abs().max()).item()
+    parity = {"vs": "decode path (tensor-core GEMVs, four activation terms) on the same tokens",
+              "tokens": int(sample.numel()), "hot_expert_tokens": int(hot_tokens.numel()),
+              "rel_rmse": float(f"{diff.item():.3e}"), "max_abs_rel": float(f"{mar:.3e}")}
     if skew:
         bank.set_router_bias(None)
     ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
@@ -326,6 +349,7 @@ def prefill_leg(rt, bank, stream, flush, T: int, seed: int, steps: int, warmup: 
         "activation_terms": [4, 3],
         "max_expert_load": int(counts.max()),
         "mean_expert_load": round(float(counts.mean()), 1),
+        "parity": parity,
     }
 
 
