@@ -417,10 +417,11 @@ def stack_leg(rt, seed: int, steps: int, warmup: int, layers: int = 40, decode_k
 def linear_leg(rt, seed: int, steps: int, warmup: int, rows: int = 248320, cols: int = 2048) -> dict:
     """The dense NVFP4 linear (the lab's nvfp4_linear entry points behind its
     vLLM provider) at the LM-head shape, 248320 x 2048, for 1 and 4 FP32
-    vectors through the tensor entry point on a torch stream. Device time per
-    call (CUDA events, median); the 286 MB of weights a call streams are far
-    larger than L2, so no flush is needed. Algorithmic bytes per call: packed
-    codes and scales (0.5625 B per weight) plus x in and y out in FP32."""
+    vectors through the tensor entry point on a torch stream: the activations'
+    NVFP4 terms, then the tensor-core weight stream (two launches). Device
+    time per call (CUDA events, median); the 286 MB of weights a call streams
+    are far larger than L2, so no flush is needed. Algorithmic bytes per call:
+    packed codes and scales (0.5625 B per weight) plus x in and y out in FP32."""
     import numpy as np
     import torch
 
@@ -432,7 +433,7 @@ def linear_leg(rt, seed: int, steps: int, warmup: int, rows: int = 248320, cols:
     stream = torch.cuda.Stream()
     peak = measured_peaks().get("hbm_gbs")
     out = {"workload": f"lm_head_{rows}x{cols}", "l2": "not flushed (weights per call >> L2)",
-           "kernel": "nvfp4_linear_kernel", "launches_per_call": 1}
+           "kernel": "linear_terms_kernel + linear_tc_kernel (tcgen05 kind::mxf4nvf4)", "launches_per_call": 2}
     try:
         for V in (1, 4):
             x = torch.from_numpy(rng.standard_normal((V, cols)).astype(np.float32)).cuda()

@@ -283,7 +283,11 @@ NVFP4_API void nvfp4_matrix_destroy(nvfp4_matrix * matrix);
 
 /* reference: nvfp4_runtime.h:240-248 (nvfp4_runtime.cpp:2110-2183).
  * Synchronous, host x and dst; last_profile gets the upload, kernel and
- * download times. */
+ * download times. On this backend NVFP4_KERNEL_SCALAR runs a CUDA-core kernel
+ * on the FP32 activations; every other kind (and nvfp4_linear_ptr_f32) runs
+ * the tcgen05 kernel, the activations as six NVFP4 terms per vector (within
+ * ~2e-6 of the output scale). Calls on one matrix share its activation-term
+ * buffers and must not overlap on the GPU. */
 NVFP4_API nvfp4_status nvfp4_linear_f32(
     nvfp4_runtime * runtime,
     const nvfp4_matrix * matrix,

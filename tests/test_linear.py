@@ -3,7 +3,8 @@ its vLLM NvFp4LinearKernel provider).
 
 CPU: the provider's contract with a fake runtime (what it uploads, how it
 reshapes, casts and adds the bias) and its registration. GPU (sm_100a): every
-linear entry point against the oracle's restatement of the lab's CPU GEMV
+linear entry point (the tensor-core kernel; the CUDA-core kernel for the scalar
+kernel kind) against the oracle's restatement of the lab's CPU GEMV
 (``nvfp4_gemv``, pinned to the lab's golden vectors), at the lab's own GEMV
 gate (2e-5 of the output scale), including ragged shapes, several passes of
 vectors, and scale bytes outside the E4M3 value range (sign bit, 0x7F)."""
@@ -226,10 +227,10 @@ def test_linear_matches_oracle(cuda_runtime, rows, cols, vectors):
 
 @pytest.mark.gpu
 def test_linear_activation_range(cuda_runtime):
-    """The kernel carries each FP32 activation as two FP16 halves after a
-    per-vector power-of-two scale: vectors far above and below FP16 range,
-    one mixing a few large entries with ordinary ones, and a zero vector all
-    meet the lab's gate, each relative to its own output scale."""
+    """Each vector's activations enter as NVFP4 terms under the vector's own
+    FP32 global scale: vectors far above and below FP16 range, one mixing a
+    few large entries with ordinary ones, and a zero vector all meet the
+    lab's gate, each relative to its own output scale."""
     rows, cols = 200, 1024
     packed, scales = _matrix(rows, cols, 41)
     x = np.random.default_rng(42).standard_normal((5, cols)).astype(np.float32)
@@ -269,10 +270,12 @@ def test_linear_scale_bytes_follow_the_lab_rule(cuda_runtime):
 @pytest.mark.gpu
 def test_linear_entry_points_agree(cuda_runtime):
     """Host, device-buffer, enqueued and tensor entry points run the same
-    kernel: bit-identical outputs."""
+    tensor-core kernel: bit-identical outputs. The scalar kernel kind runs
+    the CUDA-core kernel on the FP32 activations: within the lab's gate of
+    the tensor-core result and of the oracle."""
     import torch
 
-    from vllm_nvfp4_cuda.runtime import KERNEL_SCALAR, KERNEL_TILED
+    from vllm_nvfp4_cuda.runtime import KERNEL_SCALAR, KERNEL_SUBGROUP, KERNEL_TILED
 
     rows, cols, vectors = 515, 768, 5
     packed, scales = _matrix(rows, cols, 21)
@@ -282,10 +285,10 @@ def test_linear_entry_points_agree(cuda_runtime):
         host = cuda_runtime.linear(m, x, kernel_kind=KERNEL_TILED)
         xb = cuda_runtime.upload_buffer(x)
         ob = cuda_runtime.create_buffer(vectors * rows * 4)
-        cuda_runtime.linear_device(m, xb, vectors, ob, kernel_kind=KERNEL_SCALAR)
+        cuda_runtime.linear_device(m, xb, vectors, ob, kernel_kind=KERNEL_SUBGROUP)
         np.testing.assert_array_equal(ob.download((vectors, rows)), host)
         ob2 = cuda_runtime.create_buffer(vectors * rows * 4)
-        cuda_runtime.linear_device(m, xb, vectors, ob2, kernel_kind=KERNEL_SCALAR, enqueue=True)
+        cuda_runtime.linear_device(m, xb, vectors, ob2, kernel_kind=KERNEL_TILED, enqueue=True)
         cuda_runtime.synchronize()
         np.testing.assert_array_equal(ob2.download((vectors, rows)), host)
         xt = torch.from_numpy(x).cuda().reshape(1, vectors, cols)
@@ -293,8 +296,31 @@ def test_linear_entry_points_agree(cuda_runtime):
         torch.cuda.synchronize()
         assert tuple(yt.shape) == (1, vectors, rows)
         np.testing.assert_array_equal(yt.cpu().numpy().reshape(vectors, rows), host)
-        for b in (xb, ob, ob2):
+        ob3 = cuda_runtime.create_buffer(vectors * rows * 4)
+        cuda_runtime.linear_device(m, xb, vectors, ob3, kernel_kind=KERNEL_SCALAR)
+        scalar = ob3.download((vectors, rows))
+        ref = _oracle(packed, scales, x, 6.0)
+        for got in (scalar, host):
+            np.testing.assert_allclose(got, ref, rtol=GATE, atol=GATE * float(np.max(np.abs(ref))))
+        for b in (xb, ob, ob2, ob3):
             b.close()
+    finally:
+        m.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("vectors", [21, 22, 43])
+def test_linear_tensor_core_passes(cuda_runtime, vectors):
+    """The tensor-core kernel carries 21 vectors per pass (six activation
+    terms each in one 128-row B tile): full, one-over and two-over passes."""
+    rows, cols = 700, 1280
+    packed, scales = _matrix(rows, cols, 31 + vectors)
+    x = np.random.default_rng(vectors).standard_normal((vectors, cols)).astype(np.float32)
+    m = cuda_runtime.upload(packed, scales, 3.0)
+    try:
+        got = cuda_runtime.linear(m, x)
+        ref = _oracle(packed, scales, x, 3.0)
+        np.testing.assert_allclose(got, ref, rtol=GATE, atol=GATE * float(np.max(np.abs(ref))))
     finally:
         m.close()
 

@@ -13,7 +13,13 @@
 // row, scale bytes sanitised at upload like the bank's (sign cleared, 0x7F ->
 // 0: the lab's decoding rule, nvfp4_gemv.cl:14-27).
 //
-// Kernel: a weight stream bound by HBM for a few vectors. Each warp owns four
+// Kernels. Every call runs the tensor-core kernel (linear_tc.cu: the
+// activations as six NVFP4 terms, the weights streamed through tcgen05
+// block-scaled MMAs, within ~2e-6 of the output scale) except calls with the
+// scalar kernel kind, which run the CUDA-core kernel below on the FP32
+// activations themselves.
+//
+// CUDA-core kernel: a weight stream bound by HBM for a few vectors. Each warp owns four
 // rows at a time; lane l takes the 32-column chunks l, l+32, ... of the rows
 // (one 16-byte packed load and one 2-byte scale load per chunk and row), two
 // chunks of every row loaded before any arithmetic so that eight 16-byte
@@ -27,6 +33,7 @@
 // index so that a warp's LDS.128 hits distinct bank groups.
 
 #include "internal.h"
+#include "linear_tc.cuh"
 #include "nvfp4_common.cuh"
 
 #include <cuda_fp16.h>
@@ -48,8 +55,12 @@ struct nvfp4_matrix {
     uint8_t *packed = nullptr;
     uint8_t *scales = nullptr;
     float inv_global = 0.0f;
+    nvfp4::LinearTcState tc;               // tensor-core path: scale atoms, activation terms, tensor maps
+    volatile int *host_err = nullptr;      // pinned, device-mapped wait-timeout word (read at synchronize)
 
     ~nvfp4_matrix() {
+        nvfp4::free_linear_tc(tc);
+        if (host_err) cudaFreeHost(const_cast<int *>(host_err));
         if (packed) cudaFree(packed);
         if (scales) cudaFree(scales);
     }
@@ -217,10 +228,19 @@ void launch_pass(const LinearArgs &a, int sm_count, cudaStream_t stream) {
     check_cuda(cudaGetLastError(), "nvfp4_linear_kernel");
 }
 
-// All passes of one call: up to eight vectors per pass (fewer when the
-// activations of eight would exceed the shared-memory budget).
+// All passes of one call. The tensor-core kernel (linear_tc.cu) serves every
+// call except those that ask for the scalar kernel kind, which run the
+// CUDA-core kernel above on the FP32 activations themselves: up to eight
+// vectors per pass (fewer when the activations of eight would exceed the
+// shared-memory budget).
 void launch_linear(const nvfp4_matrix &m, const float *x, int vectors, float *dst, int sm_count,
-                   cudaStream_t stream) {
+                   cudaStream_t stream, bool tensor_cores = true) {
+    // The tensor-core kernel reads the activations as 16-byte vectors.
+    if (tensor_cores && (reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+        check_cuda(launch_linear_tc(m.tc, x, vectors, m.rows, m.cols, m.inv_global, dst, sm_count, stream),
+                   "linear_tc_kernel");
+        return;
+    }
     LinearArgs a{};
     a.packed = m.packed;
     a.scales = m.scales;
@@ -340,7 +360,18 @@ extern "C" NVFP4_API nvfp4_status nvfp4_matrix_upload(nvfp4_runtime *runtime, co
         check_cuda(cudaMemcpyAsync(m->scales, sanitized.data(), sanitized.size(), cudaMemcpyHostToDevice,
                                    runtime->stream),
                    "cudaMemcpyAsync(matrix scales)");
+        check_cuda(init_linear_tc(m->tc, m->packed, m->packed_pitch, m->scales, m->scale_pitch, rows, cols,
+                                  runtime->stream),
+                   "tensor-core linear set-up");
+        int *host_err = nullptr;
+        check_cuda(cudaHostAlloc(reinterpret_cast<void **>(&host_err), sizeof(int), cudaHostAllocMapped),
+                   "cudaHostAlloc(matrix error word)");
+        m->host_err = host_err;
+        *host_err = 0;
+        check_cuda(cudaHostGetDevicePointer(reinterpret_cast<void **>(&m->tc.host_err_dev), host_err, 0),
+                   "cudaHostGetDevicePointer(matrix error word)");
         check_cuda(cudaStreamSynchronize(runtime->stream), "cudaStreamSynchronize(matrix upload)");
+        runtime->error_words.emplace_back(m->host_err, m->tc.err);
         *out_matrix = m.release();
         clear_last_error();
         return NVFP4_STATUS_OK;
@@ -354,6 +385,10 @@ extern "C" NVFP4_API void nvfp4_matrix_destroy(nvfp4_matrix *matrix) {
     if (matrix->runtime) {
         std::lock_guard<std::mutex> lock(matrix->runtime->queue_mutex);
         cudaStreamSynchronize(matrix->runtime->stream);
+        auto &words = matrix->runtime->error_words;
+        words.erase(std::remove_if(words.begin(), words.end(),
+                                   [&](const std::pair<volatile int *, int *> &w) { return w.second == matrix->tc.err; }),
+                    words.end());
     }
     delete matrix;
 }
@@ -380,11 +415,12 @@ extern "C" NVFP4_API nvfp4_status nvfp4_linear_f32(nvfp4_runtime *runtime, const
         check_cuda(cudaMemcpyAsync(dx.p, x, in_bytes, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(linear input)");
         check_cuda(cudaEventRecord(e1.e, s), "cudaEventRecord");
         launch_linear(*matrix, static_cast<const float *>(dx.p), vectors, static_cast<float *>(dy.p),
-                      runtime->sm_count, s);
+                      runtime->sm_count, s, kernel_kind != NVFP4_KERNEL_SCALAR);
         check_cuda(cudaEventRecord(e2.e, s), "cudaEventRecord");
         check_cuda(cudaMemcpyAsync(dst, dy.p, out_bytes, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync(linear output)");
         check_cuda(cudaEventRecord(e3.e, s), "cudaEventRecord");
         check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(linear)");
+        raise_device_timeouts(runtime);
         runtime->last_profile = {elapsed_ns(e0.e, e1.e), elapsed_ns(e1.e, e2.e), elapsed_ns(e2.e, e3.e)};
         clear_last_error();
         return NVFP4_STATUS_OK;
@@ -425,9 +461,10 @@ extern "C" NVFP4_API nvfp4_status nvfp4_linear_device_f32(nvfp4_runtime *runtime
         EventLease e0(runtime), e1(runtime);
         check_cuda(cudaEventRecord(e0.e, s), "cudaEventRecord");
         launch_linear(*matrix, static_cast<const float *>(x->data), vectors, static_cast<float *>(dst->data),
-                      runtime->sm_count, s);
+                      runtime->sm_count, s, kernel_kind != NVFP4_KERNEL_SCALAR);
         check_cuda(cudaEventRecord(e1.e, s), "cudaEventRecord");
         check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(device linear)");
+        raise_device_timeouts(runtime);
         runtime->last_profile = {0, elapsed_ns(e0.e, e1.e), 0};
         clear_last_error();
         return NVFP4_STATUS_OK;
@@ -448,7 +485,7 @@ extern "C" NVFP4_API nvfp4_status nvfp4_linear_device_enqueue_f32(nvfp4_runtime 
         std::lock_guard<std::mutex> lock(runtime->queue_mutex);
         runtime->profiled("nvfp4_linear", nullptr, [&](cudaStream_t s) {
             launch_linear(*matrix, static_cast<const float *>(x->data), vectors, static_cast<float *>(dst->data),
-                          runtime->sm_count, s);
+                          runtime->sm_count, s, kernel_kind != NVFP4_KERNEL_SCALAR);
         });
         clear_last_error();
         return NVFP4_STATUS_OK;
