@@ -443,14 +443,18 @@ NVFP4_API nvfp4_status nvfp4_moe_bank_forward_ptr_bf16(
  * lab's callers run as nvfp4_buffer_upload, the bank enqueue,
  * nvfp4_runtime_synchronize and nvfp4_buffer_download
  * (vllm_nvfp4_opencl/runtime.py:370-377, nvfp4_runtime.h:140-160,416-419),
- * in one call: x (and the residual) are copied to device staging on the
- * runtime stream, the forward is enqueued behind them, dst is copied back and
- * the stream is synchronised once (device timeouts are reported as by
+ * in one call: x is copied to device staging on the runtime stream, the
+ * forward is enqueued behind it, the result reaches dst and the stream is
+ * synchronised once (device timeouts are reported as by
  * nvfp4_runtime_synchronize). x_host, residual_host, dst_host: BF16
  * [tokens, hidden] in host memory; page-locked memory (cudaHostAlloc,
  * torch pin_memory) makes the copies asynchronous DMA, pageable memory works
- * through the driver's staging. flags: NVFP4_MOE_ADD_RESIDUAL and
- * NVFP4_MOE_PRE_NORM. The first call (and any larger call) allocates the
+ * through the driver's staging. Calls of up to 64 tokens (one pass of the
+ * decode kernels) read a page-locked residual and store into a page-locked
+ * dst across the bus from the combining kernel itself, each value once, when
+ * the driver reports the whole span as one mapped allocation; otherwise
+ * both go through device staging and copies. flags: NVFP4_MOE_ADD_RESIDUAL
+ * and NVFP4_MOE_PRE_NORM. The first call (and any larger call) allocates the
  * device staging for 3 x tokens x hidden x 2 bytes, kept by the bank. */
 NVFP4_API nvfp4_status nvfp4_moe_bank_forward_host_bf16(
     nvfp4_moe_bank * bank,

@@ -141,6 +141,41 @@ def test_forward_host_matches_device_forward(cuda_runtime, wide_bank, wide_host,
     np.testing.assert_array_equal(one.view(np.int16), want1.cpu().view(torch.int16).numpy())
 
 
+@pytest.mark.parametrize("T", [1, 4, 32, 48])
+def test_forward_host_buffer_kinds(cuda_runtime, wide_bank, wide_host, T):
+    """Decode-sized host forwards read a page-locked residual and store their
+    rows into a page-locked dst over the bus; pageable buffers go through the
+    device staging. Every mix gives the device forward's bits, and pinned
+    buffers that are row windows of larger pinned tensors are read and
+    written inside the window only."""
+    import torch
+
+    H = wide_host.hidden
+    xbits = synthetic_np.tokens_bf16(T, H, 1300 + T)
+    rbits = synthetic_np.tokens_bf16(T, H, 1400 + T)
+    x, r = bits_to_bf16_tensor(xbits), bits_to_bf16_tensor(rbits)
+    want = wide_bank.forward(x, residual=r)
+    torch.cuda.synchronize()
+    want = want.cpu().view(torch.int16).numpy()
+    hx = torch.from_numpy(xbits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    r_pageable = torch.from_numpy(rbits.view(np.int16)).view(torch.bfloat16).clone()
+    r_big = torch.full((T + 5, H), -3.0, dtype=torch.bfloat16).pin_memory()
+    r_big[2:2 + T] = r_pageable
+    r_window = r_big[2:2 + T]
+    o_pageable = torch.empty(T, H, dtype=torch.bfloat16)
+    o_big = torch.full((T + 6, H), 7.0, dtype=torch.bfloat16).pin_memory()
+    o_window = o_big[3:3 + T]
+    assert not r_pageable.is_pinned() and not o_pageable.is_pinned()
+    assert r_window.is_pinned() and o_window.is_pinned() and o_window.is_contiguous()
+    for res in (r_pageable, r_window):
+        for out in (o_pageable, o_window):
+            out.zero_()
+            wide_bank.forward_host(hx, residual=res, out=out)
+            np.testing.assert_array_equal(out.view(torch.int16).numpy(), want)
+    assert bool((o_big[:3] == 7.0).all()) and bool((o_big[3 + T:] == 7.0).all())
+    assert bool((r_big[:2] == -3.0).all()) and bool((r_big[2 + T:] == -3.0).all())
+
+
 def test_forward_more_than_64_tokens(cuda_runtime, small_bank, small_host):
     import torch
 

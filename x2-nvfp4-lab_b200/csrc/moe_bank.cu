@@ -125,6 +125,45 @@ __global__ void sanitize_scales_kernel(uint8_t *dst, size_t pitch, const uint8_t
     }
 }
 
+// True when [p, p + bytes) lies inside one page-locked host allocation that
+// kernels on the current device can store to: both ends are mapped host
+// memory of the same CUDA buffer, bytes - 1 apart on the device side. *dev
+// receives the device address of p. Pageable memory, registrations the
+// driver cannot identify, and spans crossing allocations answer false.
+bool mapped_host_span(void *p, size_t bytes, void **dev) {
+    using GetAttrFn = CUresult (*)(void *, CUpointer_attribute, CUdeviceptr);
+    static GetAttrFn get_attr = [] {
+        void *fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuPointerGetAttribute", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess) {
+            cudaGetLastError();
+            return static_cast<GetAttrFn>(nullptr);
+        }
+        return reinterpret_cast<GetAttrFn>(fn);
+    }();
+    if (!get_attr || bytes == 0) return false;
+    char *last = static_cast<char *>(p) + (bytes - 1);
+    cudaPointerAttributes a{}, b{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess || cudaPointerGetAttributes(&b, last) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    if (a.type != cudaMemoryTypeHost || b.type != cudaMemoryTypeHost || !a.devicePointer || !b.devicePointer ||
+        static_cast<char *>(b.devicePointer) - static_cast<char *>(a.devicePointer) !=
+            static_cast<ptrdiff_t>(bytes - 1))
+        return false;
+    unsigned long long id_a = 0, id_b = 0;
+    if (get_attr(&id_a, CU_POINTER_ATTRIBUTE_BUFFER_ID, reinterpret_cast<CUdeviceptr>(a.devicePointer)) !=
+            CUDA_SUCCESS ||
+        get_attr(&id_b, CU_POINTER_ATTRIBUTE_BUFFER_ID, reinterpret_cast<CUdeviceptr>(b.devicePointer)) !=
+            CUDA_SUCCESS ||
+        id_a == 0 || id_a != id_b)
+        return false;
+    *dev = a.devicePointer;
+    return true;
+}
+
 void mark_uploaded(nvfp4_moe_bank *bank, int expert, int projection) {
     const size_t slots = static_cast<size_t>(bank->experts) + 1;
     const size_t index = static_cast<size_t>(projection) * slots + expert;
@@ -172,7 +211,7 @@ bool use_token_kernel(const nvfp4_moe_bank *bank, int tokens, const EpArgs *ep) 
 
 void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const void *residual,
                     void *out, int out_f32, int tokens, cudaStream_t stream, const EpArgs *ep = nullptr,
-                    bool pre_norm = false) {
+                    bool pre_norm = false, bool residual_early = false) {
     const int E = bank->experts, H = bank->hidden, I = bank->intermediate;
     const int sms = bank->runtime->sm_count;
     nvfp4_runtime *rt = bank->runtime;
@@ -229,6 +268,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
     da.down_packed = bank->packed[2];
     da.down_scales = bank->scales[2];
     da.residual = residual;
+    da.residual_early = residual_early ? 1 : 0;
     da.out = out;
     da.out_f32 = out_f32;
     da.shared_here = bank->shared_here;
@@ -759,17 +799,38 @@ extern "C" NVFP4_API nvfp4_status nvfp4_moe_bank_forward_host_bf16(nvfp4_moe_ban
                        "cudaMalloc(host forward staging)");
             bank->io_stage_bytes = 3 * bytes;
         }
-        uint8_t *dx = bank->io_stage, *dr = bank->io_stage + bytes, *dout = bank->io_stage + 2 * bytes;
+        uint8_t *dx = bank->io_stage, *dr = bank->io_stage + bytes, *dstage = bank->io_stage + 2 * bytes;
         cudaStream_t s = rt->stream;
-        check_cuda(cudaMemcpyAsync(dx, x_host, bytes, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(x)");
         const bool res = (flags & NVFP4_MOE_ADD_RESIDUAL) != 0;
-        if (res)
+        const bool pre_norm = (flags & NVFP4_MOE_PRE_NORM) != 0;
+        // A call that runs as one pass of the decode kernels reads a
+        // page-locked residual and stores its output rows into a page-locked
+        // dst over the bus itself: the combining kernel reads each residual
+        // value once (before it waits on the down kernel) and stores each
+        // output value once, and no kernel reads dst back. Pageable buffers,
+        // and every buffer of other calls, go through the device staging.
+        const bool decode = tokens <= kDecodeMaxTokens && !(pre_norm && tokens > kFusedNormMaxTokens);
+        void *res_dev = nullptr, *out_dev = nullptr;
+        const bool res_direct =
+            decode && res && mapped_host_span(const_cast<void *>(residual_host), bytes, &res_dev);
+        const bool out_direct = decode && mapped_host_span(out_host, bytes, &out_dev);
+        check_cuda(cudaMemcpyAsync(dx, x_host, bytes, cudaMemcpyHostToDevice, s), "cudaMemcpyAsync(x)");
+        if (res && !res_direct)
             check_cuda(cudaMemcpyAsync(dr, residual_host, bytes, cudaMemcpyHostToDevice, s),
                        "cudaMemcpyAsync(residual)");
+        const void *rsrc = !res ? nullptr : res_direct ? res_dev : static_cast<const void *>(dr);
+        void *dout = out_direct ? out_dev : static_cast<void *>(dstage);
         rt->direct_call(s, [&](cudaStream_t ks) {
-            enqueue_forward_bf16(bank, dx, res ? dr : nullptr, dout, tokens, ks, 0, (flags & NVFP4_MOE_PRE_NORM) != 0);
+            if (decode) {
+                enqueue_decode(bank, dx, 0, rsrc, dout, 0, tokens, ks, nullptr, pre_norm, res_direct);
+                bank->last_tokens = tokens;
+                bank->last_path = 1;
+            } else {
+                enqueue_forward_bf16(bank, dx, rsrc, dout, tokens, ks, 0, pre_norm);
+            }
         });
-        check_cuda(cudaMemcpyAsync(out_host, dout, bytes, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync(out)");
+        if (!out_direct)
+            check_cuda(cudaMemcpyAsync(out_host, dstage, bytes, cudaMemcpyDeviceToHost, s), "cudaMemcpyAsync(out)");
         check_cuda(cudaStreamSynchronize(s), "cudaStreamSynchronize(host forward)");
         raise_device_timeouts(rt);
         clear_last_error();

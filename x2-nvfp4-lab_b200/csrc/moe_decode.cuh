@@ -185,6 +185,10 @@ struct DownArgs {
     int shared_here;          // 1 if the shared expert's slot is summed here
     int T, E, H, I;
     int fuse_combine;         // in-register down kernel: the last CTA of each output tile also combines it
+    // The residual was written before the call was enqueued (the caller's
+    // page-locked host rows): moe_combine_kernel reads it before waiting on
+    // the down kernel, so its latency overlaps the down GEMV.
+    int residual_early;
     DecodeScratch s;
 };
 

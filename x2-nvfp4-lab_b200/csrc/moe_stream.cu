@@ -570,27 +570,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ------------------------------------------------------------- combine
 
 __global__ void __launch_bounds__(256) moe_combine_kernel(DownArgs a) {
-    pdl_wait();
-    pdl_launch_dependents();
     const DecodeScratch &s = a.s;
     const int H = a.H, T = a.T;
     const int t = blockIdx.y;
-    int pos[kTopK];
+    const int h = blockIdx.x * blockDim.x + threadIdx.x;  // the grid covers H: one column per thread
+    const size_t o = (size_t)t * H + h;
+    const uint16_t *res = static_cast<const uint16_t *>(a.residual);
+    float r = 0.0f;
+    if (res && a.residual_early && h < H) r = bf16_bits_to_f32(res[o]);
+    pdl_wait();
+    pdl_launch_dependents();
+    if (h >= H) return;
+    if (res && !a.residual_early) r = bf16_bits_to_f32(res[o]);
+    float v = 0.0f;
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) pos[k] = s.inv_pos[t * kTopK + k];
-    for (int h = blockIdx.x * blockDim.x + threadIdx.x; h < H; h += gridDim.x * blockDim.x) {
-        float v = 0.0f;
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k)
-            if (pos[k] >= 0) v += s.ypart[(size_t)pos[k] * H + h];
-        if (a.shared_here) v += s.ypart[(size_t)(T * kTopK + t) * H + h];
-        const size_t o = (size_t)t * H + h;
-        if (a.residual) v += bf16_bits_to_f32(static_cast<const uint16_t *>(a.residual)[o]);
-        if (a.out_f32)
-            static_cast<float *>(a.out)[o] = v;
-        else
-            static_cast<uint16_t *>(a.out)[o] = f32_to_bf16_bits(v);
+    for (int k = 0; k < kTopK; ++k) {
+        const int p = s.inv_pos[t * kTopK + k];
+        if (p >= 0) v += s.ypart[(size_t)p * H + h];
     }
+    if (a.shared_here) v += s.ypart[(size_t)(T * kTopK + t) * H + h];
+    if (res) v += r;
+    if (a.out_f32)
+        static_cast<float *>(a.out)[o] = v;
+    else
+        static_cast<uint16_t *>(a.out)[o] = f32_to_bf16_bits(v);
 }
 
 // --------------------------------------------------------------- launches
