@@ -141,28 +141,29 @@ __global__ void __launch_bounds__(kThreads, 1)
         prefetch_tensormap(&tm_us);
     }
     __syncthreads();
-    pdl_wait();  // the routing kernel's outputs are read from here on
-    pdl_launch_dependents();
     const int H = a.H, I = a.I, E = a.E;
-    // Output-tile tickets of the down kernel that follows (which reads them
-    // only after this grid completes).
-    if (blockIdx.x == 0)
-        for (int i = threadIdx.x; i < H / kDnRows; i += blockDim.x) s.tile_count[i] = 0u;
-    const int nact = *s.n_active;
     const int mtiles = I / kGuRows;
-    const int items = nact * mtiles;
     const int kboxes = (H + kBoxK - 1) / kBoxK;
     const int slices = (kboxes + BOXES - 1) / BOXES;
     constexpr int kSK = BOXES * kBoxK;
     constexpr uint32_t kTx = 2 * Cfg::kPacked + 2 * Cfg::kScales;
 
     if (warp == kConsumerWarps) {
+        pdl_wait();  // the routing kernel's outputs are read from here on
+        pdl_launch_dependents();
+        // Output-tile tickets of the down kernel that follows (which reads
+        // them only after this grid completes).
+        if (blockIdx.x == 0)
+            for (int i = lane; i < H / kDnRows; i += 32) s.tile_count[i] = 0u;
         // Metadata is prefetched one item ahead and the token ids of a
         // group are held in registers, so no global load sits between two
-        // stage refills.
-        uint32_t it = 0;
+        // stage refills. The first item's table entries are requested
+        // together with the item count (an entry past the count is never
+        // used).
         ItemMeta nxt{};
-        if (blockIdx.x < items) nxt = load_item(s, blockIdx.x, mtiles);
+        if ((int)blockIdx.x < (E + 1) * mtiles) nxt = load_item(s, blockIdx.x, mtiles);
+        const int items = *s.n_active * mtiles;
+        uint32_t it = 0;
         for (int item = blockIdx.x; item < items; item += gridDim.x) {
             const ItemMeta cur = nxt;
             if (item + (int)gridDim.x < items) nxt = load_item(s, item + gridDim.x, mtiles);
@@ -215,23 +216,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t it = 0;
     ItemMeta nxt{};
     float nx_gate = 0.0f, nx_up = 0.0f;
-    if (blockIdx.x < items) {
-        nxt = load_item(s, blockIdx.x, mtiles);
-        nx_gate = a.inv_scales[nxt.e];
-        nx_up = a.inv_scales[(E + 1) + nxt.e];
-    }
-    for (int item = blockIdx.x; item < items; item += gridDim.x) {
-        const ItemMeta cur = nxt;
-        const float inv_gate = nx_gate, inv_up = nx_up;
-        if (item + (int)gridDim.x < items) {
-            nxt = load_item(s, item + gridDim.x, mtiles);
-            nx_gate = a.inv_scales[nxt.e];
-            nx_up = a.inv_scales[(E + 1) + nxt.e];
+    int items = 0;
+    // Round item = -1 runs before the wait on the routing kernel: one slice
+    // of the product code below over stage 0's uninitialised bytes, waiting
+    // for no barrier and storing nothing, its sums dropped. The code then
+    // sits in the SM's instruction cache when the first real slice lands
+    // (fetching it cold from DRAM cost ~3 us of a one-token call).
+    for (int item = -1; item < items; item = item < 0 ? (int)blockIdx.x : item + (int)gridDim.x) {
+        const bool warm = item < 0;
+        ItemMeta cur{};
+        float inv_gate = 0.0f, inv_up = 0.0f;
+        if (!warm) {
+            cur = nxt;
+            inv_gate = nx_gate;
+            inv_up = nx_up;
+            if (item + (int)gridDim.x < items) {
+                nxt = load_item(s, item + gridDim.x, mtiles);
+                nx_gate = a.inv_scales[nxt.e];
+                nx_up = a.inv_scales[(E + 1) + nxt.e];
+            }
         }
         const int mt = cur.mt;
-        const int tstart = cur.tstart, ntok = cur.ntok;
+        const int tstart = cur.tstart, ntok = warm ? 1 : cur.ntok;
+        const int nsl = warm ? 1 : slices;
         for (int tg = 0; tg < ntok; tg += NT * 8) {
-            const int ncols = min(NT * 8, ntok - tg);
+            const int ncols = warm ? NT * 8 : min(NT * 8, ntok - tg);
             // Two accumulators per projection (k-slot halves) halve the
             // dependent MMA chains; they are added once per token group.
             float cg[NT][4], cu[NT][4], cg2[NT][4], cu2[NT][4];
@@ -240,14 +249,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int r = 0; r < 4; ++r) cg[n][r] = cu[n][r] = cg2[n][r] = cu2[n][r] = 0.0f;
 
-            for (int sl = 0; sl < slices; ++sl, ++it) {
+            for (int sl = 0; sl < nsl; ++sl, ++it) {
                 const int st = it % S;
                 const uint32_t ph = (it / S) & 1u;
                 // After a failed wait the warp keeps walking the loops (without
                 // waiting or computing) so the named barriers below still see
                 // all four consumer warps.
                 if (failed) continue;
-                if (!mbar_wait(full + st, ph, err, kSiteGateUpFull)) {
+                if (!warm && !mbar_wait(full + st, ph, err, kSiteGateUpFull)) {
                     publish_timeout(s);
                     failed = true;
                     continue;
@@ -299,8 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(empty + st);
+                if (!warm && lane == 0) mbar_arrive(empty + st);
             }
+            if (warm) break;
 #pragma unroll
             for (int n = 0; n < NT; ++n)
 #pragma unroll
@@ -338,6 +348,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
             named_barrier(1, kConsumerWarps * 32);
+        }
+        if (warm) {
+            pdl_wait();  // the routing kernel's outputs are read from here on
+            pdl_launch_dependents();
+            items = *s.n_active * mtiles;
+            it = 0;
+            if (blockIdx.x < items) {
+                nxt = load_item(s, blockIdx.x, mtiles);
+                nx_gate = a.inv_scales[nxt.e];
+                nx_up = a.inv_scales[(E + 1) + nxt.e];
+            }
         }
     }
 }
@@ -383,18 +404,38 @@ __global__ void __launch_bounds__(kThreads, 1)
         s_flag[0] = 0;
     }
     __syncthreads();
-    pdl_wait();  // routing tables and gate/up activations are read from here on
-    pdl_launch_dependents();
     const int H = a.H, I = a.I;
-    const int nact = *s.n_active;
     const int rtiles = H / kDnRows;
-    const int items = nact * rtiles;
     const int kboxes = (I + kBoxK - 1) / kBoxK;
     const int slices = (kboxes + BOXES - 1) / BOXES;
     constexpr int kSK = BOXES * kBoxK;
     constexpr uint32_t kTx = Cfg::kPacked + Cfg::kScales;
 
     if (warp == kConsumerWarps) {
+        // The routing tables are complete when this grid starts: the gate/up
+        // grid triggers its dependents only after its own wait on the
+        // routing kernel. So the weight tiles of the first S stages (which no
+        // kernel of the call writes) are requested before the wait on the
+        // gate/up grid; the activation rows it writes are copied after it.
+        const int items = *s.n_active * rtiles;
+        auto load_weights = [&](int st, int y, int sl) {
+            uint8_t *stage = smem + st * Cfg::kStage;
+            mbar_arrive_expect_tx(full + st, kTx);
+            for (int b = 0; b < BOXES; ++b)
+                tma_load_2d(stage + b * kDnRows * kBoxBytes, &tm_dp, full + st, (sl * BOXES + b) * kBoxBytes, y);
+            tma_load_2d(stage + Cfg::kPacked, &tm_ds, full + st, sl * BOXES * 16, y);
+        };
+        uint32_t pre = 0;  // stages whose weights are already requested (all start empty)
+        if (lane == 0)
+            for (int item = blockIdx.x; item < items && pre < (uint32_t)S; item += gridDim.x) {
+                const ItemMeta m = load_item(s, item, rtiles);
+                for (int tg = 0; tg < m.ntok && pre < (uint32_t)S; tg += NT * 8)
+                    for (int sl = 0; sl < slices && pre < (uint32_t)S; ++sl, ++pre)
+                        load_weights((int)pre, m.e * H + m.mt * kDnRows, sl);
+            }
+        pre = __shfl_sync(0xffffffffu, pre, 0);
+        pdl_wait();  // the gate/up activations are read from here on
+        pdl_launch_dependents();
         uint32_t it = 0;
         ItemMeta nxt{};
         if (blockIdx.x < items) nxt = load_item(s, blockIdx.x, rtiles);
@@ -408,19 +449,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int sl = 0; sl < slices; ++sl, ++it) {
                     const int st = it % S;
                     const uint32_t ph = (it / S) & 1u;
-                    int ok = 1;
-                    if (lane == 0) ok = mbar_wait(empty + st, ph ^ 1u, err, kSiteDownEmpty) ? 1 : 0;
-                    if (!__shfl_sync(0xffffffffu, ok, 0)) {
-                        if (lane == 0) publish_timeout(s);
-                        return;
-                    }
                     uint8_t *stage = smem + st * Cfg::kStage;
-                    if (lane == 0) {
-                        mbar_arrive_expect_tx(full + st, kTx);
-                        for (int b = 0; b < BOXES; ++b)
-                            tma_load_2d(stage + b * kDnRows * kBoxBytes, &tm_dp, full + st,
-                                        (sl * BOXES + b) * kBoxBytes, y);
-                        tma_load_2d(stage + Cfg::kPacked, &tm_ds, full + st, sl * BOXES * 16, y);
+                    if (it >= pre) {
+                        int ok = 1;
+                        if (lane == 0) ok = mbar_wait(empty + st, ph ^ 1u, err, kSiteDownEmpty) ? 1 : 0;
+                        if (!__shfl_sync(0xffffffffu, ok, 0)) {
+                            if (lane == 0) publish_timeout(s);
+                            return;
+                        }
+                        if (lane == 0) load_weights(st, y, sl);
                     }
                     uint8_t *tok = stage + Cfg::kPacked + Cfg::kScales;
                     const int per_row = kSK / 8;
@@ -438,6 +475,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         return;
     }
 
+    pdl_wait();  // routing tables and gate/up activations are read from here on
+    pdl_launch_dependents();
+    const int nact = *s.n_active;
+    const int items = nact * rtiles;
     const int g = lane >> 2, c = lane & 3;
     const int r0 = warp * 16 + g, r1 = r0 + 8;
     uint32_t it = 0;
