@@ -237,6 +237,19 @@ def _tensor_ptr(tensor) -> C.c_void_p:
     return C.c_void_p(tensor.data_ptr())
 
 
+_BF16 = None
+
+
+def _torch_bf16():
+    """torch.bfloat16, imported on first use (the numpy-only paths never import torch)."""
+    global _BF16
+    if _BF16 is None:
+        import torch
+
+        _BF16 = torch.bfloat16
+    return _BF16
+
+
 class DeviceBuffer:
     def __init__(self, runtime: "Runtime", handle: C.c_void_p, bytes_: int):
         self.runtime = runtime
@@ -441,6 +454,8 @@ class MoeBank:
         x, residual and out are CPU BF16 torch tensors [tokens, hidden] (pinned
         for asynchronous copies) or uint16/int16 numpy arrays of BF16 bits.
         Returns out once the result is in it."""
+        # Called once per layer call on the end-to-end path: each check is one
+        # attribute read, and pointers go to ctypes as plain integers.
         def host_ptr(a, name):
             if a is None:
                 return None, None
@@ -448,13 +463,12 @@ class MoeBank:
                 if a.dtype not in (np.uint16, np.int16) or a.ndim != 2 or a.shape[1] != self.hidden \
                         or not a.flags.c_contiguous:
                     raise ValueError(f"{name} must be contiguous BF16 bits [tokens, hidden]")
-                return C.c_void_p(a.ctypes.data), a.shape[0]
-            import torch
-
-            if a.dtype != torch.bfloat16 or a.is_cuda or a.dim() != 2 or a.shape[1] != self.hidden \
+                return a.ctypes.data, a.shape[0]
+            shape = a.shape
+            if a.dtype is not _torch_bf16() or len(shape) != 2 or shape[1] != self.hidden or a.is_cuda \
                     or not a.is_contiguous():
                 raise ValueError(f"{name} must be a contiguous CPU bfloat16 tensor [tokens, hidden]")
-            return C.c_void_p(a.data_ptr()), a.shape[0]
+            return a.data_ptr(), shape[0]
 
         xp, T = host_ptr(x, "x")
         if out is None:
