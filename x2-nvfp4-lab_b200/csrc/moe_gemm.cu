@@ -449,6 +449,336 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (threadIdx.x == 0 && *reinterpret_cast<volatile int *>(err) != 0) report(s);
 }
 
+// ------------------------------------------- down GEMM, activations resident
+//
+// The down GEMM's reduction is short (K = I = 512), so a column tile's whole
+// activation operand -- J terms x 128 slot rows x K codes, with its scale
+// factors -- fits in shared memory and tensor memory. Each CTA takes a
+// contiguous range of (column tile, weight-row tile) pairs in column-tile-
+// major order, loads each of its two or three column tiles once, and streams
+// only the weight tiles (128 rows x K codes and their atoms) through an
+// S-stage ring; moe_gemm_kernel<1> reloads the activation tiles for every
+// weight-row tile. Roles as in moe_gemm_kernel; the MMAs of a tile run in
+// its order (K step, then term), so the outputs are the same bits.
+//   shared memory: A [J][KB] 16 KB boxes | A atoms [J][4 KB] | S x (W [KB]
+//                  16 KB boxes | W atoms [KB*4][512 B]) | barriers
+//   tensor memory: accumulators 2 x 128 columns | A scale factors J x 16 KB
+//                  columns | W scale factors S x 16 KB columns
+template <int J, int KB, int S>
+struct DownResCfg {
+    static constexpr int kAtomsA = 4 * KB;                   // per term (K / 64)
+    static constexpr int kA = J * KB * kTileBytes;
+    static constexpr int kASf = J * kAtomsA * 512;
+    static constexpr int kW = KB * kTileBytes;
+    static constexpr int kWSf = kAtomsA * 512;
+    static constexpr int kStage = kW + kWSf;
+    static constexpr int kColA = 256;
+    static constexpr int kColW = kColA + J * KB * 16;
+    static constexpr int kColsUsed = kColW + S * KB * 16;
+    static constexpr size_t kBarOff = (size_t)kA + kASf + (size_t)S * kStage;
+    static constexpr size_t kSmem = 1024 + kBarOff + 1024;
+    static_assert(kA % 1024 == 0 && kASf % 1024 == 0 && kStage % 1024 == 0, "1024-byte tile alignment");
+    static_assert(kColsUsed <= 512, "tensor memory overflow");
+    static_assert(kSmem <= 232448, "shared memory overflow");
+    static_assert(KB == 2, "the scale-factor stores write eight atoms (32 columns) at a time");
+};
+
+template <int J, int KB, int S>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    moe_down_resident_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_act,
+                             GemmArgs a) {
+    using Cfg = DownResCfg<J, KB, S>;
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = align1024(smem_raw);
+    uint8_t *a_tiles = smem;
+    uint8_t *a_atoms = smem + Cfg::kA;
+    uint8_t *w_stages = a_atoms + Cfg::kASf;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + Cfg::kBarOff);
+    uint64_t *w_full = bars;              // [S] weight tiles landed (producer arrive + bytes)
+    uint64_t *w_empty = w_full + S;       // [S] MMAs of the stage committed
+    uint64_t *w_sf_in = w_empty + S;      // [S] weight atoms landed
+    uint64_t *w_sf_full = w_sf_in + S;    // [S] weight atoms in tensor memory (4 store warps)
+    uint64_t *a_full = w_sf_full + S;     // activation tiles landed
+    uint64_t *a_empty = a_full + 1;       // MMAs of the column tile committed
+    uint64_t *a_sf_in = a_empty + 1;      // activation atoms landed
+    uint64_t *a_sf_full = a_sf_in + 1;    // activation atoms in tensor memory
+    uint64_t *acc_full = a_sf_full + 1;   // [2]
+    uint64_t *acc_empty = acc_full + 2;   // [2]
+    uint64_t *drain = acc_empty + 2;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+    int *acc_ok = reinterpret_cast<int *>(tmem_slot + 1);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const PrefillScratch &s = a.s;
+    int *err = s.error;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < S; ++i) {
+            mbar_init(w_full + i, 1);
+            mbar_init(w_empty + i, 1);
+            mbar_init(w_sf_in + i, 1);
+            mbar_init(w_sf_full + i, 4);
+        }
+        mbar_init(a_full, 1);
+        mbar_init(a_empty, 1);
+        mbar_init(a_sf_in, 1);
+        mbar_init(a_sf_full, 4);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(acc_full + b, 1);
+            mbar_init(acc_empty + b, 1);
+        }
+        mbar_init(drain, 1);
+        fence_barrier_init();
+        prefetch_tensormap(&tm_w);
+        prefetch_tensormap(&tm_act);
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    pdl_wait();  // routing tables and activation terms are read from here on
+    pdl_launch_dependents();
+
+    const int mtiles = a.M / kPrefillTileM;
+    const int total = *s.n_tiles * mtiles;
+    // This CTA's contiguous range of tiles (column-tile major).
+    const int lo = (int)(((long long)blockIdx.x * total) / gridDim.x);
+    const int hi = (int)(((long long)(blockIdx.x + 1) * total) / gridDim.x);
+    constexpr int kw = 4 * KB;  // 64-column K steps
+
+    if (warp == 0) {
+        // ------------------------------------------------------ producer
+        uint32_t wit = 0, an = 0;
+        int cur_ct = -1;
+        bool ok = true;
+        TileInfo mine{};
+        const int sf_blocks = s.max_rows / kPrefillTileN;
+        for (int tile = lo; tile < hi && ok; ++tile) {
+            const int k = (tile - lo) & 31;
+            if (k == 0) mine = batch_tiles(s, tile, 1, total, mtiles, lane);
+            const TileInfo ti = lane_tile(mine, k);
+            const int ct = tile / mtiles;
+            // The tile's weight stage first: the ring runs ahead into a new
+            // column tile while the previous one's MMAs finish.
+            const int st = wit % S;
+            const uint32_t ph = (wit / S) & 1u;
+            int okw = 1;
+            if (lane == 0) okw = mbar_wait(w_empty + st, ph ^ 1u, err, kSiteGemmEmpty) ? 1 : 0;
+            if (!__shfl_sync(0xffffffffu, okw, 0)) {
+                ok = false;
+                break;
+            }
+            if (lane == 0) {
+                uint8_t *stage = w_stages + (size_t)st * Cfg::kStage;
+                const int wrow = ti.e * a.M + ti.mt * kPrefillTileM;
+                mbar_arrive_expect_tx(w_sf_in + st, Cfg::kWSf);
+                bulk_g2s(stage + Cfg::kW, a.sfa[0] + (size_t)(wrow / kPrefillTileM) * kw * 512, Cfg::kWSf,
+                         w_sf_in + st);
+                mbar_arrive_expect_tx(w_full + st, Cfg::kW);
+#pragma unroll
+                for (int kb = 0; kb < KB; ++kb)
+                    tma_load_2d(stage + kb * kTileBytes, &tm_w, w_full + st, kb * 128, wrow);
+            }
+            ++wit;
+            if (ct != cur_ct) {
+                // The activation buffer (and its tensor-memory scale
+                // factors) is refilled once the previous column tile's MMAs
+                // have committed.
+                if (lane == 0 && an > 0) okw = mbar_wait(a_empty, (an - 1) & 1u, err, kSiteGemmEmpty) ? 1 : 0;
+                if (!__shfl_sync(0xffffffffu, okw, 0)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+                    mbar_arrive_expect_tx(a_sf_in, Cfg::kASf);
+#pragma unroll
+                    for (int j = 0; j < J; ++j)
+                        bulk_g2s(a_atoms + j * (kw * 512),
+                                 a.sfb + (size_t)(j * sf_blocks + ti.n0 / kPrefillTileN) * kw * 512, kw * 512, a_sf_in);
+                    mbar_arrive_expect_tx(a_full, Cfg::kA);
+#pragma unroll
+                    for (int j = 0; j < J; ++j)
+#pragma unroll
+                        for (int kb = 0; kb < KB; ++kb)
+                            tma_load_2d(a_tiles + (j * KB + kb) * kTileBytes, &tm_act, a_full, kb * 128,
+                                        j * a.Rb + ti.n0);
+                }
+                cur_ct = ct;
+                ++an;
+            }
+        }
+        if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
+            // Drain: wait for the copies of the last stages issued and of the
+            // last activation load.
+            if (lane == 0) {
+                const uint32_t first = wit > (uint32_t)S ? wit - S : 0u;
+                for (uint32_t q = first; q < wit; ++q) {
+                    mbar_wait_drain(w_full + (q % S), (q / S) & 1u);
+                    mbar_wait_drain(w_sf_in + (q % S), (q / S) & 1u);
+                }
+                if (an > 0) {
+                    mbar_wait_drain(a_full, (an - 1) & 1u);
+                    mbar_wait_drain(a_sf_in, (an - 1) & 1u);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------------------------------------------------- MMA
+        if (lane == 0) {
+            constexpr uint32_t idesc = tc::idesc_mxf4nvf4(kPrefillTileM);
+            const uint32_t a_base = smem_u32(a_tiles);
+            const uint32_t w_base = smem_u32(w_stages);
+            uint32_t wit = 0, tcount = 0, an = 0;
+            int cur_ct = -1;
+            bool ok = true;
+            for (int tile = lo; tile < hi && ok; ++tile, ++tcount) {
+                const int ct = tile / mtiles;
+                if (ct != cur_ct) {
+                    if (cur_ct >= 0) tc::commit(a_empty);
+                    if (!mbar_wait(a_full, an & 1u, err, kSiteGemmFull) ||
+                        !mbar_wait(a_sf_full, an & 1u, err, kSiteGemmFull)) {
+                        ok = false;
+                        break;
+                    }
+                    cur_ct = ct;
+                    ++an;
+                }
+                const uint32_t buf = tcount & 1u;
+                const uint32_t use = tcount >> 1;
+                if (use > 0 && !mbar_wait(acc_empty + buf, (use - 1) & 1u, err, kSiteGemmAccEmpty)) {
+                    ok = false;
+                    break;
+                }
+                const int st = wit % S;
+                const uint32_t ph = (wit / S) & 1u;
+                if (!mbar_wait(w_full + st, ph, err, kSiteGemmFull) ||
+                    !mbar_wait(w_sf_full + st, ph, err, kSiteGemmFull)) {
+                    ok = false;
+                    break;
+                }
+                tc::fence_after_sync();
+                tc::fence_proxy_async_smem();
+                const uint32_t dacc = tmem + buf * 128;
+                const uint32_t wb = w_base + (uint32_t)st * Cfg::kStage;
+                const uint32_t tsfw = tmem + Cfg::kColW + (uint32_t)st * (KB * 16);
+#pragma unroll
+                for (int kb = 0; kb < KB; ++kb) {
+#pragma unroll
+                    for (int at = 0; at < 4; ++at) {
+#pragma unroll
+                        for (int j = 0; j < J; ++j) {
+                            const uint32_t acc = (kb | at | j) != 0 ? 1u : 0u;
+                            const uint64_t adesc =
+                                tc::smem_desc_sw128(a_base + (uint32_t)(j * KB + kb) * kTileBytes + 32 * at);
+                            const uint64_t wdesc = tc::smem_desc_sw128(wb + (uint32_t)kb * kTileBytes + 32 * at);
+                            tc::mma_mxf4nvf4(dacc, adesc, wdesc, idesc,
+                                             tmem + Cfg::kColA + (uint32_t)(j * kw + 4 * kb + at) * 4,
+                                             tsfw + (uint32_t)(4 * kb + at) * 4, acc);
+                        }
+                    }
+                }
+                tc::commit(w_empty + st);
+                tc::commit(acc_full + buf);
+                ++wit;
+            }
+            // Every MMA of this CTA has completed before tensor memory is freed.
+            tc::commit(drain);
+            mbar_wait_drain(drain, 0);
+        }
+        __syncwarp();
+    } else if (warp >= kSfWarp0) {
+        // ------------------------------------------------- scale factors
+        const uint32_t quarter = (uint32_t)(32 * (warp & 3)) << 16;
+        uint32_t wit = 0, an = 0;
+        int cur_ct = -1;
+        bool ok = true;
+        for (int tile = lo; tile < hi && ok; ++tile) {
+            const int ct = tile / mtiles;
+            if (ct != cur_ct) {
+                if (!__all_sync(0xffffffffu, mbar_wait(a_sf_in, an & 1u, err, kSiteGemmFull))) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int j = 0; j < J; ++j)
+                    tc::st_sf_atoms<8>(tmem + quarter + Cfg::kColA + (uint32_t)j * (kw * 4), a_atoms + j * (kw * 512),
+                                       512, lane);
+                tc::wait_st();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_sf_full);
+                cur_ct = ct;
+                ++an;
+            }
+            const int st = wit % S;
+            if (!__all_sync(0xffffffffu, mbar_wait(w_sf_in + st, (wit / S) & 1u, err, kSiteGemmFull))) {
+                ok = false;
+                break;
+            }
+            tc::st_sf_atoms<8>(tmem + quarter + Cfg::kColW + (uint32_t)st * (KB * 16),
+                               w_stages + (size_t)st * Cfg::kStage + Cfg::kW, 512, lane);
+            tc::wait_st();
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(w_sf_full + st);
+            ++wit;
+        }
+    } else {
+        // ----------------------------------------------------- epilogue
+        // As moe_gemm_kernel<1>: one slot row per thread, all 128 columns in
+        // registers before the accumulator is released, FP16 partials.
+        const int sub = warp & 3;
+        const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
+        const bool leader = threadIdx.x == 64;
+        uint32_t tcount = 0;
+        TileInfo mine{};
+        for (int tile = lo; tile < hi; ++tile, ++tcount) {
+            const int k = (tile - lo) & 31;
+            if (k == 0) mine = batch_tiles(s, tile, 1, total, mtiles, lane);
+            const TileInfo ti = lane_tile(mine, k);
+            const int r = 32 * sub + lane;
+            const bool valid = r < ti.nvalid;
+            const int p = ti.n0 + r;
+            float cs = 0.0f;
+            if (valid) cs = s.coef[p] * s.ga[p];
+            const uint32_t buf = tcount & 1u;
+            if (leader) *acc_ok = mbar_wait(acc_full + buf, (tcount >> 1) & 1u, err, kSiteGemmAccFull) ? 1 : 0;
+            named_barrier(1, 128);
+            if (!*reinterpret_cast<volatile int *>(acc_ok)) break;
+            tc::fence_after_sync();
+            uint32_t acc[kPrefillTileM];
+#pragma unroll
+            for (int q = 0; q < kPrefillTileM / 32; ++q)
+                tc::ld_32x32b_x32(lane_base + buf * 128 + 32 * q, *reinterpret_cast<uint32_t(*)[32]>(acc + 32 * q));
+            tc::wait_ld();
+            tc::fence_before_sync();
+            named_barrier(1, 128);
+            if (leader) mbar_arrive(acc_empty + buf);
+            if (valid) {
+                uint4 *dst = reinterpret_cast<uint4 *>(s.ypart + (size_t)p * a.M + ti.mt * kPrefillTileM);
+#pragma unroll
+                for (int q = 0; q < kPrefillTileM / 8; ++q)
+                    dst[q] = make_uint4(
+                        pack_f16x2_sat(__uint_as_float(acc[8 * q + 0]) * cs, __uint_as_float(acc[8 * q + 1]) * cs),
+                        pack_f16x2_sat(__uint_as_float(acc[8 * q + 2]) * cs, __uint_as_float(acc[8 * q + 3]) * cs),
+                        pack_f16x2_sat(__uint_as_float(acc[8 * q + 4]) * cs, __uint_as_float(acc[8 * q + 5]) * cs),
+                        pack_f16x2_sat(__uint_as_float(acc[8 * q + 6]) * cs, __uint_as_float(acc[8 * q + 7]) * cs));
+            }
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, 512);
+    }
+    if (threadIdx.x == 0 && *reinterpret_cast<volatile int *>(err) != 0) report(s);
+}
+
 template <typename K>
 cudaError_t set_smem_once(K kernel, size_t bytes, std::atomic<uint64_t> &done) {
     int dev = 0;
@@ -482,6 +812,26 @@ cudaError_t launch_cfg(const CUtensorMap &a0, const CUtensorMap &a1, const CUten
     return cudaLaunchKernelEx(&cfg, moe_gemm_kernel<MODE, J, S>, a0, a1, b, a);
 }
 
+template <int J, int KB, int S>
+cudaError_t launch_down_res(const CUtensorMap &w, const CUtensorMap &act, const GemmArgs &a, int grid,
+                            cudaStream_t stream) {
+    using Cfg = DownResCfg<J, KB, S>;
+    static std::atomic<uint64_t> done{0};
+    cudaError_t err = set_smem_once(moe_down_resident_kernel<J, KB, S>, Cfg::kSmem, done);
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, moe_down_resident_kernel<J, KB, S>, w, act, a);
+}
+
 int gemm_grid(const GemmArgs &a, int sms) {
     const long long coltiles = (long long)a.s.max_tiles;
     const long long tiles = coltiles * (a.M / kPrefillTileM);
@@ -505,6 +855,17 @@ cudaError_t launch_gemm_gate_up(const PrefillMaps &m, const GemmArgs &a, int sms
 cudaError_t launch_gemm_down(const PrefillMaps &m, const GemmArgs &a, int sms, cudaStream_t stream) {
     if (a.K % kStageK != 0 || a.M % kPrefillTileM != 0) return cudaErrorInvalidValue;
     const int grid = gemm_grid(a, sms);
+    // K = 512 (the shape's intermediate size): the column tile's activation
+    // terms stay resident for all of its weight-row tiles.
+    if (a.K == 2 * kStageK) {
+        switch (a.J) {
+            case 1: return launch_down_res<1, 2, 5>(m.w[2], m.aq, a, grid, stream);
+            case 2: return launch_down_res<2, 2, 4>(m.w[2], m.aq, a, grid, stream);
+            case 3: return launch_down_res<3, 2, 3>(m.w[2], m.aq, a, grid, stream);
+            case 4: return launch_down_res<4, 2, 2>(m.w[2], m.aq, a, grid, stream);
+            default: return cudaErrorInvalidValue;
+        }
+    }
     switch (a.J) {
         case 1: return launch_cfg<1, 1, 6>(m.w[2], m.w[2], m.aq, a, grid, stream);
         case 2: return launch_cfg<1, 2, 4>(m.w[2], m.w[2], m.aq, a, grid, stream);
