@@ -453,6 +453,226 @@ __global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_kernel(Prefi
     }
 }
 
+// prefill_select_kernel with the token held in registers: lane l keeps its
+// CH column chunks of x (columns 128q + 4l .. +3, the order of the exact
+// logit), so x is read once per token instead of once per group of four
+// exact rows; the weight loads of four chunks of four rows are in flight
+// together; the shared gate's row is the last entry of the row list
+// (candidates, then row E) instead of a separate pass; the softmax
+// exponentials run one per lane. Every rounded operation and every
+// summation order is the one of prefill_select_kernel, so the ids, weights
+// and gates are the same bits (the rare overflow case, more than
+// kMaxCandidates candidates, runs prefill_select_kernel's streaming loop).
+template <int CH>
+__global__ void __launch_bounds__(kSelectWarps * 32) prefill_select_reg_kernel(PrefillRouteArgs a, PrefillScratch s,
+                                                                              int Rp) {
+    __shared__ int s_cand[kSelectWarps][kMaxCandidates];
+    __shared__ float s_val[kSelectWarps][kMaxCandidates];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * kSelectWarps + warp;
+    if (t >= a.T) return;
+    const int E = a.E, H = a.H;
+    const uint16_t *x = a.x + (size_t)t * H;
+
+    uint2 xr[CH];
+#pragma unroll
+    for (int q = 0; q < CH; ++q) xr[q] = __ldg(reinterpret_cast<const uint2 *>(x + 128 * q + 4 * lane));
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        float val = -FLT_MAX;
+        if (e < E) {
+            val = s.approx[(size_t)t * Rp + e];
+            if (a.bias) val += a.bias[e];
+        }
+        v[i] = val;
+    }
+    // 8th largest approximate logit.
+    float a8 = -FLT_MAX;
+    {
+        unsigned taken = 0;
+#pragma unroll 1
+        for (int slot = 0; slot < kTopK; ++slot) {
+            float bv = -FLT_MAX;
+            int bi = -1;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (!((taken >> i) & 1u) && lane + 32 * i < E && (bi < 0 || v[i] > bv)) {
+                    bv = v[i];
+                    bi = i;
+                }
+            const unsigned key = bi < 0 ? 0u : float_order_key(bv);
+            const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+            const unsigned owner = __ffs(__ballot_sync(0xffffffffu, key == kmax && bi >= 0)) - 1;
+            if (lane == (int)owner) taken |= 1u << bi;
+            a8 = __shfl_sync(0xffffffffu, bv, owner);
+        }
+    }
+    // |x| for the margin (the same per-lane partial sums and butterfly).
+    float ss = 0.0f;
+#pragma unroll
+    for (int q = 0; q < CH; ++q) {
+        const float x0 = bf16_bits_to_f32(xr[q].x & 0xFFFFu), x1 = bf16_bits_to_f32(xr[q].x >> 16);
+        const float x2 = bf16_bits_to_f32(xr[q].y & 0xFFFFu), x3 = bf16_bits_to_f32(xr[q].y >> 16);
+        ss += x0 * x0 + x1 * x1 + x2 * x2 + x3 * x3;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float delta = kMarginPerColumn * (float)H * a.wnorm_max * sqrtf(ss) * 1.0001f + 1e-30f;
+    const float thresh = a8 - 2.0f * delta;
+
+    int n = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int e = lane + 32 * i;
+        const bool cand = e < E && v[i] >= thresh;
+        const unsigned m = __ballot_sync(0xffffffffu, cand);
+        const int idx = n + __popc(m & ((1u << lane) - 1u));
+        if (cand && idx < kMaxCandidates) s_cand[warp][idx] = e;
+        n += __popc(m);
+    }
+    if (n > kMaxCandidates) {
+        float top_v[kTopK];
+        int top_i[kTopK];
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) {
+            top_v[k] = -FLT_MAX;
+            top_i[k] = 0x7fffffff;
+        }
+        for (int e = 0; e < E; ++e) {
+            float val = exact_logit(a.router + (size_t)e * H, x, H, lane);
+            if (a.bias) val = __fadd_rn(val, a.bias[e]);
+            if (val > top_v[kTopK - 1]) {
+                int p = kTopK - 1;
+                while (p > 0 && val > top_v[p - 1]) {
+                    top_v[p] = top_v[p - 1];
+                    top_i[p] = top_i[p - 1];
+                    --p;
+                }
+                top_v[p] = val;
+                top_i[p] = e;
+            }
+        }
+        const float sl_o = exact_logit(a.router + (size_t)E * H, x, H, lane);
+        if (lane == 0) {
+            float den = 0.0f;
+#pragma unroll
+            for (int slot = 0; slot < kTopK; ++slot) den += expf(top_v[slot] - top_v[0]);
+            for (int slot = 0; slot < kTopK; ++slot) {
+                s.ids[t * kSlots + slot] = top_i[slot];
+                s.weights[t * kSlots + slot] = expf(top_v[slot] - top_v[0]) / den;
+            }
+            s.ids[t * kSlots + kTopK] = E;
+            s.weights[t * kSlots + kTopK] = 1.0f / (1.0f + expf(-sl_o));
+        }
+        if (lane < kTopK) {
+            const int e = top_i[lane];
+            atomicOr(&s.blk_mask[(size_t)e * s.mask_stride + (t >> 6)], 1ull << (t & 63));
+        }
+        return;
+    }
+    __syncwarp();
+    // Exact logits of the candidates, then of row E (the shared gate), four
+    // rows at a time.
+    float sl = 0.0f;
+#pragma unroll 1
+    for (int i0 = 0; i0 <= n; i0 += 4) {
+        int rows[4];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) rows[r] = i0 + r < n ? s_cand[warp][i0 + r] : E;
+        float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int q0 = 0; q0 < CH; q0 += 4) {
+            uint2 wv[4][4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r)
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+                    wv[r][u] = __ldg(reinterpret_cast<const uint2 *>(a.router + (size_t)rows[r] * H + 128 * (q0 + u) +
+                                                                     4 * lane));
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const uint2 xv = xr[q0 + u];
+                const float x0 = bf16_bits_to_f32(xv.x & 0xFFFFu), x1 = bf16_bits_to_f32(xv.x >> 16);
+                const float x2 = bf16_bits_to_f32(xv.y & 0xFFFFu), x3 = bf16_bits_to_f32(xv.y >> 16);
+#pragma unroll
+                for (int r = 0; r < 4; ++r) {
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv[r][u].x & 0xFFFFu), x0));
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv[r][u].x >> 16), x1));
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv[r][u].y & 0xFFFFu), x2));
+                    acc[r] = __fadd_rn(acc[r], __fmul_rn(bf16_bits_to_f32(wv[r][u].y >> 16), x3));
+                }
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1)
+                acc[r] = __fadd_rn(acc[r], __shfl_xor_sync(0xffffffffu, acc[r], off));
+            if (i0 + r < n) {
+                float v2 = acc[r];
+                if (a.bias) v2 = __fadd_rn(v2, a.bias[rows[r]]);
+                if (lane == 0) s_val[warp][i0 + r] = v2;
+            } else if (i0 + r == n) {
+                sl = acc[r];
+            }
+        }
+    }
+    __syncwarp();
+    // Top-8 of the candidates (lane holds candidates lane and lane + 32);
+    // lane `slot` keeps the slot-th pick.
+    float cv[2];
+    int ci[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int idx = lane + 32 * h;
+        cv[h] = idx < n ? s_val[warp][idx] : -FLT_MAX;
+        ci[h] = idx < n ? s_cand[warp][idx] : 0x7fffffff;
+    }
+    float my_v = 0.0f, top0 = 0.0f;
+    int my_i = 0;
+#pragma unroll 1
+    for (int slot = 0; slot < kTopK; ++slot) {
+        float bv = -FLT_MAX;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+            if (ci[h] != 0x7fffffff && (cv[h] > bv || (cv[h] == bv && ci[h] < bi))) {
+                bv = cv[h];
+                bi = ci[h];
+            }
+        const unsigned key = bi == 0x7fffffff ? 0u : float_order_key(bv);
+        const unsigned kmax = __reduce_max_sync(0xffffffffu, key);
+        const unsigned imin = __reduce_min_sync(0xffffffffu, key == kmax ? (unsigned)bi : 0xffffffffu);
+        const int owner_h = (ci[0] == (int)imin) ? 0 : 1;
+        const bool mine = (ci[0] == (int)imin) || (ci[1] == (int)imin);
+        const unsigned ob = __ballot_sync(0xffffffffu, mine);
+        const int owner = __ffs(ob) - 1;
+        const float val = __shfl_sync(0xffffffffu, mine ? cv[owner_h] : 0.0f, owner);
+        if (mine) ci[owner_h] = 0x7fffffff;
+        if (slot == 0) top0 = val;
+        if (lane == slot) {
+            my_v = val;
+            my_i = (int)imin;
+        }
+    }
+    // Softmax over the picks relative to the largest, the denominator added
+    // in slot order; one exponential per lane.
+    const float my_e = lane < kTopK ? expf(my_v - top0) : 0.0f;
+    float den = 0.0f;
+#pragma unroll
+    for (int slot = 0; slot < kTopK; ++slot) den += __shfl_sync(0xffffffffu, my_e, slot);
+    if (lane < kTopK) {
+        s.ids[t * kSlots + lane] = my_i;
+        s.weights[t * kSlots + lane] = my_e / den;
+        atomicOr(&s.blk_mask[(size_t)my_i * s.mask_stride + (t >> 6)], 1ull << (t & 63));
+    } else if (lane == kTopK) {
+        s.ids[t * kSlots + kTopK] = E;
+        s.weights[t * kSlots + kTopK] = 1.0f / (1.0f + expf(-sl));
+    }
+}
+
 // Exclusive prefix sum over the 256 threads of a CTA; *total gets the sum.
 __device__ __forceinline__ int block_excl_scan256(int v, int *warp_sums, int *total) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -921,7 +1141,15 @@ cudaError_t launch_prefill_route(const PrefillRouteArgs &a, const PrefillScratch
         prefill_logits_kernel<<<dim3((a.T + kLogitsTile - 1) / kLogitsTile, (R + kLogitsTile - 1) / kLogitsTile), 128,
                                 smem, stream>>>(a, s.approx, Rp);
     } else if (part == 1) {
-        prefill_select_kernel<<<(a.T + kSelectWarps - 1) / kSelectWarps, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
+        const int blocks = (a.T + kSelectWarps - 1) / kSelectWarps;
+        if (a.H == 2048)
+            prefill_select_reg_kernel<16><<<blocks, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
+        else if (a.H == 1024)
+            prefill_select_reg_kernel<8><<<blocks, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
+        else if (a.H == 512)
+            prefill_select_reg_kernel<4><<<blocks, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
+        else
+            prefill_select_kernel<<<blocks, kSelectWarps * 32, 0, stream>>>(a, s, Rp);
     } else {
         prefill_scan_kernel<<<a.E, 256, 0, stream>>>(s, a.T);
         err = cudaGetLastError();
