@@ -176,6 +176,31 @@ def test_forward_host_buffer_kinds(cuda_runtime, wide_bank, wide_host, T):
     assert bool((r_big[:2] == -3.0).all()) and bool((r_big[2 + T:] == -3.0).all())
 
 
+@pytest.mark.parametrize("T", [4, 40, 100])
+def test_forward_host_pre_norm(cuda_runtime, wide_bank, wide_host, T):
+    """The host forward with the bank's RMSNorm applied first gives the device
+    forward's bits: fused into routing (4 tokens, pinned dst written by the
+    combine kernel), a separate normalisation into the staged output rows
+    (40 tokens), and the prefill path (100 tokens)."""
+    import torch
+
+    H = wide_host.hidden
+    g = torch.Generator().manual_seed(2100 + T)
+    weight = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).cuda()
+    wide_bank.set_pre_norm(weight, 1e-6)
+    xbits = synthetic_np.tokens_bf16(T, H, 2200 + T)
+    rbits = synthetic_np.tokens_bf16(T, H, 2300 + T)
+    x, r = bits_to_bf16_tensor(xbits), bits_to_bf16_tensor(rbits)
+    want = wide_bank.forward(x, residual=r, pre_norm=True)
+    torch.cuda.synchronize()
+    want = want.cpu().view(torch.int16).numpy()
+    hx = torch.from_numpy(xbits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    hr = torch.from_numpy(rbits.view(np.int16)).view(torch.bfloat16).pin_memory()
+    for out in (torch.empty(T, H, dtype=torch.bfloat16).pin_memory(), torch.empty(T, H, dtype=torch.bfloat16)):
+        wide_bank.forward_host(hx, residual=hr, out=out, pre_norm=True)
+        np.testing.assert_array_equal(out.view(torch.int16).numpy(), want)
+
+
 def test_forward_more_than_64_tokens(cuda_runtime, small_bank, small_host):
     import torch
 
