@@ -483,6 +483,7 @@ def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmu
     refs = {name: bank.forward(x, residual=r).float() for name, (x, r) in data.items()}
     torch.cuda.synchronize()
     finalize = lambda t: rt.finalize_bf16(t)  # noqa: E731
+    align_buf = torch.zeros(1, device="cuda")
     layers = {"nccl_all_reduce": ExpertParallelLayer(bank, finalize),
               "fused_combine_p2p": ExpertParallelLayer(bank, finalize, fused_runtime=rt)}
     out = {"ranks": world, "experts_per_rank": layers["nccl_all_reduce"].range.count,
@@ -506,6 +507,9 @@ def ep_leg(rt, bank, stream, flush, pg, world: int, seed: int, steps: int, warmu
             ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n)]
             with torch.cuda.stream(stream):
                 torch.cuda._sleep(int(2e5) * n)
+                # Start every rank's first call together (both reductions
+                # synchronise the ranks at every call after that).
+                pg.all_reduce(align_buf)
                 for i in range(n):
                     flush()
                     ev[i][0].record(stream)
@@ -570,7 +574,7 @@ def token_sharded_leg(bank, rt, pg, world: int, seed: int, T: int = 4096, calls:
                       f"{calls}, max over ranks"}
 
 
-def traced_steps(rt, stream, flush, step, n: int):
+def traced_steps(rt, stream, flush, step, n: int, align=None):
     """Run `step(i)` n times with the runtime trace on (L2 flushed before each
     step) and return the trace events: per-kernel device durations."""
     import torch
@@ -579,6 +583,8 @@ def traced_steps(rt, stream, flush, step, n: int):
     rt.set_trace_enabled(True)
     with torch.cuda.stream(stream):
         torch.cuda._sleep(int(2e5) * n)
+        if align is not None:
+            align()
         for i in range(n):
             flush()
             step(i)
@@ -667,6 +673,16 @@ def run_ours(args) -> int:
         pg.barrier()
     torch.cuda.synchronize()
 
+    # Under expert parallelism every step ends in the cross-rank exchange, so
+    # a rank's first timed step would also wait out the other ranks' host-side
+    # launch skew; one all-reduce on the stream after the spin kernel starts
+    # every rank's first step together (each step's exchange keeps them so).
+    align_buf = torch.zeros(1, device="cuda") if pg else None
+
+    def align():
+        if pg:
+            pg.all_reduce(align_buf)
+
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     # Clocks are sampled from the timed decode steps through the one-token and
@@ -677,6 +693,7 @@ def run_ours(args) -> int:
         # enqueue every step before the GPU reaches it, so each event
         # pair brackets device work only.
         torch.cuda._sleep(int(2e5) * args.steps)
+        align()
         for i in range(args.steps):
             flush()
             starts[i].record(stream)
@@ -690,6 +707,7 @@ def run_ours(args) -> int:
     wo_ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     with torch.cuda.stream(stream):
         torch.cuda._sleep(int(2e5) * args.steps)
+        align()
         for i in range(args.steps):
             flush(write_only=True)
             wo_starts[i].record(stream)
@@ -700,7 +718,7 @@ def run_ours(args) -> int:
     # Per-kernel durations come from a second, traced pass over the same steps
     # (tracing records an event pair around every kernel, which would also
     # serialise the dependent launches of the timed pass).
-    events = traced_steps(rt, stream, flush, step, args.steps)
+    events = traced_steps(rt, stream, flush, step, args.steps, align if pg else None)
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
