@@ -133,8 +133,6 @@ struct DecodeTcArgs {
     const float *inv_scales;  // [3][E+1]
     int E, H, I;
     int shared_last;          // 1: the shared expert is computed here (always the last active group)
-    int fuse_combine;         // down: the CTA finishing an output tile's last item also combines the tile
-    CombineOut comb;          // the combine's inputs and output (fuse_combine only)
     DecodeScratch s;
 };
 
