@@ -205,6 +205,7 @@ struct EpArgs {
     float *part[kMaxEpRanks];          // each rank's partial buffer of this call's parity, [T][H] FP32
     unsigned *flags_peer[kMaxEpRanks]; // each rank's flag array [world][tiles]
     unsigned *flags_local;             // this rank's flag array
+    unsigned *ticket;                  // this rank's tile count of the call (zero between calls)
     unsigned epoch;                    // call number, >= 1
     int rank, world, tiles;
     int *err;                          // device error word

@@ -3,11 +3,14 @@
 //    (NCCL all-reduce) has added NVFP4_MOE_PARTIAL_F32 partials;
 //  * moe_combine_ep_kernel: the decode combine fused with the reduction over
 //    NVLink peer memory. Every rank maps every other rank's partial buffer
-//    and flag array (CUDA IPC); a CTA computes its local partial tile, stores
-//    it, raises its flag in every peer's array, waits (bounded by wall-clock
-//    time) until every peer's flag for the same tile has arrived, and adds the
-//    ranks' tiles in rank order, so the transfer of one tile overlaps the
-//    others' arithmetic and every rank writes the same BF16 output.
+//    and flag array (CUDA IPC); a CTA computes its local partial tile and
+//    stores it; the rank's CTAs count their tiles in, and the last one makes
+//    them all visible to the peers with one system-scope fence and raises the
+//    rank's flag in every peer's array (a system-scope fence per tile cost
+//    ~14 us per call); every CTA then waits (bounded by wall-clock time) for
+//    every peer's flag with acquire loads and adds the ranks' tiles in rank
+//    order, so every rank writes the same BF16 output. One rank alone needs
+//    neither fence nor flag.
 // Partial buffers alternate between two parities by call number: a rank can
 // start call e+1 while a peer still reads its call-e tile, never call e+2
 // (that needs the peer's flags of call e+1, raised after its call e ended).
@@ -52,8 +55,10 @@ struct nvfp4_ep {
 namespace nvfp4 {
 namespace {
 
-__device__ __forceinline__ unsigned ld_volatile_u32(const unsigned *p) {
-    return *reinterpret_cast<const volatile unsigned *>(p);
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
 }
 
 __global__ void __launch_bounds__(256) moe_combine_ep_kernel(DownArgs a, EpArgs e) {
@@ -61,7 +66,6 @@ __global__ void __launch_bounds__(256) moe_combine_ep_kernel(DownArgs a, EpArgs 
     const DecodeScratch &s = a.s;
     const int H = a.H, T = a.T;
     const int t = blockIdx.y;
-    const int tile = blockIdx.y * gridDim.x + blockIdx.x;
     const int h = blockIdx.x * blockDim.x + threadIdx.x;
     __shared__ int s_ok;
     float v = 0.0f;
@@ -76,31 +80,39 @@ __global__ void __launch_bounds__(256) moe_combine_ep_kernel(DownArgs a, EpArgs 
         e.part[e.rank][(size_t)t * H + h] = v;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-        // Publish the tile, then collect every peer's.
-        __threadfence_system();
-        for (int p = 0; p < e.world; ++p)
-            if (p != e.rank) *reinterpret_cast<volatile unsigned *>(e.flags_peer[p] + e.rank * e.tiles + tile) = e.epoch;
-        int ok = *reinterpret_cast<volatile int *>(e.err) == 0;
-        const unsigned long long t0 = global_ns();
-        for (int p = 0; p < e.world && ok; ++p) {
-            if (p == e.rank) continue;
-            for (uint32_t i = 0;; ++i) {
-                if ((int)(ld_volatile_u32(e.flags_local + p * e.tiles + tile) - e.epoch) >= 0) break;
-                if ((i & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
-                    atomicCAS(e.err, 0, kSiteEpPeerTile);
-                    ok = 0;
-                    break;
+    if (e.world > 1) {
+        if (threadIdx.x == 0) {
+            // Publish: the last of this rank's CTAs to count its tile in
+            // releases them all (system scope) and raises the rank's flag in
+            // every peer's array (slot `rank`).
+            __threadfence();
+            if (atomicAdd(e.ticket, 1u) == gridDim.x * gridDim.y - 1) {
+                *e.ticket = 0u;  // the next call's count (read by no other CTA of this call)
+                __threadfence_system();
+                for (int p = 0; p < e.world; ++p)
+                    if (p != e.rank) *reinterpret_cast<volatile unsigned *>(e.flags_peer[p] + e.rank) = e.epoch;
+            }
+            // Collect every peer's flag of this call.
+            int ok = *reinterpret_cast<volatile int *>(e.err) == 0;
+            const unsigned long long t0 = global_ns();
+            for (int p = 0; p < e.world && ok; ++p) {
+                if (p == e.rank) continue;
+                for (uint32_t i = 0;; ++i) {
+                    if ((int)(ld_acquire_sys_u32(e.flags_local + p) - e.epoch) >= 0) break;
+                    if ((i & 63u) == 63u && global_ns() - t0 > kWaitLimitNs) {
+                        atomicCAS(e.err, 0, kSiteEpPeerTile);
+                        ok = 0;
+                        break;
+                    }
                 }
             }
+            s_ok = ok;
         }
-        __threadfence_system();
-        s_ok = ok;
-    }
-    __syncthreads();
-    if (!s_ok) {
-        if (threadIdx.x == 0 && e.host_err) *reinterpret_cast<volatile int *>(e.host_err) = kSiteEpPeerTile;
-        return;
+        __syncthreads();
+        if (!s_ok) {
+            if (threadIdx.x == 0 && e.host_err) *reinterpret_cast<volatile int *>(e.host_err) = kSiteEpPeerTile;
+            return;
+        }
     }
     if (h >= H) return;
     float acc = 0.0f;
@@ -154,6 +166,8 @@ bool ep_next_call(nvfp4_ep *ep, int tokens, int hidden, EpArgs *out) {
         e.flags_peer[p] = reinterpret_cast<unsigned *>(ep->peer[p] + ep->flags_offset());
     }
     e.flags_local = reinterpret_cast<unsigned *>(ep->local + ep->flags_offset());
+    e.ticket = reinterpret_cast<unsigned *>(ep->local + ep->flags_offset() +
+                                            static_cast<size_t>(ep->world) * ep->max_tiles * sizeof(unsigned));
     e.epoch = ep->epoch;
     e.rank = ep->rank;
     e.world = ep->world;
