@@ -49,7 +49,7 @@ def ep_banks(cuda_runtime, ep_host):
         bank.close()
 
 
-@pytest.mark.parametrize("T", [1, 16, 32, 200])
+@pytest.mark.parametrize("T", [1, 16, 32, 48, 64, 200])
 def test_two_ranges_add_up_to_the_layer(cuda_runtime, ep_host, ep_banks, T):
     import torch
 

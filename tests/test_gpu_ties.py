@@ -135,7 +135,7 @@ def _assert_ties_present(ref, experts):
 
 
 @pytest.mark.parametrize("kernels", ["tensor_core", "in_register", "fused_token"])
-@pytest.mark.parametrize("T", [1, 4, 32])
+@pytest.mark.parametrize("T", [1, 4, 32, 48])
 def test_decode_ties(cuda_runtime, tie_bank64, tie_host64, kernels, T):
     tie_bank64.set_decode_kernels(kernels)
     try:
@@ -152,7 +152,7 @@ def test_prefill_ties(cuda_runtime, tie_bank64, tie_host64, T):
     _assert_ties_present(ref, tie_host64.experts)
 
 
-@pytest.mark.parametrize("T", [1, 32, 65])
+@pytest.mark.parametrize("T", [1, 32, 64, 65])
 def test_ties_256_experts(cuda_runtime, tie_bank256, tie_host256, T):
     """256 experts: the zero token ties 254 logits at 0, beyond the prefill
     selection's 64-candidate list (its streaming fallback)."""

@@ -52,7 +52,7 @@ struct nvfp4_moe_bank {
     int terms_x = 4, terms_act = 3;
     int scratch_terms_x = 0, scratch_terms_act = 0;
     // Decode expert-GEMV variant: NVFP4_DECODE_KERNELS_TENSOR_CORE (calls of
-    // up to kDecodeTcMaxTokens tokens on shapes with prefill kernels),
+    // 4 to kDecodeMaxTokens tokens on shapes with prefill kernels),
     // NVFP4_DECODE_KERNELS_IN_REGISTER, or NVFP4_DECODE_KERNELS_FUSED_TOKEN
     // (tensor-core, and one-token calls as one persistent kernel).
     int decode_kernels = NVFP4_DECODE_KERNELS_TENSOR_CORE;
@@ -197,7 +197,7 @@ constexpr int kDecodeTcMinTokens = 4;
 
 bool use_tensor_core_decode(const nvfp4_moe_bank *bank, int tokens) {
     return bank->decode_kernels != NVFP4_DECODE_KERNELS_IN_REGISTER && bank->tc_ready &&
-           tokens >= kDecodeTcMinTokens && tokens <= kDecodeTcMaxTokens;
+           tokens >= kDecodeTcMinTokens && tokens <= kDecodeMaxTokens;
 }
 
 // One-token calls of a bank that computes every expert run as one persistent
@@ -284,6 +284,7 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
         ta.E = E;
         ta.H = H;
         ta.I = I;
+        ta.T = tokens;
         ta.shared_last = bank->shared_here ? 1 : 0;
         ta.s = bank->ds;
         ta.sfa[0] = bank->sf_atoms[0];

@@ -35,9 +35,10 @@ struct RouteSelectSmem {
     int cnt[256];
     int off[257];
     int aidx[256];
+    int aidx1[256];          // split by token half: the expert's half-1 group (after every half-0 group)
     unsigned long long tokmask[256];
     float invd[257];
-    int nrouted;
+    int nrouted, nrouted1;
 };
 
 // Top-8 of token t by one warp from its logits in global memory: lane
@@ -122,6 +123,10 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
     const DecodeScratch &s = a.s;
     const int E = a.E, T = a.T;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // Tensor-core calls above kDecodeTcMaxTokens tokens: an expert's tokens
+    // 0-31 and 32-63 form separate groups (at most 32 tokens each, one
+    // 128-row tile of terms), every half-0 group listed first.
+    const bool split = a.quantize_x && T > kDecodeTcMaxTokens;
 #pragma unroll 1
     for (int e = threadIdx.x; e < 256; e += blockDim.x) {
         sm.cnt[e] = 0;
@@ -137,63 +142,90 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
     __syncthreads();
     // Exclusive scans (counts -> offsets, local non-empty -> compact index).
     if (warp == 0) {
-        int loc[8], aloc[8];
-        int sum = 0, asum = 0;
+        // act: the expert has a group here (split: tokens of half 0); act1:
+        // its half-1 group (split only).
+        auto acts = [&](int e, int &act, int &act1) {
+            const bool own = e < E && e >= a.e_first && e < a.e_first + a.e_count;
+            const unsigned long long m = e < E ? sm.tokmask[e] : 0ull;
+            act = own && (split ? (m & 0xFFFFFFFFull) != 0ull : sm.cnt[e] > 0) ? 1 : 0;
+            act1 = own && split && (m >> 32) != 0ull ? 1 : 0;
+        };
+        int loc[8], aloc[8], aloc1[8];
+        int sum = 0, asum = 0, asum1 = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane * 8 + i;
             const int c = e < E ? sm.cnt[e] : 0;
-            const int act = (c > 0 && e >= a.e_first && e < a.e_first + a.e_count) ? 1 : 0;
+            int act, act1;
+            acts(e, act, act1);
             loc[i] = sum;
             aloc[i] = asum;
+            aloc1[i] = asum1;
             sum += c;
             asum += act;
+            asum1 += act1;
         }
-        int inc = sum, ainc = asum;
+        int inc = sum, ainc = asum, ainc1 = asum1;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
             const int o = __shfl_up_sync(0xffffffffu, inc, off);
             const int ao = __shfl_up_sync(0xffffffffu, ainc, off);
+            const int ao1 = __shfl_up_sync(0xffffffffu, ainc1, off);
             if (lane >= off) {
                 inc += o;
                 ainc += ao;
+                ainc1 += ao1;
             }
         }
-        const int excl = inc - sum, aexcl = ainc - asum;
+        const int excl = inc - sum, aexcl = ainc - asum, aexcl1 = ainc1 - asum1;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane * 8 + i;
             if (e < E) {
-                const int c = sm.cnt[e];
-                const int act = (c > 0 && e >= a.e_first && e < a.e_first + a.e_count) ? 1 : 0;
+                int act, act1;
+                acts(e, act, act1);
                 sm.off[e] = excl + loc[i];
                 sm.aidx[e] = act ? aexcl + aloc[i] : -1;
+                sm.aidx1[e] = act1 ? aexcl1 + aloc1[i] : -1;
             }
         }
         if (lane == 31) {
             sm.off[E] = inc;
             sm.nrouted = ainc;
+            sm.nrouted1 = ainc1;
         }
     }
     __syncthreads();
     const int nrouted = sm.nrouted;
-    const int nact = nrouted + (a.shared_here ? 1 : 0);
+    // Group order: routed (half 0 when split), the shared expert's; then,
+    // when split, the half-1 groups likewise.
+    const int n0 = nrouted + (a.shared_here ? 1 : 0);
+    const int nrouted1 = split ? sm.nrouted1 : 0;
+    const int nact = split ? n0 + nrouted1 + (a.shared_here ? 1 : 0) : n0;
 #pragma unroll 1
     for (int e = threadIdx.x; e < E; e += blockDim.x) {
         s.counts[e] = sm.cnt[e];
         s.offsets[e] = sm.off[e];
+        const unsigned long long m = sm.tokmask[e];
         const int ai = sm.aidx[e];
         if (ai >= 0) {
             s.active_expert[ai] = e;
             s.tok_start[ai] = sm.off[e];
-            s.tok_count[ai] = sm.cnt[e];
+            s.tok_count[ai] = split ? __popcll(m & 0xFFFFFFFFull) : sm.cnt[e];
+        }
+        if (split && sm.aidx1[e] >= 0) {
+            const int ai1 = n0 + sm.aidx1[e];
+            s.active_expert[ai1] = e;
+            s.tok_start[ai1] = sm.off[e] + __popcll(m & 0xFFFFFFFFull);
+            s.tok_count[ai1] = __popcll(m >> 32);
         }
     }
     if (threadIdx.x == 0) {
         s.offsets[E] = sm.off[E];
         *s.n_active = nact;
+        *s.n_half0 = n0;
     }
-    // coef_tab is read only at the (active expert, token) pairs written below.
+    // coef_tab is read only at the (active group, token) pairs written below.
 #pragma unroll 1
     for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
         const int t = i / kTopK;
@@ -202,24 +234,30 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
         const int pos = sm.off[e] + rank;
         s.perm[pos] = i;
         s.tok_list[pos] = t;
-        const int ai = sm.aidx[e];
+        const int ai = split && t >= kDecodeTcMaxTokens ? (sm.aidx1[e] >= 0 ? n0 + sm.aidx1[e] : -1) : sm.aidx[e];
         s.inv_pos[i] = ai >= 0 ? pos : -1;
         s.slot_group[pos] = ai;
         if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = sm.w[i] * sm.invd[e];
     }
     if (a.shared_here) {
-        const int ai = nrouted;
+        const int ai0 = nrouted, ai1 = n0 + nrouted1;
 #pragma unroll 1
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
             const int pos = T * kTopK + t;
+            const int ai = split && t >= kDecodeTcMaxTokens ? ai1 : ai0;
             s.tok_list[pos] = t;
             s.slot_group[pos] = ai;
             s.coef_tab[ai * kDecodeMaxTokens + t] = sm.shared_w[t] * sm.invd[E];
         }
         if (threadIdx.x == 0) {
-            s.active_expert[ai] = E;
-            s.tok_start[ai] = T * kTopK;
-            s.tok_count[ai] = T;
+            s.active_expert[ai0] = E;
+            s.tok_start[ai0] = T * kTopK;
+            s.tok_count[ai0] = split ? kDecodeTcMaxTokens : T;
+            if (split) {
+                s.active_expert[ai1] = E;
+                s.tok_start[ai1] = T * kTopK + kDecodeTcMaxTokens;
+                s.tok_count[ai1] = T - kDecodeTcMaxTokens;
+            }
         }
     }
 }
@@ -516,9 +554,9 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
             for (int j = 0; j < kDecodeTcTerms; ++j) {
                 uint32_t c0, c1;
                 const uint32_t sc = quantize_block_term(v, g, c0, c1);
-                const int n = kDecodeTcTerms * t + j;
+                const int n = kDecodeTcTerms * t + j;  // rows of token half n / 128 in its own tile
                 *reinterpret_cast<uint2 *>(s.xq_tc + (size_t)n * (H / 2) + 8 * b) = make_uint2(c0, c1);
-                s.xsf_tc[sf_atom_byte(n, b)] = static_cast<uint8_t>(sc);
+                s.xsf_tc[(size_t)(n >> 7) * (H / 64) * 512 + sf_atom_byte(n & 127, b)] = static_cast<uint8_t>(sc);
             }
         }
     }
@@ -615,24 +653,24 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
     s.perm = reinterpret_cast<int *>(take(T * kTopK * 4));
     s.inv_pos = reinterpret_cast<int *>(take(T * kTopK * 4));
     s.n_active = reinterpret_cast<int *>(take(4));
-    s.active_expert = reinterpret_cast<int *>(take((size_t)(E + 1) * 4));
-    s.tok_start = reinterpret_cast<int *>(take((size_t)(E + 1) * 4));
-    s.tok_count = reinterpret_cast<int *>(take((size_t)(E + 1) * 4));
+    s.n_half0 = reinterpret_cast<int *>(take(4));
+    s.active_expert = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
+    s.tok_start = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
+    s.tok_count = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
     s.tok_list = reinterpret_cast<int *>(take(T * kSlots * 4));
-    s.coef_tab = reinterpret_cast<float *>(take((size_t)(E + 1) * T * 4));
+    s.coef_tab = reinterpret_cast<float *>(take((size_t)2 * (E + 1) * T * 4));
     s.ticket = reinterpret_cast<unsigned *>(take(kRouteTickets * 4));
     s.error = reinterpret_cast<int *>(take(4));
     s.slot_group = reinterpret_cast<int *>(take(T * kSlots * 4));
     s.act = reinterpret_cast<__half *>(take(T * kSlots * (size_t)I * 2));
     s.ypart = reinterpret_cast<float *>(take(T * kSlots * (size_t)H * 4));
     s.tile_count = reinterpret_cast<unsigned *>(take((size_t)(H / 64 + 1) * 4));
-    const size_t Ttc = kDecodeTcMaxTokens;
-    s.xq_tc = take((size_t)kDecodeTcTerms * Ttc * (H / 2));
-    s.xsf_tc = take((size_t)(H / 64) * 512);
-    s.gx_tc = reinterpret_cast<float *>(take(Ttc * 4));
-    s.aq_tc = take((size_t)kDecodeTcTerms * Ttc * kSlots * (I / 2));
-    s.asf_tc = take((size_t)(E + 1) * (I / 64) * 512);
-    s.ga_tc = reinterpret_cast<float *>(take(Ttc * kSlots * 4));
+    s.xq_tc = take((size_t)kDecodeTcTerms * T * (H / 2));
+    s.xsf_tc = take((size_t)2 * (H / 64) * 512);
+    s.gx_tc = reinterpret_cast<float *>(take(T * 4));
+    s.aq_tc = take((size_t)kDecodeTcTerms * T * kSlots * (I / 2));
+    s.asf_tc = take((size_t)2 * (E + 1) * (I / 64) * 512);
+    s.ga_tc = reinterpret_cast<float *>(take(T * kSlots * 4));
     return off;
 }
 

@@ -18,7 +18,7 @@
 //                             kFusedCombineMaxTokens tokens the CTA that
 //                             finishes an output tile's last group also
 //                             combines that tile (no combine launch);
-//   tensor-core (calls of up to kDecodeTcMaxTokens tokens on the shapes
+//   tensor-core (calls of 4 to kDecodeMaxTokens tokens on the shapes
 //   decode_tc_supported accepts; the routing kernel also writes x as four
 //   NVFP4 terms per token):
 //     moe_gate_up_tc_kernel   gate/up on tcgen05 block-scaled MMA; the four
@@ -59,11 +59,15 @@ struct DecodeScratch {
     int *perm;              // [T*8]
     int *inv_pos;           // [T*8] position of (token, slot) in perm order, -1 if not computed here
     int *n_active;          // [1]
-    int *active_expert;     // [E+1]
-    int *tok_start;         // [E+1]
-    int *tok_count;         // [E+1]
+    // Active groups: one per computed expert; tensor-core calls of more than
+    // kDecodeTcMaxTokens tokens split each expert by token half (tokens
+    // 0-31, then 32-63), every half-0 group listed before every half-1 group.
+    int *n_half0;           // [1] groups of the first token half (tensor-core calls above 32 tokens)
+    int *active_expert;     // [2(E+1)]
+    int *tok_start;         // [2(E+1)]
+    int *tok_count;         // [2(E+1)]
     int *tok_list;          // [T*9]
-    float *coef_tab;        // [(E+1)][kDecodeMaxTokens]
+    float *coef_tab;        // [2(E+1)][kDecodeMaxTokens]
     unsigned *ticket;       // [kRouteTickets] dispatch ticket, then one per 4-token block
     int *error;             // [1] device-side wait timeout flag
     int *slot_group;        // [T*9] active-group index of each dispatch position, -1 if not computed here
@@ -73,11 +77,11 @@ struct DecodeScratch {
     // Tensor-core variant: activation terms. Row 4*t + j of a B tile is term j
     // of token (or slot) t; scale bytes are stored in tcgen05 atom layout
     // [K/64][512 B] per 128-row tile: byte (n%32)*16 + (n/32)*4 + (k/16)%4.
-    uint8_t *xq_tc;         // [128][H/2]               terms of x by token
-    uint8_t *xsf_tc;        // [H/64][512]              their scale atoms
-    float *gx_tc;           // [kDecodeTcMaxTokens]     global scale of each token row
+    uint8_t *xq_tc;         // [256][H/2]               terms of x by token (rows 128h.. : token half h)
+    uint8_t *xsf_tc;        // [2][H/64][512]           their scale atoms, one 128-row tile per half
+    float *gx_tc;           // [kDecodeMaxTokens]       global scale of each token row
     uint8_t *aq_tc;         // [T*9*4][I/2]             terms of the activations by slot
-    uint8_t *asf_tc;        // [E+1][I/64][512]         scale atoms per active group (rows from tok_start)
+    uint8_t *asf_tc;        // [2(E+1)][I/64][512]      scale atoms per active group (rows from tok_start)
     float *ga_tc;           // [T*9]                    global scale of each slot row
     int *host_error;        // pinned host-mapped word the host reads at synchronize, or nullptr
 };
@@ -133,6 +137,7 @@ struct DecodeTcArgs {
     const float *inv_scales;  // [3][E+1]
     int E, H, I;
     int shared_last;          // 1: the shared expert is computed here (always the last active group)
+    int T;                    // tokens of the call (above kDecodeTcMaxTokens: groups by token half)
     DecodeScratch s;
 };
 

@@ -155,13 +155,35 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     const int mtiles = a.I / kTile;
     const int total = *s.n_active * mtiles;
-    // Strided items over the fewest CTAs that need no more waves than the
-    // whole grid: every working CTA then walks the same number of items (or
-    // one fewer), and the weight stream of the SMs left idle goes to them
-    // instead of to a last partial wave.
-    const int waves = (total + (int)gridDim.x - 1) / (int)gridDim.x;
-    const int ctas = waves > 0 ? (total + waves - 1) / waves : 0;
-    const int first = (int)blockIdx.x < ctas ? (int)blockIdx.x : total;  // this CTA's first item
+    // Calls above kDecodeTcMaxTokens tokens: the items of the half-0 groups
+    // ([0, hi)) and of the half-1 groups ([lo, total)) go to two sets of CTAs
+    // in proportion to their counts (the launch gives at least two CTAs);
+    // each set reads its half's 128-row tile of x's terms.
+    int lo = 0, hi = total, nctas = (int)gridDim.x, rank = (int)blockIdx.x, half = 0;
+    if (a.T > kDecodeTcMaxTokens) {
+        const int t0 = *s.n_half0 * mtiles;
+        int g0 = total > 0 ? (int)(((long long)gridDim.x * t0 + total / 2) / total) : 0;
+        if (t0 > 0 && g0 < 1) g0 = 1;
+        if (t0 < total && g0 > (int)gridDim.x - 1) g0 = (int)gridDim.x - 1;
+        if (rank < g0) {
+            hi = t0;
+            nctas = g0;
+        } else {
+            half = 1;
+            lo = t0;
+            rank -= g0;
+            nctas = (int)gridDim.x - g0;
+        }
+    }
+    // Within a set, strided items over the fewest CTAs that need no more
+    // waves than the set: every working CTA then walks the same number of
+    // items (or one fewer), and the weight stream of the SMs left idle goes
+    // to them instead of to a last partial wave.
+    const int span = hi - lo;
+    const int waves = nctas > 0 ? (span + nctas - 1) / nctas : 0;
+    const int ctas = waves > 0 ? (span + waves - 1) / waves : 0;
+    const bool works = rank < ctas;
+    const int first = works ? lo + rank : hi;  // this CTA's first item
     const int kstages = a.H / kStageK;
     const int kw = a.H / 64;
 
@@ -169,11 +191,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // ------------------------------------------------------ producer
         uint32_t it = 0;
         bool ok = true;
-        if (lane == 0 && (int)blockIdx.x < ctas) {
+        if (lane == 0 && works) {
             mbar_arrive_expect_tx(sfb_full, kw * 512);
-            bulk_g2s(sfb_stage, a.sfb, kw * 512, sfb_full);
+            bulk_g2s(sfb_stage, a.sfb + (size_t)half * kw * 512, kw * 512, sfb_full);
         }
-        for (int item = first; item < total && ok; item += ctas) {
+        for (int item = first; item < hi && ok; item += ctas) {
             const Item ti = load_item(s, item, mtiles);
             const int arow = ti.e * a.I + ti.mt * kTile;
             const size_t sfa_off = (size_t)(arow / kTile) * kw * 512;
@@ -197,14 +219,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     mbar_arrive_expect_tx(full + st, 3 * kTileBytes);
                     tma_load_2d(stage, &tm_g, full + st, ks * 128, arow);
                     tma_load_2d(stage + kTileBytes, &tm_u, full + st, ks * 128, arow);
-                    tma_load_2d(stage + 2 * kTileBytes, &tm_b, full + st, ks * 128, 0);
+                    tma_load_2d(stage + 2 * kTileBytes, &tm_b, full + st, ks * 128, kTile * half);
                 }
             }
         }
         if (!ok || *reinterpret_cast<volatile int *>(err) != 0) {
             // Drain the copies still in flight before the CTA exits.
             if (lane == 0) {
-                if ((int)blockIdx.x < ctas) mbar_wait_drain(sfb_full, 0);
+                if (works) mbar_wait_drain(sfb_full, 0);
                 const uint32_t first = it > (uint32_t)S ? it - S : 0u;
                 for (uint32_t k = first; k < it; ++k) {
                     mbar_wait_drain(full + (k % S), (k / S) & 1u);
@@ -219,11 +241,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             const uint32_t smem_base = smem_u32(smem);
             uint32_t it = 0, tcount = 0;
             bool ok = true;
-            if ((int)blockIdx.x < ctas) {
+            if (works) {
                 ok = mbar_wait(sfb_ready, 0, err, kSiteGemmFull);
                 tc::fence_after_sync();
             }
-            for (int item = first; item < total && ok; item += ctas, ++tcount) {
+            for (int item = first; item < hi && ok; item += ctas, ++tcount) {
                 if (tcount > 0 && !mbar_wait(acc_empty, (tcount - 1) & 1u, err, kSiteGemmAccEmpty)) {
                     ok = false;
                     break;
@@ -270,7 +292,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bool ok = true;
         // First x's kw scale atoms (every item's B, kw a multiple of 4),
         // four per store.
-        if ((int)blockIdx.x < ctas) {
+        if (works) {
             ok = __all_sync(0xffffffffu, mbar_wait(sfb_full, 0, err, kSiteGemmFull));
             if (ok) {
 #pragma unroll 1
@@ -282,7 +304,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (lane == 0) mbar_arrive(sfb_ready);
             }
         }
-        for (int item = first; item < total && ok; item += ctas) {
+        for (int item = first; item < hi && ok; item += ctas) {
             for (int ks = 0; ks < kstages; ++ks, ++it) {
                 const int st = it % S;
                 if (!__all_sync(0xffffffffu, mbar_wait(sfa_in + st, (it / S) & 1u, err, kSiteGemmFull))) {
@@ -303,13 +325,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const int et = threadIdx.x - 64;
         const uint32_t lane_base = tmem + ((uint32_t)(32 * sub) << 16);
         uint32_t tcount = 0;
-        for (int item = first; item < total; item += ctas, ++tcount) {
+        for (int item = first; item < hi; item += ctas, ++tcount) {
             const Item ti = load_item(s, item, mtiles);
             int *ctok = col_tok + 32 * (tcount & 1);
             float *cscale = col_scale + 32 * (tcount & 1);
             if (et < ti.ntok) {
                 const int t = s.tok_list[ti.tstart + et];
-                ctok[et] = t;
+                ctok[et] = t - kDecodeTcMaxTokens * half;  // its column block in this half's tile
                 cscale[et] = s.gx_tc[t];
             }
             const float ig = a.inv_scales[ti.e], iu = a.inv_scales[(a.E + 1) + ti.e];
@@ -818,9 +840,15 @@ cudaError_t launch_tc(Kern kernel, size_t smem, std::atomic<uint64_t> &done, int
 }
 
 int tc_grid(int T, int E, int mtiles, int sms) {
-    const int routed_ub = E < T * kTopK ? E : T * kTopK;
-    const int items_ub = (routed_ub + 1) * mtiles;
-    return items_ub < sms ? items_ub : sms;
+    // Upper bound on the active groups: routed experts plus the shared one,
+    // per token half above kDecodeTcMaxTokens tokens.
+    auto groups = [&](int t) { return (E < t * kTopK ? E : t * kTopK) + 1; };
+    const int groups_ub = T > kDecodeTcMaxTokens ? groups(kDecodeTcMaxTokens) + groups(T - kDecodeTcMaxTokens)
+                                                 : groups(T);
+    const int items_ub = groups_ub * mtiles;
+    const int grid = items_ub < sms ? items_ub : sms;
+    // The gate/up kernel gives each token half at least one CTA.
+    return T > kDecodeTcMaxTokens && grid < 2 ? 2 : grid;
 }
 
 }  // namespace
@@ -831,16 +859,16 @@ bool decode_tc_supported(int H, int I) {
 
 cudaError_t make_decode_tc_maps(DecodeTcMaps &m, const DecodeScratch &s, int H, int I) {
     if (H % 256 != 0 || I % 256 != 0) return cudaErrorInvalidValue;
-    cudaError_t err = make_tensor_map_u8(&m.xq, s.xq_tc, H / 2, H / 2, (uint64_t)kDecodeTcTerms * kDecodeTcMaxTokens,
+    cudaError_t err = make_tensor_map_u8(&m.xq, s.xq_tc, H / 2, H / 2, (uint64_t)kDecodeTcTerms * kDecodeMaxTokens,
                                          128, kTile, CU_TENSOR_MAP_SWIZZLE_128B);
     if (err != cudaSuccess) return err;
     return make_tensor_map_u8(&m.aq, s.aq_tc, I / 2, I / 2,
-                              (uint64_t)kDecodeTcTerms * kDecodeTcMaxTokens * kSlots, 128, kTile,
+                              (uint64_t)kDecodeTcTerms * kDecodeMaxTokens * kSlots, 128, kTile,
                               CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 cudaError_t launch_quantize_act_tc(const DecodeScratch &s, int T, int I, cudaStream_t stream) {
-    if (T < 1 || T > kDecodeTcMaxTokens || I % 256 != 0) return cudaErrorInvalidValue;
+    if (T < 1 || T > kDecodeMaxTokens || I % 256 != 0) return cudaErrorInvalidValue;
     const int rows = T * kSlots;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((rows + 7) / 8);
@@ -856,7 +884,7 @@ cudaError_t launch_quantize_act_tc(const DecodeScratch &s, int T, int I, cudaStr
 
 cudaError_t launch_gate_up_tc(const CUtensorMap &w_gate, const CUtensorMap &w_up, const DecodeTcMaps &m,
                               const DecodeTcArgs &a, int T, int sms, cudaStream_t stream) {
-    if (T < 1 || T > kDecodeTcMaxTokens || !decode_tc_supported(a.H, a.I)) return cudaErrorInvalidValue;
+    if (T < 1 || T > kDecodeMaxTokens || T != a.T || !decode_tc_supported(a.H, a.I)) return cudaErrorInvalidValue;
     static std::atomic<uint64_t> done{0};
     return launch_tc(moe_gate_up_tc_kernel, kGuSmem, done, tc_grid(T, a.E, a.I / kTile, sms), stream, w_gate, w_up,
                      m.xq, a);
@@ -864,7 +892,7 @@ cudaError_t launch_gate_up_tc(const CUtensorMap &w_gate, const CUtensorMap &w_up
 
 cudaError_t launch_down_tc(const CUtensorMap &w_down, const DecodeTcMaps &m, const DecodeTcArgs &a, int T, int sms,
                            cudaStream_t stream) {
-    if (T < 1 || T > kDecodeTcMaxTokens || !decode_tc_supported(a.H, a.I)) return cudaErrorInvalidValue;
+    if (T < 1 || T > kDecodeMaxTokens || T != a.T || !decode_tc_supported(a.H, a.I)) return cudaErrorInvalidValue;
     const int grid = tc_grid(T, a.E, a.H / kTile, sms);
     if (a.I == 256) {
         static std::atomic<uint64_t> done{0};
