@@ -587,7 +587,7 @@ NVFP4_API nvfp4_status nvfp4_moe_finalize_bf16(
  * tokens). TENSOR_CORE (default) streams the weights through tcgen05
  * block-scaled NVFP4 MMAs with the activations as four NVFP4 terms per row
  * (relative RMSE about 1e-4 against FP32 activations); it serves calls of 4
- * to 32 tokens on banks with hidden a multiple of 256 up to 2048 and
+ * to 64 tokens on banks with hidden a multiple of 256 up to 2048 and
  * intermediate 256 or 512, and other calls use IN_REGISTER, which decodes
  * E2M1/E4M3 to f16 in registers and keeps the activations in f16 (faster
  * below 4 tokens). FUSED_TOKEN is TENSOR_CORE except for one-token calls of

@@ -294,9 +294,20 @@ void enqueue_decode(nvfp4_moe_bank *bank, const void *x, int x_is_f32, const voi
             check_cuda(launch_gate_up_tc(bank->pmaps.w[0], bank->pmaps.w[1], bank->tc_maps, ta, tokens, sms, s),
                        "moe_gate_up_tc_kernel");
         });
+        // Above kDecodeTcMaxTokens tokens the activation quantiser and the
+        // down kernel walk the down groups (an expert's two token halves
+        // merged where they fit one tile).
+        DecodeScratch dv = bank->ds;
+        if (tokens > kDecodeTcMaxTokens) {
+            dv.n_active = dv.n_down;
+            dv.active_expert = dv.down_expert;
+            dv.tok_start = dv.down_start;
+            dv.tok_count = dv.down_count;
+        }
         rt->profiled_kernel("moe_quantize_act", stream, [&](cudaStream_t s) {
-            check_cuda(launch_quantize_act_tc(bank->ds, tokens, I, s), "quantize_act_tc_kernel");
+            check_cuda(launch_quantize_act_tc(dv, tokens, I, s), "quantize_act_tc_kernel");
         });
+        ta.s = dv;
         ta.sfa[0] = bank->sf_atoms[2];
         ta.sfa[1] = bank->sf_atoms[2];
         ta.sfb = bank->ds.asf_tc;

@@ -36,9 +36,10 @@ struct RouteSelectSmem {
     int off[257];
     int aidx[256];
     int aidx1[256];          // split by token half: the expert's half-1 group (after every half-0 group)
+    int didx[256];           // split calls: the expert's first down group
     unsigned long long tokmask[256];
     float invd[257];
-    int nrouted, nrouted1;
+    int nrouted, nrouted1, ndown;
 };
 
 // Top-8 of token t by one warp from its logits in global memory: lane
@@ -143,56 +144,65 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
     // Exclusive scans (counts -> offsets, local non-empty -> compact index).
     if (warp == 0) {
         // act: the expert has a group here (split: tokens of half 0); act1:
-        // its half-1 group (split only).
-        auto acts = [&](int e, int &act, int &act1) {
+        // its half-1 group (split only); dact: its down groups (split only:
+        // one, or one per half above kDecodeTcMaxTokens tokens).
+        auto acts = [&](int e, int &act, int &act1, int &dact) {
             const bool own = e < E && e >= a.e_first && e < a.e_first + a.e_count;
             const unsigned long long m = e < E ? sm.tokmask[e] : 0ull;
-            act = own && (split ? (m & 0xFFFFFFFFull) != 0ull : sm.cnt[e] > 0) ? 1 : 0;
+            const int c = e < E ? sm.cnt[e] : 0;
+            act = own && (split ? (m & 0xFFFFFFFFull) != 0ull : c > 0) ? 1 : 0;
             act1 = own && split && (m >> 32) != 0ull ? 1 : 0;
+            dact = own && split && c > 0 ? (c > kDecodeTcMaxTokens ? 2 : 1) : 0;
         };
-        int loc[8], aloc[8], aloc1[8];
-        int sum = 0, asum = 0, asum1 = 0;
+        int loc[8], aloc[8], aloc1[8], dloc[8];
+        int sum = 0, asum = 0, asum1 = 0, dsum = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane * 8 + i;
             const int c = e < E ? sm.cnt[e] : 0;
-            int act, act1;
-            acts(e, act, act1);
+            int act, act1, dact;
+            acts(e, act, act1, dact);
             loc[i] = sum;
             aloc[i] = asum;
             aloc1[i] = asum1;
+            dloc[i] = dsum;
             sum += c;
             asum += act;
             asum1 += act1;
+            dsum += dact;
         }
-        int inc = sum, ainc = asum, ainc1 = asum1;
+        int inc = sum, ainc = asum, ainc1 = asum1, dinc = dsum;
 #pragma unroll
         for (int off = 1; off < 32; off <<= 1) {
             const int o = __shfl_up_sync(0xffffffffu, inc, off);
             const int ao = __shfl_up_sync(0xffffffffu, ainc, off);
             const int ao1 = __shfl_up_sync(0xffffffffu, ainc1, off);
+            const int dof = __shfl_up_sync(0xffffffffu, dinc, off);
             if (lane >= off) {
                 inc += o;
                 ainc += ao;
                 ainc1 += ao1;
+                dinc += dof;
             }
         }
-        const int excl = inc - sum, aexcl = ainc - asum, aexcl1 = ainc1 - asum1;
+        const int excl = inc - sum, aexcl = ainc - asum, aexcl1 = ainc1 - asum1, dexcl = dinc - dsum;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             const int e = lane * 8 + i;
             if (e < E) {
-                int act, act1;
-                acts(e, act, act1);
+                int act, act1, dact;
+                acts(e, act, act1, dact);
                 sm.off[e] = excl + loc[i];
                 sm.aidx[e] = act ? aexcl + aloc[i] : -1;
                 sm.aidx1[e] = act1 ? aexcl1 + aloc1[i] : -1;
+                sm.didx[e] = dact ? dexcl + dloc[i] : -1;
             }
         }
         if (lane == 31) {
             sm.off[E] = inc;
             sm.nrouted = ainc;
             sm.nrouted1 = ainc1;
+            sm.ndown = dinc;
         }
     }
     __syncthreads();
@@ -219,13 +229,32 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
             s.tok_start[ai1] = sm.off[e] + __popcll(m & 0xFFFFFFFFull);
             s.tok_count[ai1] = __popcll(m >> 32);
         }
+        const int dg = split ? sm.didx[e] : -1;
+        if (dg >= 0) {
+            const int c = sm.cnt[e], lo = __popcll(m & 0xFFFFFFFFull);
+            const bool two = c > kDecodeTcMaxTokens;
+            s.down_expert[dg] = e;
+            s.down_start[dg] = sm.off[e];
+            s.down_count[dg] = two ? lo : c;
+            if (two) {
+                s.down_expert[dg + 1] = e;
+                s.down_start[dg + 1] = sm.off[e] + lo;
+                s.down_count[dg + 1] = c - lo;
+            }
+        }
     }
+    // Split calls: the down kernel's groups follow the routed ones with the
+    // shared expert's two (one per token half).
+    const int ndr = split ? sm.ndown : 0;
     if (threadIdx.x == 0) {
         s.offsets[E] = sm.off[E];
         *s.n_active = nact;
         *s.n_half0 = n0;
+        if (split) *s.n_down = ndr + (a.shared_here ? 2 : 0);
     }
-    // coef_tab is read only at the (active group, token) pairs written below.
+    // coef_tab is read only at the (group, token) pairs written below; the
+    // groups of slot_group and coef_tab are the down kernel's (split calls:
+    // the down groups).
 #pragma unroll 1
     for (int i = threadIdx.x; i < T * kTopK; i += blockDim.x) {
         const int t = i / kTopK;
@@ -234,7 +263,9 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
         const int pos = sm.off[e] + rank;
         s.perm[pos] = i;
         s.tok_list[pos] = t;
-        const int ai = split && t >= kDecodeTcMaxTokens ? (sm.aidx1[e] >= 0 ? n0 + sm.aidx1[e] : -1) : sm.aidx[e];
+        const int dg = sm.didx[e];
+        const int ai = split ? (dg >= 0 ? dg + (sm.cnt[e] > kDecodeTcMaxTokens && t >= kDecodeTcMaxTokens ? 1 : 0) : -1)
+                             : sm.aidx[e];
         s.inv_pos[i] = ai >= 0 ? pos : -1;
         s.slot_group[pos] = ai;
         if (ai >= 0) s.coef_tab[ai * kDecodeMaxTokens + t] = sm.w[i] * sm.invd[e];
@@ -244,7 +275,7 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
 #pragma unroll 1
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
             const int pos = T * kTopK + t;
-            const int ai = split && t >= kDecodeTcMaxTokens ? ai1 : ai0;
+            const int ai = split ? ndr + (t >= kDecodeTcMaxTokens ? 1 : 0) : ai0;
             s.tok_list[pos] = t;
             s.slot_group[pos] = ai;
             s.coef_tab[ai * kDecodeMaxTokens + t] = sm.shared_w[t] * sm.invd[E];
@@ -257,6 +288,11 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
                 s.active_expert[ai1] = E;
                 s.tok_start[ai1] = T * kTopK + kDecodeTcMaxTokens;
                 s.tok_count[ai1] = T - kDecodeTcMaxTokens;
+                for (int h = 0; h < 2; ++h) {
+                    s.down_expert[ndr + h] = E;
+                    s.down_start[ndr + h] = T * kTopK + kDecodeTcMaxTokens * h;
+                    s.down_count[ndr + h] = h == 0 ? kDecodeTcMaxTokens : T - kDecodeTcMaxTokens;
+                }
             }
         }
     }
@@ -657,6 +693,10 @@ size_t decode_scratch_carve(DecodeScratch &s, void *base, int E, int H, int I) {
     s.active_expert = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
     s.tok_start = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
     s.tok_count = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
+    s.n_down = reinterpret_cast<int *>(take(4));
+    s.down_expert = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
+    s.down_start = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
+    s.down_count = reinterpret_cast<int *>(take((size_t)2 * (E + 1) * 4));
     s.tok_list = reinterpret_cast<int *>(take(T * kSlots * 4));
     s.coef_tab = reinterpret_cast<float *>(take((size_t)2 * (E + 1) * T * 4));
     s.ticket = reinterpret_cast<unsigned *>(take(kRouteTickets * 4));

@@ -66,6 +66,14 @@ struct DecodeScratch {
     int *active_expert;     // [2(E+1)]
     int *tok_start;         // [2(E+1)]
     int *tok_count;         // [2(E+1)]
+    // Tensor-core calls above kDecodeTcMaxTokens tokens: the down kernel's
+    // groups (an expert's tokens together up to kDecodeTcMaxTokens, else one
+    // group per token half; B rows are the group's own slot rows, so one tile
+    // serves any 32 of them). slot_group and coef_tab then index these.
+    int *n_down;            // [1]
+    int *down_expert;       // [2(E+1)]
+    int *down_start;        // [2(E+1)]
+    int *down_count;        // [2(E+1)]
     int *tok_list;          // [T*9]
     float *coef_tab;        // [2(E+1)][kDecodeMaxTokens]
     unsigned *ticket;       // [kRouteTickets] dispatch ticket, then one per 4-token block
