@@ -244,7 +244,7 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
         }
     }
     // Split calls: the down kernel's groups follow the routed ones with the
-    // shared expert's two (one per token half).
+    // shared expert's two (tokens 32.., then 0-31).
     const int ndr = split ? sm.ndown : 0;
     if (threadIdx.x == 0) {
         s.offsets[E] = sm.off[E];
@@ -275,7 +275,7 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
 #pragma unroll 1
         for (int t = threadIdx.x; t < T; t += blockDim.x) {
             const int pos = T * kTopK + t;
-            const int ai = split ? ndr + (t >= kDecodeTcMaxTokens ? 1 : 0) : ai0;
+            const int ai = split ? ndr + (t >= kDecodeTcMaxTokens ? 0 : 1) : ai0;
             s.tok_list[pos] = t;
             s.slot_group[pos] = ai;
             s.coef_tab[ai * kDecodeMaxTokens + t] = sm.shared_w[t] * sm.invd[E];
@@ -288,10 +288,12 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
                 s.active_expert[ai1] = E;
                 s.tok_start[ai1] = T * kTopK + kDecodeTcMaxTokens;
                 s.tok_count[ai1] = T - kDecodeTcMaxTokens;
+                // Its second half first: the down kernel spreads the last
+                // group's tiles (here the full 32-token half) over its CTAs.
                 for (int h = 0; h < 2; ++h) {
-                    s.down_expert[ndr + h] = E;
-                    s.down_start[ndr + h] = T * kTopK + kDecodeTcMaxTokens * h;
-                    s.down_count[ndr + h] = h == 0 ? kDecodeTcMaxTokens : T - kDecodeTcMaxTokens;
+                    s.down_expert[ndr + 1 - h] = E;
+                    s.down_start[ndr + 1 - h] = T * kTopK + kDecodeTcMaxTokens * h;
+                    s.down_count[ndr + 1 - h] = h == 0 ? kDecodeTcMaxTokens : T - kDecodeTcMaxTokens;
                 }
             }
         }

@@ -472,14 +472,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const int mtiles = a.H / kTile;
     const int total = *s.n_active * mtiles;
     // Items over the fewest CTAs that need no more waves than the grid, each
-    // CTA taking the same count (or one fewer). The shared expert's group
-    // (the last, with a row for every token) has the costliest items: its
-    // tiles go one each to evenly spaced CTAs, first in their lists, and the
-    // other items split into contiguous runs around them, so consecutive
-    // items of a CTA mostly share their group.
+    // CTA taking the same count (or one fewer). The shared expert's groups
+    // (the last one, or above kDecodeTcMaxTokens tokens the last two: a row
+    // for every token) have the costliest items: their tiles go one each to
+    // evenly spaced CTAs, first in their lists, and the other items split
+    // into contiguous runs around them, so consecutive items of a CTA mostly
+    // share their group.
     const int waves = (total + (int)gridDim.x - 1) / (int)gridDim.x;
     const int ctas = waves > 0 ? (total + waves - 1) / waves : 0;
-    const int sh = a.shared_last && total > 0 && mtiles <= ctas ? mtiles : 0;
+    const int shg = a.T > kDecodeTcMaxTokens && 2 * mtiles <= ctas ? 2 : 1;
+    const int sh = a.shared_last && total > 0 && shg * mtiles <= ctas ? shg * mtiles : 0;
     const int routed = total - sh;
     int sh_lo = 0, sh_hi = 0, r_lo = 0, r_hi = 0;
     if ((int)blockIdx.x < ctas) {
