@@ -146,33 +146,30 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
         // act: the expert has a group here (split: tokens of half 0); act1:
         // its half-1 group (split only); dact: its down groups (split only:
         // one, or one per half above kDecodeTcMaxTokens tokens).
-        auto acts = [&](int e, int &act, int &act1, int &dact) {
+        auto acts = [&](int e, int &c, int &act, int &act1, int &dact) {
             const bool own = e < E && e >= a.e_first && e < a.e_first + a.e_count;
             const unsigned long long m = e < E ? sm.tokmask[e] : 0ull;
-            const int c = e < E ? sm.cnt[e] : 0;
+            c = e < E ? sm.cnt[e] : 0;
             act = own && (split ? (m & 0xFFFFFFFFull) != 0ull : c > 0) ? 1 : 0;
             act1 = own && split && (m >> 32) != 0ull ? 1 : 0;
             dact = own && split && c > 0 ? (c > kDecodeTcMaxTokens ? 2 : 1) : 0;
         };
-        int loc[8], aloc[8], aloc1[8], dloc[8];
+        // Lane l owns experts 8l .. 8l+7: their sums, an exclusive warp scan
+        // of the sums, then the running offsets. The loops stay rolled: this
+        // code runs once per call with cold instruction caches, where code
+        // size is time (unrolled, the scan took 2 us).
         int sum = 0, asum = 0, asum1 = 0, dsum = 0;
-#pragma unroll
+#pragma unroll 1
         for (int i = 0; i < 8; ++i) {
-            const int e = lane * 8 + i;
-            const int c = e < E ? sm.cnt[e] : 0;
-            int act, act1, dact;
-            acts(e, act, act1, dact);
-            loc[i] = sum;
-            aloc[i] = asum;
-            aloc1[i] = asum1;
-            dloc[i] = dsum;
+            int c, act, act1, dact;
+            acts(lane * 8 + i, c, act, act1, dact);
             sum += c;
             asum += act;
             asum1 += act1;
             dsum += dact;
         }
         int inc = sum, ainc = asum, ainc1 = asum1, dinc = dsum;
-#pragma unroll
+#pragma unroll 1
         for (int off = 1; off < 32; off <<= 1) {
             const int o = __shfl_up_sync(0xffffffffu, inc, off);
             const int ao = __shfl_up_sync(0xffffffffu, ainc, off);
@@ -185,18 +182,22 @@ __device__ __forceinline__ void route_dispatch(const RouteArgs &a, RouteSelectSm
                 dinc += dof;
             }
         }
-        const int excl = inc - sum, aexcl = ainc - asum, aexcl1 = ainc1 - asum1, dexcl = dinc - dsum;
-#pragma unroll
+        int run = inc - sum, arun = ainc - asum, arun1 = ainc1 - asum1, drun = dinc - dsum;
+#pragma unroll 1
         for (int i = 0; i < 8; ++i) {
             const int e = lane * 8 + i;
+            int c, act, act1, dact;
+            acts(e, c, act, act1, dact);
             if (e < E) {
-                int act, act1, dact;
-                acts(e, act, act1, dact);
-                sm.off[e] = excl + loc[i];
-                sm.aidx[e] = act ? aexcl + aloc[i] : -1;
-                sm.aidx1[e] = act1 ? aexcl1 + aloc1[i] : -1;
-                sm.didx[e] = dact ? dexcl + dloc[i] : -1;
+                sm.off[e] = run;
+                sm.aidx[e] = act ? arun : -1;
+                sm.aidx1[e] = act1 ? arun1 : -1;
+                sm.didx[e] = dact ? drun : -1;
             }
+            run += c;
+            arun += act;
+            arun1 += act1;
+            drun += dact;
         }
         if (lane == 31) {
             sm.off[E] = inc;
