@@ -475,10 +475,13 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
         // Several tokens: one FP32 chain per token in the fixed order above.
         // The loop body has no branches (missing tokens of a short block read
         // the block's last token and are not stored), so the four chains
-        // interleave; the format branch sits outside the loop.
-        float acc[kRouteTokens];
+        // interleave; the format branch sits outside the loop. Tokens go in
+        // pairs through the packed f32x2 multiply and add (each element
+        // rounded as the scalar instruction rounds it), half the instructions.
+        static_assert(kRouteTokens % 2 == 0, "token pairs");
+        unsigned long long acc2[kRouteTokens / 2];
 #pragma unroll
-        for (int j = 0; j < kRouteTokens; ++j) acc[j] = 0.0f;
+        for (int j = 0; j < kRouteTokens / 2; ++j) acc2[j] = 0ull;  // (+0, +0)
         const uint16_t *wr = route_w + (size_t)warp * H;
         int xoff[kRouteTokens];
 #pragma unroll
@@ -493,12 +496,15 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
                 float4 xv[kRouteTokens];
 #pragma unroll
                 for (int j = 0; j < kRouteTokens; ++j) xv[j] = load_x(xoff[j] + k);
+                const unsigned long long ww0 = f32x2_pack(w0, w0), ww1 = f32x2_pack(w1, w1);
+                const unsigned long long ww2 = f32x2_pack(w2, w2), ww3 = f32x2_pack(w3, w3);
 #pragma unroll
-                for (int j = 0; j < kRouteTokens; ++j) {
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w0, xv[j].x));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w1, xv[j].y));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w2, xv[j].z));
-                    acc[j] = __fadd_rn(acc[j], __fmul_rn(w3, xv[j].w));
+                for (int j = 0; j < kRouteTokens / 2; ++j) {
+                    const float4 xa = xv[2 * j], xb = xv[2 * j + 1];
+                    acc2[j] = f32x2_add_rn(acc2[j], f32x2_mul_rn(ww0, f32x2_pack(xa.x, xb.x)));
+                    acc2[j] = f32x2_add_rn(acc2[j], f32x2_mul_rn(ww1, f32x2_pack(xa.y, xb.y)));
+                    acc2[j] = f32x2_add_rn(acc2[j], f32x2_mul_rn(ww2, f32x2_pack(xa.z, xb.z)));
+                    acc2[j] = f32x2_add_rn(acc2[j], f32x2_mul_rn(ww3, f32x2_pack(xa.w, xb.w)));
                 }
             }
         };
@@ -511,6 +517,9 @@ __global__ void __launch_bounds__(128) moe_route_kernel(RouteArgs a) {
                                    bf16_bits_to_f32(b.y & 0xFFFFu), bf16_bits_to_f32(b.y >> 16));
             });
         }
+        float acc[kRouteTokens];
+#pragma unroll
+        for (int j = 0; j < kRouteTokens / 2; ++j) f32x2_unpack(acc2[j], acc[2 * j], acc[2 * j + 1]);
 #pragma unroll
         for (int j = 0; j < kRouteTokens; ++j) {
             float v = acc[j];

@@ -88,6 +88,32 @@ __device__ __forceinline__ float bf16_bits_to_f32(uint32_t bits16) {
     return __uint_as_float(bits16 << 16);
 }
 
+// Packed FP32 pairs (sm_100a f32x2 arithmetic): element lo in the low word.
+// Each element is rounded to nearest even exactly as add.rn.f32 / mul.rn.f32
+// round it (subnormals kept), so a pair of independent chains gives the same
+// bits as two scalar chains.
+__device__ __forceinline__ unsigned long long f32x2_pack(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+
+__device__ __forceinline__ void f32x2_unpack(unsigned long long v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+
+__device__ __forceinline__ unsigned long long f32x2_mul_rn(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+__device__ __forceinline__ unsigned long long f32x2_add_rn(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
 // Round-to-nearest-even FP32 -> BF16 bits (finite inputs; NaN stays NaN).
 __device__ __forceinline__ uint16_t f32_to_bf16_bits(float v) {
     return __bfloat16_as_ushort(__float2bfloat16_rn(v));
