@@ -120,14 +120,17 @@ def test_variants_alternate(cuda_runtime, tc_bank, tc_host, T):
 
 @pytest.mark.parametrize("T", [32, 64])
 def test_tensor_core_decode_hot_expert(cuda_runtime, T):
-    """Skewed routing: one expert takes most of the tokens (full 128-row B
-    tiles; at 64 tokens in both token halves)."""
+    """Skewed routing: experts that take most of the tokens (full 128-row B
+    tiles; at 64 tokens experts with more than 32 tokens, whose down
+    products run as two groups, one per token half)."""
     host = synthetic_np.make_bank(64, 256, 256, 63, skew=True)
     bank = upload_bank(cuda_runtime, host)
     got, xf, rf = _run(bank, host, T, 650)
     ref = moe_layer(host, xf, rf)
     _check_routing(bank, ref, T)
     assert ref.counts.max() >= T // 2
+    if T > 32:
+        assert (ref.counts > 32).any()
     assert rel_rmse(got, ref.out) <= REL_RMSE_TOL
     assert max_abs_rel(got, ref.out) <= MAX_ABS_REL_TOL
     bank.close()
